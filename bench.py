@@ -1,0 +1,436 @@
+#!/usr/bin/env python
+"""Benchmark of the EXL3 trellis-decode GEMV path on B200 (driver contract: one JSON line).
+
+Workload (the config its metric is quoted on): the dense EXL3 GEMV
+sweep, shapes (out x in) 2048x7168, 7168x2048, 4096x14336, rates K in {2, 3, 4} (n = 32, 48,
+64), batch M in {1, 2, 4, 8, 16, 64}: 54 projections.  One step runs every projection over a
+ring of distinct weight copies whose total exceeds twice the 126 MB L2, so no launch reads a
+weight another left in L2.  Weights are seeded random trellis words with sign-only scales (the
+reference's synthetic-bank recipe, src/exl3/synth.zig:16-41): the decode cost does not depend on
+the values.  Activations are bf16 N(0,1).
+
+metric: compressed-HBM GB/s of the GEMVs (algorithmic bytes: trellis + suh + svh + x + y per
+launch) over the device time of the step, graph-replayed with inputs resident in HBM.  e2e: the
+same bytes over the time of the same projections called one by one through the C ABI with the
+activations copied from pinned host memory and the outputs copied back, inside the timed region.
+At N > 1 every rank runs its own sweep (the GEMV does not shard: replicas), value sums the ranks'
+bytes over the slowest rank's time.  The MoE decode layer rides along as "moe".
+
+--impl reference times the reference's CPU decode + matmul (`format.project`,
+src/exl3/expert_exl3.zig:546; Zig is not installed, so its C++ restatement in oracle/) on the
+host cores over the M = 1 projections of the sweep.
+"""
+
+import argparse
+import ctypes
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SHAPES = [(7168, 2048), (2048, 7168), (14336, 4096)]  # (in, out): out x in = 2048x7168, 7168x2048, 4096x14336
+RATES = [32, 48, 64]
+ROWS = [1, 2, 4, 8, 16, 64]
+L2_BYTES = 126 * 1024 * 1024
+METRIC = "EXL3 GEMV compressed-HBM GB/s (% peak); MoE layer tokens/s at 1/2/4/8 B200"
+UNIT = "GB/s"
+
+
+def alg_bytes(in_f, out_f, n, m):
+    return in_f * out_f * n // 128 + 2 * (in_f + out_f) + 2 * m * in_f + 2 * m * out_f
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p.get("bf16_tflops", 1618.5)), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+
+    def __init__(self, index):
+        self.index = index
+        self.samples = []
+        self.proc = None
+        self.thread = None
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "200", "-i", str(self.index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 7:
+                self.samples.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[3 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ---------------------------------------------------------------------------------------------
+def run_reference(args):
+    """The reference's CPU decode + matmul (oracle restatement) on the host cores."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    from oracle import oracle as orc
+    from oracle import synth
+
+    threads = orc.num_threads()
+    packs = []
+    for (in_f, out_f) in SHAPES:
+        for n in RATES:
+            tr, su, sv = synth.random_bank(in_f * 7 + n, 1, in_f, out_f, n)
+            packs.append((in_f, out_f, n, tr[0], su[0], sv[0], synth.activations(n, 1, in_f)))
+    sample = packs  # every (shape, rate) at M = 1: 9 projections per step
+    for _ in range(args.warmup):
+        in_f, out_f, n, tr, su, sv, x = sample[0]
+        orc.project(x, tr, su, sv, in_f, out_f, n, orc.CB_MCG, 16)
+    t0 = time.perf_counter()
+    total = 0
+    for _ in range(args.steps):
+        for in_f, out_f, n, tr, su, sv, x in sample:
+            orc.project(x, tr, su, sv, in_f, out_f, n, orc.CB_MCG, 16)
+            total += alg_bytes(in_f, out_f, n, 1)
+    dt = time.perf_counter() - t0
+    value = total / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u16 trellis -> f32 accumulate", "data": "synthetic (seeded random trellis words)",
+        "config": {"workload": "gemv_sweep_m1_sample", "shapes_out_x_in": ["2048x7168", "7168x2048", "4096x14336"],
+                   "n": RATES, "rows": 1},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": "9 projections per step: every sweep shape at n=32/48/64, M=1 (format.project restated in C++, OpenMP)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-moe", action="store_true")
+    ap.add_argument("--profile", default=None, choices=["gemv", "moe"],
+                    help="a small fixed case for ncu: --warmup launches, then --steps launches, no graphs")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    if args.profile:
+        return run_profile(args)
+
+    import torch
+    import torch.distributed as dist
+
+    import sushi_b200 as sx
+    from sushi_b200 import _lib
+    from oracle import synth
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    L = _lib.load()
+    stream = torch.cuda.current_stream()
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    dec = sx.Decode(sx.Codebook.MCG, 16).c()
+
+    # ---------------- weights: a ring of distinct copies per (shape, rate)
+    rings = {}
+    for (in_f, out_f) in SHAPES:
+        for n in RATES:
+            size = in_f * out_f * n // 128
+            copies = max(2, -(-2 * L2_BYTES // size))
+            tr = torch.randint(-32768, 32768, (copies, in_f // 16, out_f // 16, n), dtype=torch.int16, device="cuda")
+            su = (torch.randint(0, 2, (copies, in_f), device="cuda").half() * 2 - 1) * 0.05
+            sv = torch.randint(0, 2, (copies, out_f), device="cuda").half() * 2 - 1
+            projs = [_lib.SxProj(tr[c].data_ptr(), su[c].data_ptr(), sv[c].data_ptr(), 1, in_f, out_f, n, 0)
+                     for c in range(copies)]
+            rings[(in_f, out_f, n)] = (tr, su, sv, projs)
+    maxm = max(ROWS)
+    xbuf = {in_f: torch.randn((maxm, in_f), device="cuda").to(torch.bfloat16) for in_f, _ in SHAPES}
+    ybuf = {out_f: torch.empty((maxm, out_f), device="cuda", dtype=torch.bfloat16) for _, out_f in SHAPES}
+    configs = [(in_f, out_f, n, m) for (in_f, out_f) in SHAPES for n in RATES for m in ROWS]
+
+    def launch(in_f, out_f, n, m, proj):
+        st = L.sx_linear(sptr, ctypes.byref(proj), ctypes.byref(dec), xbuf[in_f].data_ptr(), 2, m, ybuf[out_f].data_ptr())
+        if st:
+            raise RuntimeError(L.sx_status_name(st).decode())
+
+    # one graph per config: every ring copy once (each launch reads weights no recent launch read)
+    graphs, launches_per_step, bytes_per_step = [], 0, 0
+    for (in_f, out_f, n, m) in configs:
+        projs = rings[(in_f, out_f, n)][3]
+        for p in projs:  # warm (sets kernel attributes) before capture
+            launch(in_f, out_f, n, m, p)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for p in projs:
+                launch(in_f, out_f, n, m, p)
+        graphs.append((g, len(projs), alg_bytes(in_f, out_f, n, m) * len(projs)))
+        chunks = -(-m // 16)
+        launches_per_step += len(projs) * chunks
+        bytes_per_step += alg_bytes(in_f, out_f, n, m) * len(projs)
+    torch.cuda.synchronize()
+
+    def step(events=None):
+        for i, (g, _, _) in enumerate(graphs):
+            if events is not None:
+                events[i][0].record(stream)
+            g.replay()
+            if events is not None:
+                events[i][1].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    per_cfg = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in graphs]
+    cfg_ms = np.zeros(len(graphs))
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            step(per_cfg)
+            torch.cuda.synchronize()
+            cfg_ms += np.array([a.elapsed_time(b) for a, b in per_cfg])
+        t1.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    kernel_ms = float(cfg_ms.sum()) / args.steps  # device time of the GEMV launches per step
+    total_ms = t0.elapsed_time(t1) / args.steps
+    if world > 1:
+        tt = torch.tensor([kernel_ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        kernel_ms = float(tt.item())
+    value = world * bytes_per_step / (kernel_ms * 1e-3) / 1e9
+
+    # ---------------- e2e: the C ABI called per projection with pinned host activations
+    hx = {in_f: torch.randn((maxm, in_f)).to(torch.bfloat16).pin_memory() for in_f, _ in SHAPES}
+    hy = {out_f: torch.empty((maxm, out_f), dtype=torch.bfloat16).pin_memory() for _, out_f in SHAPES}
+    h2d = sum(2 * m * in_f for (in_f, _, _, m) in configs)
+    d2h = sum(2 * m * out_f for (_, out_f, _, m) in configs)
+    e2e_bytes = sum(alg_bytes(*c) for c in configs)
+
+    def e2e_step(k):
+        for (in_f, out_f, n, m) in configs:
+            projs = rings[(in_f, out_f, n)][3]
+            xbuf[in_f][:m].copy_(hx[in_f][:m], non_blocking=True)
+            launch(in_f, out_f, n, m, projs[k % len(projs)])
+            hy[out_f][:m].copy_(ybuf[out_f][:m], non_blocking=True)
+
+    for k in range(args.warmup):
+        e2e_step(k)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for k in range(args.steps):
+        e2e_step(k + 7)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        tt = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+    e2e_value = world * e2e_bytes / (e2e_ms * 1e-3) / 1e9
+
+    hbm_peak, tf_peak, peak_kind = measured_peaks()
+    per_config = {}
+    for (in_f, out_f, n, m), (g, copies, b), ms in zip(configs, graphs, cfg_ms / args.steps):
+        per_config[f"{out_f}x{in_f}_n{n}_m{m}"] = round(b / (ms * 1e-3) / 1e9, 1)
+    headline = per_config.get("4096x14336_n32_m1")
+
+    out = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(kernel_ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u16 trellis (K=2/3/4) decoded to f16, bf16 activations, f32 accumulate",
+        "data": "synthetic (seeded random trellis words, sign-only scales; bf16 N(0,1) activations)",
+        "config": {"workload": "gemv_sweep (BASELINE configs[1])", "shapes_out_x_in": ["2048x7168", "7168x2048", "4096x14336"],
+                   "n": RATES, "rows": ROWS, "codebook": "mcg", "window": 16,
+                   "l2": "ring of distinct weight copies > 2x L2 per (shape, rate)", "parallelism": f"replicas x{world}"},
+        "roofline": {"bound": "hbm", "achieved": round(bytes_per_step / (kernel_ms * 1e-3) / 1e9, 2), "peak": hbm_peak,
+                     "unit": "GB/s", "frac": round(bytes_per_step / (kernel_ms * 1e-3) / 1e9 / hbm_peak, 4),
+                     "traffic": None, "peak_kind": peak_kind, "kernel": "sx::gemv_kernel (per-GPU)"},
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks.summary(),
+        "headline_4096x14336_k2_m1_gbs": headline,
+        "per_config_gbs": per_config,
+        "wall_ms_per_step": round(total_ms, 3),
+    }
+
+    if not args.no_moe:
+        out["moe"] = moe_bench(sx, _lib, torch, args, stream, sptr)
+
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+def moe_bench(sx, _lib, torch, args, stream, sptr):
+    """BASELINE configs[2] on one GPU: hidden 2048, 512 experts of 512, top-10, K2 (n32) MCG
+    random banks, softmax router over fp32 logits; tokens/s of router top-k + routed experts."""
+    from oracle import synth
+
+    E, D, I, k = 512, 2048, 512, 10
+    copies = 2  # the 512-expert bank is 384 MiB: two copies keep every layer's reads out of L2
+    banks = []
+    for c in range(copies):
+        parts = []
+        for (i_f, o_f) in ((D, I), (D, I), (I, D)):
+            tr = torch.randint(-32768, 32768, (E, i_f // 16, o_f // 16, 32), dtype=torch.int16, device="cuda")
+            su = (torch.randint(0, 2, (E, i_f), device="cuda").half() * 2 - 1) * 0.05
+            sv = torch.randint(0, 2, (E, o_f), device="cuda").half() * 2 - 1
+            parts.append(sx.Proj(tr, su, sv))
+        banks.append(sx.Bank(*parts))
+    dec = sx.Decode(sx.Codebook.MCG, 16)
+    res = {}
+    wr = torch.randn((D, E), device="cuda").mul_(0.02).to(torch.bfloat16)
+    for T in (1, 8, 64):
+        x = torch.randn((T, D), device="cuda").to(torch.bfloat16)
+
+        def layer(c):
+            logits = (x @ wr).float()
+            inds, scores = sx.router_topk(logits, k)
+            return sx.moe(x, banks[c % copies], inds, scores, dec)
+
+        for i in range(args.warmup):
+            layer(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(10, args.steps * 4)
+        e0.record(stream)
+        for i in range(reps):
+            layer(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        inds, _ = sx.router_topk((x @ wr).float(), k)
+        active = int(torch.unique(inds).numel())
+        bytes_ = active * 3 * (D * I * 32 // 128 + 2 * (D + I))
+        res[f"T{T}"] = {"tokens_per_s": round(T / (ms * 1e-3), 1), "ms_per_layer": round(ms, 4),
+                        "active_experts": active, "expert_gbs": round(bytes_ / (ms * 1e-3) / 1e9, 1)}
+    return res
+
+
+def run_profile(args):
+    """ncu case: the 4096x14336 K2 (n32) M=1 projection (config 1's rate, the sweep's largest
+    shape) over 12 distinct weight copies (176 MB > L2), or one MoE decode layer (T=8)."""
+    import torch
+
+    import sushi_b200 as sx
+
+    torch.cuda.set_device(0)
+    dec = sx.Decode(sx.Codebook.MCG, 16)
+    if args.profile == "gemv":
+        in_f, out_f, n, copies = 14336, 4096, 32, 12
+        tr = torch.randint(-32768, 32768, (copies, in_f // 16, out_f // 16, n), dtype=torch.int16, device="cuda")
+        su = (torch.randint(0, 2, (copies, in_f), device="cuda").half() * 2 - 1) * 0.05
+        sv = torch.randint(0, 2, (copies, out_f), device="cuda").half() * 2 - 1
+        projs = [sx.Proj(tr[c], su[c], sv[c]) for c in range(copies)]
+        x = torch.randn((1, in_f), device="cuda").to(torch.bfloat16)
+        for i in range(args.warmup + args.steps):
+            sx.linear(x, projs[i % copies], dec)
+    else:
+        E, D, I, k, T = 512, 2048, 512, 10, 8
+        parts = []
+        for (i_f, o_f) in ((D, I), (D, I), (I, D)):
+            tr = torch.randint(-32768, 32768, (E, i_f // 16, o_f // 16, 32), dtype=torch.int16, device="cuda")
+            su = (torch.randint(0, 2, (E, i_f), device="cuda").half() * 2 - 1) * 0.05
+            sv = torch.randint(0, 2, (E, o_f), device="cuda").half() * 2 - 1
+            parts.append(sx.Proj(tr, su, sv))
+        bank = sx.Bank(*parts)
+        x = torch.randn((T, D), device="cuda").to(torch.bfloat16)
+        logits = torch.randn((T, E), device="cuda")
+        for i in range(args.warmup + args.steps):
+            inds, scores = sx.router_topk(logits, k)
+            sx.moe(x, bank, inds, scores, dec)
+    torch.cuda.synchronize()
+    assert sx.device_error() == 0
+    print("profile case done", flush=True)
+
+
+def cpu_baseline():
+    from oracle import oracle as orc
+    from oracle import synth
+
+    in_f, out_f, n = 14336, 4096, 32
+    tr, su, sv = synth.random_bank(5, 1, in_f, out_f, n)
+    x = synth.activations(5, 1, in_f)
+    orc.project(x, tr[0], su[0], sv[0], in_f, out_f, n, orc.CB_MCG, 16)
+    t0 = time.perf_counter()
+    reps = 3
+    for _ in range(reps):
+        orc.project(x, tr[0], su[0], sv[0], in_f, out_f, n, orc.CB_MCG, 16)
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": round(alg_bytes(in_f, out_f, n, 1) / dt / 1e9, 3), "unit": UNIT, "cores": orc.num_threads(),
+            "kind": "port", "sample": "4096x14336 K2 M=1 projection x3 (format.project restated in C++, OpenMP over output tiles)"}
+
+
+if __name__ == "__main__":
+    main()

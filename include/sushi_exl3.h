@@ -1,0 +1,172 @@
+/*
+ * sushi_exl3.h: C ABI of libsushi_exl3_cuda.so, the B200 (sm_100a) EXL3 / STQ trellis kernels.
+ *
+ * This is the drop-in boundary for the reference's `sushi_exl3` Zig module
+ * (beamivalice/sushi 1.7.2, src/exl3/root.zig), whose host code reaches Metal through MLX.
+ * A Zig host declares these functions `extern fn` and calls them where root.zig / linear.zig /
+ * moe_router.zig dispatch Metal kernels today.  Every pointer is a device pointer borrowed from
+ * the caller; outputs go to caller-allocated buffers; no call allocates device memory.  Scratch,
+ * where a call needs any, is a caller-owned workspace sized by the matching *_workspace_bytes()
+ * query.  Calls are stream-ordered on the stream given and stateless: the decode parameters
+ * travel with each call (the reference sets a process global before each dispatch instead,
+ * src/exl3/expert_exl3_kernels.zig:938).  No call aborts, traps or prints; each returns a status.
+ *
+ * Pack layout (docs/pack-format.md "Routed-expert tensors"): a projection's trellis is U16
+ * [E, in/16, out/16, n] in pack order, or [E, out/32, in/16, 2, n] pair-major
+ * (src/exl3/layout.zig:141); suh is F16 [E, in], svh is F16 [E, out]; n is the packed halfwords
+ * per 16x16 tile (even, 16..128; K = n/16 bits per weight).  The weight a bank applies is
+ * W = diag(suh) H128 inner H128 diag(svh), y = x . W (src/exl3/expert_exl3.zig:440-566).
+ */
+#ifndef SUSHI_EXL3_H
+#define SUSHI_EXL3_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  Each non-zero code mirrors one of the reference's named refusals. */
+typedef int32_t sx_status;
+enum {
+    SX_OK = 0,
+    SX_ERR_BAD_SHAPE = 1,                  /* error.BadExl3Shape (src/exl3/root.zig:104-130) */
+    SX_ERR_BAD_DTYPE = 2,                  /* error.BadExl3Dtype (src/exl3/root.zig:110-113) */
+    SX_ERR_INVALID_CLAMP = 3,              /* error.InvalidExl3Clamp (src/exl3/root.zig:103) */
+    SX_ERR_TOPK_EXCEEDS_REDUCE_BANK = 4,   /* error.Exl3TopKExceedsReduceBank (src/exl3/root.zig:421) */
+    SX_ERR_CODEBOOK_TABLE_UNKNOWN = 5,     /* error.Exl3CodebookTableUnknown (src/exl3/expert_exl3.zig:162) */
+    SX_ERR_TRELLIS_GEOMETRY = 6,           /* error.Exl3TrellisGeometry (src/exl3/layout.zig:57-63) */
+    SX_ERR_CODEBOOK_TABLE_RATE_MISSING = 7,/* error.Exl3CodebookTableRateMissing (src/exl3/layout.zig:92) */
+    SX_ERR_WINDOW_UNSUPPORTED = 8,         /* error.Exl3WindowUnsupported (src/exl3/root.zig:223) */
+    SX_ERR_CODEBOOK_UNSUPPORTED = 9,       /* error.ExpertLayoutUnsupported for an unknown codebook */
+    SX_ERR_CODEBOOK_TABLE_WINDOW_MISMATCH = 10, /* error.Exl3CodebookTableWindowMismatch (codebook_tables.zig:276) */
+    SX_ERR_TOPK_EXCEEDS_EXPERTS = 11,      /* error.Exl3TopKExceedsExperts (src/exl3/layout.zig:117) */
+    SX_ERR_ROUTER_DECLINED = 12,           /* moeRouterTopK returned null (src/moe_router.zig:466-490) */
+    SX_ERR_NULL_POINTER = 13,
+    SX_ERR_WORKSPACE_TOO_SMALL = 14,
+    SX_ERR_CUDA = 15,                      /* a CUDA runtime call failed (launch, attribute) */
+    SX_ERR_DEVICE_TIMEOUT = 16,            /* a bounded device-side wait gave up (see sx_device_error) */
+    SX_ERR_NCCL = 17,                      /* an NCCL call failed (expert-parallel calls) */
+    SX_ERR_TILE_ORDER_UNSUPPORTED = 18,    /* error.Exl3TileOrderUnsupported (docs/pack-format.md) */
+    SX_ERR_GROUP_GEOMETRY = 19             /* error.Exl3GroupGeometry (src/exl3/layout.zig:80-95) */
+};
+
+/* The status's name ("SX_OK", "SX_ERR_BAD_SHAPE", ...); a static string. */
+const char* sx_status_name(sx_status s);
+
+/* Element types of activations and outputs. */
+typedef enum { SX_DT_F32 = 0, SX_DT_F16 = 1, SX_DT_BF16 = 2 } sx_dtype;
+
+/* Codebooks, numbered as the reference's `Codebook` enum (src/exl3/expert_exl3.zig:54-61). */
+typedef enum { SX_CB_MUL1 = 0, SX_CB_MCG = 1, SX_CB_SPEC1 = 2, SX_CB_PAIR1 = 3, SX_CB_STD1 = 4 } sx_codebook;
+
+/* Codebook tables, numbered as the reference's `tables` (src/exl3/codebook_tables.zig:101-106,
+ * 216-220): 0 pair1-w16-v1, 1 spec1-w15, 2 spec1-w16, 3 std1, 4 spec1-test-per-rate (the
+ * reference's test-only table whose row differs at every rate).  -1 names no table. */
+enum { SX_TABLE_NONE = -1, SX_TABLE_PAIR1_W16_V1 = 0, SX_TABLE_SPEC1_W15 = 1, SX_TABLE_SPEC1_W16 = 2,
+       SX_TABLE_STD1 = 3, SX_TABLE_SPEC1_TEST = 4 };
+
+/* How a pack's trellis decodes: format.Decode (src/exl3/expert_exl3.zig:141-174).
+ * window_bits is the codeword width the search hashed, 8..16 (16 masks nothing). */
+typedef struct sx_decode {
+    int32_t codebook;     /* sx_codebook */
+    int32_t window_bits;  /* 8..16 */
+    int32_t table;        /* SX_TABLE_*; required for SPEC1 and STD1 */
+} sx_decode;
+
+/* Tile orders (src/exl3/expert_exl3.zig:249-257). */
+typedef enum { SX_TILE_PACK = 0, SX_TILE_PAIR_MAJOR = 1 } sx_tile_order;
+
+/* One projection's bank: root.Proj (src/exl3/root.zig:30). */
+typedef struct sx_proj {
+    const uint16_t* trellis;  /* U16, see tile_order */
+    const uint16_t* suh;      /* F16 bits [experts, in_features] */
+    const uint16_t* svh;      /* F16 bits [experts, out_features] */
+    int32_t experts;
+    int32_t in_features;      /* multiple of 128 */
+    int32_t out_features;     /* multiple of 128 */
+    int32_t n;                /* packed halfwords per tile: even, 16..128 */
+    int32_t tile_order;       /* sx_tile_order */
+} sx_proj;
+
+/* A routed MoE layer's three banks: root.Bank (src/exl3/root.zig:39). */
+typedef struct sx_bank {
+    sx_proj gate, up, down;
+} sx_bank;
+
+/* Opaque CUDA stream (cudaStream_t / CUstream). */
+typedef void* sx_stream;
+
+/* ------------------------------------------------------------------ decode
+ * The dequantised inner matrix of expert `expert`: `out` [in, out] F16 bits, row-major, bit-exact
+ * with the reference's host decode `reconstructInner` (src/exl3/expert_exl3.zig:416-438). */
+sx_status sx_dequant_inner(sx_stream stream, const sx_proj* proj, int32_t expert, const sx_decode* dec,
+                           uint16_t* out);
+
+/* Every codeword's decoded weight (or PAIR1 weight pair) at rate n: out[cw] for cw in 0..65535,
+ * F16 bits; PAIR1 writes weight 2j in the low half and 2j+1 in the high half of out32[cw].  The
+ * device codebook against the host truth over all codewords, as firstPair1PairMismatch does
+ * (src/exl3/expert_exl3.zig:361-369). */
+sx_status sx_decode_codewords(sx_stream stream, int32_t n, const sx_decode* dec, uint32_t* out32);
+
+/* ------------------------------------------------------------------ dense linears
+ * y = x . W for `rows` rows through the one-bank projection `proj` (experts == 1):
+ * linear.linear (src/exl3/linear.zig:27-35), trunk.matmul (src/exl3/trunk.zig:53).
+ * x [rows, in] and y [rows, out], row-major, both of `dtype` (BF16, F16 or F32; the output is in
+ * the input's dtype as the reference's).  The prepared input is rounded to f16 as the reference's
+ * prepareInput does; products accumulate in f32; y is rounded once.  rows >= 1. */
+sx_status sx_linear(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x, sx_dtype dtype,
+                    int32_t rows, void* y);
+
+/* linear.linearGrouped (src/exl3/linear.zig:38-54): x [G, rows, in] through the G-bank proj
+ * (experts == G, bank g serves x[g]) into y [G, rows, out]. */
+sx_status sx_linear_grouped(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x,
+                            sx_dtype dtype, int32_t rows, void* y);
+
+/* ------------------------------------------------------------------ router
+ * Router modes (src/moe_router.zig:105). */
+typedef enum { SX_ROUTER_SOFTMAX = 0, SX_ROUTER_SIGMOID_BIAS = 1, SX_ROUTER_SIGMOID_BIAS_GROUPED = 2 } sx_router_mode;
+
+/* moeRouterTopK (src/moe_router.zig:442): per row of logits [rows, experts] (F32), the top-k
+ * experts by key (softmax: the logit; sigmoid modes: sigmoid(logit) + bias[e], with the group
+ * limit for the grouped mode), ties to the lowest id, and their weights (softmax probabilities
+ * renormalised over the picks; sigmoid modes: sigmoid scores, renormalised when `renorm` and k > 1,
+ * times `scale`).  inds [rows, k] U32, scores [rows, k] F32.  Returns SX_ERR_ROUTER_DECLINED where
+ * the reference's kernel declines (k outside 1..32, more than 2048 experts, a group limit it
+ * cannot take), so the caller keeps its own chain. */
+sx_status sx_router_topk(sx_stream stream, const float* logits, const float* bias, int32_t rows, int32_t experts,
+                         int32_t k, int32_t mode, int32_t renorm, float scale, int32_t n_group, int32_t topk_group,
+                         uint32_t* inds, float* scores);
+
+/* ------------------------------------------------------------------ routed experts
+ * The workspace sx_moe needs for `rows` rows at top-k `topk` over `bank` (bytes). */
+size_t sx_moe_workspace_bytes(const sx_bank* bank, int32_t rows, int32_t topk);
+
+/* Routed SwiGLU experts: root.moe / moeWithShared / moeWithGatedShared / moeClamped
+ * (src/exl3/root.zig:51-125).  x [rows, hidden] (BF16, F16 or F32), inds [rows, topk] U32 expert
+ * ids, scores [rows, topk] F32 weights; y [rows, hidden] in x's dtype:
+ *   y[r] = sum_k scores[r,k] * down_e(silu(gate_e(x[r])) * up_e(x[r]))      e = inds[r,k]
+ * with the gate upper-clamped and up clipped to +-clamp_limit first when clamp_limit > 0 (the
+ * clamped SwiGLU, src/exl3/root.zig:96-125; 1..128, else SX_ERR_INVALID_CLAMP).  When `shared`
+ * ([rows, hidden], x's dtype) is given it is added to every row; with `shared_gate` ([rows] x's
+ * dtype logits) it is added as sigmoid(gate) * shared (moeWithGatedShared).  topk <= 32.
+ * `workspace` holds at least sx_moe_workspace_bytes(bank, rows, topk). */
+sx_status sx_moe(sx_stream stream, const sx_bank* bank, const sx_decode* dec, const void* x, sx_dtype dtype,
+                 int32_t rows, const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
+                 const void* shared_gate, int32_t clamp_limit, void* y, void* workspace, size_t workspace_bytes);
+
+/* ------------------------------------------------------------------ device error latch
+ * Every bounded device-side wait that gives up records a code in a per-device latch instead of
+ * hanging; the call that launched it may already have returned SX_OK.  Returns the latched code
+ * (0 = none) and clears it; synchronises `stream` first. */
+int32_t sx_device_error(sx_stream stream);
+
+/* The library's version string. */
+const char* sx_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SUSHI_EXL3_H */

@@ -362,6 +362,30 @@ int orc_decode_pair(uint16_t cw, uint32_t n, uint16_t out[2]) {
     return 0;
 }
 void orc_unpack_tile(const uint16_t* words, uint32_t n, uint16_t* out) { unpack_tile(words, n, out); }
+
+// Every codeword's decode at rate n (window-masked first): out32[cw] = weight bits, and for PAIR1
+// weight 2j's bits low and 2j+1's high (the layout firstPair1PairMismatch reads,
+// src/exl3/expert_exl3.zig:359-369).  Returns -1 for a decode without a row at this rate.
+int orc_decode_all(int codebook, uint32_t n, int window_bits, int table, uint32_t* out32) {
+    const uint16_t mask = window_mask(window_bits);
+    Pair p{};
+    uint32_t mult = 0, hmask = 0;
+    if (codebook == CB_PAIR1 && !pair1_row(n, &p)) return -1;
+    if ((codebook == CB_SPEC1 || codebook == CB_STD1) && !hash_row(table, n, &mult, &hmask)) return -1;
+    for (uint32_t cw = 0; cw < 65536u; cw++) {
+        const uint16_t m = (uint16_t)(cw & mask);
+        if (codebook == CB_PAIR1) {
+            uint16_t w[2];
+            decode_pair(m, p, w);
+            out32[cw] = (uint32_t)w[0] | ((uint32_t)w[1] << 16);
+        } else if (codebook == CB_SPEC1 || codebook == CB_STD1) {
+            out32[cw] = decode_hash_mask(m, mult, hmask);
+        } else {
+            out32[cw] = codebook == CB_MCG ? decode_mcg(m) : decode_mul1(m);
+        }
+    }
+    return 0;
+}
 void orc_tensor_core_perm(int64_t* out) { for (int i = 0; i < TILE_VALUES; i++) out[i] = (int64_t)PERM.p[i]; }
 int orc_decode_tile(const uint16_t* words, uint32_t n, int codebook, int window_bits, int table, uint16_t* out) {
     return decode_tile(words, n, Dec{codebook, window_bits, table}, out);

@@ -62,6 +62,7 @@ def _declare(L):
         "orc_hash_row": (ctypes.c_int, [ctypes.c_int, ctypes.c_uint32, _u32p]),
         "orc_decode_pair": (ctypes.c_int, [ctypes.c_uint16, ctypes.c_uint32, _u16p]),
         "orc_unpack_tile": (None, [_u16p, ctypes.c_uint32, _u16p]),
+        "orc_decode_all": (ctypes.c_int, [ctypes.c_int, ctypes.c_uint32, ctypes.c_int, ctypes.c_int, _u32p]),
         "orc_tensor_core_perm": (None, [_i64p]),
         "orc_decode_tile": (ctypes.c_int, [_u16p, ctypes.c_uint32, ctypes.c_int, ctypes.c_int, ctypes.c_int, _u16p]),
         "orc_hadamard128": (None, [_f32p]),
@@ -166,6 +167,14 @@ def unpack_tile(words, n):
     words = _c(words, np.uint16)
     out = np.empty(256, np.uint16)
     lib().orc_unpack_tile(_p(words, _u16p), n, _p(out, _u16p))
+    return out
+
+
+def decode_all(codebook, n, window_bits=16, table=TABLE_NONE):
+    """Every codeword's decode (u32 per codeword; PAIR1 packs the pair)."""
+    out = np.empty(1 << 16, np.uint32)
+    if lib().orc_decode_all(codebook, n, window_bits, table, _p(out, _u32p)):
+        raise ValueError("decode without a codebook row at this rate")
     return out
 
 

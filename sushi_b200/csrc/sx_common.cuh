@@ -1,0 +1,141 @@
+// Device helpers shared by the sm_100a kernels: the error latch, bounded mbarrier waits, bulk
+// (TMA) copies, the legacy-layout MMA used for the decode GEMVs, and the warp Hadamard-128.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sx {
+
+// Codes a kernel latches when a bounded wait gives up (read by sx_device_error).
+enum DeviceError : int {
+    DEV_OK = 0,
+    DEV_TIMEOUT_FULL = 1,     // a consumer waited too long for a stage's bytes
+    DEV_TIMEOUT_EMPTY = 2,    // the producer waited too long for a stage to drain
+};
+
+extern __device__ int g_device_error;
+
+__device__ __forceinline__ void latch_error(int code) { atomicCAS(&g_device_error, 0, code); }
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ------------------------------------------------------------------ mbarriers
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for the barrier's phase with `parity` to complete, for at most ~2 s of wall time.  On a
+// timeout it latches `code` and returns false; the caller then skips its work but still reaches
+// every later block- and cluster-wide barrier, so no thread is left waiting.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 0;; i++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 255u && global_timer_ns() - t0 > kWaitLimitNs) {
+            latch_error(code);
+            return false;
+        }
+    }
+}
+
+// ------------------------------------------------------------------ bulk copies (TMA, 1-D)
+// global -> this CTA's shared memory, completing `bytes` on `bar`.  dst and src 16-byte aligned,
+// bytes a multiple of 16.  No multicast.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// ------------------------------------------------------------------ MMA (m16n8k16, f16 -> f32)
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ------------------------------------------------------------------ conversions
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+__device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
+__device__ __forceinline__ float round_f16(float f) { return __half2float(__float2half_rn(f)); }
+
+// dtype codes as sx_dtype: 0 f32, 1 f16, 2 bf16
+__device__ __forceinline__ float load_act(const void* p, size_t i, int dt) {
+    if (dt == 0) return static_cast<const float*>(p)[i];
+    if (dt == 1) return __half2float(static_cast<const __half*>(p)[i]);
+    return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+}
+
+__device__ __forceinline__ void store_act(void* p, size_t i, int dt, float v) {
+    if (dt == 0) static_cast<float*>(p)[i] = v;
+    else if (dt == 1) static_cast<__half*>(p)[i] = __float2half_rn(v);
+    else static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+}
+
+// ------------------------------------------------------------------ Hadamard-128 over a warp
+// Lane L holds elements 4L..4L+3 of a 128-vector; returns H128 . v (Sylvester order, scaled by
+// 1/sqrt(128)), the transform of src/exl3/expert_exl3.zig:400-414 computed by butterflies.
+__device__ __forceinline__ void warp_hadamard128(float (&v)[4]) {
+    float a0 = v[0] + v[1], a1 = v[0] - v[1], a2 = v[2] + v[3], a3 = v[2] - v[3];
+    v[0] = a0 + a2;
+    v[1] = a1 + a3;
+    v[2] = a0 - a2;
+    v[3] = a1 - a3;
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+        const bool upper = (lane & m) != 0;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float other = __shfl_xor_sync(0xffffffffu, v[i], m);
+            v[i] = upper ? other - v[i] : v[i] + other;
+        }
+    }
+    const float s = 0.08838834764831845f;
+#pragma unroll
+    for (int i = 0; i < 4; i++) v[i] *= s;
+}
+
+}  // namespace sx

@@ -1,0 +1,158 @@
+// Fused EXL3 projection for 1..16 rows: y = svh * H128( W_inner . H128(suh * x) )
+// (kernel template; instantiated per codebook in sx_gemv_{mcg,mul1,hash,pair1}.cu).
+//
+// One launch does the reference's three host stages (src/exl3/expert_exl3.zig:490-544,
+// prepareInput -> innerGemv -> finishOutput; on the GPU, project_rows.zig:759's rows kernel plus
+// its finish dispatch):
+//   * A CTA owns one 128-wide output block and a contiguous range of input blocks (sx_core.cuh);
+//     the CTAs that split one output block's k range form a thread-block cluster (<= 16 CTAs).
+//   * While the producer warp fills the tile ring, the consumer warps prepare the CTA's input
+//     slice (f16(x) * suh, Hadamard-128 by warp butterflies, rounded to f16 as prepareInput does)
+//     straight into MMA B-fragment order.
+//   * The cluster's rank-0 CTA sums its peers' partials over distributed shared memory (DSMEM),
+//     applies Hadamard-128, svh and the codebook scale, and writes y once in the input's dtype.
+//     No global scratch.
+#pragma once
+
+#include <cooperative_groups.h>
+
+#include "sx_core.cuh"
+#include "sx_kernels.h"
+
+namespace cg = cooperative_groups;
+
+namespace sx {
+
+template <int KIND, int NB>
+cudaError_t dispatch_n(const GemvArgs& a, int n, int groups, int S, cudaStream_t stream);
+
+template <int KIND, int N, int NB>
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    cg::cluster_group cluster = cg::this_cluster();
+    const int ob = blockIdx.x;     // output block (128 outputs)
+    const int split = blockIdx.y;  // k-split index == cluster rank
+    const int g = blockIdx.z;      // bank (grouped linears)
+    const int S = gridDim.y;
+    const int KB = a.in / 128;
+    const int kb0 = (int)(((long long)split * KB) / S);
+    const int kbl = (int)(((long long)(split + 1) * KB) / S) - kb0;
+    const int kbl_max = (KB + S - 1) / S;
+    const CoreSmem s = core_smem<N, 1, NB>(smem, kbl_max);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int OT = a.out / 16;
+    const uint16_t* suh = a.suh + (size_t)g * a.in;
+    const uint16_t* svh = a.svh + (size_t)g * a.out;
+
+    core_init_barriers<N, 1>(s);
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        if (lane == 0) {
+            const uint16_t* const tr[1] = {a.trellis + (size_t)g * ((size_t)KB * 8 * OT * N)};
+            core_produce<N, 1>(s, tr, OT, ob, kb0, kbl);
+        }
+    } else {
+        // prepare: rows x input blocks, one warp per (block, row)
+        for (int item = warp; item < kbl * NB * 8; item += kConsumerWarps) {
+            const int kbi = item / (NB * 8);
+            const int m = item % (NB * 8);
+            const int base = (kb0 + kbi) * 128 + lane * 4;
+            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (m < a.rows) {
+                const size_t xoff = (size_t)g * a.x_group_stride + (size_t)m * a.in + base;
+#pragma unroll
+                for (int i = 0; i < 4; i++) v[i] = round_f16(load_act(a.x, xoff + i, a.xdt)) * h2f(suh[base + i]);
+                warp_hadamard128(v);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++) bfrag_put<NB>(s.bfrag, kbi, m, lane * 4 + i, f2h(v[i]));
+        }
+        for (int i = threadIdx.x; i < NB * 8 * 128; i += kConsumerWarps * 32) s.red[i] = 0.0f;
+        consumers_sync();
+
+        const DecParams dp[1] = {{a.wmask, a.mult, a.mask0, a.mask1, a.rot}};
+        float acc[1][8][NB][4];
+        core_consume<KIND, N, 1, NB>(s, kbl, dp, acc);
+        core_reduce<1, NB>(s.red, acc);
+    }
+
+    // rank 0 sums the cluster's partials over DSMEM and finishes
+    cluster.sync();
+    if (split == 0 && warp < kConsumerWarps) {
+        for (int m = warp; m < a.rows; m += kConsumerWarps) {
+            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int r = 0; r < S; r++) {
+                const float* peer = cluster.map_shared_rank(s.red, r);
+#pragma unroll
+                for (int i = 0; i < 4; i++) v[i] += peer[m * 128 + lane * 4 + i];
+            }
+            warp_hadamard128(v);
+            const size_t yoff = (size_t)g * a.y_group_stride + (size_t)m * a.out + (size_t)ob * 128 + lane * 4;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int o = ob * 128 + lane * 4 + i;
+                store_act(a.y, yoff + i, a.xdt, v[i] * a.out_scale * h2f(svh[o]));
+            }
+        }
+    }
+    cluster.sync();
+}
+
+template <int KIND, int N, int NB>
+static cudaError_t launch_gemv_t(const GemvArgs& a, int groups, int S, cudaStream_t stream) {
+    const int KB = a.in / 128;
+    const int kbl_max = (KB + S - 1) / S;
+    const CoreLayout L = core_layout<N, 1, NB>(kbl_max);
+    auto kern = gemv_kernel<KIND, N, NB>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
+    if (e != cudaSuccess) return e;
+    if (S > 8) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.out / 128, S, groups);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = L.total;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = S;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+#define SX_N_LIST(X) \
+    X(16) X(18) X(20) X(22) X(24) X(26) X(28) X(30) X(32) X(34) X(36) X(38) X(40) X(42) X(44) X(46) X(48) X(50) X(52) \
+    X(54) X(56) X(58) X(60) X(62) X(64) X(66) X(68) X(70) X(72) X(74) X(76) X(78) X(80) X(82) X(84) X(86) X(88) X(90) \
+    X(92) X(94) X(96) X(98) X(100) X(102) X(104) X(106) X(108) X(110) X(112) X(114) X(116) X(118) X(120) X(122) X(124) \
+    X(126) X(128)
+
+#define SX_N_LIST_PAIR1(X) \
+    X(24) X(26) X(28) X(30) X(32) X(34) X(36) X(38) X(40) X(42) X(44) X(46) X(48) X(50) X(52) X(54) X(56) X(58) X(60) \
+    X(62) X(64)
+
+// PAIR1 has rows at n = 24..64 only (src/exl3/expert_exl3.zig:49-52); the others span 16..128.
+template <int KIND, int NB>
+cudaError_t dispatch_n(const GemvArgs& a, int n, int groups, int S, cudaStream_t stream) {
+#define SX_CASE(NN) \
+    case NN: return launch_gemv_t<KIND, NN, NB>(a, groups, S, stream);
+    if constexpr (KIND == K_PAIR1) {
+        switch (n) {
+            SX_N_LIST_PAIR1(SX_CASE)
+            default: return cudaErrorInvalidValue;
+        }
+    } else {
+        switch (n) {
+            SX_N_LIST(SX_CASE)
+            default: return cudaErrorInvalidValue;
+        }
+    }
+#undef SX_CASE
+}
+
+}  // namespace sx

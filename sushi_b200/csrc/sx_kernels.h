@@ -1,0 +1,38 @@
+// Host-side declarations of the kernel launchers (internal to libsushi_exl3_cuda.so).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace sx {
+
+struct GemvArgs {
+    const uint16_t* trellis;   // [G][in/16][out/16][n]
+    const uint16_t* suh;       // [G][in]
+    const uint16_t* svh;       // [G][out]
+    const void* x;             // [G][rows][in]
+    void* y;                   // [G][rows][out]
+    int in, out, rows;
+    int xdt;                   // sx_dtype of x and y
+    long long x_group_stride;  // elements between banks' inputs
+    long long y_group_stride;
+    uint32_t wmask, mult, mask0, mask1, rot;
+    float out_scale;
+};
+
+cudaError_t launch_gemv(const GemvArgs& a, int kind, int n, int groups, int S, cudaStream_t stream);
+size_t gemv_smem_bytes(int n, int nb, int in, int S);
+
+struct DequantArgs {
+    const uint16_t* trellis;  // one expert's [in/16][out/16][n] (pack order)
+    uint16_t* dst;            // [in_f][out_f] f16 bits
+    int in_f, out_f, n;
+    uint32_t wmask, mult, mask0, mask1, rot;
+};
+
+cudaError_t launch_dequant(const DequantArgs& a, int kind, cudaStream_t stream);
+cudaError_t launch_decode_codewords(int kind, int n, uint32_t wmask, uint32_t mult, uint32_t mask0, uint32_t mask1,
+                                    uint32_t rot, uint32_t* out32, cudaStream_t stream);
+
+}  // namespace sx

@@ -1,0 +1,239 @@
+// Routed SwiGLU experts: sx_moe (root.moe / moeWithShared / moeWithGatedShared / moeClamped,
+// src/exl3/root.zig:51-125) and its workspace query.  Kernels in sx_moe_impl.cuh.
+#include <algorithm>
+
+#include "sx_internal.h"
+#include "sx_moe_impl.cuh"
+
+namespace sx {
+
+template <int KIND>
+cudaError_t moe_launch_kind(const MoeArgs& a, int n_gu, int n_d, int S_gu, int S_d, int W_max, cudaStream_t stream);
+
+namespace {
+
+// ------------------------------------------------------------------ 1. routing metadata
+__global__ void __launch_bounds__(1024) route_prep_kernel(MoeArgs a) {
+    extern __shared__ int rp[];
+    int* cnt = rp;             // [E]
+    int* off = rp + a.E;       // [E]
+    const int tid = threadIdx.x;
+    const int RK = a.R * a.K;
+    for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (int s = tid; s < RK; s += blockDim.x) {
+        const uint32_t e = a.inds[s];
+        if (e < (uint32_t)a.E) atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    // Warp 0 scans: slot offsets, active-expert ranks and work-item ranks (8-row chunks).
+    if (tid < 32) {
+        const int lane = tid;
+        const int per = (a.E + 31) / 32;
+        const int e0 = lane * per, e1 = min(a.E, e0 + per);
+        int s_sum = 0, a_sum = 0, w_sum = 0;
+        for (int e = e0; e < e1; e++) {
+            s_sum += cnt[e];
+            a_sum += cnt[e] > 0;
+            w_sum += (cnt[e] + 7) / 8;
+        }
+        int s_ex = s_sum, a_ex = a_sum, w_ex = w_sum;
+#pragma unroll
+        for (int m = 1; m < 32; m <<= 1) {
+            const int ts = __shfl_up_sync(0xffffffffu, s_ex, m);
+            const int ta = __shfl_up_sync(0xffffffffu, a_ex, m);
+            const int tw = __shfl_up_sync(0xffffffffu, w_ex, m);
+            if (lane >= m) {
+                s_ex += ts;
+                a_ex += ta;
+                w_ex += tw;
+            }
+        }
+        s_ex -= s_sum;
+        a_ex -= a_sum;
+        w_ex -= w_sum;
+        for (int e = e0; e < e1; e++) {
+            const int c = cnt[e];
+            off[e] = s_ex;
+            if (c > 0) {
+                a.act_expert[a_ex] = e;
+                a.act_start[a_ex] = s_ex;
+                a.act_count[a_ex] = c;
+                for (int ch = 0; ch < (c + 7) / 8; ch++) {
+                    a.work_act[w_ex + ch] = a_ex;
+                    a.work_chunk[w_ex + ch] = ch;
+                }
+                a_ex++;
+                w_ex += (c + 7) / 8;
+            }
+            s_ex += c;
+        }
+        if (lane == 31) a.meta[0] = w_ex;
+    }
+    __syncthreads();
+    for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;  // reused as cursors
+    __syncthreads();
+    for (int s = tid; s < RK; s += blockDim.x) {
+        const uint32_t e = a.inds[s];
+        if (e < (uint32_t)a.E) {
+            const int pos = atomicAdd(&cnt[e], 1);
+            a.order[off[e] + pos] = s;
+        }
+    }
+}
+
+
+constexpr size_t kAlign = 256;
+size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+struct MoeWs {
+    size_t meta, act_expert, act_start, act_count, work_act, work_chunk, order, hprep, yslot, total;
+    int A_max, W_max;
+};
+
+MoeWs moe_ws_layout(int E, int R, int K, int D, int I) {
+    MoeWs w;
+    const int RK = R * K;
+    w.A_max = std::min(E, RK);
+    w.W_max = w.A_max + RK / 8 + 1;
+    size_t off = 0;
+    w.meta = off; off = align_up(off + 16 * sizeof(int));
+    w.act_expert = off; off = align_up(off + (size_t)w.A_max * sizeof(int));
+    w.act_start = off; off = align_up(off + (size_t)w.A_max * sizeof(int));
+    w.act_count = off; off = align_up(off + (size_t)w.A_max * sizeof(int));
+    w.work_act = off; off = align_up(off + (size_t)w.W_max * sizeof(int));
+    w.work_chunk = off; off = align_up(off + (size_t)w.W_max * sizeof(int));
+    w.order = off; off = align_up(off + (size_t)RK * sizeof(int));
+    w.hprep = off; off = align_up(off + (size_t)RK * I * sizeof(uint16_t));
+    w.yslot = off; off = align_up(off + (size_t)RK * D * sizeof(float));
+    w.total = off;
+    return w;
+}
+
+__global__ void __launch_bounds__(256) moe_reduce_kernel(MoeArgs a) {
+    const int r = blockIdx.x;
+    for (int d = threadIdx.x; d < a.D; d += blockDim.x) {
+        float acc = 0.0f;
+        for (int k = 0; k < a.K; k++) {
+            const int slot = r * a.K + k;
+            if (a.inds[slot] < (uint32_t)a.E) acc += a.yslot[(size_t)slot * a.D + d];
+        }
+        // The routed sum is rounded to the output dtype before a shared expert is added
+        // (docs/engine-exl3-experts.md "Streamed serial decode"; src/exl3/root.zig:56-92).
+        float y = acc;
+        if (a.xdt != 0) y = a.xdt == 1 ? __half2float(__float2half_rn(y)) : __bfloat162float(__float2bfloat16_rn(y));
+        if (a.shared) {
+            float sh = load_act(a.shared, (size_t)r * a.D + d, a.xdt);
+            if (a.shared_gate) {
+                const float gl = load_act(a.shared_gate, r, a.xdt);
+                float sg = 1.0f / (1.0f + expf(-gl));
+                if (a.xdt == 2) {
+                    sg = __bfloat162float(__float2bfloat16_rn(sg));
+                    sh = __bfloat162float(__float2bfloat16_rn(sg * sh));
+                } else if (a.xdt == 1) {
+                    sg = __half2float(__float2half_rn(sg));
+                    sh = __half2float(__float2half_rn(sg * sh));
+                } else {
+                    sh = sg * sh;
+                }
+            }
+            y = y + sh;
+        }
+        store_act(a.y, (size_t)r * a.D + d, a.xdt, y);
+    }
+}
+
+int pick_split(int units, int kb) {
+    const int want = 2 * sm_count();
+    int S = (want + units - 1) / std::max(units, 1);
+    return std::max(1, std::min(S, std::min(8, kb)));
+}
+
+}  // namespace
+
+}  // namespace sx
+
+using namespace sx;
+
+extern "C" size_t sx_moe_workspace_bytes(const sx_bank* bank, int32_t rows, int32_t topk) {
+    if (!bank || rows < 1 || topk < 1) return 0;
+    const int D = bank->gate.in_features, I = bank->gate.out_features;
+    return moe_ws_layout(bank->gate.experts, rows, topk, D, I).total;
+}
+
+extern "C" sx_status sx_moe(sx_stream stream, const sx_bank* bank, const sx_decode* dec, const void* x, sx_dtype dtype,
+                            int32_t rows, const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
+                            const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
+                            size_t workspace_bytes) {
+    if (!bank || !x || !inds || !scores || !y) return SX_ERR_NULL_POINTER;
+    if (clamp_limit < 0 || clamp_limit > 128) return SX_ERR_INVALID_CLAMP;
+    if (rows < 1 || topk < 1) return SX_ERR_BAD_SHAPE;
+    if (topk > 32) return SX_ERR_TOPK_EXCEEDS_REDUCE_BANK;
+    if (!dtype_ok(dtype)) return SX_ERR_BAD_DTYPE;
+    if (shared_gate && !shared) return SX_ERR_NULL_POINTER;
+    const int E = bank->gate.experts;
+    const int D = bank->gate.in_features, I = bank->gate.out_features;
+    // validateClampedProjection for gate, up and down (src/exl3/root.zig:117-135).
+    sx_status st;
+    if ((st = check_proj(&bank->gate, E)) || (st = check_proj(&bank->up, E)) || (st = check_proj(&bank->down, E))) return st;
+    if (bank->up.in_features != D || bank->up.out_features != I || bank->down.in_features != I ||
+        bank->down.out_features != D)
+        return SX_ERR_BAD_SHAPE;
+    if (bank->gate.tile_order != SX_TILE_PACK || bank->up.tile_order != SX_TILE_PACK || bank->down.tile_order != SX_TILE_PACK)
+        return SX_ERR_TILE_ORDER_UNSUPPORTED;
+    if (topk > E) return SX_ERR_TOPK_EXCEEDS_EXPERTS;
+    if (bank->gate.n != bank->up.n) return SX_ERR_TRELLIS_GEOMETRY;  // mixed gate/up rates: not served yet
+    const MoeWs L = moe_ws_layout(E, rows, topk, D, I);
+    if (!workspace || workspace_bytes < L.total) return SX_ERR_WORKSPACE_TOO_SMALL;
+    if (E > 8192) return SX_ERR_BAD_SHAPE;
+
+    MoeArgs a{};
+    int kind_gu, kind_d;
+    if ((st = resolve_decode(dec, bank->gate.n, &kind_gu, &a.dp_gu))) return st;
+    if ((st = resolve_decode(dec, bank->down.n, &kind_d, &a.dp_down))) return st;
+    a.x = x;
+    a.xdt = dtype;
+    a.R = rows;
+    a.K = topk;
+    a.D = D;
+    a.I = I;
+    a.E = E;
+    a.inds = inds;
+    a.scores = scores;
+    a.gate_tr = bank->gate.trellis; a.gate_suh = bank->gate.suh; a.gate_svh = bank->gate.svh;
+    a.up_tr = bank->up.trellis;     a.up_suh = bank->up.suh;     a.up_svh = bank->up.svh;
+    a.down_tr = bank->down.trellis; a.down_suh = bank->down.suh; a.down_svh = bank->down.svh;
+    a.scale_gu = kind_scale(kind_gu);
+    a.scale_down = kind_scale(kind_d);
+    a.clamp = (float)clamp_limit;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    a.meta = reinterpret_cast<int*>(ws + L.meta);
+    a.act_expert = reinterpret_cast<int*>(ws + L.act_expert);
+    a.act_start = reinterpret_cast<int*>(ws + L.act_start);
+    a.act_count = reinterpret_cast<int*>(ws + L.act_count);
+    a.work_act = reinterpret_cast<int*>(ws + L.work_act);
+    a.work_chunk = reinterpret_cast<int*>(ws + L.work_chunk);
+    a.order = reinterpret_cast<int*>(ws + L.order);
+    a.hprep = reinterpret_cast<uint16_t*>(ws + L.hprep);
+    a.yslot = reinterpret_cast<float*>(ws + L.yslot);
+    a.shared = shared;
+    a.shared_gate = shared_gate;
+    a.y = y;
+
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    route_prep_kernel<<<1, 1024, 2 * (size_t)E * sizeof(int), s>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return SX_ERR_CUDA;
+    const int S_gu = pick_split(L.A_max * (I / 128), D / 128);
+    const int S_d = pick_split(L.A_max * (D / 128), I / 128);
+    switch (kind_gu) {
+        case K_MCG: e = moe_launch_kind<K_MCG>(a, bank->gate.n, bank->down.n, S_gu, S_d, L.W_max, s); break;
+        case K_MUL1: e = moe_launch_kind<K_MUL1>(a, bank->gate.n, bank->down.n, S_gu, S_d, L.W_max, s); break;
+        case K_HASH: e = moe_launch_kind<K_HASH>(a, bank->gate.n, bank->down.n, S_gu, S_d, L.W_max, s); break;
+        case K_PAIR1: e = moe_launch_kind<K_PAIR1>(a, bank->gate.n, bank->down.n, S_gu, S_d, L.W_max, s); break;
+        default: return SX_ERR_CODEBOOK_UNSUPPORTED;
+    }
+    if (e != cudaSuccess) return SX_ERR_CUDA;
+    moe_reduce_kernel<<<rows, 256, 0, s>>>(a);
+    return cuda_status(cudaGetLastError());
+}

@@ -1,0 +1,222 @@
+// Routed SwiGLU experts, decode chain (kernel templates; instantiated per codebook in
+// sx_moe_{mcg,mul1,hash,pair1}.cu).  The reference runs four dispatches per MoE layer
+// (src/exl3/expert_exl3_kernels.zig:2683 moeSwigluFused: pair prepare, split-K pair GEMV, fused
+// mid+down GEMV, finish reduce); this chain is:
+//   1. route_prep (one CTA): histogram of the slots' experts, scan, scatter -> slots sorted by
+//      expert, the active experts, and a work list of (active expert, 8-row chunk).
+//   2. moe_pair: per work item and 128-wide block of the intermediate, gate AND up of the expert
+//      for the chunk's rows (NP = 2 core, split-K cluster).  Its rank-0 epilogue does the
+//      reference's mid (:2243 MID_SOURCE): H128, svh, SwiGLU in f32 (gate upper-clamped and up
+//      clipped when a limit is set), times the down projection's suh, H128 over the same block,
+//      rounded to f16: the down projection's prepared input.
+//   3. moe_down: per work item and 128-wide output block, the down GEMV over the prepared rows,
+//      H128, svh, times the slot's score, into a per-slot f32 plane.
+//   4. moe_reduce: per token, the slots' planes summed in k order, rounded to the output dtype,
+//      plus the shared expert (optionally sigmoid-gated), as moeWithShared/moeWithGatedShared do.
+#pragma once
+
+#include <cooperative_groups.h>
+
+#include "sx_core.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace sx {
+
+struct MoeArgs {
+    const void* x;          // [R][D]
+    int xdt;
+    int R, K, D, I, E;
+    const uint32_t* inds;   // [R*K]
+    const float* scores;    // [R*K]
+    const uint16_t* gate_tr; const uint16_t* gate_suh; const uint16_t* gate_svh;
+    const uint16_t* up_tr;   const uint16_t* up_suh;   const uint16_t* up_svh;
+    const uint16_t* down_tr; const uint16_t* down_suh; const uint16_t* down_svh;
+    DecParams dp_gu, dp_down;
+    float scale_gu, scale_down;
+    float clamp;            // 0 = none
+    // workspace
+    int* meta;              // [0] = number of work items
+    int* act_expert;        // [A_max]
+    int* act_start;         // [A_max]
+    int* act_count;         // [A_max]
+    int* work_act;          // [W_max]
+    int* work_chunk;        // [W_max]
+    int* order;             // [R*K] slots sorted by expert
+    uint16_t* hprep;        // [R*K][I] f16: the down projection's prepared input
+    float* yslot;           // [R*K][D] f32: score * expert output
+    // output
+    const void* shared;     // [R][D] x dtype, or null
+    const void* shared_gate;// [R] x dtype logits, or null
+    void* y;                // [R][D] x dtype
+};
+
+// Work item -> (expert, first sorted slot, rows of the chunk).
+struct WorkItem {
+    int e, first, rows;
+};
+
+__device__ __forceinline__ bool work_item(const MoeArgs& a, int w, WorkItem& it) {
+    if (w >= a.meta[0]) return false;
+    const int ai = a.work_act[w];
+    const int ch = a.work_chunk[w];
+    it.e = a.act_expert[ai];
+    it.first = a.act_start[ai] + ch * 8;
+    it.rows = min(8, a.act_count[ai] - ch * 8);
+    return true;
+}
+
+// ------------------------------------------------------------------ 2. gate + up + mid
+template <int KIND, int N>
+__global__ void __launch_bounds__(kThreads, 1) moe_pair_kernel(MoeArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int slot_of[8];
+    cg::cluster_group cluster = cg::this_cluster();
+    WorkItem it;
+    if (!work_item(a, blockIdx.x, it)) return;  // every CTA of the cluster shares blockIdx.x
+    const int ob = blockIdx.y;
+    const int S = cluster.dim_blocks().z;
+    const int split = blockIdx.z % S;
+    const int KB = a.D / 128;
+    const int kb0 = (int)(((long long)split * KB) / S);
+    const int kbl = (int)(((long long)(split + 1) * KB) / S) - kb0;
+    const int kbl_max = (KB + S - 1) / S;
+    const CoreSmem s = core_smem<N, 2, 1>(smem, kbl_max);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int OT = a.I / 16;
+    const size_t per = (size_t)(a.D / 16) * OT * N;
+    if (threadIdx.x < 8) slot_of[threadIdx.x] = threadIdx.x < it.rows ? a.order[it.first + threadIdx.x] : 0;
+    core_init_barriers<N, 2>(s);
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        if (lane == 0) {
+            const uint16_t* const tr[2] = {a.gate_tr + (size_t)it.e * per, a.up_tr + (size_t)it.e * per};
+            core_produce<N, 2>(s, tr, OT, ob, kb0, kbl);
+        }
+    } else {
+        const uint16_t* suh_p[2] = {a.gate_suh + (size_t)it.e * a.D, a.up_suh + (size_t)it.e * a.D};
+        for (int item = warp; item < 2 * kbl * 8; item += kConsumerWarps) {
+            const int p = item / (kbl * 8);
+            const int kbi = (item / 8) % kbl;
+            const int m = item % 8;
+            const int base = (kb0 + kbi) * 128 + lane * 4;
+            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (m < it.rows) {
+                const size_t xoff = (size_t)(slot_of[m] / a.K) * a.D + base;
+#pragma unroll
+                for (int i = 0; i < 4; i++) v[i] = round_f16(load_act(a.x, xoff + i, a.xdt)) * h2f(suh_p[p][base + i]);
+                warp_hadamard128(v);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++) bfrag_put<1>(s.bfrag + p * s.bfrag_proj_stride, kbi, m, lane * 4 + i, f2h(v[i]));
+        }
+        for (int i = threadIdx.x; i < 2 * 8 * 128; i += kConsumerWarps * 32) s.red[i] = 0.0f;
+        consumers_sync();
+        const DecParams dp[2] = {a.dp_gu, a.dp_gu};
+        float acc[2][8][1][4];
+        core_consume<KIND, N, 2, 1>(s, kbl, dp, acc);
+        core_reduce<2, 1>(s.red, acc);
+    }
+
+    cluster.sync();
+    if (split == 0 && warp < it.rows) {
+        const int m = warp;
+        float g[4] = {0.0f, 0.0f, 0.0f, 0.0f}, u[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int r = 0; r < S; r++) {
+            const float* peer = cluster.map_shared_rank(s.red, r);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                g[i] += peer[m * 128 + lane * 4 + i];
+                u[i] += peer[8 * 128 + m * 128 + lane * 4 + i];
+            }
+        }
+        warp_hadamard128(g);
+        warp_hadamard128(u);
+        float h[4];
+        const uint16_t* gsv = a.gate_svh + (size_t)it.e * a.I;
+        const uint16_t* usv = a.up_svh + (size_t)it.e * a.I;
+        const uint16_t* dsu = a.down_suh + (size_t)it.e * a.I;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int o = ob * 128 + lane * 4 + i;
+            float gv = g[i] * a.scale_gu * h2f(gsv[o]);
+            float uv = u[i] * a.scale_gu * h2f(usv[o]);
+            if (a.clamp > 0.0f) {
+                gv = fminf(gv, a.clamp);
+                uv = fminf(fmaxf(uv, -a.clamp), a.clamp);
+            }
+            h[i] = gv / (1.0f + expf(-gv)) * uv * h2f(dsu[o]);
+        }
+        warp_hadamard128(h);
+        uint16_t* dst = a.hprep + (size_t)slot_of[m] * a.I + ob * 128 + lane * 4;
+#pragma unroll
+        for (int i = 0; i < 4; i++) dst[i] = f2h(h[i]);
+    }
+    cluster.sync();
+}
+
+// ------------------------------------------------------------------ 3. down
+template <int KIND, int N>
+__global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(MoeArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int slot_of[8];
+    cg::cluster_group cluster = cg::this_cluster();
+    WorkItem it;
+    if (!work_item(a, blockIdx.x, it)) return;
+    const int ob = blockIdx.y;
+    const int S = cluster.dim_blocks().z;
+    const int split = blockIdx.z % S;
+    const int KB = a.I / 128;
+    const int kb0 = (int)(((long long)split * KB) / S);
+    const int kbl = (int)(((long long)(split + 1) * KB) / S) - kb0;
+    const int kbl_max = (KB + S - 1) / S;
+    const CoreSmem s = core_smem<N, 1, 1>(smem, kbl_max);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int OT = a.D / 16;
+    const size_t per = (size_t)(a.I / 16) * OT * N;
+    if (threadIdx.x < 8) slot_of[threadIdx.x] = threadIdx.x < it.rows ? a.order[it.first + threadIdx.x] : 0;
+    core_init_barriers<N, 1>(s);
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        if (lane == 0) {
+            const uint16_t* const tr[1] = {a.down_tr + (size_t)it.e * per};
+            core_produce<N, 1>(s, tr, OT, ob, kb0, kbl);
+        }
+    } else {
+        for (int item = warp; item < kbl * 8; item += kConsumerWarps) {
+            const int kbi = item / 8, m = item % 8;
+            const uint16_t* src = a.hprep + (size_t)slot_of[m] * a.I + (kb0 + kbi) * 128 + lane * 4;
+#pragma unroll
+            for (int i = 0; i < 4; i++) bfrag_put<1>(s.bfrag, kbi, m, lane * 4 + i, m < it.rows ? src[i] : (uint16_t)0);
+        }
+        for (int i = threadIdx.x; i < 8 * 128; i += kConsumerWarps * 32) s.red[i] = 0.0f;
+        consumers_sync();
+        const DecParams dp[1] = {a.dp_down};
+        float acc[1][8][1][4];
+        core_consume<KIND, N, 1, 1>(s, kbl, dp, acc);
+        core_reduce<1, 1>(s.red, acc);
+    }
+
+    cluster.sync();
+    if (split == 0 && warp < it.rows) {
+        const int m = warp;
+        float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int r = 0; r < S; r++) {
+            const float* peer = cluster.map_shared_rank(s.red, r);
+#pragma unroll
+            for (int i = 0; i < 4; i++) d[i] += peer[m * 128 + lane * 4 + i];
+        }
+        warp_hadamard128(d);
+        const int slot = slot_of[m];
+        const float sc = a.scores[slot] * a.scale_down;
+        const uint16_t* dsv = a.down_svh + (size_t)it.e * a.D;
+        float* dst = a.yslot + (size_t)slot * a.D + ob * 128 + lane * 4;
+#pragma unroll
+        for (int i = 0; i < 4; i++) dst[i] = d[i] * h2f(dsv[ob * 128 + lane * 4 + i]) * sc;
+    }
+    cluster.sync();
+}
+
+}  // namespace sx

@@ -1,0 +1,73 @@
+// Per-codebook launch of the MoE pair and down kernels over the admitted rates (included by
+// sx_moe_{mcg,mul1,hash,pair1}.cu).
+#pragma once
+
+#include "sx_moe_impl.cuh"
+
+namespace sx {
+
+template <typename Kern>
+static cudaError_t launch_clustered(Kern kern, dim3 grid, int S, size_t smem, cudaStream_t stream, const MoeArgs& a) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = S;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+template <int KIND, int N>
+static cudaError_t launch_pair_t(const MoeArgs& a, int S, int W_max, cudaStream_t stream) {
+    const int KB = a.D / 128;
+    const CoreLayout L = core_layout<N, 2, 1>((KB + S - 1) / S);
+    return launch_clustered(moe_pair_kernel<KIND, N>, dim3(W_max, a.I / 128, S), S, L.total, stream, a);
+}
+
+template <int KIND, int N>
+static cudaError_t launch_down_t(const MoeArgs& a, int S, int W_max, cudaStream_t stream) {
+    const int KB = a.I / 128;
+    const CoreLayout L = core_layout<N, 1, 1>((KB + S - 1) / S);
+    return launch_clustered(moe_down_kernel<KIND, N>, dim3(W_max, a.D / 128, S), S, L.total, stream, a);
+}
+
+#define SX_MOE_N_LIST(X) \
+    X(16) X(18) X(20) X(22) X(24) X(26) X(28) X(30) X(32) X(34) X(36) X(38) X(40) X(42) X(44) X(46) X(48) X(50) X(52) \
+    X(54) X(56) X(58) X(60) X(62) X(64) X(66) X(68) X(70) X(72) X(74) X(76) X(78) X(80) X(82) X(84) X(86) X(88) X(90) \
+    X(92) X(94) X(96) X(98) X(100) X(102) X(104) X(106) X(108) X(110) X(112) X(114) X(116) X(118) X(120) X(122) X(124) \
+    X(126) X(128)
+
+#define SX_MOE_N_LIST_PAIR1(X) \
+    X(24) X(26) X(28) X(30) X(32) X(34) X(36) X(38) X(40) X(42) X(44) X(46) X(48) X(50) X(52) X(54) X(56) X(58) X(60) \
+    X(62) X(64)
+
+template <int KIND>
+cudaError_t moe_launch_kind(const MoeArgs& a, int n_gu, int n_d, int S_gu, int S_d, int W_max, cudaStream_t stream) {
+    cudaError_t e = cudaErrorInvalidValue;
+#define SX_PAIR_CASE(NN) \
+    case NN: e = launch_pair_t<KIND, NN>(a, S_gu, W_max, stream); break;
+#define SX_DOWN_CASE(NN) \
+    case NN: e = launch_down_t<KIND, NN>(a, S_d, W_max, stream); break;
+    if constexpr (KIND == K_PAIR1) {
+        switch (n_gu) { SX_MOE_N_LIST_PAIR1(SX_PAIR_CASE) default: return cudaErrorInvalidValue; }
+        if (e != cudaSuccess) return e;
+        switch (n_d) { SX_MOE_N_LIST_PAIR1(SX_DOWN_CASE) default: return cudaErrorInvalidValue; }
+    } else {
+        switch (n_gu) { SX_MOE_N_LIST(SX_PAIR_CASE) default: return cudaErrorInvalidValue; }
+        if (e != cudaSuccess) return e;
+        switch (n_d) { SX_MOE_N_LIST(SX_DOWN_CASE) default: return cudaErrorInvalidValue; }
+    }
+#undef SX_PAIR_CASE
+#undef SX_DOWN_CASE
+    return e;
+}
+
+}  // namespace sx

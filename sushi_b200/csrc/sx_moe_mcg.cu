@@ -1,0 +1,6 @@
+// MoE decode-chain instantiations for the MCG codebook family.
+#include "sx_moe_launch.cuh"
+
+namespace sx {
+template cudaError_t moe_launch_kind<K_MCG>(const MoeArgs&, int, int, int, int, int, cudaStream_t);
+}  // namespace sx

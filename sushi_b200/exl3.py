@@ -1,0 +1,293 @@
+"""Host-side mirror of the reference's `sushi_exl3` module surface, over the CUDA C ABI.
+
+Names, argument meaning and refusals follow the reference (beamivalice/sushi 1.7.2):
+  Decode / Codebook / Rate          src/exl3/expert_exl3.zig:54-226
+  Proj / Bank                       src/exl3/root.zig:30-39
+  linear / linear_grouped           src/exl3/linear.zig:27-54
+  moe / moe_with_shared / moe_with_gated_shared / moe_clamped
+                                    src/exl3/root.zig:51-125
+  router_topk                       src/moe_router.zig:442 (moeRouterTopK)
+  dequant_inner                     src/exl3/expert_exl3.zig:416 (reconstructInner)
+A refusal raises `Exl3Error` whose `.name` is the status name mirroring the reference's error
+(e.g. "SX_ERR_BAD_SHAPE" for error.BadExl3Shape).  Tensors are torch CUDA tensors: torch is the
+device-memory plumbing here, the arithmetic runs in libsushi_exl3_cuda.so.
+"""
+
+import ctypes
+import enum
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+TILE = 16
+HAD_DIM = 128
+
+
+class Codebook(enum.IntEnum):
+    MUL1 = 0
+    MCG = 1
+    SPEC1 = 2
+    PAIR1 = 3
+    STD1 = 4
+
+    @classmethod
+    def from_name(cls, name):
+        return {"mul1": cls.MUL1, "mcg": cls.MCG, "spec1": cls.SPEC1, "pair1": cls.PAIR1, "std1": cls.STD1}.get(name)
+
+    def tabled_hash_mask(self):
+        return self in (Codebook.SPEC1, Codebook.STD1)
+
+    def has_table(self):
+        return self.tabled_hash_mask() or self == Codebook.PAIR1
+
+
+TABLES = ("pair1-w16-v1", "spec1-w15", "spec1-w16", "std1", "spec1-test-per-rate")
+
+
+def table_index(name):
+    return TABLES.index(name)
+
+
+@dataclass(frozen=True)
+class Decode:
+    """format.Decode: codebook, codeword window (8..16; 16 masks nothing) and the STQ table."""
+
+    codebook: Codebook
+    window_bits: int = 16
+    table: Optional[int] = None
+
+    @staticmethod
+    def tabled(codebook, window_bits=16):
+        """Decode.tabled (src/exl3/expert_exl3.zig:152): SPEC1 under spec1-w15, STD1 under std1."""
+        t = {Codebook.SPEC1: table_index("spec1-w15"), Codebook.STD1: table_index("std1")}.get(Codebook(codebook))
+        return Decode(Codebook(codebook), window_bits, t)
+
+    def c(self):
+        return _lib.SxDecode(int(self.codebook), int(self.window_bits), -1 if self.table is None else int(self.table))
+
+
+class TileOrder(enum.IntEnum):
+    PACK = 0
+    PAIR_MAJOR = 1
+
+
+@dataclass
+class Proj:
+    """root.Proj: trellis U16 [E, in/16, out/16, n], suh F16 [E, in], svh F16 [E, out] (torch CUDA).
+    A 3-D trellis / 1-D scales are a one-bank projection."""
+
+    trellis: torch.Tensor
+    suh: torch.Tensor
+    svh: torch.Tensor
+    tile_order: TileOrder = TileOrder.PACK
+
+    def dims(self):
+        t = self.trellis
+        if self.tile_order == TileOrder.PAIR_MAJOR:
+            if t.dim() != 5 or t.shape[3] != 2:
+                raise Exl3Error(19)
+            return t.shape[0], t.shape[2] * 16, t.shape[1] * 32, t.shape[4]
+        if t.dim() == 3:
+            return 1, t.shape[0] * 16, t.shape[1] * 16, t.shape[2]
+        if t.dim() != 4:
+            raise Exl3Error(1)
+        return t.shape[0], t.shape[1] * 16, t.shape[2] * 16, t.shape[3]
+
+    def c(self):
+        experts, in_f, out_f, n = self.dims()
+        for a in (self.trellis, self.suh, self.svh):
+            if not a.is_cuda or not a.is_contiguous():
+                raise Exl3Error(1)
+        if self.trellis.dtype not in (torch.uint16, torch.int16) or self.suh.dtype not in (torch.float16, torch.uint16, torch.int16) \
+                or self.svh.dtype not in (torch.float16, torch.uint16, torch.int16):
+            raise Exl3Error(2)
+        if self.suh.numel() != experts * in_f or self.svh.numel() != experts * out_f:
+            raise Exl3Error(1)
+        return _lib.SxProj(self.trellis.data_ptr(), self.suh.data_ptr(), self.svh.data_ptr(), experts, in_f, out_f, n,
+                           int(self.tile_order))
+
+
+@dataclass
+class Bank:
+    gate: Proj
+    up: Proj
+    down: Proj
+
+    def c(self):
+        return _lib.SxBank(self.gate.c(), self.up.c(), self.down.c())
+
+
+class Exl3Error(RuntimeError):
+    def __init__(self, status):
+        self.status = int(status)
+        self.name = _lib.load().sx_status_name(self.status).decode()
+        super().__init__(self.name)
+
+
+_DT = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+
+def _check(status):
+    if status != 0:
+        raise Exl3Error(status)
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def lib():
+    return _lib.load()
+
+
+def linear(x, proj: Proj, dec: Decode):
+    """linear.linear: x [rows, in] (bf16/f16/f32) through the one-bank proj -> [rows, out] in x's dtype."""
+    if x.dim() != 2 or not x.is_contiguous():
+        raise Exl3Error(1)
+    if x.dtype not in _DT:
+        raise Exl3Error(2)
+    _, in_f, out_f, _ = proj.dims()
+    if x.shape[1] != in_f:
+        raise Exl3Error(1)
+    y = torch.empty((x.shape[0], out_f), dtype=x.dtype, device=x.device)
+    p, d = proj.c(), dec.c()
+    _check(lib().sx_linear(_stream(), ctypes.byref(p), ctypes.byref(d), x.data_ptr(), _DT[x.dtype], x.shape[0],
+                           y.data_ptr()))
+    return y
+
+
+def linear_grouped(x, proj: Proj, dec: Decode):
+    """linear.linearGrouped: x [G, rows, in] through the G-bank proj (bank g serves x[g]) -> [G, rows, out]."""
+    if x.dim() != 3 or not x.is_contiguous():
+        raise Exl3Error(1)
+    if x.dtype not in _DT:
+        raise Exl3Error(2)
+    experts, in_f, out_f, _ = proj.dims()
+    if x.shape[0] != experts or x.shape[2] != in_f:
+        raise Exl3Error(1)
+    y = torch.empty((x.shape[0], x.shape[1], out_f), dtype=x.dtype, device=x.device)
+    p, d = proj.c(), dec.c()
+    _check(lib().sx_linear_grouped(_stream(), ctypes.byref(p), ctypes.byref(d), x.data_ptr(), _DT[x.dtype],
+                                   x.shape[1], y.data_ptr()))
+    return y
+
+
+def dequant_inner(proj: Proj, expert: int, dec: Decode):
+    """reconstructInner on the device: the [in, out] f16 inner matrix of one expert, as int16 bits."""
+    _, in_f, out_f, _ = proj.dims()
+    out = torch.empty((in_f, out_f), dtype=torch.int16, device=proj.trellis.device)
+    p, d = proj.c(), dec.c()
+    _check(lib().sx_dequant_inner(_stream(), ctypes.byref(p), expert, ctypes.byref(d), out.data_ptr()))
+    return out
+
+
+def decode_codewords(n: int, dec: Decode, device="cuda"):
+    """Every codeword's decode at rate n (int32: weight bits low, PAIR1's partner high)."""
+    out = torch.empty(65536, dtype=torch.int32, device=device)
+    d = dec.c()
+    _check(lib().sx_decode_codewords(_stream(), n, ctypes.byref(d), out.data_ptr()))
+    return out
+
+
+class RouterMode(enum.IntEnum):
+    SOFTMAX = 0
+    SIGMOID_BIAS = 1
+    SIGMOID_BIAS_GROUPED = 2
+
+
+def router_topk(logits, k, mode=RouterMode.SOFTMAX, bias=None, route_norm=True, route_scale=1.0, n_group=0,
+                topk_group=0):
+    """moeRouterTopK: logits [..., E] f32 -> (inds [..., k] int32, scores [..., k] f32), or None where the
+    reference's fused kernel declines (the caller keeps its own chain)."""
+    lg = logits.reshape(-1, logits.shape[-1]).contiguous()
+    if lg.dtype != torch.float32:
+        lg = lg.float()
+    rows, experts = lg.shape
+    inds = torch.empty((rows, k), dtype=torch.int32, device=lg.device)
+    scores = torch.empty((rows, k), dtype=torch.float32, device=lg.device)
+    b = None if bias is None else bias.float().contiguous()
+    st = lib().sx_router_topk(_stream(), lg.data_ptr(), None if b is None else b.data_ptr(), rows, experts, k, int(mode),
+                              1 if route_norm else 0, float(route_scale), n_group, topk_group, inds.data_ptr(),
+                              scores.data_ptr())
+    if st == 12:  # SX_ERR_ROUTER_DECLINED
+        return None
+    _check(st)
+    shape = tuple(logits.shape[:-1]) + (k,)
+    return inds.reshape(shape), scores.reshape(shape)
+
+
+_WS_CACHE = {}
+
+
+def _workspace(nbytes, device):
+    key = (str(device),)
+    ws = _WS_CACHE.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
+        _WS_CACHE[key] = ws
+    return ws
+
+
+def moe(x, bank: Bank, inds, scores, dec: Decode, shared=None, shared_gate=None, clamp_limit=0, workspace=None):
+    """root.moe (and its shared / gated-shared / clamped forms): routed SwiGLU experts over x [..., D]
+    for top-k inds/scores [..., K]; returns x's shape and dtype."""
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1]).contiguous()
+    rows = x2.shape[0]
+    ix = inds.reshape(rows, -1).to(torch.int32).contiguous()
+    sc = scores.reshape(rows, -1).float().contiguous()
+    topk = ix.shape[1]
+    if sc.shape != ix.shape:
+        raise Exl3Error(1)
+    if x2.dtype not in _DT:
+        raise Exl3Error(2)
+    b = bank.c()
+    need = lib().sx_moe_workspace_bytes(ctypes.byref(b), rows, topk)
+    ws = workspace if workspace is not None else _workspace(need, x.device)
+    y = torch.empty_like(x2)
+    d = dec.c()
+    sh = None if shared is None else shared.reshape(rows, -1).to(x2.dtype).contiguous()
+    sg = None if shared_gate is None else shared_gate.reshape(rows).to(x2.dtype).contiguous()
+    _check(lib().sx_moe(_stream(), ctypes.byref(b), ctypes.byref(d), x2.data_ptr(), _DT[x2.dtype], rows, ix.data_ptr(),
+                        sc.data_ptr(), topk, None if sh is None else sh.data_ptr(),
+                        None if sg is None else sg.data_ptr(), int(clamp_limit), y.data_ptr(), ws.data_ptr(),
+                        ws.numel()))
+    return y.reshape(shape)
+
+
+def moe_with_shared(x, bank, inds, scores, dec, shared):
+    return moe(x, bank, inds, scores, dec, shared=shared)
+
+
+def moe_with_gated_shared(x, bank, inds, scores, dec, down, gate):
+    return moe(x, bank, inds, scores, dec, shared=down, shared_gate=gate)
+
+
+def moe_clamped(x, bank, inds, scores, dec, limit):
+    if limit <= 0 or limit > 128:
+        raise Exl3Error(3)
+    return moe(x, bank, inds, scores, dec, clamp_limit=limit)
+
+
+def device_error():
+    """The latched code of a bounded device wait that gave up (0 = none); clears it."""
+    return lib().sx_device_error(_stream())
+
+
+def table_row(table, n):
+    out = (ctypes.c_uint32 * 4)()
+    if lib().sx_table_row(table, n, out) != 0:
+        return None
+    return tuple(int(v) for v in out)
+
+
+def table_info(table):
+    name, digest = ctypes.c_char_p(), ctypes.c_char_p()
+    cb, win, fields, n_lo, rows = (ctypes.c_int32() for _ in range(5))
+    _check(lib().sx_table_info(table, ctypes.byref(name), ctypes.byref(cb), ctypes.byref(win), ctypes.byref(digest),
+                               ctypes.byref(fields), ctypes.byref(n_lo), ctypes.byref(rows)))
+    return {"name": name.value.decode(), "codebook": Codebook(cb.value), "window_bits": win.value,
+            "digest": digest.value.decode(), "fields": fields.value, "n_lo": n_lo.value, "rows": rows.value}

@@ -1,0 +1,128 @@
+"""The C ABI on the host (no GPU): the library loads, exports every symbol include/sushi_exl3.h
+declares, names every status, holds the reference's codebook tables (pinned by their sha256
+digests, src/exl3/codebook_tables.zig:281-460), and refuses bad calls by name before touching the
+device (src/exl3/root.zig:98-135 admission)."""
+
+import ctypes
+import hashlib
+import os
+import re
+
+import pytest
+
+from sushi_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+FAKE = 0x10000  # an aligned, never-dereferenced device address: refusals return before any access
+
+
+@pytest.fixture(scope="module")
+def L():
+    return _lib.load()
+
+
+def test_every_declared_symbol_is_exported(L):
+    header = open(os.path.join(ROOT, "include", "sushi_exl3.h")).read()
+    declared = set(re.findall(r"^\w[\w\s\*]*?\b(sx_\w+)\(", header, re.M))
+    assert {"sx_linear", "sx_moe", "sx_router_topk", "sx_dequant_inner"} <= declared
+    for name in declared:
+        assert hasattr(L, name), name
+    assert set(declared) <= set(_lib.SIGNATURES), "the ctypes binding covers every declared function"
+
+
+def test_status_names(L):
+    names = {i: L.sx_status_name(i).decode() for i in range(0, 20)}
+    assert names[0] == "SX_OK"
+    assert names[1] == "SX_ERR_BAD_SHAPE"
+    assert names[4] == "SX_ERR_TOPK_EXCEEDS_REDUCE_BANK"
+    assert names[12] == "SX_ERR_ROUTER_DECLINED"
+    assert len(set(names.values())) == 20
+    assert L.sx_status_name(999).decode() == "SX_ERR_UNKNOWN"
+    assert b"sushi" in L.sx_version()
+
+
+def _digest(fields, ns, rows):
+    h = hashlib.sha256()
+    for n, r in zip(ns, rows):
+        h.update((str(n) + "".join("," + format(v, "08x") for v in r[:fields]) + "\n").encode())
+    return h.hexdigest()[:8]
+
+
+PINNED = {"pair1-w16-v1": "c089b4eb", "spec1-w15": "37f72431", "spec1-w16": "753ffa03", "std1": "c5dba171",
+          "spec1-test-per-rate": "a2f2fe40"}
+
+
+def test_library_tables_keep_the_reference_digests():
+    import sushi_b200 as sx
+
+    for t in range(5):
+        info = sx.table_info(t)
+        ns = [info["n_lo"] + 2 * i for i in range(info["rows"])]
+        rows = [sx.table_row(t, n) for n in ns]
+        assert all(r is not None for r in rows)
+        assert _digest(info["fields"], ns, rows) == PINNED[info["name"]] == info["digest"], info["name"]
+    assert sx.table_row(1, 14) is None and sx.table_row(3, 16) is None and sx.table_row(0, 66) is None
+
+
+def _proj(in_f=256, out_f=128, n=32, experts=1):
+    return _lib.SxProj(FAKE, FAKE, FAKE, experts, in_f, out_f, n, 0)
+
+
+def _dec(cb=1, w=16, table=-1):
+    return _lib.SxDecode(cb, w, table)
+
+
+@pytest.mark.parametrize(
+    "proj,dec,dtype,rows,want",
+    [
+        (_proj(in_f=200), _dec(), 2, 1, "SX_ERR_BAD_SHAPE"),
+        (_proj(out_f=130), _dec(), 2, 1, "SX_ERR_BAD_SHAPE"),
+        (_proj(n=31), _dec(), 2, 1, "SX_ERR_TRELLIS_GEOMETRY"),
+        (_proj(n=130), _dec(), 2, 1, "SX_ERR_TRELLIS_GEOMETRY"),
+        (_proj(), _dec(), 7, 1, "SX_ERR_BAD_DTYPE"),
+        (_proj(), _dec(), 2, 0, "SX_ERR_BAD_SHAPE"),
+        (_proj(), _dec(w=7), 2, 1, "SX_ERR_WINDOW_UNSUPPORTED"),
+        (_proj(), _dec(cb=2), 2, 1, "SX_ERR_CODEBOOK_TABLE_UNKNOWN"),
+        (_proj(n=16), _dec(cb=4, table=3), 2, 1, "SX_ERR_CODEBOOK_TABLE_RATE_MISSING"),
+        (_proj(), _dec(cb=3, w=15), 2, 1, "SX_ERR_CODEBOOK_TABLE_WINDOW_MISMATCH"),
+        (_proj(), _dec(cb=9), 2, 1, "SX_ERR_CODEBOOK_UNSUPPORTED"),
+        (_proj(experts=2), _dec(), 2, 1, "SX_ERR_BAD_SHAPE"),
+    ],
+)
+def test_linear_refusals_before_launch(L, proj, dec, dtype, rows, want):
+    st = L.sx_linear(None, ctypes.byref(proj), ctypes.byref(dec), FAKE, dtype, rows, FAKE)
+    assert L.sx_status_name(st).decode() == want
+
+
+def test_misaligned_trellis_is_refused(L):
+    p = _lib.SxProj(FAKE + 2, FAKE, FAKE, 1, 256, 128, 32, 0)
+    st = L.sx_linear(None, ctypes.byref(p), ctypes.byref(_dec()), FAKE, 2, 1, FAKE)
+    assert L.sx_status_name(st).decode() == "SX_ERR_BAD_SHAPE"
+
+
+def test_moe_refusals_before_launch(L):
+    g = _lib.SxProj(FAKE, FAKE, FAKE, 8, 256, 128, 32, 0)
+    d = _lib.SxProj(FAKE, FAKE, FAKE, 8, 128, 256, 32, 0)
+    bank = _lib.SxBank(g, g, d)
+    dec = _dec()
+    call = lambda topk=4, clamp=0, ws=1 << 30, bank=bank: L.sx_status_name(L.sx_moe(
+        None, ctypes.byref(bank), ctypes.byref(dec), FAKE, 2, 3, FAKE, FAKE, topk, None, None, clamp, FAKE, FAKE,
+        ws)).decode()
+    assert call(topk=33) == "SX_ERR_TOPK_EXCEEDS_REDUCE_BANK"
+    assert call(topk=9) == "SX_ERR_TOPK_EXCEEDS_EXPERTS"
+    assert call(clamp=129) == "SX_ERR_INVALID_CLAMP"
+    assert call(ws=16) == "SX_ERR_WORKSPACE_TOO_SMALL"
+    bad = _lib.SxBank(g, g, _lib.SxProj(FAKE, FAKE, FAKE, 8, 256, 256, 32, 0))
+    assert call(bank=bad) == "SX_ERR_BAD_SHAPE"
+    assert L.sx_moe_workspace_bytes(ctypes.byref(bank), 3, 4) > 3 * 4 * (128 * 2 + 256 * 4)
+
+
+def test_router_declines_before_launch(L):
+    st = L.sx_router_topk(None, FAKE, None, 1, 64, 33, 0, 1, 1.0, 0, 0, FAKE, FAKE)
+    assert L.sx_status_name(st).decode() == "SX_ERR_ROUTER_DECLINED"
+    st = L.sx_router_topk(None, FAKE, None, 1, 4096, 8, 0, 1, 1.0, 0, 0, FAKE, FAKE)
+    assert L.sx_status_name(st).decode() == "SX_ERR_ROUTER_DECLINED"
+    st = L.sx_router_topk(None, FAKE, None, 1, 64, 8, 1, 1, 1.0, 0, 0, FAKE, FAKE)  # sigmoid without bias
+    assert L.sx_status_name(st).decode() == "SX_ERR_ROUTER_DECLINED"
+    st = L.sx_router_topk(None, FAKE, FAKE, 1, 64, 8, 2, 1, 1.0, 3, 1, FAKE, FAKE)  # 64 % 3 != 0
+    assert L.sx_status_name(st).decode() == "SX_ERR_ROUTER_DECLINED"

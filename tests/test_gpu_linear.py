@@ -1,0 +1,119 @@
+"""Fused EXL3 projection (sx_linear) against the f32 truth and the reference's CPU projection.
+
+Truth: y = x . W in f64 with W the reference's dense f32 twin `decodeDense`
+(src/exl3/linear.zig:406-431), as its f32-truth bars score the Metal arms
+(src/exl3/f32_truth.zig:56-63).  Bar: max |y - truth| / max |truth| <= 1e-2 (BASELINE.json's
+north star) and relative RMS <= 5e-3.  The reference's own CPU projection `format.project`
+(src/exl3/expert_exl3.zig:546), which rounds its inner sums and output to f16, is checked
+against the same bars.
+"""
+
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+from oracle import synth
+from tests.helpers import MAX_REL_TOL, REL_RMS_TOL, dec_args, dev, max_rel, rel_rms, random_pack, to_f32
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def sx():
+    import sushi_b200
+
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    return sushi_b200
+
+
+def _x(seed, rows, in_f, dtype):
+    x = synth.activations(seed, rows, in_f)
+    t = torch.from_numpy(x).cuda().to(dtype)
+    return t, t.float().cpu().numpy()
+
+
+def _check(sx, tr, su, sv, in_f, out_f, n, cb, w, rows, dtype=None, seed=0):
+    dtype = dtype or torch.bfloat16
+    oargs, dec = dec_args(cb, w)
+    proj = sx.Proj(dev(tr, torch), dev(su, torch), dev(sv, torch))
+    xt, xv = _x(seed + rows, rows, in_f, dtype)
+    y = to_f32(sx.linear(xt, proj, dec))
+    W = orc.decode_dense(tr, su, sv, in_f, out_f, n, *oargs)
+    truth = orc.matvec_f64(W, xv)
+    assert np.isfinite(y).all()
+    assert max_rel(y, truth) <= MAX_REL_TOL, max_rel(y, truth)
+    assert rel_rms(y, truth) <= REL_RMS_TOL, rel_rms(y, truth)
+    return y, truth, xv
+
+
+@pytest.mark.parametrize("n", [16, 24, 32, 36, 40, 42, 48, 56, 64, 80, 96, 112, 128])
+def test_linear_mcg_every_rate_class(sx, n):
+    tr, su, sv = random_pack(n, 256, 384, n)
+    _check(sx, tr, su, sv, 256, 384, n, orc.CB_MCG, 16, rows=1)
+
+
+@pytest.mark.parametrize("rows", [1, 2, 3, 4, 7, 8, 9, 16, 17, 33, 64])
+def test_linear_rows(sx, rows):
+    tr, su, sv = random_pack(11, 512, 256, 32)
+    _check(sx, tr, su, sv, 512, 256, 32, orc.CB_MCG, 16, rows=rows)
+
+
+@pytest.mark.parametrize(
+    "cb,w,n",
+    [(orc.CB_MUL1, 16, 32), (orc.CB_MUL1, 16, 64), (orc.CB_MCG, 12, 40), (orc.CB_MCG, 8, 48), (orc.CB_SPEC1, 15, 16),
+     (orc.CB_SPEC1, 15, 32), (orc.CB_SPEC1, 15, 64), (orc.CB_SPEC1, 15, 128), (orc.CB_STD1, 15, 40),
+     (orc.CB_PAIR1, 16, 24), (orc.CB_PAIR1, 16, 32), (orc.CB_PAIR1, 16, 48), (orc.CB_PAIR1, 16, 64)],
+)
+def test_linear_codebooks(sx, cb, w, n):
+    tr, su, sv = random_pack(100 + n + cb, 384, 256, n)
+    _check(sx, tr, su, sv, 384, 256, n, cb, w, rows=3)
+
+
+@pytest.mark.parametrize("dtype", ["float32", "float16", "bfloat16"])
+def test_linear_dtypes(sx, dtype):
+    tr, su, sv = random_pack(21, 256, 256, 32)
+    _check(sx, tr, su, sv, 256, 256, 32, orc.CB_MCG, 16, rows=2, dtype=getattr(torch, dtype))
+
+
+@pytest.mark.parametrize("in_f,out_f", [(128, 128), (7168, 256), (256, 7168), (2048, 1024)])
+def test_linear_geometry_splits(sx, in_f, out_f):
+    tr, su, sv = random_pack(in_f + out_f, in_f, out_f, 32)
+    _check(sx, tr, su, sv, in_f, out_f, 32, orc.CB_MCG, 16, rows=1)
+
+
+def test_linear_encoded_pack_and_reference_projection(sx):
+    # A pack the quantizer restatement wrote (w12 keeps the CPU search quick), with outlier channels.
+    w = synth.dense_weight(7, 512, 384, 0.02, outlier_frac=0.01)
+    tr, su, sv, _ = synth.encode_weight(w, 7, "blk.0.ffn", 32, orc.CB_MCG, 12)
+    y, truth, xv = _check(sx, tr, su, sv, 512, 384, 32, orc.CB_MCG, 12, rows=2)
+    ref = orc.project(xv, tr, su, sv, 512, 384, 32, orc.CB_MCG, 12)
+    assert max_rel(ref, truth) <= MAX_REL_TOL
+    assert max_rel(y, ref) <= 2 * MAX_REL_TOL
+
+
+def test_linear_grouped(sx):
+    tr, su, sv = random_pack(33, 256, 128, 40, experts=3)
+    proj = sx.Proj(dev(tr, torch), dev(su, torch), dev(sv, torch))
+    _, dec = dec_args(orc.CB_MCG, 16)
+    xs = [synth.activations(40 + g, 2, 256) for g in range(3)]
+    xt = torch.from_numpy(np.stack(xs)).cuda().to(torch.bfloat16)
+    y = to_f32(sx.linear_grouped(xt, proj, dec))
+    for g in range(3):
+        W = orc.decode_dense(tr[g], su[g], sv[g], 256, 128, 40, orc.CB_MCG, 16)
+        truth = orc.matvec_f64(W, xt[g].float().cpu().numpy())
+        assert max_rel(y[g], truth) <= MAX_REL_TOL
+
+
+def test_linear_refusals(sx):
+    tr, su, sv = random_pack(3, 256, 128, 32)
+    proj = sx.Proj(dev(tr, torch), dev(su, torch), dev(sv, torch))
+    _, dec = dec_args(orc.CB_MCG, 16)
+    with pytest.raises(sx.Exl3Error) as e:
+        sx.linear(torch.zeros((1, 128), device="cuda", dtype=torch.bfloat16), proj, dec)
+    assert e.value.name == "SX_ERR_BAD_SHAPE"
+    with pytest.raises(sx.Exl3Error) as e:
+        sx.linear(torch.zeros((1, 256), device="cuda", dtype=torch.int32), proj, dec)
+    assert e.value.name == "SX_ERR_BAD_DTYPE"
+    assert sx.device_error() == 0

@@ -1,0 +1,155 @@
+"""Router top-k and the routed-expert chain against the oracle's truth.
+
+Router: inds exactly the oracle's (ties to the lowest id, src/moe_router.zig:130-150), weights
+within 1e-5.  MoE: y against the f64 routed sum of the reference's f32-truth slot
+(src/exl3/f32_truth.zig:85-98, routedErr :109-156) over dense twins of every expert, within the
+stated GEMV bar (max relative 1e-2, relative RMS 5e-3).
+"""
+
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+from oracle import synth
+from tests.helpers import MAX_REL_TOL, REL_RMS_TOL, dec_args, dev, max_rel, rel_rms, random_pack, to_f32
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def sx():
+    import sushi_b200
+
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    return sushi_b200
+
+
+@pytest.mark.parametrize("T,E,k", [(1, 512, 10), (8, 512, 10), (64, 512, 10), (5, 256, 8), (3, 64, 1), (2, 2048, 32)])
+def test_router_softmax(sx, T, E, k):
+    rng = np.random.default_rng(T * 1000 + E + k)
+    logits = rng.standard_normal((T, E)).astype(np.float32)
+    inds, scores = sx.router_topk(torch.from_numpy(logits).cuda(), k)
+    wi, ww = orc.router_truth(logits, k)
+    np.testing.assert_array_equal(inds.cpu().numpy(), wi)
+    np.testing.assert_allclose(scores.cpu().numpy(), ww, rtol=1e-5, atol=1e-7)
+
+
+def test_router_ties_go_to_lowest_id(sx):
+    logits = np.zeros((2, 64), np.float32)
+    logits[0, [5, 9, 40]] = 1.0
+    inds, _ = sx.router_topk(torch.from_numpy(logits).cuda(), 4)
+    assert inds.cpu().numpy()[0].tolist() == [5, 9, 40, 0]
+    assert inds.cpu().numpy()[1].tolist() == [0, 1, 2, 3]
+
+
+@pytest.mark.parametrize("grouped", [False, True])
+def test_router_sigmoid_bias(sx, grouped):
+    rng = np.random.default_rng(9 + grouped)
+    T, E, k = 6, 256, 8
+    logits = rng.standard_normal((T, E)).astype(np.float32)
+    bias = (rng.standard_normal(E) * 0.1).astype(np.float32)
+    mode = sx.RouterMode.SIGMOID_BIAS_GROUPED if grouped else sx.RouterMode.SIGMOID_BIAS
+    kw = dict(n_group=8, topk_group=4) if grouped else {}
+    inds, scores = sx.router_topk(torch.from_numpy(logits).cuda(), k, mode, torch.from_numpy(bias).cuda(),
+                                  route_norm=True, route_scale=2.5, **kw)
+    wi, ww = orc.router_truth(logits, k, "sigmoid_bias_grouped" if grouped else "sigmoid_bias", bias, True, 2.5, **kw)
+    np.testing.assert_array_equal(inds.cpu().numpy(), wi)
+    np.testing.assert_allclose(scores.cpu().numpy(), ww, rtol=1e-5, atol=1e-7)
+
+
+def test_router_declines_like_the_reference(sx):
+    lg = torch.zeros((1, 64), device="cuda")
+    assert sx.router_topk(lg, 33) is None
+    assert sx.router_topk(torch.zeros((1, 4096), device="cuda"), 8) is None
+    assert sx.router_topk(lg, 4, sx.RouterMode.SIGMOID_BIAS_GROUPED, torch.zeros(64, device="cuda"), n_group=3,
+                          topk_group=1) is None
+
+
+def _bank(seed, E, D, I, n_gu, n_d):
+    g = random_pack(seed, D, I, n_gu, experts=E)
+    u = random_pack(seed + 1, D, I, n_gu, experts=E)
+    d = random_pack(seed + 2, I, D, n_d, experts=E, suh_mag=0.05)
+    return g, u, d
+
+
+def _truth(bank_np, D, I, n_gu, n_d, oargs, x, inds, wts, limit=0.0):
+    dense = {}
+    y = np.zeros((x.shape[0], D), np.float64)
+    for r in range(x.shape[0]):
+        for k in range(inds.shape[1]):
+            e = int(inds[r, k])
+            if e not in dense:
+                g, u, d = bank_np
+                dense[e] = (orc.decode_dense(g[0][e], g[1][e], g[2][e], D, I, n_gu, *oargs),
+                            orc.decode_dense(u[0][e], u[1][e], u[2][e], D, I, n_gu, *oargs),
+                            orc.decode_dense(d[0][e], d[1][e], d[2][e], I, D, n_d, *oargs))
+            y[r] += wts[r, k] * orc.expert_truth(dense[e], x[r], limit)
+    return y
+
+
+def _sx_bank(sx, bank_np):
+    return sx.Bank(*[sx.Proj(dev(p[0], torch), dev(p[1], torch), dev(p[2], torch)) for p in bank_np])
+
+
+def _route(seed, T, E, k):
+    rng = np.random.default_rng(seed)
+    inds = np.stack([rng.choice(E, size=k, replace=False) for _ in range(T)]).astype(np.int32)
+    wts = (0.05 + rng.random((T, k)) * 0.25).astype(np.float32)
+    return inds, wts
+
+
+@pytest.mark.parametrize("T", [1, 3, 8, 16, 37])
+def test_moe_chain_matches_f32_truth(sx, T):
+    E, D, I, k = 24, 512, 256, 4
+    bank_np = _bank(T, E, D, I, 32, 32)
+    oargs, dec = dec_args(orc.CB_MCG, 16)
+    x = synth.activations(T, T, D)
+    inds, wts = _route(T + 5, T, E, k)
+    xt = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    y = to_f32(sx.moe(xt, _sx_bank(sx, bank_np), torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda(), dec))
+    truth = _truth(bank_np, D, I, 32, 32, oargs, xt.float().cpu().numpy(), inds, wts)
+    assert np.isfinite(y).all()
+    assert max_rel(y, truth) <= MAX_REL_TOL, max_rel(y, truth)
+    assert rel_rms(y, truth) <= REL_RMS_TOL, rel_rms(y, truth)
+    assert sx.device_error() == 0
+
+
+@pytest.mark.parametrize("cb,w,n_gu,n_d", [(orc.CB_PAIR1, 16, 24, 40), (orc.CB_SPEC1, 15, 16, 32), (orc.CB_MUL1, 16, 48, 32)])
+def test_moe_codebooks_and_mixed_down_rate(sx, cb, w, n_gu, n_d):
+    E, D, I, k, T = 12, 256, 128, 3, 5
+    bank_np = _bank(cb * 10 + n_gu, E, D, I, n_gu, n_d)
+    oargs, dec = dec_args(cb, w)
+    x = synth.activations(77, T, D)
+    inds, wts = _route(cb, T, E, k)
+    xt = torch.from_numpy(x).cuda().to(torch.float16)
+    y = to_f32(sx.moe(xt, _sx_bank(sx, bank_np), torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda(), dec))
+    truth = _truth(bank_np, D, I, n_gu, n_d, oargs, xt.float().cpu().numpy(), inds, wts)
+    assert max_rel(y, truth) <= MAX_REL_TOL, max_rel(y, truth)
+
+
+def test_moe_clamped_and_shared(sx):
+    E, D, I, k, T = 8, 256, 128, 2, 4
+    bank_np = _bank(5, E, D, I, 32, 32)
+    oargs, dec = dec_args(orc.CB_MCG, 16)
+    x = synth.activations(5, T, D) * 4.0
+    inds, wts = _route(6, T, E, k)
+    xt = torch.from_numpy(x).cuda().to(torch.float32)
+    b = _sx_bank(sx, bank_np)
+    ii, ww = torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda()
+    y = to_f32(sx.moe_clamped(xt, b, ii, ww, dec, 2))
+    truth = _truth(bank_np, D, I, 32, 32, oargs, x, inds, wts, limit=2.0)
+    assert max_rel(y, truth) <= MAX_REL_TOL, max_rel(y, truth)
+    shared = torch.randn((T, D), device="cuda")
+    gate = torch.randn((T,), device="cuda")
+    y2 = to_f32(sx.moe_with_gated_shared(xt, b, ii, ww, dec, shared, gate))
+    base = _truth(bank_np, D, I, 32, 32, oargs, x, inds, wts)
+    want = base + (1 / (1 + np.exp(-gate.cpu().numpy().astype(np.float64))))[:, None] * shared.cpu().numpy()
+    assert max_rel(y2, want) <= MAX_REL_TOL
+    with pytest.raises(sx.Exl3Error) as e:
+        sx.moe(xt, b, torch.zeros((T, 33), dtype=torch.int32, device="cuda"), torch.zeros((T, 33), device="cuda"), dec)
+    assert e.value.name == "SX_ERR_TOPK_EXCEEDS_REDUCE_BANK"
+    with pytest.raises(sx.Exl3Error) as e:
+        sx.moe_clamped(xt, b, ii, ww, dec, 129)
+    assert e.value.name == "SX_ERR_INVALID_CLAMP"
