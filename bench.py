@@ -183,7 +183,9 @@ def main():
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     L = _lib.load()
-    stream = torch.cuda.current_stream()
+    # graphs are captured on a side stream; every launch of the bench runs on it
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     sptr = ctypes.c_void_p(stream.cuda_stream)
     dec = sx.Decode(sx.Codebook.MCG, 16).c()
 

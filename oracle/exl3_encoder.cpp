@@ -82,37 +82,81 @@ struct Encoder {
         back.assign((size_t)TILE_LEN * stride, 0);
         best.assign(stride, 0.0f);
         bfresh.assign(stride, 0);
+        for (auto& row : tab_t)
+            for (auto& t : row) t.clear();
         return 0;
     }
 
     // One Viterbi step after the first, for every edge: the reference's per-edge loop over
     // fresh bits, run fresh-outer so the edge loop vectorises.  Each edge still visits fresh
     // values in ascending order with a strict `<`, so best and back are the reference's.
+    // Edges are walked as e = (p << k) | r with the codebook table pre-permuted to
+    // [fresh][r][p], so both the table and the predecessor cost (index (fresh << (kr-k)) | p)
+    // are read contiguously.
+    std::vector<float> tab_t[9][9];
+    std::vector<float> best_t;
+    std::vector<uint32_t> bf_t;
+
+    const float* permuted_table(int k, int k_next) {
+        std::vector<float>& t = tab_t[k][k_next];
+        if (t.empty()) {
+            const int kr = w - k_next;
+            const size_t kk = (size_t)1 << k_next, R = (size_t)1 << k, P = (size_t)1 << (kr - k);
+            t.resize(kk * R * P);
+            for (size_t f = 0; f < kk; f++)
+                for (size_t r = 0; r < R; r++)
+                    for (size_t p = 0; p < P; p++) t[(f * R + r) * P + p] = table[(f << kr) | (p << k) | r];
+        }
+        return t.data();
+    }
+
     void step_rest(float* prev, float* curr, uint8_t* back_row, int k, int k_next, float target) {
         const int kr = w - k_next;
         const size_t kk = (size_t)1 << k_next;
         const size_t edges = (size_t)1 << kr;
+        if (kr >= k) {
+            const size_t R = (size_t)1 << k, P = (size_t)1 << (kr - k);
+            const float* tt = permuted_table(k, k_next);
+            if (best_t.size() < edges) {
+                best_t.resize(edges);
+                bf_t.resize(edges);
+            }
+            float* bst = best_t.data();
+            uint32_t* bf = bf_t.data();
+            for (size_t e = 0; e < edges; e++) { bst[e] = 65504.0f; bf[e] = 0; }
+            for (size_t fresh = 0; fresh < kk; fresh++) {
+                const float* pv = prev + (fresh << (kr - k));
+                for (size_t r = 0; r < R; r++) {
+                    const float* tab = tt + (fresh * R + r) * P;
+                    float* b = bst + r * P;
+                    uint32_t* bb = bf + r * P;
+                    for (size_t p = 0; p < P; p++) {
+                        const float dh = tab[p] - target;
+                        const float err = std::fma(dh, dh, pv[p]);
+                        const bool take = err < b[p];
+                        b[p] = take ? err : b[p];
+                        bb[p] = take ? (uint32_t)fresh : bb[p];
+                    }
+                }
+            }
+            for (size_t r = 0; r < R; r++)
+                for (size_t p = 0; p < P; p++) {
+                    const size_t e = (p << k) | r;
+                    curr[e] = f16_round(bst[r * P + p]);
+                    back_row[e] = (uint8_t)bf[r * P + p];
+                }
+            return;
+        }
         float* bst = best.data();
         uint8_t* bf = bfresh.data();
         for (size_t e = 0; e < edges; e++) { bst[e] = 65504.0f; bf[e] = 0; }
         for (size_t fresh = 0; fresh < kk; fresh++) {
             const float* tab = table.data() + (fresh << kr);
-            if (kr >= k) {
-                const float* pv = prev + (fresh << (kr - k));
-                for (size_t e = 0; e < edges; e++) {
-                    float dh = tab[e] - target;
-                    float err = std::fma(dh, dh, pv[e >> k]);
-                    bool take = err < bst[e];
-                    bst[e] = take ? err : bst[e];
-                    bf[e] = take ? (uint8_t)fresh : bf[e];
-                }
-            } else {
-                for (size_t e = 0; e < edges; e++) {
-                    size_t cw = (fresh << kr) | e;
-                    float dh = tab[e] - target;
-                    float err = std::fma(dh, dh, prev[cw >> k]);
-                    if (err < bst[e]) { bst[e] = err; bf[e] = (uint8_t)fresh; }
-                }
+            for (size_t e = 0; e < edges; e++) {
+                const size_t cw = (fresh << kr) | e;
+                const float dh = tab[e] - target;
+                const float err = std::fma(dh, dh, prev[cw >> k]);
+                if (err < bst[e]) { bst[e] = err; bf[e] = (uint8_t)fresh; }
             }
         }
         for (size_t e = 0; e < edges; e++) {
