@@ -49,7 +49,8 @@ enum {
     SX_ERR_DEVICE_TIMEOUT = 16,            /* a bounded device-side wait gave up (see sx_device_error) */
     SX_ERR_NCCL = 17,                      /* an NCCL call failed (expert-parallel calls) */
     SX_ERR_TILE_ORDER_UNSUPPORTED = 18,    /* error.Exl3TileOrderUnsupported (docs/pack-format.md) */
-    SX_ERR_GROUP_GEOMETRY = 19             /* error.Exl3GroupGeometry (src/exl3/layout.zig:80-95) */
+    SX_ERR_GROUP_GEOMETRY = 19,            /* error.Exl3GroupGeometry (src/exl3/layout.zig:80-95) */
+    SX_ERR_STATIC_SCRATCH_TOO_SMALL = 20   /* the call needs more scratch than sx_moe_static_scratch holds */
 };
 
 /* The status's name ("SX_OK", "SX_ERR_BAD_SHAPE", ...); a static string. */
@@ -155,6 +156,30 @@ size_t sx_moe_workspace_bytes(const sx_bank* bank, int32_t rows, int32_t topk);
 sx_status sx_moe(sx_stream stream, const sx_bank* bank, const sx_decode* dec, const void* x, sx_dtype dtype,
                  int32_t rows, const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
                  const void* shared_gate, int32_t clamp_limit, void* y, void* workspace, size_t workspace_bytes);
+
+/* ------------------------------------------------------------------ routed experts, no allocation
+ * sx_moe for callers that cannot allocate device memory at all.  Some hosts never call cudaMalloc
+ * on the path that runs the layer: a caller recording the layer into a CUDA graph (an allocation
+ * inside stream capture is not allowed), a caller whose allocator bills and owns every device
+ * byte (memory admission that a hidden allocation would bypass), or a latency-critical loop that
+ * cannot afford the device-wide synchronisation cudaMalloc implies.  They cannot hand sx_moe a
+ * workspace either, so this entry point takes none: its scratch is a fixed buffer compiled into
+ * the library (sx_moe_static_scratch_bytes(), 8 MiB), held by every GPU that loads the library
+ * until the process exits.  No counterpart in the reference, whose MLX host allocates per call.
+ *
+ * Arguments, semantics and refusals are sx_moe's.  A call whose workspace
+ * (sx_moe_workspace_bytes(bank, rows, topk)) exceeds the buffer returns
+ * SX_ERR_STATIC_SCRATCH_TOO_SMALL before launching anything.  The first call on a device looks up
+ * the buffer's device address (cudaGetSymbolAddress) with that device current; make that first
+ * call before any stream capture.  Every call on a device shares the one buffer and the buffer
+ * keeps the last call's contents (nothing in it needs to start at zero): calls that overlap on
+ * the GPU race, so issue them on one stream or order them. */
+sx_status sx_moe_static_scratch(sx_stream stream, const sx_bank* bank, const sx_decode* dec, const void* x,
+                                sx_dtype dtype, int32_t rows, const uint32_t* inds, const float* scores, int32_t topk,
+                                const void* shared, const void* shared_gate, int32_t clamp_limit, void* y);
+
+/* The size of sx_moe_static_scratch's buffer in bytes. */
+size_t sx_moe_static_scratch_bytes(void);
 
 /* ------------------------------------------------------------------ device error latch
  * Every bounded device-side wait that gives up records a code in a per-device latch instead of

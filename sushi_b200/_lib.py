@@ -48,6 +48,8 @@ SIGNATURES = {
     "sx_router_topk": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, ctypes.c_float, _I, _I, _P, _P]),
     "sx_moe_workspace_bytes": (_SZ, [ctypes.POINTER(SxBank), _I, _I]),
     "sx_moe": (_I, [_P, ctypes.POINTER(SxBank), ctypes.POINTER(SxDecode), _P, _I, _I, _P, _P, _I, _P, _P, _I, _P, _P, _SZ]),
+    "sx_moe_static_scratch": (_I, [_P, ctypes.POINTER(SxBank), ctypes.POINTER(SxDecode), _P, _I, _I, _P, _P, _I, _P, _P, _I, _P]),
+    "sx_moe_static_scratch_bytes": (_SZ, []),
     "sx_device_error": (_I, [_P]),
 }
 

@@ -159,6 +159,7 @@ const char* sx_status_name(sx_status s) {
         case SX_ERR_NCCL: return "SX_ERR_NCCL";
         case SX_ERR_TILE_ORDER_UNSUPPORTED: return "SX_ERR_TILE_ORDER_UNSUPPORTED";
         case SX_ERR_GROUP_GEOMETRY: return "SX_ERR_GROUP_GEOMETRY";
+        case SX_ERR_STATIC_SCRATCH_TOO_SMALL: return "SX_ERR_STATIC_SCRATCH_TOO_SMALL";
         default: return "SX_ERR_UNKNOWN";
     }
 }
