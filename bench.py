@@ -209,7 +209,8 @@ def main():
     def launch(in_f, out_f, n, m, proj):
         st = L.sx_linear(sptr, ctypes.byref(proj), ctypes.byref(dec), xbuf[in_f].data_ptr(), 2, m, ybuf[out_f].data_ptr())
         if st:
-            raise RuntimeError(L.sx_status_name(st).decode())
+            raise RuntimeError(f"{L.sx_status_name(st).decode()} {L.sx_last_error_detail().decode()} "
+                               f"(out {out_f} in {in_f} n {n} rows {m})")
 
     # one graph per config: every ring copy once (each launch reads weights no recent launch read)
     graphs, launches_per_step, bytes_per_step = [], 0, 0

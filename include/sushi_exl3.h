@@ -187,6 +187,10 @@ size_t sx_moe_static_scratch_bytes(void);
  * (0 = none) and clears it; synchronises `stream` first. */
 int32_t sx_device_error(sx_stream stream);
 
+/* Detail of the last SX_ERR_CUDA this thread got: the failing CUDA call's error name and where
+ * ("cudaLaunchKernelEx gemv: cudaErrorInvalidValue"); "" when there is none. */
+const char* sx_last_error_detail(void);
+
 /* The library's version string. */
 const char* sx_version(void);
 

@@ -51,6 +51,7 @@ SIGNATURES = {
     "sx_moe_static_scratch": (_I, [_P, ctypes.POINTER(SxBank), ctypes.POINTER(SxDecode), _P, _I, _I, _P, _P, _I, _P, _P, _I, _P]),
     "sx_moe_static_scratch_bytes": (_SZ, []),
     "sx_device_error": (_I, [_P]),
+    "sx_last_error_detail": (ctypes.c_char_p, []),
 }
 
 # Library extras (not in the Zig-facing header): table introspection for the config parser.

@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdio>
 #include <cstring>
 
 #include "../../include/sushi_exl3.h"
@@ -13,7 +14,19 @@
 
 namespace sx {
 
-sx_status cuda_status(cudaError_t e) { return e == cudaSuccess ? SX_OK : SX_ERR_CUDA; }
+namespace {
+thread_local char g_detail[256] = "";
+}
+
+void note_cuda_error(cudaError_t e, const char* where) {
+    snprintf(g_detail, sizeof(g_detail), "%s: %s", where, cudaGetErrorName(e));
+}
+
+sx_status cuda_status(cudaError_t e, const char* where) {
+    if (e == cudaSuccess) return SX_OK;
+    note_cuda_error(e, where);
+    return SX_ERR_CUDA;
+}
 
 // Decode-parameter resolution: format.Decode.requireTable / hashMask / pair1Pair
 // (src/exl3/expert_exl3.zig:141-174, :49-52) and the window admission of root.zig:217-224.
@@ -25,7 +38,14 @@ sx_status resolve_decode(const sx_decode* dec, int n, int* kind, DecParams* dp) 
     dp->wmask = (1u << dec->window_bits) - 1u;
     uint32_t row[4];
     switch (dec->codebook) {
-        case SX_CB_MCG: *kind = K_MCG; return SX_OK;
+        case SX_CB_MCG:
+            // decodeMcg (src/exl3/expert_exl3.zig:267-273): p = cw * 0xCBAC1FED, pair =
+            // 0x3B603B60 ^ (p & 0x8FFF8FFF); the kernels take the constants as values.
+            *kind = K_MCG;
+            dp->mult = 0xCBAC1FEDu;
+            dp->mask0 = 0x8FFF8FFFu;
+            dp->mask1 = 0x3B603B60u;
+            return SX_OK;
         case SX_CB_MUL1: *kind = K_MUL1; return SX_OK;
         case SX_CB_SPEC1:
         case SX_CB_STD1:
@@ -77,17 +97,6 @@ int sm_count() {
     return cached;
 }
 
-// Split-K of the fused GEMV: enough CTAs for about two per SM, within one cluster (<= 16) and
-// within the shared memory a CTA may hold.
-int gemv_split(int out, int in, int groups, int n, int nb) {
-    const int OB = out / 128, KB = in / 128;
-    const int want = 2 * sm_count();
-    int S = (want + OB * groups - 1) / (OB * groups);
-    S = std::max(1, std::min(S, std::min(16, KB)));
-    while (S < std::min(16, KB) && gemv_smem_bytes(n, nb, in, S) > 220 * 1024) S++;
-    return S;
-}
-
 sx_status linear_impl(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x, sx_dtype dtype,
                       int32_t rows, void* y, int groups) {
     sx_status st = check_proj(proj, groups);
@@ -124,9 +133,8 @@ sx_status linear_impl(sx_stream stream, const sx_proj* proj, const sx_decode* de
         a.mask1 = dp.mask1;
         a.rot = dp.rot;
         a.out_scale = kind_scale(kind);
-        const int S = gemv_split(out, in, groups, proj->n, (r + 7) / 8);
-        cudaError_t e = launch_gemv(a, kind, proj->n, groups, S, s);
-        if (e != cudaSuccess) return SX_ERR_CUDA;
+        cudaError_t e = launch_gemv(a, kind, proj->n, groups, s);
+        if (e != cudaSuccess) return cuda_status(e, "gemv launch");
     }
     return SX_OK;
 }
@@ -163,6 +171,8 @@ const char* sx_status_name(sx_status s) {
         default: return "SX_ERR_UNKNOWN";
     }
 }
+
+const char* sx_last_error_detail(void) { return g_detail; }
 
 const char* sx_version(void) { return "sushi-exl3-b200 0.1.0 (reference sushi 1.7.2)"; }
 
@@ -207,7 +217,7 @@ sx_status sx_dequant_inner(sx_stream stream, const sx_proj* proj, int32_t expert
     a.mask0 = dp.mask0;
     a.mask1 = dp.mask1;
     a.rot = dp.rot;
-    return cuda_status(launch_dequant(a, kind, reinterpret_cast<cudaStream_t>(stream)));
+    return cuda_status(launch_dequant(a, kind, reinterpret_cast<cudaStream_t>(stream)), "dequant launch");
 }
 
 sx_status sx_decode_codewords(sx_stream stream, int32_t n, const sx_decode* dec, uint32_t* out32) {
@@ -217,7 +227,8 @@ sx_status sx_decode_codewords(sx_stream stream, int32_t n, const sx_decode* dec,
     sx_status st = resolve_decode(dec, n, &kind, &dp);
     if (st) return st;
     return cuda_status(launch_decode_codewords(kind, n, dp.wmask, dp.mult, dp.mask0, dp.mask1, dp.rot, out32,
-                                               reinterpret_cast<cudaStream_t>(stream)));
+                                               reinterpret_cast<cudaStream_t>(stream)),
+                       "codewords launch");
 }
 
 sx_status sx_linear(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x, sx_dtype dtype,

@@ -88,16 +88,34 @@ __device__ __forceinline__ void lane_stream(const uint32_t* tile_words, const La
     }
 }
 
-// Codeword j of the lane (window-masked), from its stream registers.
-template <int N, int J>
+// 2^(16-b) for b = 0..16, in constant memory so the compiler cannot see the value: (r * c) >> 16
+// then stays a multiply on the FMA pipe plus one ALU shift, instead of the shift-and-mask pair on
+// the half-rate ALU pipe that a literal power of two turns into.
+extern __constant__ uint32_t c_pow2_16[17];
+
+// Codeword j of the lane (window-masked), from its stream registers.  At window 16 a codeword
+// inside one register is (r * 2^(16-b)) >> 16; other windows mask at run time.
+template <int N, int J, bool W16>
 __device__ __forceinline__ uint32_t codeword(const uint32_t (&r)[Funnel<N>::NR], uint32_t wmask) {
     constexpr int s = Funnel<N>::shift(J);
     constexpr int i = s / 32;
     constexpr int b = s % 32;
-    if constexpr (b + 16 <= 32) {
-        return (r[i] >> b) & wmask;
+    if constexpr (W16) {
+        if constexpr (b == 0) {
+            return r[i] & 0xFFFFu;
+        } else if constexpr (b == 16) {
+            return r[i] >> 16;
+        } else if constexpr (b < 16) {
+            return (r[i] * c_pow2_16[b]) >> 16;
+        } else {
+            return __funnelshift_r(r[i], r[i + 1], b) & 0xFFFFu;
+        }
     } else {
-        return __funnelshift_r(r[i], r[i + 1], b) & wmask;
+        if constexpr (b + 16 <= 32) {
+            return (r[i] >> b) & wmask;
+        } else {
+            return __funnelshift_r(r[i], r[i + 1], b) & wmask;
+        }
     }
 }
 
@@ -107,7 +125,7 @@ __device__ __forceinline__ uint32_t rotl32(uint32_t v, uint32_t r) { return __fu
 // holds two f16 halves whose SUM is the weight (times the codebook's output scale): the MMA is run
 // with its k dimension doubled, both halves against the same input, so the tensor core performs
 // the half sum (src/exl3/expert_exl3.zig:267-301).  MUL1's register holds (weight, 0).
-template <int KIND, int N>
+template <int KIND, int N, bool W16>
 __device__ __forceinline__ void decode_lane_q(const uint32_t* tile_words, const LaneFunnel<N>& lf, const DecParams& dp,
                                               uint32_t (&q)[8]) {
     uint32_t r[Funnel<N>::NR];
@@ -115,7 +133,7 @@ __device__ __forceinline__ void decode_lane_q(const uint32_t* tile_words, const 
     if constexpr (KIND == K_PAIR1) {
 #define SX_PAIR(J)                                                   \
     {                                                                \
-        const uint32_t cw = codeword<N, J>(r, dp.wmask);             \
+        const uint32_t cw = codeword<N, J, W16>(r, dp.wmask);        \
         const uint32_t p = cw * dp.mult;                             \
         q[J - 1] = p & dp.mask0;                                     \
         q[J] = rotl32(p, dp.rot) & dp.mask1;                         \
@@ -124,19 +142,21 @@ __device__ __forceinline__ void decode_lane_q(const uint32_t* tile_words, const 
 #undef SX_PAIR
     } else {
         uint32_t cw[8];
-        cw[0] = codeword<N, 0>(r, dp.wmask);
-        cw[1] = codeword<N, 1>(r, dp.wmask);
-        cw[2] = codeword<N, 2>(r, dp.wmask);
-        cw[3] = codeword<N, 3>(r, dp.wmask);
-        cw[4] = codeword<N, 4>(r, dp.wmask);
-        cw[5] = codeword<N, 5>(r, dp.wmask);
-        cw[6] = codeword<N, 6>(r, dp.wmask);
-        cw[7] = codeword<N, 7>(r, dp.wmask);
+        cw[0] = codeword<N, 0, W16>(r, dp.wmask);
+        cw[1] = codeword<N, 1, W16>(r, dp.wmask);
+        cw[2] = codeword<N, 2, W16>(r, dp.wmask);
+        cw[3] = codeword<N, 3, W16>(r, dp.wmask);
+        cw[4] = codeword<N, 4, W16>(r, dp.wmask);
+        cw[5] = codeword<N, 5, W16>(r, dp.wmask);
+        cw[6] = codeword<N, 6, W16>(r, dp.wmask);
+        cw[7] = codeword<N, 7, W16>(r, dp.wmask);
 #pragma unroll
         for (int j = 0; j < 8; j++) {
             if constexpr (KIND == K_MCG) {
-                const uint32_t p = cw[j] * 0xCBAC1FEDu;
-                q[j] = (p & 0x8FFF8FFFu) ^ 0x3B603B60u;
+                // dp carries MCG's multiplier, mask and xor (0xCBAC1FED, 0x8FFF8FFF, 0x3B603B60) as
+                // run-time values: with two immediates the mask-and-xor would take two LOP3s.
+                const uint32_t p = cw[j] * dp.mult;
+                q[j] = (p & dp.mask0) ^ dp.mask1;
             } else if constexpr (KIND == K_HASH) {
                 q[j] = (cw[j] * dp.mult) & dp.mask0;
             } else {  // MUL1: f16(fma(f16(0x6400 + bytesum(cw * M)), 0x1EEE, 0xC931))
@@ -147,6 +167,24 @@ __device__ __forceinline__ void decode_lane_q(const uint32_t* tile_words, const 
             }
         }
     }
+}
+
+// The same eight words, written straight into the two MMAs' A-register quads:
+// a1 = {v0, v4, v1, v5} (inputs 2c, 2c+1 of outputs g, g+8), a2 = {v2, v6, v3, v7} (inputs
+// 2c+8, 2c+9), so the quads need no register shuffling before the MMAs.
+template <int KIND, int N, bool W16>
+__device__ __forceinline__ void decode_lane_mma(const uint32_t* tile_words, const LaneFunnel<N>& lf, const DecParams& dp,
+                                                uint32_t (&a1)[4], uint32_t (&a2)[4]) {
+    uint32_t q[8];
+    decode_lane_q<KIND, N, W16>(tile_words, lf, dp, q);
+    a1[0] = q[0];
+    a1[1] = q[4];
+    a1[2] = q[1];
+    a1[3] = q[5];
+    a2[0] = q[2];
+    a2[1] = q[6];
+    a2[2] = q[3];
+    a2[3] = q[7];
 }
 
 // Output scale of the doubled-k MMA: the hash-mask and PAIR1 weights are the half sum times 4096

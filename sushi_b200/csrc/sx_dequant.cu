@@ -11,6 +11,9 @@ namespace sx {
 
 __device__ int g_device_error = 0;
 
+__constant__ uint32_t c_pow2_16[17] = {65536u, 32768u, 16384u, 8192u, 4096u, 2048u, 1024u, 512u, 256u,
+                                       128u,   64u,    32u,    16u,   8u,    4u,    2u,    1u};
+
 template <int KIND, int N>
 __global__ void __launch_bounds__(256) dequant_kernel(DequantArgs a) {
     const int OT = a.out_f / 16;
@@ -25,14 +28,14 @@ __global__ void __launch_bounds__(256) dequant_kernel(DequantArgs a) {
     uint32_t r[Funnel<N>::NR];
     lane_stream<N>(words, lf, r);
     uint32_t cw[8];
-    cw[0] = codeword<N, 0>(r, a.wmask);
-    cw[1] = codeword<N, 1>(r, a.wmask);
-    cw[2] = codeword<N, 2>(r, a.wmask);
-    cw[3] = codeword<N, 3>(r, a.wmask);
-    cw[4] = codeword<N, 4>(r, a.wmask);
-    cw[5] = codeword<N, 5>(r, a.wmask);
-    cw[6] = codeword<N, 6>(r, a.wmask);
-    cw[7] = codeword<N, 7>(r, a.wmask);
+    cw[0] = codeword<N, 0, false>(r, a.wmask);
+    cw[1] = codeword<N, 1, false>(r, a.wmask);
+    cw[2] = codeword<N, 2, false>(r, a.wmask);
+    cw[3] = codeword<N, 3, false>(r, a.wmask);
+    cw[4] = codeword<N, 4, false>(r, a.wmask);
+    cw[5] = codeword<N, 5, false>(r, a.wmask);
+    cw[6] = codeword<N, 6, false>(r, a.wmask);
+    cw[7] = codeword<N, 7, false>(r, a.wmask);
     const DecParams dp{a.wmask, a.mult, a.mask0, a.mask1, a.rot};
     const int gq = lane >> 2, cq = lane & 3;
 #pragma unroll

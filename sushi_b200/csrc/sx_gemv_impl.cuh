@@ -23,11 +23,17 @@ namespace cg = cooperative_groups;
 
 namespace sx {
 
-template <int KIND, int NB>
-cudaError_t dispatch_n(const GemvArgs& a, int n, int groups, int S, cudaStream_t stream);
+template <int KIND, int NB, bool W16>
+cudaError_t dispatch_n(const GemvArgs& a, int n, int groups, cudaStream_t stream);
 
-template <int KIND, int N, int NB>
-__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
+// Consumer warps of the GEMV: 16, each decoding 4 of a stage's 64 tiles (more warps in flight to
+// hide the decode chain's latency than 8 warps x 8 tiles).
+constexpr int kGemvCW = 16;
+constexpr int kGemvThreads = (kGemvCW + 1) * 32;
+
+template <int KIND, int N, int NB, bool W16>
+__global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) gemv_kernel(GemvArgs a) {
+    constexpr int CW = kGemvCW;
     extern __shared__ __align__(128) uint8_t smem[];
     cg::cluster_group cluster = cg::this_cluster();
     const int ob = blockIdx.x;     // output block (128 outputs)
@@ -38,25 +44,26 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
     const int kb0 = (int)(((long long)split * KB) / S);
     const int kbl = (int)(((long long)(split + 1) * KB) / S) - kb0;
     const int kbl_max = (KB + S - 1) / S;
-    const CoreSmem s = core_smem<N, 1, NB>(smem, kbl_max);
+    const int mg = a.rows < 8 ? a.rows : 8;
+    const CoreSmem s = core_smem<N, 1, NB>(smem, kbl_max, mg);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int OT = a.out / 16;
     const uint16_t* suh = a.suh + (size_t)g * a.in;
     const uint16_t* svh = a.svh + (size_t)g * a.out;
 
-    core_init_barriers<N, 1>(s);
+    core_init_barriers<N, 1, CW>(s);
     __syncthreads();
 
-    if (warp == kConsumerWarps) {
+    if (warp == CW) {
         if (lane == 0) {
             const uint16_t* const tr[1] = {a.trellis + (size_t)g * ((size_t)KB * 8 * OT * N)};
             core_produce<N, 1>(s, tr, OT, ob, kb0, kbl);
         }
     } else {
-        // prepare: rows x input blocks, one warp per (block, row)
-        for (int item = warp; item < kbl * NB * 8; item += kConsumerWarps) {
-            const int kbi = item / (NB * 8);
-            const int m = item % (NB * 8);
+        // prepare: rows x input blocks, one warp per (block, row) of the stored rows
+        for (int item = warp; item < kbl * NB * mg; item += CW) {
+            const int kbi = item / (NB * mg);
+            const int m = ((item / mg) % NB) * 8 + item % mg;
             const int base = (kb0 + kbi) * 128 + lane * 4;
             float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             if (m < a.rows) {
@@ -66,21 +73,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
                 warp_hadamard128(v);
             }
 #pragma unroll
-            for (int i = 0; i < 4; i++) bfrag_put<NB>(s.bfrag, kbi, m, lane * 4 + i, f2h(v[i]));
+            for (int i = 0; i < 4; i++) bfrag_put<NB>(s.bfrag, mg, kbi, m, lane * 4 + i, f2h(v[i]));
         }
-        for (int i = threadIdx.x; i < NB * 8 * 128; i += kConsumerWarps * 32) s.red[i] = 0.0f;
-        consumers_sync();
+        for (int i = threadIdx.x; i < NB * 8 * 128; i += CW * 32) s.red[i] = 0.0f;
+        consumers_sync<CW>();
 
         const DecParams dp[1] = {{a.wmask, a.mult, a.mask0, a.mask1, a.rot}};
-        float acc[1][8][NB][4];
-        core_consume<KIND, N, 1, NB>(s, kbl, dp, acc);
-        core_reduce<1, NB>(s.red, acc);
+        float acc[1][64 / CW][NB][4];
+        core_consume<KIND, N, 1, NB, W16, CW>(s, kbl, dp, acc);
+        core_reduce<1, NB, CW>(s.red, acc);
     }
 
     // rank 0 sums the cluster's partials over DSMEM and finishes
     cluster.sync();
-    if (split == 0 && warp < kConsumerWarps) {
-        for (int m = warp; m < a.rows; m += kConsumerWarps) {
+    if (split == 0 && warp < CW) {
+        for (int m = warp; m < a.rows; m += CW) {
             float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             for (int r = 0; r < S; r++) {
                 const float* peer = cluster.map_shared_rank(s.red, r);
@@ -99,21 +106,71 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
     cluster.sync();
 }
 
-template <int KIND, int N, int NB>
-static cudaError_t launch_gemv_t(const GemvArgs& a, int groups, int S, cudaStream_t stream) {
+// The split-K cluster size for a launch: the largest S <= 16 (and <= the input blocks) whose
+// clusters are all co-resident in one wave, so no cluster waits for another to drain; S = 1 when
+// even unsplit output blocks exceed a wave.  Cached per kernel and geometry.
+struct SplitKey {
+    const void* kern;
+    int out, in, groups, mg;
+    bool operator==(const SplitKey& o) const {
+        return kern == o.kern && out == o.out && in == o.in && groups == o.groups && mg == o.mg;
+    }
+};
+
+int cached_split(const SplitKey& k);
+void remember_split(const SplitKey& k, int S);
+
+template <int KIND, int N, int NB, bool W16>
+static cudaError_t launch_gemv_t(const GemvArgs& a, int groups, cudaStream_t stream) {
     const int KB = a.in / 128;
-    const int kbl_max = (KB + S - 1) / S;
-    const CoreLayout L = core_layout<N, 1, NB>(kbl_max);
-    auto kern = gemv_kernel<KIND, N, NB>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
+    const int OB = a.out / 128;
+    const int mg = a.rows < 8 ? a.rows : 8;
+    auto kern = gemv_kernel<KIND, N, NB, W16>;
+    const SplitKey key{(const void*)kern, a.out, a.in, groups, mg};
+    int S = cached_split(key);
+    cudaError_t e;
+    if (S <= 0) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+        // Fallback when no split is co-resident: the largest one (the most CTAs, the least
+        // shared memory per CTA), which then runs in several waves.
+        const int s_max = KB < 16 ? KB : 16;
+        S = s_max;
+        for (int cand = s_max; cand >= 1; cand--) {
+            const CoreLayout L = core_layout<N, 1, NB>((KB + cand - 1) / cand, mg);
+            if (L.total > 200 * 1024) break;  // smaller splits only need more
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
+            if (e != cudaSuccess) return e;
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(OB, cand, groups);
+            cfg.blockDim = dim3(kGemvThreads, 1, 1);
+            cfg.dynamicSmemBytes = L.total;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = 1;
+            attr[0].val.clusterDim.y = cand;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int clusters = 0;
+            if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) == cudaSuccess && clusters >= OB * groups) {
+                S = cand;
+                break;
+            }
+            cudaGetLastError();
+        }
+        remember_split(key, S);
+    }
+    const CoreLayout L = core_layout<N, 1, NB>((KB + S - 1) / S, mg);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
     if (e != cudaSuccess) return e;
     if (S > 8) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return e;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.out / 128, S, groups);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.gridDim = dim3(OB, S, groups);
+    cfg.blockDim = dim3(kGemvThreads, 1, 1);
     cfg.dynamicSmemBytes = L.total;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -137,10 +194,10 @@ static cudaError_t launch_gemv_t(const GemvArgs& a, int groups, int S, cudaStrea
     X(62) X(64)
 
 // PAIR1 has rows at n = 24..64 only (src/exl3/expert_exl3.zig:49-52); the others span 16..128.
-template <int KIND, int NB>
-cudaError_t dispatch_n(const GemvArgs& a, int n, int groups, int S, cudaStream_t stream) {
+template <int KIND, int NB, bool W16>
+cudaError_t dispatch_n(const GemvArgs& a, int n, int groups, cudaStream_t stream) {
 #define SX_CASE(NN) \
-    case NN: return launch_gemv_t<KIND, NN, NB>(a, groups, S, stream);
+    case NN: return launch_gemv_t<KIND, NN, NB, W16>(a, groups, stream);
     if constexpr (KIND == K_PAIR1) {
         switch (n) {
             SX_N_LIST_PAIR1(SX_CASE)

@@ -1,0 +1,6 @@
+// GEMV instantiations: PAIR1 codebook family, 1 row group(s).
+#include "sx_gemv_impl.cuh"
+
+namespace sx {
+template cudaError_t dispatch_n<K_PAIR1, 1, true>(const GemvArgs&, int, int, cudaStream_t);
+}  // namespace sx

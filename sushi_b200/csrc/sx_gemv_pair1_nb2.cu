@@ -1,0 +1,6 @@
+// GEMV instantiations: PAIR1 codebook family, 2 row group(s).
+#include "sx_gemv_impl.cuh"
+
+namespace sx {
+template cudaError_t dispatch_n<K_PAIR1, 2, true>(const GemvArgs&, int, int, cudaStream_t);
+}  // namespace sx

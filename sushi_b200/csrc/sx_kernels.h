@@ -21,8 +21,7 @@ struct GemvArgs {
     float out_scale;
 };
 
-cudaError_t launch_gemv(const GemvArgs& a, int kind, int n, int groups, int S, cudaStream_t stream);
-size_t gemv_smem_bytes(int n, int nb, int in, int S);
+cudaError_t launch_gemv(const GemvArgs& a, int kind, int n, int groups, cudaStream_t stream);
 
 struct DequantArgs {
     const uint16_t* trellis;  // one expert's [in/16][out/16][n] (pack order)

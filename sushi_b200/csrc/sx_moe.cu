@@ -223,7 +223,7 @@ extern "C" sx_status sx_moe(sx_stream stream, const sx_bank* bank, const sx_deco
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     route_prep_kernel<<<1, 1024, 2 * (size_t)E * sizeof(int), s>>>(a);
     cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return SX_ERR_CUDA;
+    if (e != cudaSuccess) return cuda_status(e, "route_prep launch");
     const int S_gu = pick_split(L.A_max * (I / 128), D / 128);
     const int S_d = pick_split(L.A_max * (D / 128), I / 128);
     switch (kind_gu) {
@@ -233,7 +233,7 @@ extern "C" sx_status sx_moe(sx_stream stream, const sx_bank* bank, const sx_deco
         case K_PAIR1: e = moe_launch_kind<K_PAIR1>(a, bank->gate.n, bank->down.n, S_gu, S_d, L.W_max, s); break;
         default: return SX_ERR_CODEBOOK_UNSUPPORTED;
     }
-    if (e != cudaSuccess) return SX_ERR_CUDA;
+    if (e != cudaSuccess) return cuda_status(e, "moe pair/down launch");
     moe_reduce_kernel<<<rows, 256, 0, s>>>(a);
-    return cuda_status(cudaGetLastError());
+    return cuda_status(cudaGetLastError(), "moe reduce launch");
 }

@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_pair_kernel(MoeArgs a) {
     const int OT = a.I / 16;
     const size_t per = (size_t)(a.D / 16) * OT * N;
     if (threadIdx.x < 8) slot_of[threadIdx.x] = threadIdx.x < it.rows ? a.order[it.first + threadIdx.x] : 0;
-    core_init_barriers<N, 2>(s);
+    core_init_barriers<N, 2, kConsumerWarps>(s);
     __syncthreads();
 
     if (warp == kConsumerWarps) {
@@ -109,14 +109,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_pair_kernel(MoeArgs a) {
                 warp_hadamard128(v);
             }
 #pragma unroll
-            for (int i = 0; i < 4; i++) bfrag_put<1>(s.bfrag + p * s.bfrag_proj_stride, kbi, m, lane * 4 + i, f2h(v[i]));
+            for (int i = 0; i < 4; i++) bfrag_put<1>(s.bfrag + p * s.bfrag_proj_stride, 8, kbi, m, lane * 4 + i, f2h(v[i]));
         }
         for (int i = threadIdx.x; i < 2 * 8 * 128; i += kConsumerWarps * 32) s.red[i] = 0.0f;
-        consumers_sync();
+        consumers_sync<kConsumerWarps>();
         const DecParams dp[2] = {a.dp_gu, a.dp_gu};
         float acc[2][8][1][4];
-        core_consume<KIND, N, 2, 1>(s, kbl, dp, acc);
-        core_reduce<2, 1>(s.red, acc);
+        core_consume<KIND, N, 2, 1, false, kConsumerWarps>(s, kbl, dp, acc);
+        core_reduce<2, 1, kConsumerWarps>(s.red, acc);
     }
 
     cluster.sync();
@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(MoeArgs a) {
     const int OT = a.D / 16;
     const size_t per = (size_t)(a.I / 16) * OT * N;
     if (threadIdx.x < 8) slot_of[threadIdx.x] = threadIdx.x < it.rows ? a.order[it.first + threadIdx.x] : 0;
-    core_init_barriers<N, 1>(s);
+    core_init_barriers<N, 1, kConsumerWarps>(s);
     __syncthreads();
 
     if (warp == kConsumerWarps) {
@@ -189,14 +189,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(MoeArgs a) {
             const int kbi = item / 8, m = item % 8;
             const uint16_t* src = a.hprep + (size_t)slot_of[m] * a.I + (kb0 + kbi) * 128 + lane * 4;
 #pragma unroll
-            for (int i = 0; i < 4; i++) bfrag_put<1>(s.bfrag, kbi, m, lane * 4 + i, m < it.rows ? src[i] : (uint16_t)0);
+            for (int i = 0; i < 4; i++) bfrag_put<1>(s.bfrag, 8, kbi, m, lane * 4 + i, m < it.rows ? src[i] : (uint16_t)0);
         }
         for (int i = threadIdx.x; i < 8 * 128; i += kConsumerWarps * 32) s.red[i] = 0.0f;
-        consumers_sync();
+        consumers_sync<kConsumerWarps>();
         const DecParams dp[1] = {a.dp_down};
         float acc[1][8][1][4];
-        core_consume<KIND, N, 1, 1>(s, kbl, dp, acc);
-        core_reduce<1, 1>(s.red, acc);
+        core_consume<KIND, N, 1, 1, false, kConsumerWarps>(s, kbl, dp, acc);
+        core_reduce<1, 1, kConsumerWarps>(s.red, acc);
     }
 
     cluster.sync();

@@ -173,5 +173,5 @@ extern "C" sx_status sx_router_topk(sx_stream stream, const float* logits, const
     const size_t smem = (size_t)2 * experts * sizeof(float);
     router_kernel<<<rows, kRouterThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
         logits, bias, experts, k, mode, renorm, scale, n_group, topk_group, inds, scores);
-    return cuda_status(cudaGetLastError());
+    return cuda_status(cudaGetLastError(), "router launch");
 }

@@ -123,8 +123,10 @@ class Bank:
 class Exl3Error(RuntimeError):
     def __init__(self, status):
         self.status = int(status)
-        self.name = _lib.load().sx_status_name(self.status).decode()
-        super().__init__(self.name)
+        L = _lib.load()
+        self.name = L.sx_status_name(self.status).decode()
+        detail = L.sx_last_error_detail().decode() if self.name == "SX_ERR_CUDA" else ""
+        super().__init__(f"{self.name} ({detail})" if detail else self.name)
 
 
 _DT = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
