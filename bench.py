@@ -207,7 +207,9 @@ def main():
     configs = [(in_f, out_f, n, m) for (in_f, out_f) in SHAPES for n in RATES for m in ROWS]
 
     def launch(in_f, out_f, n, m, proj):
-        st = L.sx_linear(sptr, ctypes.byref(proj), ctypes.byref(dec), xbuf[in_f].data_ptr(), 2, m, ybuf[out_f].data_ptr())
+        # weights are loaded once: launches may stream them while the previous launch finishes
+        st = L.sx_linear_ex(sptr, ctypes.byref(proj), ctypes.byref(dec), xbuf[in_f].data_ptr(), 2, m,
+                            ybuf[out_f].data_ptr(), 1)
         if st:
             raise RuntimeError(f"{L.sx_status_name(st).decode()} {L.sx_last_error_detail().decode()} "
                                f"(out {out_f} in {in_f} n {n} rows {m})")

@@ -120,6 +120,21 @@ sx_status sx_decode_codewords(sx_stream stream, int32_t n, const sx_decode* dec,
 sx_status sx_linear(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x, sx_dtype dtype,
                     int32_t rows, void* y);
 
+/* Flags of sx_linear_ex. */
+enum {
+    /* The projection's trellis, suh and svh are not written by the work queued on `stream` just
+     * before this call.  The launch then uses programmatic dependent launch: its CTAs start
+     * streaming weights while the previous kernel on the stream finishes, and wait for it only
+     * before reading x and writing y.  Decode loops whose weights are loaded once set it. */
+    SX_LINEAR_WEIGHTS_STATIC = 1u
+};
+
+/* sx_linear with launch flags (SX_LINEAR_*); flags == 0 is sx_linear.  No reference counterpart:
+ * the reference's Metal dispatch has no launch overlap to ask for.  Unknown flag bits:
+ * SX_ERR_BAD_SHAPE. */
+sx_status sx_linear_ex(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x, sx_dtype dtype,
+                       int32_t rows, void* y, uint32_t flags);
+
 /* linear.linearGrouped (src/exl3/linear.zig:38-54): x [G, rows, in] through the G-bank proj
  * (experts == G, bank g serves x[g]) into y [G, rows, out]. */
 sx_status sx_linear_grouped(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x,
@@ -187,7 +202,7 @@ size_t sx_moe_static_scratch_bytes(void);
  * (0 = none) and clears it; synchronises `stream` first. */
 int32_t sx_device_error(sx_stream stream);
 
-/* Detail of the last SX_ERR_CUDA this thread got: the failing CUDA call's error name and where
+/* Detail of the last SX_ERR_CUDA or SX_ERR_NCCL this thread got: the failing call's error and where
  * ("cudaLaunchKernelEx gemv: cudaErrorInvalidValue"); "" when there is none. */
 const char* sx_last_error_detail(void);
 

@@ -14,6 +14,7 @@ from .exl3 import (  # noqa: E402
     Codebook,
     Decode,
     Exl3Error,
+    LINEAR_WEIGHTS_STATIC,
     Proj,
     RouterMode,
     TileOrder,
@@ -32,7 +33,7 @@ from .exl3 import (  # noqa: E402
 )
 
 __all__ = [
-    "Bank", "Codebook", "Decode", "Exl3Error", "Proj", "RouterMode", "TileOrder", "decode_codewords",
+    "Bank", "Codebook", "Decode", "Exl3Error", "LINEAR_WEIGHTS_STATIC", "Proj", "RouterMode", "TileOrder", "decode_codewords",
     "dequant_inner", "device_error", "linear", "linear_grouped", "moe", "moe_clamped", "moe_with_gated_shared",
     "moe_with_shared", "router_topk", "table_info", "table_row",
 ]

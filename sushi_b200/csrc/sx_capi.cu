@@ -22,6 +22,8 @@ void note_cuda_error(cudaError_t e, const char* where) {
     snprintf(g_detail, sizeof(g_detail), "%s: %s", where, cudaGetErrorName(e));
 }
 
+void note_detail(const char* what, const char* why) { snprintf(g_detail, sizeof(g_detail), "%s: %s", what, why); }
+
 sx_status cuda_status(cudaError_t e, const char* where) {
     if (e == cudaSuccess) return SX_OK;
     note_cuda_error(e, where);
@@ -98,7 +100,8 @@ int sm_count() {
 }
 
 sx_status linear_impl(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x, sx_dtype dtype,
-                      int32_t rows, void* y, int groups) {
+                      int32_t rows, void* y, int groups, uint32_t flags) {
+    if (flags & ~(uint32_t)SX_LINEAR_WEIGHTS_STATIC) return SX_ERR_BAD_SHAPE;
     sx_status st = check_proj(proj, groups);
     if (st) return st;
     if (proj->tile_order != SX_TILE_PACK) return SX_ERR_TILE_ORDER_UNSUPPORTED;
@@ -133,6 +136,8 @@ sx_status linear_impl(sx_stream stream, const sx_proj* proj, const sx_decode* de
         a.mask1 = dp.mask1;
         a.rot = dp.rot;
         a.out_scale = kind_scale(kind);
+        // A later 16-row chunk follows this call's own launch, which writes only y.
+        a.pdl = (flags & SX_LINEAR_WEIGHTS_STATIC) || r0 > 0;
         cudaError_t e = launch_gemv(a, kind, proj->n, groups, s);
         if (e != cudaSuccess) return cuda_status(e, "gemv launch");
     }
@@ -234,13 +239,19 @@ sx_status sx_decode_codewords(sx_stream stream, int32_t n, const sx_decode* dec,
 sx_status sx_linear(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x, sx_dtype dtype,
                     int32_t rows, void* y) {
     if (proj && proj->experts != 1) return SX_ERR_BAD_SHAPE;
-    return linear_impl(stream, proj, dec, x, dtype, rows, y, 1);
+    return linear_impl(stream, proj, dec, x, dtype, rows, y, 1, 0);
+}
+
+sx_status sx_linear_ex(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x, sx_dtype dtype,
+                       int32_t rows, void* y, uint32_t flags) {
+    if (proj && proj->experts != 1) return SX_ERR_BAD_SHAPE;
+    return linear_impl(stream, proj, dec, x, dtype, rows, y, 1, flags);
 }
 
 sx_status sx_linear_grouped(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x,
                             sx_dtype dtype, int32_t rows, void* y) {
     if (!proj) return SX_ERR_NULL_POINTER;
-    return linear_impl(stream, proj, dec, x, dtype, rows, y, proj->experts);
+    return linear_impl(stream, proj, dec, x, dtype, rows, y, proj->experts, 0);
 }
 
 int32_t sx_device_error(sx_stream stream) {

@@ -5,16 +5,20 @@
 // contiguous range of 128-wide input blocks, for up to 8*NB rows.
 //   * producer warp: streams each input block's 8 x 8 tiles of every projection into a ring of
 //     shared-memory stages with 1-D bulk (TMA) copies, 8*n*2 contiguous bytes per tile row.
-//   * CW consumer warps (8 or 16): each decodes TPW = 64/CW tiles of every stage (input-tile row
-//     w / (8/TPW), output tiles from (w % (8/TPW)) * TPW) for NP projections and runs two
-//     m16n8k16 MMAs per tile and row group (doubled k: the tensor core adds each weight's two f16
-//     halves, sx_decode.cuh).
-//   * the warps' accumulators are summed in a fixed order into shared memory.
+//   * CW consumer warps (8 or 16): warp w decodes the TPW = 64/CW tiles of output tile w % 8 in
+//     input-tile rows (w / 8)*TPW.. of every stage for NP projections and runs two m16n8k16 MMAs
+//     per tile and row group (doubled k: the tensor core adds each weight's two f16 halves,
+//     sx_decode.cuh), accumulating its output tile's k sum in registers.
+//   * the block's partial sums land in shared memory (core_reduce), in a fixed order.
 #pragma once
+
+#include <cooperative_groups.h>
 
 #include "sx_decode.cuh"
 
 namespace sx {
+
+namespace cg = cooperative_groups;
 
 constexpr int kConsumerWarps = 8;  // the MoE kernels' consumer warps
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
@@ -32,7 +36,7 @@ struct CoreLayout {
 
 // Shared memory of one CTA: the stage ring, the B fragments of kbl_max input blocks per
 // projection (each projection prepares the input with its own suh) for mg rows per 8-row group
-// (mg = min(8, rows): only the lanes of live rows load fragments), the NP x (8*NB) x 128 f32
+// (mg = min(8, rows); the lanes of later rows read row mg-1's), the NP x (8*NB) x 128 f32
 // reduction, the ring's barriers.
 template <int N, int NP, int NB>
 __host__ __device__ inline CoreLayout core_layout(int kbl_max, int mg = 8) {
@@ -116,7 +120,7 @@ __device__ __forceinline__ bool core_produce(const CoreSmem& s, const uint16_t* 
 // One prepared value v of row m at position pos (0..127) of local input block kbi, into the
 // B-fragment slot its MMA lane reads: lane (g = m%8, c), register slot by the input's row in
 // the tile (sx_decode.cuh: MMA1 takes inputs 2c, 2c+1 and MMA2 2c+8, 2c+9, each duplicated).
-// Rows m with m % 8 >= mg are not stored (their lanes read zeros).
+// Rows m with m % 8 >= mg are not stored.
 template <int NB>
 __device__ __forceinline__ void bfrag_put(uint4* bfrag, int mg, int kbi, int m, int pos, uint16_t h) {
     const int nb = m >> 3, gg = m & 7;
@@ -134,29 +138,35 @@ __device__ __forceinline__ void consumers_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
 }
 
-// Consumers: decode + MMA over kbl stages; acc[p][t][nb][e] per lane for its TPW tiles.
+// Consumers: decode + MMA over kbl stages.  Warp w owns output tile ot = w % 8 of the block and
+// input-tile rows h*TPW .. h*TPW+TPW-1 of every stage (h = w / 8, TPW = 64 / CW), so the k sum of
+// its output tile stays in its registers across the whole range; with 16 warps two warps share an
+// output tile and core_reduce adds the pair.  acc[p][nb][e] is the lane's m16n8 fragment (outputs
+// gq, gq+8 of the tile; rows 2cq, 2cq+1 of row group nb).
 template <int KIND, int N, int NP, int NB, bool W16, int CW>
 __device__ __forceinline__ bool core_consume(const CoreSmem& s, int kbl, const DecParams (&dp)[NP],
-                                             float (&acc)[NP][64 / CW][NB][4]) {
+                                             float (&acc)[NP][NB][4]) {
+    static_assert(CW == 8 || CW == 16, "8 or 16 consumer warps");
     constexpr int NST = Ring<N, NP>::NST;
     constexpr int TILE_WORDS = N / 2;
     constexpr int TPW = 64 / CW;
-    constexpr int WPR = 8 / TPW;  // warps per input-tile row
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int trow = warp / WPR;
-    const int t0 = (warp % WPR) * TPW;
+    const int ot = warp & 7;
+    const int tr0 = (warp >> 3) * TPW;
     LaneFunnel<N> lf;
     lf.init(lane);
+    // two accumulator sets (even and odd rows) so consecutive tiles' MMAs do not chain
+    float acc2[NP][NB][4];
 #pragma unroll
     for (int p = 0; p < NP; p++)
 #pragma unroll
-        for (int j = 0; j < TPW; j++)
+        for (int nb = 0; nb < NB; nb++)
 #pragma unroll
-            for (int nb = 0; nb < NB; nb++)
-#pragma unroll
-                for (int e = 0; e < 4; e++) acc[p][j][nb][e] = 0.0f;
+            for (int e = 0; e < 4; e++) acc[p][nb][e] = acc2[p][nb][e] = 0.0f;
+    // Lanes of rows past the stored mg read row mg-1's fragments instead of branching: their
+    // output columns belong to rows no caller reads.
     const int gq = lane >> 2;
-    const bool live = gq < s.mg;
+    const int bf_lane = min(gq, s.mg - 1) * 4 + (lane & 3);
     bool ok = true;
     for (int i = 0; i < kbl; i++) {
         const int st = i % NST;
@@ -164,23 +174,20 @@ __device__ __forceinline__ bool core_consume(const CoreSmem& s, int kbl, const D
         if (ok) {
 #pragma unroll
             for (int p = 0; p < NP; p++) {
-                uint4 b[NB];
-#pragma unroll
-                for (int nb = 0; nb < NB; nb++)
-                    b[nb] = live ? s.bfrag[p * s.bfrag_proj_stride + (((i * 8 + trow) * NB + nb) * s.mg + gq) * 4 +
-                                           (lane & 3)]
-                                 : make_uint4(0u, 0u, 0u, 0u);
-                const uint32_t* row = reinterpret_cast<const uint32_t*>(s.stages + (size_t)st * Ring<N, NP>::STAGE_BYTES +
-                                                                        p * Ring<N, NP>::PROJ_BYTES) +
-                                      (trow * 8 + t0) * TILE_WORDS;
+                const uint32_t* base = reinterpret_cast<const uint32_t*>(s.stages + (size_t)st * Ring<N, NP>::STAGE_BYTES +
+                                                                         p * Ring<N, NP>::PROJ_BYTES) +
+                                       (tr0 * 8 + ot) * TILE_WORDS;
+                const uint4* bf = s.bfrag + p * s.bfrag_proj_stride + (size_t)(i * 8 + tr0) * NB * s.mg * 4 + bf_lane;
 #pragma unroll
                 for (int j = 0; j < TPW; j++) {
                     uint32_t a1[4], a2[4];
-                    decode_lane_mma<KIND, N, W16>(row + j * TILE_WORDS, lf, dp[p], a1, a2);
+                    decode_lane_mma<KIND, N, W16>(base + j * 8 * TILE_WORDS, lf, dp[p], a1, a2);
 #pragma unroll
                     for (int nb = 0; nb < NB; nb++) {
-                        mma16816(acc[p][j][nb], a1[0], a1[1], a1[2], a1[3], b[nb].x, b[nb].y);
-                        mma16816(acc[p][j][nb], a2[0], a2[1], a2[2], a2[3], b[nb].z, b[nb].w);
+                        const uint4 b = bf[(j * NB + nb) * s.mg * 4];
+                        float(&d)[4] = (j & 1) ? acc2[p][nb] : acc[p][nb];
+                        mma16816(d, a1[0], a1[1], a1[2], a1[3], b.x, b.y);
+                        mma16816(d, a2[0], a2[1], a2[2], a2[3], b.z, b.w);
                     }
                 }
             }
@@ -188,37 +195,81 @@ __device__ __forceinline__ bool core_consume(const CoreSmem& s, int kbl, const D
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.empty[st]);
     }
+#pragma unroll
+    for (int p = 0; p < NP; p++)
+#pragma unroll
+        for (int nb = 0; nb < NB; nb++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) acc[p][nb][e] += acc2[p][nb][e];
     return ok;
 }
 
-// Sum of the consumer warps' accumulators, warp 0 first, into red[p][m][o] (m < 8*NB rows,
-// o < 128 outputs of the block).  `red` must be zeroed and published before.
+// The block's partial sums into red[p][m][o] (m < 8*NB rows, o < 128 outputs), every entry
+// written.  With 16 warps, warps 8..15 store first and warps 0..7 add theirs after a barrier of
+// the consumer warps (a fixed order; the sum of two terms is the same either way).
 template <int NP, int NB, int CW>
-__device__ __forceinline__ void core_reduce(float* red, const float (&acc)[NP][64 / CW][NB][4]) {
-    constexpr int TPW = 64 / CW;
-    constexpr int WPR = 8 / TPW;
+__device__ __forceinline__ void core_reduce(float* red, const float (&acc)[NP][NB][4]) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gq = lane >> 2, cq = lane & 3;
-    const int t0 = (warp % WPR) * TPW;
-    for (int w = 0; w < CW; w++) {
-        if (warp == w) {
+    const int o0 = (warp & 7) * 16 + gq;
+    auto put = [&](bool add) {
 #pragma unroll
-            for (int p = 0; p < NP; p++)
+        for (int p = 0; p < NP; p++)
 #pragma unroll
-                for (int j = 0; j < TPW; j++)
-#pragma unroll
-                    for (int nb = 0; nb < NB; nb++) {
-                        float* rp = red + (size_t)p * NB * 8 * 128;
-                        const int m0 = nb * 8 + 2 * cq;
-                        const int o0 = (t0 + j) * 16 + gq;
-                        rp[m0 * 128 + o0] += acc[p][j][nb][0];
-                        rp[(m0 + 1) * 128 + o0] += acc[p][j][nb][1];
-                        rp[m0 * 128 + o0 + 8] += acc[p][j][nb][2];
-                        rp[(m0 + 1) * 128 + o0 + 8] += acc[p][j][nb][3];
-                    }
-        }
+            for (int nb = 0; nb < NB; nb++) {
+                float* rp = red + (size_t)p * NB * 8 * 128;
+                const int m0 = nb * 8 + 2 * cq;
+                float* q0 = rp + m0 * 128 + o0;
+                float* q1 = rp + (m0 + 1) * 128 + o0;
+                if (add) {
+                    q0[0] += acc[p][nb][0];
+                    q1[0] += acc[p][nb][1];
+                    q0[8] += acc[p][nb][2];
+                    q1[8] += acc[p][nb][3];
+                } else {
+                    q0[0] = acc[p][nb][0];
+                    q1[0] = acc[p][nb][1];
+                    q0[8] = acc[p][nb][2];
+                    q1[8] = acc[p][nb][3];
+                }
+            }
+    };
+    if (CW == 8) {
+        put(false);
+    } else {
+        if (warp >= 8) put(false);
         consumers_sync<CW>();
+        if (warp < 8) put(true);
     }
 }
+
+// Sum over the cluster's S CTAs, in rank order, of the four floats red[off + 4*lane ..] of each:
+// the loads go out four ranks at a time so distributed shared memory's latency is paid S/4 times.
+__device__ __forceinline__ float4 cluster_sum4(cg::cluster_group& cluster, float* red, int S, int off) {
+    const int lane = threadIdx.x & 31;
+    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    auto add = [&](const float4& t) {
+        v.x += t.x;
+        v.y += t.y;
+        v.z += t.z;
+        v.w += t.w;
+    };
+    int r = 0;
+    for (; r + 4 <= S; r += 4) {
+        float4 t[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+            t[q] = *reinterpret_cast<const float4*>(cluster.map_shared_rank(red, r + q) + off + lane * 4);
+#pragma unroll
+        for (int q = 0; q < 4; q++) add(t[q]);
+    }
+    for (; r < S; r++) add(*reinterpret_cast<const float4*>(cluster.map_shared_rank(red, r) + off + lane * 4));
+    return v;
+}
+
+// Programmatic dependent launch: wait for the grid this one depends on (a no-op when launched
+// without the attribute), and let the next grid on the stream start launching.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 }  // namespace sx

@@ -14,12 +14,8 @@
 //     No global scratch.
 #pragma once
 
-#include <cooperative_groups.h>
-
 #include "sx_core.cuh"
 #include "sx_kernels.h"
-
-namespace cg = cooperative_groups;
 
 namespace sx {
 
@@ -53,13 +49,17 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) gemv_kernel(Gem
 
     core_init_barriers<N, 1, CW>(s);
     __syncthreads();
+    grid_launch_dependents();
 
     if (warp == CW) {
+        // The weights are read-only to the grids around this one, so they stream before the
+        // dependency wait (launches with programmatic serialisation only).
         if (lane == 0) {
             const uint16_t* const tr[1] = {a.trellis + (size_t)g * ((size_t)KB * 8 * OT * N)};
             core_produce<N, 1>(s, tr, OT, ob, kb0, kbl);
         }
     } else {
+        grid_dependency_wait();  // x may come from the previous grid
         // prepare: rows x input blocks, one warp per (block, row) of the stored rows
         for (int item = warp; item < kbl * NB * mg; item += CW) {
             const int kbi = item / (NB * mg);
@@ -75,11 +75,10 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) gemv_kernel(Gem
 #pragma unroll
             for (int i = 0; i < 4; i++) bfrag_put<NB>(s.bfrag, mg, kbi, m, lane * 4 + i, f2h(v[i]));
         }
-        for (int i = threadIdx.x; i < NB * 8 * 128; i += CW * 32) s.red[i] = 0.0f;
         consumers_sync<CW>();
 
         const DecParams dp[1] = {{a.wmask, a.mult, a.mask0, a.mask1, a.rot}};
-        float acc[1][64 / CW][NB][4];
+        float acc[1][NB][4];
         core_consume<KIND, N, 1, NB, W16, CW>(s, kbl, dp, acc);
         core_reduce<1, NB, CW>(s.red, acc);
     }
@@ -88,12 +87,8 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) gemv_kernel(Gem
     cluster.sync();
     if (split == 0 && warp < CW) {
         for (int m = warp; m < a.rows; m += CW) {
-            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            for (int r = 0; r < S; r++) {
-                const float* peer = cluster.map_shared_rank(s.red, r);
-#pragma unroll
-                for (int i = 0; i < 4; i++) v[i] += peer[m * 128 + lane * 4 + i];
-            }
+            const float4 t = cluster_sum4(cluster, s.red, S, m * 128);
+            float v[4] = {t.x, t.y, t.z, t.w};
             warp_hadamard128(v);
             const size_t yoff = (size_t)g * a.y_group_stride + (size_t)m * a.out + (size_t)ob * 128 + lane * 4;
 #pragma unroll
@@ -173,13 +168,15 @@ static cudaError_t launch_gemv_t(const GemvArgs& a, int groups, cudaStream_t str
     cfg.blockDim = dim3(kGemvThreads, 1, 1);
     cfg.dynamicSmemBytes = L.total;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;
     attr[0].val.clusterDim.y = S;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = a.pdl ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kern, a);
 }
 

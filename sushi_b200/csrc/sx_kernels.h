@@ -19,6 +19,7 @@ struct GemvArgs {
     long long y_group_stride;
     uint32_t wmask, mult, mask0, mask1, rot;
     float out_scale;
+    int pdl;                   // host side: launch with programmatic stream serialisation
 };
 
 cudaError_t launch_gemv(const GemvArgs& a, int kind, int n, int groups, cudaStream_t stream);

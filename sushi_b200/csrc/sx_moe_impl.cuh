@@ -111,10 +111,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_pair_kernel(MoeArgs a) {
 #pragma unroll
             for (int i = 0; i < 4; i++) bfrag_put<1>(s.bfrag + p * s.bfrag_proj_stride, 8, kbi, m, lane * 4 + i, f2h(v[i]));
         }
-        for (int i = threadIdx.x; i < 2 * 8 * 128; i += kConsumerWarps * 32) s.red[i] = 0.0f;
         consumers_sync<kConsumerWarps>();
         const DecParams dp[2] = {a.dp_gu, a.dp_gu};
-        float acc[2][8][1][4];
+        float acc[2][1][4];
         core_consume<KIND, N, 2, 1, false, kConsumerWarps>(s, kbl, dp, acc);
         core_reduce<2, 1, kConsumerWarps>(s.red, acc);
     }
@@ -122,15 +121,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_pair_kernel(MoeArgs a) {
     cluster.sync();
     if (split == 0 && warp < it.rows) {
         const int m = warp;
-        float g[4] = {0.0f, 0.0f, 0.0f, 0.0f}, u[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        for (int r = 0; r < S; r++) {
-            const float* peer = cluster.map_shared_rank(s.red, r);
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                g[i] += peer[m * 128 + lane * 4 + i];
-                u[i] += peer[8 * 128 + m * 128 + lane * 4 + i];
-            }
-        }
+        const float4 gs = cluster_sum4(cluster, s.red, S, m * 128);
+        const float4 us = cluster_sum4(cluster, s.red, S, 8 * 128 + m * 128);
+        float g[4] = {gs.x, gs.y, gs.z, gs.w}, u[4] = {us.x, us.y, us.z, us.w};
         warp_hadamard128(g);
         warp_hadamard128(u);
         float h[4];
@@ -191,10 +184,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(MoeArgs a) {
 #pragma unroll
             for (int i = 0; i < 4; i++) bfrag_put<1>(s.bfrag, 8, kbi, m, lane * 4 + i, m < it.rows ? src[i] : (uint16_t)0);
         }
-        for (int i = threadIdx.x; i < 8 * 128; i += kConsumerWarps * 32) s.red[i] = 0.0f;
         consumers_sync<kConsumerWarps>();
         const DecParams dp[1] = {a.dp_down};
-        float acc[1][8][1][4];
+        float acc[1][1][4];
         core_consume<KIND, N, 1, 1, false, kConsumerWarps>(s, kbl, dp, acc);
         core_reduce<1, 1, kConsumerWarps>(s.red, acc);
     }
@@ -202,12 +194,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(MoeArgs a) {
     cluster.sync();
     if (split == 0 && warp < it.rows) {
         const int m = warp;
-        float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        for (int r = 0; r < S; r++) {
-            const float* peer = cluster.map_shared_rank(s.red, r);
-#pragma unroll
-            for (int i = 0; i < 4; i++) d[i] += peer[m * 128 + lane * 4 + i];
-        }
+        const float4 ds = cluster_sum4(cluster, s.red, S, m * 128);
+        float d[4] = {ds.x, ds.y, ds.z, ds.w};
         warp_hadamard128(d);
         const int slot = slot_of[m];
         const float sc = a.scores[slot] * a.scale_down;

@@ -125,7 +125,7 @@ class Exl3Error(RuntimeError):
         self.status = int(status)
         L = _lib.load()
         self.name = L.sx_status_name(self.status).decode()
-        detail = L.sx_last_error_detail().decode() if self.name == "SX_ERR_CUDA" else ""
+        detail = L.sx_last_error_detail().decode() if self.name in ("SX_ERR_CUDA", "SX_ERR_NCCL") else ""
         super().__init__(f"{self.name} ({detail})" if detail else self.name)
 
 
@@ -145,8 +145,15 @@ def lib():
     return _lib.load()
 
 
-def linear(x, proj: Proj, dec: Decode):
-    """linear.linear: x [rows, in] (bf16/f16/f32) through the one-bank proj -> [rows, out] in x's dtype."""
+LINEAR_WEIGHTS_STATIC = 1
+
+
+def linear(x, proj: Proj, dec: Decode, flags: int = 0, out=None):
+    """linear.linear: x [rows, in] (bf16/f16/f32) through the one-bank proj -> [rows, out] in x's dtype.
+
+    flags: LINEAR_WEIGHTS_STATIC when nothing queued just before this call writes the projection's
+    weights (the launch may then stream them while the previous kernel finishes).  out: an optional
+    preallocated [rows, out] tensor of x's dtype."""
     if x.dim() != 2 or not x.is_contiguous():
         raise Exl3Error(1)
     if x.dtype not in _DT:
@@ -154,10 +161,19 @@ def linear(x, proj: Proj, dec: Decode):
     _, in_f, out_f, _ = proj.dims()
     if x.shape[1] != in_f:
         raise Exl3Error(1)
-    y = torch.empty((x.shape[0], out_f), dtype=x.dtype, device=x.device)
+    if out is None:
+        y = torch.empty((x.shape[0], out_f), dtype=x.dtype, device=x.device)
+    else:
+        if out.shape != (x.shape[0], out_f) or out.dtype != x.dtype or not out.is_contiguous():
+            raise Exl3Error(1)
+        y = out
     p, d = proj.c(), dec.c()
-    _check(lib().sx_linear(_stream(), ctypes.byref(p), ctypes.byref(d), x.data_ptr(), _DT[x.dtype], x.shape[0],
-                           y.data_ptr()))
+    if flags:
+        _check(lib().sx_linear_ex(_stream(), ctypes.byref(p), ctypes.byref(d), x.data_ptr(), _DT[x.dtype], x.shape[0],
+                                  y.data_ptr(), flags))
+    else:
+        _check(lib().sx_linear(_stream(), ctypes.byref(p), ctypes.byref(d), x.data_ptr(), _DT[x.dtype], x.shape[0],
+                               y.data_ptr()))
     return y
 
 

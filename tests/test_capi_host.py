@@ -94,6 +94,11 @@ def test_linear_refusals_before_launch(L, proj, dec, dtype, rows, want):
     assert L.sx_status_name(st).decode() == want
 
 
+def test_linear_ex_refuses_unknown_flags(L):
+    st = L.sx_linear_ex(None, ctypes.byref(_proj()), ctypes.byref(_dec()), FAKE, 2, 1, FAKE, 2)
+    assert L.sx_status_name(st).decode() == "SX_ERR_BAD_SHAPE"
+
+
 def test_misaligned_trellis_is_refused(L):
     p = _lib.SxProj(FAKE + 2, FAKE, FAKE, 1, 256, 128, 32, 0)
     st = L.sx_linear(None, ctypes.byref(p), ctypes.byref(_dec()), FAKE, 2, 1, FAKE)

@@ -117,3 +117,24 @@ def test_linear_refusals(sx):
         sx.linear(torch.zeros((1, 256), device="cuda", dtype=torch.int32), proj, dec)
     assert e.value.name == "SX_ERR_BAD_DTYPE"
     assert sx.device_error() == 0
+
+
+@pytest.mark.parametrize("rows", [1, 5, 33])
+def test_linear_static_weights_overlap_matches(sx, rows):
+    """sx_linear_ex with SX_LINEAR_WEIGHTS_STATIC (programmatic dependent launch) gives the same
+    bits as sx_linear, over a chain where each launch reads the previous launch's output."""
+    tr, su, sv = random_pack(21, 512, 512, 32)
+    _, dec = dec_args(orc.CB_MCG, 16)
+    proj = sx.Proj(dev(tr, torch), dev(su, torch), dev(sv, torch))
+    x0, _ = _x(3, rows, 512, torch.bfloat16)
+    outs = []
+    for flags in (0, sx.LINEAR_WEIGHTS_STATIC):
+        a = x0.clone()
+        b = torch.empty_like(a)
+        for _ in range(6):  # a -> b -> a ...: each launch's x is the previous launch's y
+            sx.linear(a, proj, dec, flags=flags, out=b)
+            a, b = b, a
+        torch.cuda.synchronize()
+        outs.append(a.clone())
+    assert torch.equal(outs[0], outs[1])
+    assert torch.isfinite(outs[0].float()).all()
