@@ -196,6 +196,55 @@ sx_status sx_moe_static_scratch(sx_stream stream, const sx_bank* bank, const sx_
 /* The size of sx_moe_static_scratch's buffer in bytes. */
 size_t sx_moe_static_scratch_bytes(void);
 
+/* ------------------------------------------------------------------ expert parallel
+ * The routed layer with its experts sharded over `world` GPUs (one process or thread per GPU):
+ * rank g holds experts [g*E/world, (g+1)*E/world) of an E-expert layer as a local bank of E/world
+ * experts.  Each rank routes its own tokens; a token's hidden row travels once to every rank that
+ * owns one of its experts, together with its slots there (dispatch), the ranks run their local
+ * expert chains, and each token's partial sums come back to its owner (combine), which adds them
+ * in rank order, rounds to the output dtype and adds the shared expert.  Dispatch and combine are
+ * NCCL all-to-alls (grouped ncclSend/ncclRecv) of fixed-size blocks: `rows_cap` rows per peer,
+ * so no host synchronisation sits between the steps.  No reference counterpart: the reference
+ * serves its experts from one GPU.  The library loads NCCL (libnccl.so.2) when an sx_ep call
+ * first needs it. */
+typedef struct sx_ep sx_ep;
+
+/* A new NCCL unique id (128 bytes) for sx_ep_init: made on one rank and handed to every rank by
+ * the host's own means. */
+sx_status sx_ep_unique_id(uint8_t id[128]);
+
+/* Joins the `world`-rank communicator named by `id` as `rank`, on the current CUDA device.
+ * Collective: every rank calls it. */
+sx_status sx_ep_init(const uint8_t id[128], int32_t world, int32_t rank, sx_ep** out);
+
+/* Frees the communicator (ncclCommDestroy).  Synchronise the streams that used it first. */
+sx_status sx_ep_destroy(sx_ep* ep);
+
+/* Aborts the communicator (ncclCommAbort) and frees it: a host watchdog's way out of a collective
+ * that a failed peer will never complete. */
+sx_status sx_ep_abort(sx_ep* ep);
+
+/* Workspace of sx_ep_moe in bytes, for a local bank `local_bank` at `rows_cap` rows per rank. */
+size_t sx_ep_workspace_bytes(const sx_ep* ep, const sx_bank* local_bank, int32_t rows_cap, int32_t topk,
+                             sx_dtype dtype);
+
+/* The expert-parallel routed layer.  Collective over the communicator: every rank calls it with
+ * the same rows_cap, topk, experts_total and dtype, in the same order as its other sx_ep calls.
+ * local_bank: this rank's experts_total/world experts (gate, up, down as in sx_moe).  x [rows,
+ * hidden] (16-byte aligned), inds [rows, topk] U32 GLOBAL expert ids (ids >= experts_total are
+ * skipped), scores [rows, topk] F32, shared / shared_gate / clamp_limit as sx_moe; 0 <= rows <=
+ * rows_cap (ranks may hold different row counts).  y [rows, hidden] in x's dtype:
+ *   y[r] = round( sum over ranks d in order of P_d[r] ) (+ shared), P_d[r] = the k-order f32 sum
+ * of score * expert output over r's slots whose expert rank d owns.  experts_total must be
+ * world * local_bank experts.  `workspace` holds sx_ep_workspace_bytes(...) bytes. */
+sx_status sx_ep_moe(sx_ep* ep, sx_stream stream, const sx_bank* local_bank, int32_t experts_total,
+                    const sx_decode* dec, const void* x, sx_dtype dtype, int32_t rows, int32_t rows_cap,
+                    const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
+                    const void* shared_gate, int32_t clamp_limit, void* y, void* workspace, size_t workspace_bytes);
+
+/* The communicator's world size and rank (either pointer may be null). */
+sx_status sx_ep_info(const sx_ep* ep, int32_t* world, int32_t* rank);
+
 /* ------------------------------------------------------------------ device error latch
  * Every bounded device-side wait that gives up records a code in a per-device latch instead of
  * hanging; the call that launched it may already have returned SX_OK.  Returns the latched code

@@ -14,6 +14,7 @@ from .exl3 import (  # noqa: E402
     Codebook,
     Decode,
     Exl3Error,
+    ExpertParallel,
     LINEAR_WEIGHTS_STATIC,
     Proj,
     RouterMode,
@@ -28,12 +29,13 @@ from .exl3 import (  # noqa: E402
     moe_with_gated_shared,
     moe_with_shared,
     router_topk,
+    share_unique_id,
     table_info,
     table_row,
 )
 
 __all__ = [
-    "Bank", "Codebook", "Decode", "Exl3Error", "LINEAR_WEIGHTS_STATIC", "Proj", "RouterMode", "TileOrder", "decode_codewords",
+    "Bank", "Codebook", "Decode", "Exl3Error", "ExpertParallel", "LINEAR_WEIGHTS_STATIC", "Proj", "RouterMode", "TileOrder", "decode_codewords",
     "dequant_inner", "device_error", "linear", "linear_grouped", "moe", "moe_clamped", "moe_with_gated_shared",
-    "moe_with_shared", "router_topk", "table_info", "table_row",
+    "moe_with_shared", "router_topk", "share_unique_id", "table_info", "table_row",
 ]

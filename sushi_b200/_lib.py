@@ -51,6 +51,14 @@ SIGNATURES = {
     "sx_moe": (_I, [_P, ctypes.POINTER(SxBank), ctypes.POINTER(SxDecode), _P, _I, _I, _P, _P, _I, _P, _P, _I, _P, _P, _SZ]),
     "sx_moe_static_scratch": (_I, [_P, ctypes.POINTER(SxBank), ctypes.POINTER(SxDecode), _P, _I, _I, _P, _P, _I, _P, _P, _I, _P]),
     "sx_moe_static_scratch_bytes": (_SZ, []),
+    "sx_ep_unique_id": (_I, [_P]),
+    "sx_ep_init": (_I, [_P, _I, _I, _P]),
+    "sx_ep_destroy": (_I, [_P]),
+    "sx_ep_abort": (_I, [_P]),
+    "sx_ep_info": (_I, [_P, _P, _P]),
+    "sx_ep_workspace_bytes": (_SZ, [_P, ctypes.POINTER(SxBank), _I, _I, _I]),
+    "sx_ep_moe": (_I, [_P, _P, ctypes.POINTER(SxBank), _I, ctypes.POINTER(SxDecode), _P, _I, _I, _I, _P, _P, _I, _P,
+                       _P, _I, _P, _P, _SZ]),
     "sx_device_error": (_I, [_P]),
     "sx_last_error_detail": (ctypes.c_char_p, []),
 }

@@ -1,0 +1,401 @@
+// Expert-parallel routed layer: sx_ep_* (include/sushi_exl3.h).
+//
+// Rank g of `world` holds experts [g*El, (g+1)*El) (El = E/world).  One call:
+//   1. ep_plan (one CTA per destination rank d): scans the rank's rows in order and lists the rows
+//      with at least one slot on d; pos[r][d] = the row's place in d's list, or -1.
+//   2. ep_gather (one CTA per (list place, d)): copies the listed row of x into the send block of
+//      d, with its slots as d-local expert ids (other ranks' slots and unused places carry the
+//      sentinel id 0xFFFFFFFF, which the expert chain skips) and scores.
+//   3. dispatch: all-to-all of the fixed-size blocks (rows_cap rows per peer) as grouped
+//      ncclSend/ncclRecv; this rank's own block is a device-to-device copy.
+//   4. the local expert chain (moe_impl) over the world*rows_cap received rows, writing each row's
+//      k-order f32 sum over its slots here (the partial) instead of a rounded output.
+//   5. combine: all-to-all of the partials back to the rows' owners.
+//   6. ep_combine (one CTA per own row): the partials of the ranks the row went to, added in rank
+//      order, rounded to the output dtype, plus the shared expert (routed_finish).
+// NCCL is loaded with dlopen on first use, so the rest of the library has no NCCL dependency.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <new>
+
+#include "sx_internal.h"
+#include "sx_moe_impl.cuh"
+
+struct sx_ep {
+    ncclComm_t comm;
+    int world, rank, device;
+};
+
+namespace sx {
+namespace {
+
+constexpr uint32_t kSentinel = 0xFFFFFFFFu;
+
+// ------------------------------------------------------------------ NCCL, loaded at run time
+struct NcclApi {
+    decltype(&ncclGetUniqueId) get_unique_id = nullptr;
+    decltype(&ncclCommInitRank) comm_init_rank = nullptr;
+    decltype(&ncclCommDestroy) comm_destroy = nullptr;
+    decltype(&ncclCommAbort) comm_abort = nullptr;
+    decltype(&ncclGroupStart) group_start = nullptr;
+    decltype(&ncclGroupEnd) group_end = nullptr;
+    decltype(&ncclSend) send = nullptr;
+    decltype(&ncclRecv) recv = nullptr;
+    decltype(&ncclGetErrorString) error_string = nullptr;
+    bool ok = false;
+    char why[160] = "";
+};
+
+NcclApi g_nccl;
+std::once_flag g_nccl_once;
+
+template <typename F>
+bool bind(void* h, const char* name, F& fn) {
+    fn = reinterpret_cast<F>(dlsym(h, name));
+    return fn != nullptr;
+}
+
+const NcclApi& nccl() {
+    std::call_once(g_nccl_once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) {
+            snprintf(g_nccl.why, sizeof(g_nccl.why), "dlopen libnccl.so.2 failed");
+            return;
+        }
+        NcclApi& a = g_nccl;
+        a.ok = bind(h, "ncclGetUniqueId", a.get_unique_id) && bind(h, "ncclCommInitRank", a.comm_init_rank) &&
+               bind(h, "ncclCommDestroy", a.comm_destroy) && bind(h, "ncclCommAbort", a.comm_abort) &&
+               bind(h, "ncclGroupStart", a.group_start) && bind(h, "ncclGroupEnd", a.group_end) &&
+               bind(h, "ncclSend", a.send) && bind(h, "ncclRecv", a.recv) &&
+               bind(h, "ncclGetErrorString", a.error_string);
+        if (!a.ok) snprintf(a.why, sizeof(a.why), "libnccl.so.2 lacks a needed symbol");
+    });
+    return g_nccl;
+}
+
+sx_status nccl_status(ncclResult_t r, const char* where) {
+    if (r == ncclSuccess) return SX_OK;
+    note_detail(where, g_nccl.error_string ? g_nccl.error_string(r) : "nccl error");
+    return SX_ERR_NCCL;
+}
+
+sx_status nccl_missing() {
+    note_detail("nccl", g_nccl.why);
+    return SX_ERR_NCCL;
+}
+
+// ------------------------------------------------------------------ kernels
+struct EpArgs {
+    const void* x;          // [rows][D] own rows
+    const uint32_t* inds;   // [rows][K] global expert ids
+    const float* scores;    // [rows][K]
+    int rows, cap, K, D, esz, world, El, Etot;
+    int* list;              // [world][cap] own row listed at each send place, -1 past the count
+    int* pos;               // [cap][world] the own row's place in each destination's block, or -1
+    uint8_t* send_x;        // [world][cap][D] x dtype
+    uint32_t* send_inds;    // [world][cap][K] destination-local ids or the sentinel
+    float* send_scores;     // [world][cap][K]
+};
+
+// Block-wide exclusive scan of 0/1 flags over 256 threads; returns the prefix, sets *total.
+__device__ __forceinline__ int block_scan_256(int flag, int* warp_sums, int* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const unsigned ballot = __ballot_sync(0xffffffffu, flag);
+    const int in_warp = __popc(ballot & ((1u << lane) - 1u));
+    if (lane == 0) warp_sums[warp] = __popc(ballot);
+    __syncthreads();
+    int before = 0, all = 0;
+#pragma unroll
+    for (int w = 0; w < 8; w++) {
+        const int c = warp_sums[w];
+        before += w < warp ? c : 0;
+        all += c;
+    }
+    __syncthreads();
+    *total = all;
+    return before + in_warp;
+}
+
+__global__ void __launch_bounds__(256) ep_plan_kernel(EpArgs a) {
+    __shared__ int warp_sums[8];
+    const int d = blockIdx.x;
+    int base = 0;
+    for (int r0 = 0; r0 < a.rows; r0 += 256) {
+        const int r = r0 + threadIdx.x;
+        int flag = 0;
+        if (r < a.rows) {
+            for (int k = 0; k < a.K; k++) {
+                const uint32_t e = a.inds[(size_t)r * a.K + k];
+                if (e < (uint32_t)a.Etot && (int)(e / (uint32_t)a.El) == d) flag = 1;
+            }
+        }
+        int total;
+        const int idx = block_scan_256(flag, warp_sums, &total);
+        if (r < a.rows) {
+            a.pos[(size_t)r * a.world + d] = flag ? base + idx : -1;
+            if (flag) a.list[(size_t)d * a.cap + base + idx] = r;
+        }
+        base += total;
+    }
+    for (int i = base + threadIdx.x; i < a.cap; i += blockDim.x) a.list[(size_t)d * a.cap + i] = -1;
+}
+
+__global__ void __launch_bounds__(128) ep_gather_kernel(EpArgs a) {
+    const int i = blockIdx.x, d = blockIdx.y;
+    const size_t place = (size_t)d * a.cap + i;
+    const int r = a.list[place];
+    uint32_t* mi = a.send_inds + place * a.K;
+    float* ms = a.send_scores + place * a.K;
+    if (r < 0) {
+        for (int k = threadIdx.x; k < a.K; k += blockDim.x) {
+            mi[k] = kSentinel;
+            ms[k] = 0.0f;
+        }
+        return;
+    }
+    for (int k = threadIdx.x; k < a.K; k += blockDim.x) {
+        const uint32_t e = a.inds[(size_t)r * a.K + k];
+        const bool here = e < (uint32_t)a.Etot && (int)(e / (uint32_t)a.El) == d;
+        mi[k] = here ? e - (uint32_t)(d * a.El) : kSentinel;
+        ms[k] = here ? a.scores[(size_t)r * a.K + k] : 0.0f;
+    }
+    const size_t row_bytes = (size_t)a.D * a.esz;  // a multiple of 256 (D % 128 == 0)
+    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.x) + (size_t)r * row_bytes);
+    uint4* dst = reinterpret_cast<uint4*>(a.send_x + place * row_bytes);
+    for (size_t v = threadIdx.x; v < row_bytes / 16; v += blockDim.x) dst[v] = src[v];
+}
+
+struct CombineArgs {
+    const float* part;       // [world][cap][D]: from rank d, the partials of the rows sent to d
+    const int* pos;          // [cap][world]
+    const void* shared;
+    const void* shared_gate;
+    void* y;
+    int rows, cap, D, world, xdt;
+};
+
+__global__ void __launch_bounds__(256) ep_combine_kernel(CombineArgs a) {
+    const int r = blockIdx.x;
+    for (int d = threadIdx.x; d < a.D; d += blockDim.x) {
+        float acc = 0.0f;
+        for (int g = 0; g < a.world; g++) {
+            const int p = a.pos[(size_t)r * a.world + g];
+            if (p >= 0) acc += a.part[((size_t)g * a.cap + p) * a.D + d];
+        }
+        const float y = routed_finish(acc, a.xdt, a.shared, a.shared_gate, (size_t)r * a.D + d, r);
+        store_act(a.y, (size_t)r * a.D + d, a.xdt, y);
+    }
+}
+
+// ------------------------------------------------------------------ workspace
+constexpr size_t kAlign = 256;
+size_t up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+struct EpWs {
+    size_t list, pos, send_x, send_inds, send_scores, recv_x, recv_inds, recv_scores, part_send, part_recv, moe, total;
+    size_t moe_bytes;
+};
+
+EpWs ep_ws_layout(const sx_bank* bank, int world, int cap, int K, int esz) {
+    EpWs w{};
+    const int D = bank->gate.in_features;
+    const size_t places = (size_t)world * cap;
+    size_t off = 0;
+    w.list = off; off = up(off + places * sizeof(int));
+    w.pos = off; off = up(off + places * sizeof(int));
+    w.send_x = off; off = up(off + places * D * esz);
+    w.send_inds = off; off = up(off + places * K * sizeof(uint32_t));
+    w.send_scores = off; off = up(off + places * K * sizeof(float));
+    w.recv_x = off; off = up(off + places * D * esz);
+    w.recv_inds = off; off = up(off + places * K * sizeof(uint32_t));
+    w.recv_scores = off; off = up(off + places * K * sizeof(float));
+    w.part_send = off; off = up(off + places * D * sizeof(float));
+    w.part_recv = off; off = up(off + places * D * sizeof(float));
+    w.moe_bytes = sx_moe_workspace_bytes(bank, (int32_t)places, K);
+    w.moe = off; off = up(off + w.moe_bytes);
+    w.total = off;
+    return w;
+}
+
+size_t dtype_size(int dt) { return dt == SX_DT_F32 ? 4 : 2; }
+
+// One all-to-all of `bytes` per peer: block p of `send` goes to rank p, block p of `recv` comes
+// from rank p; the own block is a device copy.
+sx_status all_to_all(const sx_ep* ep, const void* send, void* recv, size_t bytes, cudaStream_t s) {
+    const NcclApi& n = nccl();
+    const uint8_t* sb = static_cast<const uint8_t*>(send);
+    uint8_t* rb = static_cast<uint8_t*>(recv);
+    cudaError_t ce = cudaMemcpyAsync(rb + (size_t)ep->rank * bytes, sb + (size_t)ep->rank * bytes, bytes,
+                                     cudaMemcpyDeviceToDevice, s);
+    if (ce != cudaSuccess) return cuda_status(ce, "ep own block copy");
+    if (ep->world == 1) return SX_OK;
+    sx_status st = nccl_status(n.group_start(), "ncclGroupStart");
+    if (st) return st;
+    for (int p = 0; p < ep->world && !st; p++) {
+        if (p == ep->rank) continue;
+        st = nccl_status(n.send(sb + (size_t)p * bytes, bytes, ncclUint8, p, ep->comm, s), "ncclSend");
+        if (!st) st = nccl_status(n.recv(rb + (size_t)p * bytes, bytes, ncclUint8, p, ep->comm, s), "ncclRecv");
+    }
+    const sx_status end = nccl_status(n.group_end(), "ncclGroupEnd");
+    return st ? st : end;
+}
+
+}  // namespace
+}  // namespace sx
+
+using namespace sx;
+
+extern "C" {
+
+sx_status sx_ep_unique_id(uint8_t id[128]) {
+    if (!id) return SX_ERR_NULL_POINTER;
+    const NcclApi& n = nccl();
+    if (!n.ok) return nccl_missing();
+    static_assert(sizeof(ncclUniqueId) == 128, "NCCL unique id is 128 bytes");
+    ncclUniqueId u;
+    sx_status st = nccl_status(n.get_unique_id(&u), "ncclGetUniqueId");
+    if (st) return st;
+    memcpy(id, &u, 128);
+    return SX_OK;
+}
+
+sx_status sx_ep_init(const uint8_t id[128], int32_t world, int32_t rank, sx_ep** out) {
+    if (!id || !out) return SX_ERR_NULL_POINTER;
+    *out = nullptr;
+    if (world < 1 || rank < 0 || rank >= world) return SX_ERR_BAD_SHAPE;
+    const NcclApi& n = nccl();
+    if (!n.ok) return nccl_missing();
+    ncclUniqueId u;
+    memcpy(&u, id, 128);
+    sx_ep* ep = new (std::nothrow) sx_ep;
+    if (!ep) return SX_ERR_BAD_SHAPE;
+    ep->world = world;
+    ep->rank = rank;
+    cudaGetDevice(&ep->device);
+    sx_status st = nccl_status(n.comm_init_rank(&ep->comm, world, u, rank), "ncclCommInitRank");
+    if (st) {
+        delete ep;
+        return st;
+    }
+    *out = ep;
+    return SX_OK;
+}
+
+sx_status sx_ep_destroy(sx_ep* ep) {
+    if (!ep) return SX_ERR_NULL_POINTER;
+    const sx_status st = nccl_status(nccl().comm_destroy(ep->comm), "ncclCommDestroy");
+    delete ep;
+    return st;
+}
+
+sx_status sx_ep_abort(sx_ep* ep) {
+    if (!ep) return SX_ERR_NULL_POINTER;
+    const sx_status st = nccl_status(nccl().comm_abort(ep->comm), "ncclCommAbort");
+    delete ep;
+    return st;
+}
+
+sx_status sx_ep_info(const sx_ep* ep, int32_t* world, int32_t* rank) {
+    if (!ep) return SX_ERR_NULL_POINTER;
+    if (world) *world = ep->world;
+    if (rank) *rank = ep->rank;
+    return SX_OK;
+}
+
+size_t sx_ep_workspace_bytes(const sx_ep* ep, const sx_bank* local_bank, int32_t rows_cap, int32_t topk,
+                             sx_dtype dtype) {
+    if (!ep || !local_bank || rows_cap < 1 || topk < 1 || !dtype_ok(dtype)) return 0;
+    return ep_ws_layout(local_bank, ep->world, rows_cap, topk, (int)dtype_size(dtype)).total;
+}
+
+sx_status sx_ep_moe(sx_ep* ep, sx_stream stream, const sx_bank* local_bank, int32_t experts_total,
+                    const sx_decode* dec, const void* x, sx_dtype dtype, int32_t rows, int32_t rows_cap,
+                    const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
+                    const void* shared_gate, int32_t clamp_limit, void* y, void* workspace, size_t workspace_bytes) {
+    if (!ep || !local_bank) return SX_ERR_NULL_POINTER;
+    if (rows > 0 && (!x || !inds || !scores || !y)) return SX_ERR_NULL_POINTER;
+    if (shared_gate && !shared) return SX_ERR_NULL_POINTER;
+    if (rows < 0 || rows_cap < 1 || rows > rows_cap || topk < 1) return SX_ERR_BAD_SHAPE;
+    if (topk > 32) return SX_ERR_TOPK_EXCEEDS_REDUCE_BANK;
+    if (!dtype_ok(dtype)) return SX_ERR_BAD_DTYPE;
+    if (clamp_limit < 0 || clamp_limit > 128) return SX_ERR_INVALID_CLAMP;
+    const int El = local_bank->gate.experts;
+    if (El < 1 || (long long)El * ep->world != experts_total) return SX_ERR_BAD_SHAPE;
+    if (topk > experts_total) return SX_ERR_TOPK_EXCEEDS_EXPERTS;
+    const int D = local_bank->gate.in_features;
+    if (D % 128) return SX_ERR_BAD_SHAPE;
+    if (reinterpret_cast<uintptr_t>(x) % 16) return SX_ERR_BAD_SHAPE;  // rows move as 16-byte vectors
+    const int esz = (int)dtype_size(dtype);
+    const EpWs L = ep_ws_layout(local_bank, ep->world, rows_cap, topk, esz);
+    if (!workspace || workspace_bytes < L.total) return SX_ERR_WORKSPACE_TOO_SMALL;
+    if (!nccl().ok) return nccl_missing();
+
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const int G = ep->world, C = rows_cap;
+    const size_t places = (size_t)G * C;
+
+    EpArgs a{};
+    a.x = x;
+    a.inds = inds;
+    a.scores = scores;
+    a.rows = rows;
+    a.cap = C;
+    a.K = topk;
+    a.D = D;
+    a.esz = esz;
+    a.world = G;
+    a.El = El;
+    a.Etot = experts_total;
+    a.list = reinterpret_cast<int*>(ws + L.list);
+    a.pos = reinterpret_cast<int*>(ws + L.pos);
+    a.send_x = ws + L.send_x;
+    a.send_inds = reinterpret_cast<uint32_t*>(ws + L.send_inds);
+    a.send_scores = reinterpret_cast<float*>(ws + L.send_scores);
+
+    // 1-2. plan and gather this rank's send blocks
+    ep_plan_kernel<<<G, 256, 0, s>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_status(e, "ep plan launch");
+    ep_gather_kernel<<<dim3(C, G), 128, 0, s>>>(a);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "ep gather launch");
+
+    // 3. dispatch
+    sx_status st;
+    if ((st = all_to_all(ep, ws + L.send_x, ws + L.recv_x, (size_t)C * D * esz, s))) return st;
+    if ((st = all_to_all(ep, ws + L.send_inds, ws + L.recv_inds, (size_t)C * topk * 4, s))) return st;
+    if ((st = all_to_all(ep, ws + L.send_scores, ws + L.recv_scores, (size_t)C * topk * 4, s))) return st;
+
+    // 4. the local experts over every received row, partials in f32
+    float* part_send = reinterpret_cast<float*>(ws + L.part_send);
+    st = moe_impl(stream, local_bank, dec, ws + L.recv_x, dtype, (int32_t)places,
+                  reinterpret_cast<const uint32_t*>(ws + L.recv_inds), reinterpret_cast<const float*>(ws + L.recv_scores),
+                  topk, nullptr, nullptr, clamp_limit, nullptr, ws + L.moe, L.moe_bytes, part_send);
+    if (st) return st;
+
+    // 5. combine: partials back to the rows' owners
+    if ((st = all_to_all(ep, part_send, ws + L.part_recv, (size_t)C * D * sizeof(float), s))) return st;
+
+    // 6. rank-order sum, rounding, shared expert
+    if (rows == 0) return SX_OK;
+    CombineArgs c{};
+    c.part = reinterpret_cast<const float*>(ws + L.part_recv);
+    c.pos = a.pos;
+    c.shared = shared;
+    c.shared_gate = shared_gate;
+    c.y = y;
+    c.rows = rows;
+    c.cap = C;
+    c.D = D;
+    c.world = G;
+    c.xdt = dtype;
+    ep_combine_kernel<<<rows, 256, 0, s>>>(c);
+    return cuda_status(cudaGetLastError(), "ep combine launch");
+}
+
+}  // extern "C"

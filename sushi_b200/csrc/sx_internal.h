@@ -14,4 +14,11 @@ sx_status check_proj(const sx_proj* p, int need_experts);
 bool dtype_ok(int dt);
 int sm_count();
 
+// sx_moe's body; with `partial` set, the routed k-order sums land there in f32, unrounded and
+// without the shared expert (an expert-parallel rank's share of its peers' tokens), and y is unused.
+sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, const void* x, sx_dtype dtype,
+                   int32_t rows, const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
+                   const void* shared_gate, int32_t clamp_limit, void* y, void* workspace, size_t workspace_bytes,
+                   float* partial);
+
 }  // namespace sx

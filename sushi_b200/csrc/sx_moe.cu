@@ -118,27 +118,13 @@ __global__ void __launch_bounds__(256) moe_reduce_kernel(MoeArgs a) {
             const int slot = r * a.K + k;
             if (a.inds[slot] < (uint32_t)a.E) acc += a.yslot[(size_t)slot * a.D + d];
         }
+        if (a.partial) {  // an expert-parallel rank's share: combined and rounded by the token's owner
+            a.partial[(size_t)r * a.D + d] = acc;
+            continue;
+        }
         // The routed sum is rounded to the output dtype before a shared expert is added
         // (docs/engine-exl3-experts.md "Streamed serial decode"; src/exl3/root.zig:56-92).
-        float y = acc;
-        if (a.xdt != 0) y = a.xdt == 1 ? __half2float(__float2half_rn(y)) : __bfloat162float(__float2bfloat16_rn(y));
-        if (a.shared) {
-            float sh = load_act(a.shared, (size_t)r * a.D + d, a.xdt);
-            if (a.shared_gate) {
-                const float gl = load_act(a.shared_gate, r, a.xdt);
-                float sg = 1.0f / (1.0f + expf(-gl));
-                if (a.xdt == 2) {
-                    sg = __bfloat162float(__float2bfloat16_rn(sg));
-                    sh = __bfloat162float(__float2bfloat16_rn(sg * sh));
-                } else if (a.xdt == 1) {
-                    sg = __half2float(__float2half_rn(sg));
-                    sh = __half2float(__float2half_rn(sg * sh));
-                } else {
-                    sh = sg * sh;
-                }
-            }
-            y = y + sh;
-        }
+        const float y = routed_finish(acc, a.xdt, a.shared, a.shared_gate, (size_t)r * a.D + d, r);
         store_act(a.y, (size_t)r * a.D + d, a.xdt, y);
     }
 }
@@ -161,11 +147,13 @@ extern "C" size_t sx_moe_workspace_bytes(const sx_bank* bank, int32_t rows, int3
     return moe_ws_layout(bank->gate.experts, rows, topk, D, I).total;
 }
 
-extern "C" sx_status sx_moe(sx_stream stream, const sx_bank* bank, const sx_decode* dec, const void* x, sx_dtype dtype,
-                            int32_t rows, const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
-                            const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
-                            size_t workspace_bytes) {
-    if (!bank || !x || !inds || !scores || !y) return SX_ERR_NULL_POINTER;
+namespace sx {
+
+sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, const void* x, sx_dtype dtype,
+                   int32_t rows, const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
+                   const void* shared_gate, int32_t clamp_limit, void* y, void* workspace, size_t workspace_bytes,
+                   float* partial) {
+    if (!bank || !x || !inds || !scores || (!y && !partial)) return SX_ERR_NULL_POINTER;
     if (clamp_limit < 0 || clamp_limit > 128) return SX_ERR_INVALID_CLAMP;
     if (rows < 1 || topk < 1) return SX_ERR_BAD_SHAPE;
     if (topk > 32) return SX_ERR_TOPK_EXCEEDS_REDUCE_BANK;
@@ -181,7 +169,8 @@ extern "C" sx_status sx_moe(sx_stream stream, const sx_bank* bank, const sx_deco
         return SX_ERR_BAD_SHAPE;
     if (bank->gate.tile_order != SX_TILE_PACK || bank->up.tile_order != SX_TILE_PACK || bank->down.tile_order != SX_TILE_PACK)
         return SX_ERR_TILE_ORDER_UNSUPPORTED;
-    if (topk > E) return SX_ERR_TOPK_EXCEEDS_EXPERTS;
+    // (an expert-parallel rank's rows carry every slot, most of them other ranks' sentinels)
+    if (topk > E && !partial) return SX_ERR_TOPK_EXCEEDS_EXPERTS;
     if (bank->gate.n != bank->up.n) return SX_ERR_TRELLIS_GEOMETRY;  // mixed gate/up rates: not served yet
     const MoeWs L = moe_ws_layout(E, rows, topk, D, I);
     if (!workspace || workspace_bytes < L.total) return SX_ERR_WORKSPACE_TOO_SMALL;
@@ -219,6 +208,7 @@ extern "C" sx_status sx_moe(sx_stream stream, const sx_bank* bank, const sx_deco
     a.shared = shared;
     a.shared_gate = shared_gate;
     a.y = y;
+    a.partial = partial;
 
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     route_prep_kernel<<<1, 1024, 2 * (size_t)E * sizeof(int), s>>>(a);
@@ -236,4 +226,14 @@ extern "C" sx_status sx_moe(sx_stream stream, const sx_bank* bank, const sx_deco
     if (e != cudaSuccess) return cuda_status(e, "moe pair/down launch");
     moe_reduce_kernel<<<rows, 256, 0, s>>>(a);
     return cuda_status(cudaGetLastError(), "moe reduce launch");
+}
+
+}  // namespace sx
+
+extern "C" sx_status sx_moe(sx_stream stream, const sx_bank* bank, const sx_decode* dec, const void* x, sx_dtype dtype,
+                            int32_t rows, const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
+                            const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
+                            size_t workspace_bytes) {
+    return moe_impl(stream, bank, dec, x, dtype, rows, inds, scores, topk, shared, shared_gate, clamp_limit, y,
+                    workspace, workspace_bytes, nullptr);
 }

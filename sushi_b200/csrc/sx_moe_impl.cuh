@@ -49,7 +49,36 @@ struct MoeArgs {
     const void* shared;     // [R][D] x dtype, or null
     const void* shared_gate;// [R] x dtype logits, or null
     void* y;                // [R][D] x dtype
+    float* partial;         // [R][D] f32: when set, the k-order sum lands here unrounded (no shared)
 };
+
+// A token's routed sum `acc` (f32) made into its output value: rounded to the output dtype, then
+// the shared expert added (optionally sigmoid-gated, with MLX's bf16/f16 rounding steps), as
+// moeWithShared / moeWithGatedShared do (src/exl3/root.zig:56-92; moe_shared_fold.folded,
+// src/moe_shared_fold.zig:24).  idx = r * D + d.
+__device__ __forceinline__ float routed_finish(float acc, int xdt, const void* shared, const void* shared_gate, size_t idx,
+                                               int r) {
+    float y = acc;
+    if (xdt != 0) y = xdt == 1 ? __half2float(__float2half_rn(y)) : __bfloat162float(__float2bfloat16_rn(y));
+    if (shared) {
+        float sh = load_act(shared, idx, xdt);
+        if (shared_gate) {
+            const float gl = load_act(shared_gate, r, xdt);
+            float sg = 1.0f / (1.0f + expf(-gl));
+            if (xdt == 2) {
+                sg = __bfloat162float(__float2bfloat16_rn(sg));
+                sh = __bfloat162float(__float2bfloat16_rn(sg * sh));
+            } else if (xdt == 1) {
+                sg = __half2float(__float2half_rn(sg));
+                sh = __half2float(__float2half_rn(sg * sh));
+            } else {
+                sh = sg * sh;
+            }
+        }
+        y = y + sh;
+    }
+    return y;
+}
 
 // Work item -> (expert, first sorted slot, rows of the chunk).
 struct WorkItem {

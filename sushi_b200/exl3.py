@@ -290,6 +290,87 @@ def moe_clamped(x, bank, inds, scores, dec, limit):
     return moe(x, bank, inds, scores, dec, clamp_limit=limit)
 
 
+def share_unique_id(group=None) -> bytes:
+    """The NCCL unique id for sx_ep_init, made on the group's rank 0 (sx_ep_unique_id) and handed
+    to every rank by the group's broadcast (any torch.distributed backend, gloo included)."""
+    import torch.distributed as dist
+
+    box = [ExpertParallel.unique_id() if dist.get_rank(group) == 0 else None]
+    dist.broadcast_object_list(box, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+    if not isinstance(box[0], bytes) or len(box[0]) != 128:
+        raise Exl3Error(17)
+    return box[0]
+
+
+class ExpertParallel:
+    """An expert-parallel communicator (sx_ep_*): rank `rank` of `world` holds experts
+    [rank*E/world, (rank+1)*E/world) of each E-expert layer as a local Bank of E/world experts.
+    Dispatch and combine are NCCL all-to-alls over the GPUs (include/sushi_exl3.h, sx_ep_moe)."""
+
+    def __init__(self, unique_id: bytes, world: int, rank: int):
+        if len(unique_id) != 128:
+            raise Exl3Error(1)
+        self.world, self.rank = int(world), int(rank)
+        buf = (ctypes.c_uint8 * 128).from_buffer_copy(unique_id)
+        h = ctypes.c_void_p()
+        _check(lib().sx_ep_init(buf, self.world, self.rank, ctypes.byref(h)))
+        self._h = h
+        self._ws = None
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = (ctypes.c_uint8 * 128)()
+        _check(lib().sx_ep_unique_id(buf))
+        return bytes(buf)
+
+    @classmethod
+    def from_process_group(cls, group=None):
+        """Every rank of a torch.distributed group joins one communicator (share_unique_id)."""
+        import torch.distributed as dist
+
+        return cls(share_unique_id(group), dist.get_world_size(group), dist.get_rank(group))
+
+    def workspace_bytes(self, local_bank: "Bank", rows_cap: int, topk: int, dtype=torch.bfloat16) -> int:
+        b = local_bank.c()
+        return int(lib().sx_ep_workspace_bytes(self._h, ctypes.byref(b), int(rows_cap), int(topk), _DT[dtype]))
+
+    def moe(self, x, local_bank: "Bank", experts_total: int, inds, scores, dec: Decode, rows_cap: int,
+            shared=None, shared_gate=None, clamp_limit=0, workspace=None):
+        """sx_ep_moe: this rank's rows x [rows, D] with GLOBAL expert ids inds [rows, K]; every rank
+        calls it with the same rows_cap, K, experts_total and dtype.  Returns y [rows, D]."""
+        x2 = x.reshape(-1, x.shape[-1]).contiguous()
+        rows = x2.shape[0]
+        if x2.dtype not in _DT:
+            raise Exl3Error(2)
+        ix = inds.reshape(rows, -1).to(torch.int32).contiguous()
+        sc = scores.reshape(rows, -1).float().contiguous()
+        topk = ix.shape[1]
+        if sc.shape != ix.shape:
+            raise Exl3Error(1)
+        b = local_bank.c()
+        need = self.workspace_bytes(local_bank, rows_cap, topk, x2.dtype)
+        if workspace is None:
+            if self._ws is None or self._ws.numel() < need:
+                self._ws = torch.empty(max(need, 1), dtype=torch.uint8, device=x2.device)
+            ws = self._ws
+        else:
+            ws = workspace
+        y = torch.empty_like(x2)
+        d = dec.c()
+        sh = None if shared is None else shared.reshape(rows, -1).to(x2.dtype).contiguous()
+        sg = None if shared_gate is None else shared_gate.reshape(rows).to(x2.dtype).contiguous()
+        _check(lib().sx_ep_moe(self._h, _stream(), ctypes.byref(b), int(experts_total), ctypes.byref(d), x2.data_ptr(),
+                               _DT[x2.dtype], rows, int(rows_cap), ix.data_ptr(), sc.data_ptr(), topk,
+                               None if sh is None else sh.data_ptr(), None if sg is None else sg.data_ptr(),
+                               int(clamp_limit), y.data_ptr(), ws.data_ptr(), ws.numel()))
+        return y.reshape(x.shape)
+
+    def destroy(self):
+        if self._h:
+            _check(lib().sx_ep_destroy(self._h))
+            self._h = None
+
+
 def device_error():
     """The latched code of a bounded device wait that gave up (0 = none); clears it."""
     return lib().sx_device_error(_stream())

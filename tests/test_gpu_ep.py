@@ -1,0 +1,175 @@
+"""Expert-parallel routed layer (sx_ep_moe) on the GPU.
+
+One GPU: a world-1 communicator sends every row to itself, so sx_ep_moe must give the same bits
+as sx_moe (the partial is the same k-order f32 sum; the combine adds it to 0).  Two GPUs (skipped
+on one): each rank holds half of the experts and its own rows; its output must match the
+single-GPU sx_moe over the full bank within the stated bar (the partials of two ranks are added
+in rank order instead of k order, so a few outputs differ in their last bit) and the f32 truth.
+"""
+
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+from oracle import synth
+from tests.helpers import MAX_REL_TOL, REL_RMS_TOL, dec_args, dev, max_rel, rel_rms, random_pack, to_f32
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def sx():
+    import sushi_b200
+
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    return sushi_b200
+
+
+def _bank_np(seed, E, D, I, n):
+    return (random_pack(seed, D, I, n, experts=E), random_pack(seed + 1, D, I, n, experts=E),
+            random_pack(seed + 2, I, D, n, experts=E, suh_mag=0.05))
+
+
+def _bank(sx, bank_np, e0=None, e1=None):
+    sl = slice(e0, e1)
+    return sx.Bank(*[sx.Proj(dev(np.ascontiguousarray(p[0][sl]), torch), dev(np.ascontiguousarray(p[1][sl]), torch),
+                             dev(np.ascontiguousarray(p[2][sl]), torch)) for p in bank_np])
+
+
+def _route(seed, T, E, k):
+    rng = np.random.default_rng(seed)
+    inds = np.stack([rng.choice(E, size=k, replace=False) for _ in range(T)]).astype(np.int32)
+    wts = (0.05 + rng.random((T, k)) * 0.25).astype(np.float32)
+    return inds, wts
+
+
+@pytest.mark.parametrize("T", [1, 6, 19])
+def test_ep_world1_is_bit_identical_to_moe(sx, T):
+    E, D, I, k = 16, 256, 128, 4
+    bank_np = _bank_np(40 + T, E, D, I, 32)
+    _, dec = dec_args(orc.CB_MCG, 16)
+    b = _bank(sx, bank_np)
+    xt = torch.from_numpy(synth.activations(T, T, D)).cuda().to(torch.bfloat16)
+    inds, wts = _route(T, T, E, k)
+    ii, ww = torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda()
+    shared = torch.randn((T, D), device="cuda").to(torch.bfloat16)
+    gate = torch.randn((T,), device="cuda").to(torch.bfloat16)
+    ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0)
+    try:
+        for kw in ({}, {"shared": shared}, {"shared": shared, "shared_gate": gate}):
+            want = sx.moe(xt, b, ii, ww, dec, **kw)
+            got = ep.moe(xt, b, E, ii, ww, dec, rows_cap=T, **kw)
+            torch.cuda.synchronize()
+            assert torch.equal(want, got), kw
+        assert sx.device_error() == 0
+    finally:
+        ep.destroy()
+
+
+def test_ep_world1_spare_capacity_and_skipped_ids(sx):
+    """rows_cap above rows (unused places carry sentinel slots) and ids >= E (skipped)."""
+    E, D, I, k, T = 8, 256, 128, 3, 5
+    bank_np = _bank_np(7, E, D, I, 32)
+    _, dec = dec_args(orc.CB_MCG, 16)
+    b = _bank(sx, bank_np)
+    xt = torch.from_numpy(synth.activations(3, T, D)).cuda().to(torch.float32)
+    inds, wts = _route(9, T, E, k)
+    inds[1, 2] = E + 5
+    ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0)
+    try:
+        got = to_f32(ep.moe(xt, b, E, torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda(), dec, rows_cap=16))
+        want = to_f32(sx.moe(xt, b, torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda(), dec))
+    finally:
+        ep.destroy()
+    assert np.isfinite(got).all()
+    assert max_rel(got, want) <= 1e-5
+
+
+def test_ep_refusals(sx):
+    E, D, I = 8, 256, 128
+    b = _bank(sx, _bank_np(1, E, D, I, 32))
+    _, dec = dec_args(orc.CB_MCG, 16)
+    ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0)
+    x = torch.zeros((4, D), device="cuda", dtype=torch.bfloat16)
+    ii = torch.zeros((4, 2), device="cuda", dtype=torch.int32)
+    ww = torch.zeros((4, 2), device="cuda")
+    try:
+        with pytest.raises(sx.Exl3Error) as e:
+            ep.moe(x, b, E + 1, ii, ww, dec, rows_cap=4)  # experts_total != world * local experts
+        assert e.value.name == "SX_ERR_BAD_SHAPE"
+        with pytest.raises(sx.Exl3Error) as e:
+            ep.moe(x, b, E, ii, ww, dec, rows_cap=3)  # rows > rows_cap
+        assert e.value.name == "SX_ERR_BAD_SHAPE"
+        with pytest.raises(sx.Exl3Error) as e:
+            ep.moe(x, b, E, ii, ww, dec, rows_cap=4, clamp_limit=200)
+        assert e.value.name == "SX_ERR_INVALID_CLAMP"
+    finally:
+        ep.destroy()
+
+
+# ------------------------------------------------------------------ two GPUs
+def _rank_main(rank, world, port, out_dir):
+    import torch.distributed as dist
+
+    import sushi_b200 as sx
+
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        E, D, I, k, T = 16, 256, 128, 4, 7 + 3 * rank
+        bank_np = _bank_np(123, E, D, I, 32)
+        _, dec = dec_args(orc.CB_MCG, 16)
+        El = E // world
+        local = _bank(sx, bank_np, rank * El, (rank + 1) * El)
+        full = _bank(sx, bank_np)
+        xt = torch.from_numpy(synth.activations(50 + rank, T, D)).cuda().to(torch.bfloat16)
+        inds, wts = _route(60 + rank, T, E, k)
+        ii, ww = torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda()
+        ep = sx.ExpertParallel.from_process_group()
+        got = to_f32(ep.moe(xt, local, E, ii, ww, dec, rows_cap=16))
+        torch.cuda.synchronize()
+        ep.destroy()
+        want = to_f32(sx.moe(xt, full, ii, ww, dec))
+        np.save(os.path.join(out_dir, f"got{rank}.npy"), got)
+        np.save(os.path.join(out_dir, f"want{rank}.npy"), want)
+        np.save(os.path.join(out_dir, f"x{rank}.npy"), xt.float().cpu().numpy())
+        np.save(os.path.join(out_dir, f"inds{rank}.npy"), inds)
+        np.save(os.path.join(out_dir, f"wts{rank}.npy"), wts)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_two_gpus_match_single_gpu(tmp_path):
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.start_processes(_rank_main, args=(2, port, str(tmp_path)), nprocs=2, start_method="spawn", join=True)
+    E, D, I = 16, 256, 128
+    bank_np = _bank_np(123, E, D, I, 32)
+    oargs, _ = dec_args(orc.CB_MCG, 16)
+    for rank in range(2):
+        got = np.load(tmp_path / f"got{rank}.npy")
+        want = np.load(tmp_path / f"want{rank}.npy")
+        assert np.isfinite(got).all()
+        assert np.abs(got - want).max() <= 2 ** -7 * np.abs(want).max(), rank  # a last-bit bf16 difference
+        inds, wts = np.load(tmp_path / f"inds{rank}.npy"), np.load(tmp_path / f"wts{rank}.npy")
+        x = np.load(tmp_path / f"x{rank}.npy")
+        truth = np.zeros((x.shape[0], D))
+        for r in range(x.shape[0]):
+            for j in range(inds.shape[1]):
+                e = int(inds[r, j])
+                dense = tuple(orc.decode_dense(p[0][e], p[1][e], p[2][e], a, b_, 32, *oargs)
+                              for p, a, b_ in zip(bank_np, (D, D, I), (I, I, D)))
+                truth[r] += wts[r, j] * orc.expert_truth(dense, x[r])
+        assert max_rel(got, truth) <= MAX_REL_TOL
+        assert rel_rms(got, truth) <= REL_RMS_TOL
