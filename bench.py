@@ -338,48 +338,80 @@ def main():
 
 
 def moe_bench(sx, _lib, torch, args, stream, sptr):
-    """BASELINE configs[2] on one GPU: hidden 2048, 512 experts of 512, top-10, K2 (n32) MCG
-    random banks, softmax router over fp32 logits; tokens/s of router top-k + routed experts."""
-    from oracle import synth
+    """hidden 2048, 512 experts of 512, top-10, K2 (n32) MCG random banks,
+    softmax router over fp32 logits from a bf16 2048x512 matrix; tokens/s of router + routed
+    experts for T tokens per rank.  One GPU: sx_moe over the whole bank.  N GPUs: expert parallel
+    (sx_ep_moe), rank g holding experts [g*512/N, (g+1)*512/N), every rank routing its own T tokens
+    (weak scaling: N*T tokens per step); tokens/s = N*T over the slowest rank's layer time.  Each
+    measurement replays a CUDA graph of layers over a ring of distinct bank copies (> 2x L2)."""
+    import torch.distributed as dist
 
+    world, rank, _ = dist_env()
     E, D, I, k = 512, 2048, 512, 10
-    copies = 2  # the 512-expert bank is 384 MiB: two copies keep every layer's reads out of L2
+    El = E // world
+    bank_bytes = El * 3 * (D * I * 32 // 128 + 2 * (D + I))
+    copies = max(2, -(-2 * L2_BYTES // bank_bytes))
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(1000 + rank)
     banks = []
     for c in range(copies):
         parts = []
         for (i_f, o_f) in ((D, I), (D, I), (I, D)):
-            tr = torch.randint(-32768, 32768, (E, i_f // 16, o_f // 16, 32), dtype=torch.int16, device="cuda")
-            su = (torch.randint(0, 2, (E, i_f), device="cuda").half() * 2 - 1) * 0.05
-            sv = torch.randint(0, 2, (E, o_f), device="cuda").half() * 2 - 1
+            tr = torch.randint(-32768, 32768, (El, i_f // 16, o_f // 16, 32), dtype=torch.int16, device="cuda",
+                               generator=gen)
+            su = (torch.randint(0, 2, (El, i_f), device="cuda", generator=gen).half() * 2 - 1) * 0.05
+            sv = torch.randint(0, 2, (El, o_f), device="cuda", generator=gen).half() * 2 - 1
             parts.append(sx.Proj(tr, su, sv))
         banks.append(sx.Bank(*parts))
     dec = sx.Decode(sx.Codebook.MCG, 16)
-    res = {}
-    wr = torch.randn((D, E), device="cuda").mul_(0.02).to(torch.bfloat16)
+    ep = sx.ExpertParallel.from_process_group() if world > 1 else None
+    res = {"experts_per_rank": El, "ranks": world, "copies": copies, "scaling": "weak (T tokens per rank)"}
+    rgen = torch.Generator(device="cuda")
+    rgen.manual_seed(7)  # the router is replicated: same weights on every rank
+    wr = (torch.randn((D, E), device="cuda", generator=rgen) * 0.02).to(torch.bfloat16)
     for T in (1, 8, 64):
-        x = torch.randn((T, D), device="cuda").to(torch.bfloat16)
+        x = torch.randn((T, D), device="cuda", generator=gen).to(torch.bfloat16)
 
         def layer(c):
             logits = (x @ wr).float()
             inds, scores = sx.router_topk(logits, k)
-            return sx.moe(x, banks[c % copies], inds, scores, dec)
+            if ep is None:
+                return sx.moe(x, banks[c % copies], inds, scores, dec)
+            return ep.moe(x, banks[c % copies], E, inds, scores, dec, rows_cap=T)
 
-        for i in range(args.warmup):
+        for i in range(max(3, args.warmup)):
             layer(i)
+        torch.cuda.synchronize()
+        reps = 2 * copies
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(reps):
+                layer(i)
+        g.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        reps = max(10, args.steps * 4)
+        rounds = max(3, args.steps)
         e0.record(stream)
-        for i in range(reps):
-            layer(i)
+        for _ in range(rounds):
+            g.replay()
         e1.record(stream)
         torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / reps
+        ms = e0.elapsed_time(e1) / (rounds * reps)
+        if world > 1:
+            tt = torch.tensor([ms], device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms = float(tt.item())
+        del g
         inds, _ = sx.router_topk((x @ wr).float(), k)
         active = int(torch.unique(inds).numel())
-        bytes_ = active * 3 * (D * I * 32 // 128 + 2 * (D + I))
-        res[f"T{T}"] = {"tokens_per_s": round(T / (ms * 1e-3), 1), "ms_per_layer": round(ms, 4),
-                        "active_experts": active, "expert_gbs": round(bytes_ / (ms * 1e-3) / 1e9, 1)}
+        res[f"T{T}"] = {"tokens_per_s": round(world * T / (ms * 1e-3), 1), "ms_per_layer": round(ms, 4),
+                        "tokens_per_rank": T, "active_experts_rank0_tokens": active}
+    if ep is not None:
+        torch.cuda.synchronize()
+        ep.destroy()
     return res
 
 
