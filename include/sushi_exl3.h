@@ -135,6 +135,16 @@ enum {
 sx_status sx_linear_ex(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x, sx_dtype dtype,
                        int32_t rows, void* y, uint32_t flags);
 
+/* The many-row projection on the tensor cores: the reference's sorted-window GEMM for rows past
+ * the decode chain (src/exl3/linear.zig:365; kernels.moePrefill's inner GEMM,
+ * src/exl3/expert_exl3_kernels.zig:1379-1408).  Same arguments and result bar as sx_linear, plus
+ * a workspace of sx_linear_gemm_workspace_bytes(proj, rows) bytes (16-byte aligned) for the
+ * prepared rows.  The weights are decoded to the reference's f16 inner weights in shared memory
+ * and multiplied by tcgen05 MMAs with f32 accumulation. */
+size_t sx_linear_gemm_workspace_bytes(const sx_proj* proj, int32_t rows);
+sx_status sx_linear_gemm(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x, sx_dtype dtype,
+                         int32_t rows, void* y, void* workspace, size_t workspace_bytes);
+
 /* linear.linearGrouped (src/exl3/linear.zig:38-54): x [G, rows, in] through the G-bank proj
  * (experts == G, bank g serves x[g]) into y [G, rows, out]. */
 sx_status sx_linear_grouped(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x,

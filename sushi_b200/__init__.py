@@ -23,6 +23,7 @@ from .exl3 import (  # noqa: E402
     dequant_inner,
     device_error,
     linear,
+    linear_gemm,
     linear_grouped,
     moe,
     moe_clamped,
@@ -36,6 +37,6 @@ from .exl3 import (  # noqa: E402
 
 __all__ = [
     "Bank", "Codebook", "Decode", "Exl3Error", "ExpertParallel", "LINEAR_WEIGHTS_STATIC", "Proj", "RouterMode", "TileOrder", "decode_codewords",
-    "dequant_inner", "device_error", "linear", "linear_grouped", "moe", "moe_clamped", "moe_with_gated_shared",
+    "dequant_inner", "device_error", "linear", "linear_gemm", "linear_grouped", "moe", "moe_clamped", "moe_with_gated_shared",
     "moe_with_shared", "router_topk", "share_unique_id", "table_info", "table_row",
 ]

@@ -1,0 +1,351 @@
+// Tensor-core EXL3 projection for many rows (kernel template; instantiated per codebook in
+// sx_gemm_{mcg,mul1,hash,pair1}.cu): the reference's sorted-window GEMM (src/exl3/linear.zig:365,
+// kernels.moePrefill src/exl3/expert_exl3_kernels.zig:2861, innerGemmSortedTable* :1379-1408)
+// rebuilt on tcgen05.
+//
+//   D[o][t] = sum_k W[k][o] * P[t][k]      (o: 128 outputs of a block, t: NT rows, k: inputs)
+//
+// * A = the weights, M = 128 outputs: eight decoder warps decode each 64-input chunk's 32 trellis
+//   tiles (streamed into shared memory by 1-D bulk copies) into f16 with the reference's
+//   rounding (the f16 sum of the codebook's two halves, or MUL1's f16 fma: the bit-exact inner
+//   weights of sx_dequant_inner) and store them as a K-major, 128-byte-swizzled tile.
+// * B = the prepared rows P = f16(H128(f16(x) * suh)), N = NT rows: a 2-D TMA tile (128-byte
+//   swizzle) from a [rows, in] f16 matrix that a prep kernel wrote.  Rows past the matrix read 0.
+// * One thread issues tcgen05.mma kind::f16 (f16 x f16 -> f32 in tensor memory) per 16-input
+//   step and commits each stage's completion to the stage's empty barrier.
+// * Split-K: the CTAs of a cluster (grid z) take contiguous input ranges; every CTA moves its
+//   accumulator from tensor memory to shared memory and the rank-0 CTA sums the cluster's
+//   partials over DSMEM in rank order, applies H128, svh and the codebook scale, and writes.
+// Every wait is bounded (sx_common.cuh); a timed-out CTA skips its work, reaches every barrier
+// and frees its tensor memory.
+#pragma once
+
+#include <cuda.h>
+
+#include "sx_core.cuh"
+
+namespace sx {
+
+constexpr int kGemmDecWarps = 8;                        // decoders, then the epilogue
+constexpr int kGemmThreads = (kGemmDecWarps + 2) * 32;  // + producer warp + MMA warp
+constexpr int kGemmKC = 64;                             // inputs per stage (one 128-byte swizzle row)
+constexpr int kGemmRows = 128;                          // NT: rows per CTA tile (the MMA's N)
+
+enum GemmMode : int {
+    GEMM_OUT_ACT = 0,   // y[row][o] in the activation dtype
+    GEMM_OUT_F32 = 1,   // yf[row][o] f32
+    GEMM_OUT_SLOT = 2,  // yf[order[row]][o] = value * scores[order[row]] (f32 per routed slot)
+};
+
+struct GemmArgs {
+    const uint16_t* trellis;   // expert 0's [in/16][out/16][n]
+    size_t tr_expert;          // elements between experts
+    const uint16_t* svh;       // [E][out]
+    int in, out;
+    DecParams dp;
+    float scale;               // the codebook's output scale
+    // rows: dense (rows > 0) or the routed work list of sx_moe's route_prep (chunks of NT rows)
+    int rows;
+    const int* meta;           // [0] = work items
+    const int* act_expert;
+    const int* act_start;
+    const int* act_count;
+    const int* work_act;
+    const int* work_chunk;
+    // output
+    int mode;
+    void* y;                   // GEMM_OUT_ACT
+    int ydt;
+    float* yf;                 // GEMM_OUT_F32 / GEMM_OUT_SLOT
+    const int* order;          // GEMM_OUT_SLOT: sorted position -> slot
+    const float* scores;       // GEMM_OUT_SLOT: [slots]
+};
+
+template <int N, int NT>
+struct GemmLayout {
+    static constexpr int A_BYTES = 128 * kGemmKC * 2;   // 16 KB
+    static constexpr int B_BYTES = NT * kGemmKC * 2;    // 8 or 16 KB
+    static constexpr int T_BYTES = 4 * 8 * N * 2;       // 32 trellis tiles
+    static constexpr int NST = 4;
+    static constexpr int A_OFF = 0;
+    static constexpr int B_OFF = A_OFF + NST * A_BYTES;
+    static constexpr int T_OFF = B_OFF + NST * B_BYTES;
+    static constexpr int BAR_OFF = (T_OFF + NST * T_BYTES + 15) / 16 * 16;
+    static constexpr int TOTAL = BAR_OFF + (3 * NST + 1) * 8 + 16;
+    static constexpr int RED_BYTES = NT * 128 * 4;      // the accumulator in f32, reusing A and B
+    static_assert(RED_BYTES <= T_OFF, "accumulator staging fits in the A/B ring");
+    static constexpr int ALLOC = TOTAL + 1024;          // room to align the base to 1024 bytes
+};
+
+// ------------------------------------------------------------------ tcgen05 / TMA helpers
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1u << 16;                // leading byte offset (unused for swizzled K-major): 16 B
+    d |= (uint64_t)(1024u >> 4) << 32;      // stride byte offset: 1024 B between 8-row groups
+    d |= (uint64_t)1u << 46;                // descriptor version (sm_100)
+    d |= (uint64_t)2u << 61;                // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor: f16 A and B, f32 D, both K-major, M = 128, N = nt.
+__host__ __device__ constexpr uint32_t idesc_f16_m128(int nt) {
+    return (1u << 4) | ((uint32_t)(nt >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// 2-D TMA tile load into this CTA's shared memory (no multicast).
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// 32 consecutive f32 columns of this warp's 32 tensor-memory lanes.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// Byte offset of element (row, k) of a K-major 128-byte-swizzled tile (64 f16 per row, 8-row
+// groups of 1024 bytes, 16-byte chunk c of row r stored at chunk c ^ (r % 8)).
+__device__ __forceinline__ uint32_t sw128_offset(int row, int k) {
+    return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((((k >> 3) ^ row) & 7) << 4) + (k & 7) * 2);
+}
+
+// Two adjacent weights as f16x2: the f16 sums of each word's two halves (MCG, hash-mask, PAIR1:
+// the reference's f16 addition) or MUL1's value (its high half is 0).
+__device__ __forceinline__ uint32_t half_sums2(uint32_t qa, uint32_t qb) {
+    const uint32_t lo = __byte_perm(qa, qb, 0x5410);
+    const uint32_t hi = __byte_perm(qa, qb, 0x7632);
+    const __half2 s = __hadd2(*reinterpret_cast<const __half2*>(&lo), *reinterpret_cast<const __half2*>(&hi));
+    return *reinterpret_cast<const uint32_t*>(&s);
+}
+
+struct GemmItem {
+    int e, row0, rows;
+};
+
+__device__ __forceinline__ bool gemm_item(const GemmArgs& a, int w, int NT, GemmItem& it) {
+    if (a.rows > 0) {
+        it.e = 0;
+        it.row0 = w * NT;
+        it.rows = min(NT, a.rows - it.row0);
+        return it.rows > 0;
+    }
+    if (w >= a.meta[0]) return false;
+    const int ai = a.work_act[w];
+    it.e = a.act_expert[ai];
+    it.row0 = a.act_start[ai] + a.work_chunk[w] * NT;
+    it.rows = min(NT, a.act_count[ai] - a.work_chunk[w] * NT);
+    return true;
+}
+
+template <int KIND, int N, int NT, bool W16>
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap pmap, GemmArgs a) {
+    using Lay = GemmLayout<N, NT>;
+    constexpr int NST = Lay::NST;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint32_t tmem_slot;
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    cg::cluster_group cluster = cg::this_cluster();
+    GemmItem it;
+    if (!gemm_item(a, blockIdx.x, NT, it)) return;  // every CTA of a cluster shares blockIdx.x
+    const int ob = blockIdx.y;
+    const int S = gridDim.z;
+    const int split = blockIdx.z;
+    const int KC = a.in / kGemmKC;  // chunks of 64 inputs
+    const int c0 = (int)(((long long)split * KC) / S);
+    const int ncs = (int)(((long long)(split + 1) * KC) / S) - c0;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lay::BAR_OFF);
+    uint64_t* decoded = full + NST;
+    uint64_t* empty = decoded + NST;
+    uint64_t* acc_full = empty + NST;
+    float* red = reinterpret_cast<float*>(smem);  // [NT][128], after the main loop
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NST; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&decoded[i], kGemmDecWarps);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_init(acc_full, 1);
+        fence_mbar_init();
+    }
+    if (warp == kGemmDecWarps + 1) {  // the MMA warp owns the tensor memory
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                     "n"(NT < 32 ? 32 : NT)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    const int OT = a.out / 16;
+    const uint16_t* tr = a.trellis + (size_t)it.e * a.tr_expert;
+
+    if (warp == kGemmDecWarps) {
+        // ---------------- producer: trellis rows (bulk) and the prepared rows' tile (TMA)
+        if (lane == 0) {
+            const uint32_t row_bytes = 8u * N * 2u;
+            for (int i = 0; i < ncs; i++) {
+                const int st = i % NST;
+                if (i >= NST && !mbar_wait(&empty[st], ((i / NST) - 1) & 1, DEV_TIMEOUT_EMPTY)) break;
+                mbar_arrive_expect_tx(&full[st], Lay::T_BYTES + Lay::B_BYTES);
+                const int kc = c0 + i;
+#pragma unroll 1
+                for (int r = 0; r < 4; r++) {
+                    const size_t tk = (size_t)kc * 4 + r;
+                    bulk_g2s(smem + Lay::T_OFF + st * Lay::T_BYTES + r * row_bytes, tr + (tk * OT + (size_t)ob * 8) * N,
+                             row_bytes, &full[st]);
+                }
+                tma_load_2d(smem + Lay::B_OFF + st * Lay::B_BYTES, &pmap, kc * kGemmKC, it.row0, &full[st]);
+            }
+        }
+    } else if (warp == kGemmDecWarps + 1) {
+        // ---------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16_m128(NT);
+            bool ok = true;
+            for (int i = 0; i < ncs; i++) {
+                const int st = i % NST;
+                if (ok) ok = mbar_wait(&decoded[st], (i / NST) & 1, DEV_TIMEOUT_FULL);
+                tc_fence_after();
+                if (ok) {
+                    const uint32_t a0 = smem_u32(smem + Lay::A_OFF + st * Lay::A_BYTES);
+                    const uint32_t b0 = smem_u32(smem + Lay::B_OFF + st * Lay::B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < kGemmKC / 16; kk++)
+                        tc_mma_f16(tmem, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32), idesc,
+                                   (i > 0 || kk > 0) ? 1u : 0u);
+                }
+                tc_commit(&empty[st]);  // frees the stage once these MMAs have read it
+            }
+            tc_commit(acc_full);
+        }
+    } else {
+        // ---------------- decoders: warp w decodes trellis row w/2, output tiles (w%2)*4 .. +3
+        LaneFunnel<N> lf;
+        lf.init(lane);
+        const int ti = warp >> 1;
+        const int to0 = (warp & 1) * 4;
+        const int g = lane >> 2, c = lane & 3;
+        // this lane's four 32-bit stores in a decoded tile (output tile to, trellis row ti)
+        const uint32_t off_lo = sw128_offset(g, ti * 16 + 2 * c);      // out g,   in 2c, 2c+1
+        const uint32_t off_hi = sw128_offset(g, ti * 16 + 2 * c + 8);  // out g,   in 2c+8, 2c+9
+        bool ok = true;
+        for (int i = 0; i < ncs; i++) {
+            const int st = i % NST;
+            if (ok) ok = mbar_wait(&full[st], (i / NST) & 1, DEV_TIMEOUT_FULL);
+            if (ok) {
+                const uint32_t* trow =
+                    reinterpret_cast<const uint32_t*>(smem + Lay::T_OFF + st * Lay::T_BYTES) + (ti * 8 + to0) * (N / 2);
+                uint8_t* at = smem + Lay::A_OFF + st * Lay::A_BYTES;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    uint32_t q[8];
+                    decode_lane_q<KIND, N, W16>(trow + j * (N / 2), lf, a.dp, q);
+                    // output rows (to0 + j)*16 + g and + 8: 8-row groups 2*(to0+j) and 2*(to0+j)+1
+                    uint8_t* base = at + (to0 + j) * 2048;
+                    *reinterpret_cast<uint32_t*>(base + off_lo) = half_sums2(q[0], q[1]);
+                    *reinterpret_cast<uint32_t*>(base + off_hi) = half_sums2(q[2], q[3]);
+                    *reinterpret_cast<uint32_t*>(base + 1024 + off_lo) = half_sums2(q[4], q[5]);
+                    *reinterpret_cast<uint32_t*>(base + 1024 + off_hi) = half_sums2(q[6], q[7]);
+                }
+                fence_proxy_async_smem();
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&decoded[st]);
+        }
+
+        // ---------------- epilogue 1: the accumulator to shared memory, red[t][o]
+        const bool acc_ok = mbar_wait(acc_full, 0, DEV_TIMEOUT_FULL);
+        tc_fence_after();
+        if (warp < 4) {
+            const int o = warp * 32 + lane;
+#pragma unroll 1
+            for (int col = 0; col < NT; col += 32) {
+                float v[32];
+                tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)col, v);
+#pragma unroll
+                for (int j = 0; j < 32; j++) red[(col + j) * 128 + o] = acc_ok ? v[j] : 0.0f;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kGemmDecWarps + 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(NT < 32 ? 32 : NT)
+                     : "memory");
+    }
+
+    // ---------------- epilogue 2: rank 0 sums the cluster's partials, H128, svh, scale, store
+    if (S > 1) cluster.sync();
+    if (split == 0 && warp < kGemmDecWarps) {
+        const uint16_t* svh = a.svh + (size_t)it.e * a.out;
+        float sv[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) sv[i] = h2f(svh[ob * 128 + lane * 4 + i]) * a.scale;
+        for (int t = warp; t < it.rows; t += kGemmDecWarps) {
+            float4 s4;
+            if (S > 1) {
+                s4 = cluster_sum4(cluster, red, S, t * 128);
+            } else {
+                s4 = *reinterpret_cast<const float4*>(red + t * 128 + lane * 4);
+            }
+            float v[4] = {s4.x, s4.y, s4.z, s4.w};
+            warp_hadamard128(v);
+            const int row = it.row0 + t;
+            const size_t o = (size_t)ob * 128 + lane * 4;
+            if (a.mode == GEMM_OUT_ACT) {
+#pragma unroll
+                for (int i = 0; i < 4; i++) store_act(a.y, (size_t)row * a.out + o + i, a.ydt, v[i] * sv[i]);
+            } else if (a.mode == GEMM_OUT_F32) {
+                float4 w4 = make_float4(v[0] * sv[0], v[1] * sv[1], v[2] * sv[2], v[3] * sv[3]);
+                *reinterpret_cast<float4*>(a.yf + (size_t)row * a.out + o) = w4;
+            } else {
+                const int slot = a.order[row];
+                const float sc = a.scores[slot];
+                float4 w4 = make_float4(v[0] * sv[0] * sc, v[1] * sv[1] * sc, v[2] * sv[2] * sc, v[3] * sv[3] * sc);
+                *reinterpret_cast<float4*>(a.yf + (size_t)slot * a.out + o) = w4;
+            }
+        }
+    }
+    if (S > 1) cluster.sync();
+}
+
+}  // namespace sx

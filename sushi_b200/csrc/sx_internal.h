@@ -14,6 +14,14 @@ sx_status check_proj(const sx_proj* p, int need_experts);
 bool dtype_ok(int dt);
 int sm_count();
 
+struct GemmArgs;
+// The tensor-core projection (sx_gemm.cu): the TMA map of a [rows, in] f16 matrix of prepared
+// rows, the split-K choice, and the launch over codebook families and rates.
+cudaError_t prep_map(CUtensorMap* m, const uint16_t* P, int rows, int in);
+int gemm_split(long long ctas, int chunks);
+cudaError_t gemm_launch(int kind, const CUtensorMap& pmap, const GemmArgs& a, int n, int items, int S,
+                        cudaStream_t stream);
+
 // sx_moe's body; with `partial` set, the routed k-order sums land there in f32, unrounded and
 // without the shared expert (an expert-parallel rank's share of its peers' tokens), and y is unused.
 sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, const void* x, sx_dtype dtype,

@@ -2,6 +2,7 @@
 // src/exl3/root.zig:51-125) and its workspace query.  Kernels in sx_moe_impl.cuh.
 #include <algorithm>
 
+#include "sx_gemm_impl.cuh"
 #include "sx_internal.h"
 #include "sx_moe_impl.cuh"
 
@@ -35,7 +36,7 @@ __global__ void __launch_bounds__(1024) route_prep_kernel(MoeArgs a) {
         for (int e = e0; e < e1; e++) {
             s_sum += cnt[e];
             a_sum += cnt[e] > 0;
-            w_sum += (cnt[e] + 7) / 8;
+            w_sum += (cnt[e] + a.chunk - 1) / a.chunk;
         }
         int s_ex = s_sum, a_ex = a_sum, w_ex = w_sum;
 #pragma unroll
@@ -59,12 +60,12 @@ __global__ void __launch_bounds__(1024) route_prep_kernel(MoeArgs a) {
                 a.act_expert[a_ex] = e;
                 a.act_start[a_ex] = s_ex;
                 a.act_count[a_ex] = c;
-                for (int ch = 0; ch < (c + 7) / 8; ch++) {
+                for (int ch = 0; ch < (c + a.chunk - 1) / a.chunk; ch++) {
                     a.work_act[w_ex + ch] = a_ex;
                     a.work_chunk[w_ex + ch] = ch;
                 }
                 a_ex++;
-                w_ex += (c + 7) / 8;
+                w_ex += (c + a.chunk - 1) / a.chunk;
             }
             s_ex += c;
         }
@@ -87,15 +88,22 @@ constexpr size_t kAlign = 256;
 size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 struct MoeWs {
-    size_t meta, act_expert, act_start, act_count, work_act, work_chunk, order, hprep, yslot, total;
-    int A_max, W_max;
+    size_t meta, act_expert, act_start, act_count, work_act, work_chunk, order, hprep, yslot, tg, tu, gf, uf, total;
+    int A_max, W_max, chunk;
+    bool gemm;
 };
+
+// More rows than the decode chain serves go through the tensor-core path (the reference's
+// DECODE_ROWS_MAX, src/exl3/expert_exl3_kernels.zig:152).
+constexpr int kDecodeRowsMax = 16;
 
 MoeWs moe_ws_layout(int E, int R, int K, int D, int I) {
     MoeWs w;
     const int RK = R * K;
+    w.gemm = R > kDecodeRowsMax;
+    w.chunk = w.gemm ? kGemmRows : 8;
     w.A_max = std::min(E, RK);
-    w.W_max = w.A_max + RK / 8 + 1;
+    w.W_max = w.A_max + RK / w.chunk + 1;
     size_t off = 0;
     w.meta = off; off = align_up(off + 16 * sizeof(int));
     w.act_expert = off; off = align_up(off + (size_t)w.A_max * sizeof(int));
@@ -106,6 +114,13 @@ MoeWs moe_ws_layout(int E, int R, int K, int D, int I) {
     w.order = off; off = align_up(off + (size_t)RK * sizeof(int));
     w.hprep = off; off = align_up(off + (size_t)RK * I * sizeof(uint16_t));
     w.yslot = off; off = align_up(off + (size_t)RK * D * sizeof(float));
+    w.tg = w.tu = w.gf = w.uf = 0;
+    if (w.gemm) {
+        w.tg = off; off = align_up(off + (size_t)RK * D * sizeof(uint16_t));
+        w.tu = off; off = align_up(off + (size_t)RK * D * sizeof(uint16_t));
+        w.gf = off; off = align_up(off + (size_t)RK * I * sizeof(float));
+        w.uf = off; off = align_up(off + (size_t)RK * I * sizeof(float));
+    }
     w.total = off;
     return w;
 }
@@ -126,6 +141,83 @@ __global__ void __launch_bounds__(256) moe_reduce_kernel(MoeArgs a) {
         // (docs/engine-exl3-experts.md "Streamed serial decode"; src/exl3/root.zig:56-92).
         const float y = routed_finish(acc, a.xdt, a.shared, a.shared_gate, (size_t)r * a.D + d, r);
         store_act(a.y, (size_t)r * a.D + d, a.xdt, y);
+    }
+}
+
+// ------------------------------------------------------------------ tensor-core path
+// Work item w (chunk of kGemmRows sorted positions of one expert) of route_prep's list.
+__device__ __forceinline__ bool chunk_item(const MoeArgs& a, int w, int& e, int& first, int& rows) {
+    if (w >= a.meta[0]) return false;
+    const int ai = a.work_act[w];
+    e = a.act_expert[ai];
+    first = a.act_start[ai] + a.work_chunk[w] * a.chunk;
+    rows = min(a.chunk, a.act_count[ai] - a.work_chunk[w] * a.chunk);
+    return true;
+}
+
+// The gate and up projections' prepared inputs of every sorted position p (slot order[p], token
+// order[p] / K): f16(H128(f16(x) * suh)) per 128-input block, as prepareInput does.  One warp per
+// position and block.
+__global__ void __launch_bounds__(256) moe_prep_kernel(MoeArgs a) {
+    int e, first, rows;
+    if (!chunk_item(a, blockIdx.x, e, first, rows)) return;
+    const int kb = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int base = kb * 128 + lane * 4;
+    const uint16_t* sg = a.gate_suh + (size_t)e * a.D;
+    const uint16_t* su = a.up_suh + (size_t)e * a.D;
+    for (int t = warp; t < rows; t += 8) {
+        const int p = first + t;
+        const int tok = a.order[p] / a.K;
+        float g[4], u[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float v = round_f16(load_act(a.x, (size_t)tok * a.D + base + i, a.xdt));
+            g[i] = v * h2f(sg[base + i]);
+            u[i] = v * h2f(su[base + i]);
+        }
+        warp_hadamard128(g);
+        warp_hadamard128(u);
+        uint2 hg, hu;
+        hg.x = (uint32_t)f2h(g[0]) | ((uint32_t)f2h(g[1]) << 16);
+        hg.y = (uint32_t)f2h(g[2]) | ((uint32_t)f2h(g[3]) << 16);
+        hu.x = (uint32_t)f2h(u[0]) | ((uint32_t)f2h(u[1]) << 16);
+        hu.y = (uint32_t)f2h(u[2]) | ((uint32_t)f2h(u[3]) << 16);
+        *reinterpret_cast<uint2*>(a.tg + (size_t)p * a.D + base) = hg;
+        *reinterpret_cast<uint2*>(a.tu + (size_t)p * a.D + base) = hu;
+    }
+}
+
+// The reference's mid (expert_exl3_kernels.zig:2243 MID_SOURCE) on the gate and up outputs of
+// every sorted position: SwiGLU in f32 (gate upper-clamped, up clipped when a limit is set), times
+// the down projection's suh, H128, rounded to f16: the down projection's prepared input.
+__global__ void __launch_bounds__(256) moe_mid_kernel(MoeArgs a) {
+    int e, first, rows;
+    if (!chunk_item(a, blockIdx.x, e, first, rows)) return;
+    const int ib = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int o0 = ib * 128 + lane * 4;
+    const uint16_t* dsu = a.down_suh + (size_t)e * a.I;
+    for (int t = warp; t < rows; t += 8) {
+        const int p = first + t;
+        const float4 g4 = *reinterpret_cast<const float4*>(a.gf + (size_t)p * a.I + o0);
+        const float4 u4 = *reinterpret_cast<const float4*>(a.uf + (size_t)p * a.I + o0);
+        const float gg[4] = {g4.x, g4.y, g4.z, g4.w}, uu[4] = {u4.x, u4.y, u4.z, u4.w};
+        float h[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            float gv = gg[i], uv = uu[i];
+            if (a.clamp > 0.0f) {
+                gv = fminf(gv, a.clamp);
+                uv = fminf(fmaxf(uv, -a.clamp), a.clamp);
+            }
+            h[i] = gv / (1.0f + expf(-gv)) * uv * h2f(dsu[o0 + i]);
+        }
+        warp_hadamard128(h);
+        uint2 hh;
+        hh.x = (uint32_t)f2h(h[0]) | ((uint32_t)f2h(h[1]) << 16);
+        hh.y = (uint32_t)f2h(h[2]) | ((uint32_t)f2h(h[3]) << 16);
+        *reinterpret_cast<uint2*>(a.hprep + (size_t)p * a.I + o0) = hh;
     }
 }
 
@@ -209,11 +301,71 @@ sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, 
     a.shared_gate = shared_gate;
     a.y = y;
     a.partial = partial;
+    a.chunk = L.chunk;
 
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     route_prep_kernel<<<1, 1024, 2 * (size_t)E * sizeof(int), s>>>(a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_status(e, "route_prep launch");
+    if (L.gemm) {
+        // Tensor-core path (kernels.moePrefill, src/exl3/expert_exl3_kernels.zig:2861): prepared
+        // gate/up inputs per sorted position, the gate and up GEMMs, the mid, the down GEMM into the
+        // per-slot planes; the same k-order reduce as the decode chain.
+        if (reinterpret_cast<uintptr_t>(ws) % 16) return SX_ERR_BAD_SHAPE;
+        a.tg = reinterpret_cast<uint16_t*>(ws + L.tg);
+        a.tu = reinterpret_cast<uint16_t*>(ws + L.tu);
+        a.gf = reinterpret_cast<float*>(ws + L.gf);
+        a.uf = reinterpret_cast<float*>(ws + L.uf);
+        const int RK = rows * topk;
+        moe_prep_kernel<<<dim3(L.W_max, D / 128), 256, 0, s>>>(a);
+        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "moe prep launch");
+        CUtensorMap mg, mu, mh;
+        if ((e = prep_map(&mg, a.tg, RK, D)) != cudaSuccess || (e = prep_map(&mu, a.tu, RK, D)) != cudaSuccess ||
+            (e = prep_map(&mh, a.hprep, RK, I)) != cudaSuccess)
+            return cuda_status(e, "cuTensorMapEncodeTiled");
+        GemmArgs g{};
+        g.rows = 0;
+        g.meta = a.meta;
+        g.act_expert = a.act_expert;
+        g.act_start = a.act_start;
+        g.act_count = a.act_count;
+        g.work_act = a.work_act;
+        g.work_chunk = a.work_chunk;
+        g.mode = GEMM_OUT_F32;
+        g.in = D;
+        g.out = I;
+        g.dp = a.dp_gu;
+        g.scale = a.scale_gu;
+        const int S_gu = gemm_split((long long)L.A_max * (I / 128), D / kGemmKC);
+        const struct { const sx_proj* p; float* out; const CUtensorMap* m; } gu[2] = {{&bank->gate, a.gf, &mg},
+                                                                                        {&bank->up, a.uf, &mu}};
+        for (const auto& q : gu) {
+            g.trellis = q.p->trellis;
+            g.tr_expert = (size_t)(D / 16) * (I / 16) * q.p->n;
+            g.svh = q.p->svh;
+            g.yf = q.out;
+            if ((e = gemm_launch(kind_gu, *q.m, g, q.p->n, L.W_max, S_gu, s)) != cudaSuccess)
+                return cuda_status(e, "moe gate/up gemm launch");
+        }
+        moe_mid_kernel<<<dim3(L.W_max, I / 128), 256, 0, s>>>(a);
+        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "moe mid launch");
+        g.mode = GEMM_OUT_SLOT;
+        g.in = I;
+        g.out = D;
+        g.dp = a.dp_down;
+        g.scale = a.scale_down;
+        g.trellis = bank->down.trellis;
+        g.tr_expert = (size_t)(I / 16) * (D / 16) * bank->down.n;
+        g.svh = bank->down.svh;
+        g.yf = a.yslot;
+        g.order = a.order;
+        g.scores = a.scores;
+        const int S_d = gemm_split((long long)L.A_max * (D / 128), I / kGemmKC);
+        if ((e = gemm_launch(kind_d, mh, g, bank->down.n, L.W_max, S_d, s)) != cudaSuccess)
+            return cuda_status(e, "moe down gemm launch");
+        moe_reduce_kernel<<<rows, 256, 0, s>>>(a);
+        return cuda_status(cudaGetLastError(), "moe reduce launch");
+    }
     const int S_gu = pick_split(L.A_max * (I / 128), D / 128);
     const int S_d = pick_split(L.A_max * (D / 128), I / 128);
     switch (kind_gu) {

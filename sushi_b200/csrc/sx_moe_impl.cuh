@@ -50,6 +50,12 @@ struct MoeArgs {
     const void* shared_gate;// [R] x dtype logits, or null
     void* y;                // [R][D] x dtype
     float* partial;         // [R][D] f32: when set, the k-order sum lands here unrounded (no shared)
+    int chunk;              // rows per work item: 8 (decode chain) or kGemmRows (tensor-core path)
+    // tensor-core path (sorted positions p): prepared gate/up inputs, gate/up outputs
+    uint16_t* tg;           // [R*K][D] f16
+    uint16_t* tu;           // [R*K][D] f16
+    float* gf;              // [R*K][I] f32
+    float* uf;              // [R*K][I] f32
 };
 
 // A token's routed sum `acc` (f32) made into its output value: rounded to the output dtype, then

@@ -177,6 +177,25 @@ def linear(x, proj: Proj, dec: Decode, flags: int = 0, out=None):
     return y
 
 
+def linear_gemm(x, proj: Proj, dec: Decode, workspace=None):
+    """sx_linear_gemm: the many-row projection on the tensor cores (tcgen05), same result bar as
+    linear; x [rows, in] -> [rows, out] in x's dtype."""
+    if x.dim() != 2 or not x.is_contiguous():
+        raise Exl3Error(1)
+    if x.dtype not in _DT:
+        raise Exl3Error(2)
+    _, in_f, out_f, _ = proj.dims()
+    if x.shape[1] != in_f:
+        raise Exl3Error(1)
+    y = torch.empty((x.shape[0], out_f), dtype=x.dtype, device=x.device)
+    p, d = proj.c(), dec.c()
+    need = lib().sx_linear_gemm_workspace_bytes(ctypes.byref(p), x.shape[0])
+    ws = workspace if workspace is not None else _workspace(need, x.device)
+    _check(lib().sx_linear_gemm(_stream(), ctypes.byref(p), ctypes.byref(d), x.data_ptr(), _DT[x.dtype], x.shape[0],
+                                y.data_ptr(), ws.data_ptr(), ws.numel()))
+    return y
+
+
 def linear_grouped(x, proj: Proj, dec: Decode):
     """linear.linearGrouped: x [G, rows, in] through the G-bank proj (bank g serves x[g]) -> [G, rows, out]."""
     if x.dim() != 3 or not x.is_contiguous():
