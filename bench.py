@@ -39,6 +39,7 @@ SHAPES = [(7168, 2048), (2048, 7168), (14336, 4096)]  # (in, out): out x in = 20
 RATES = [32, 48, 64]
 ROWS = [1, 2, 4, 8, 16, 64]
 L2_BYTES = 126 * 1024 * 1024
+GEMM_ROWS = 16  # sweep rows at or above this go through the tensor-core projection
 METRIC = "EXL3 GEMV compressed-HBM GB/s (% peak); MoE layer tokens/s at 1/2/4/8 B200"
 UNIT = "GB/s"
 
@@ -161,7 +162,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-moe", action="store_true")
-    ap.add_argument("--profile", default=None, choices=["gemv", "moe"],
+    ap.add_argument("--profile", default=None, choices=["gemv", "moe", "gemm", "prefill"],
                     help="a small fixed case for ncu: --warmup launches, then --steps launches, no graphs")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -206,10 +207,15 @@ def main():
     ybuf = {out_f: torch.empty((maxm, out_f), device="cuda", dtype=torch.bfloat16) for _, out_f in SHAPES}
     configs = [(in_f, out_f, n, m) for (in_f, out_f) in SHAPES for n in RATES for m in ROWS]
 
+    gemm_ws = torch.empty(max(in_f for in_f, _ in SHAPES) * maxm * 2 + 256, dtype=torch.uint8, device="cuda")
+
     def launch(in_f, out_f, n, m, proj):
-        # weights are loaded once: launches may stream them while the previous launch finishes
-        st = L.sx_linear_ex(sptr, ctypes.byref(proj), ctypes.byref(dec), xbuf[in_f].data_ptr(), 2, m,
-                            ybuf[out_f].data_ptr(), 1)
+        if m >= GEMM_ROWS:  # the tensor-core path (sx_linear_gemm) from 16 rows
+            st = L.sx_linear_gemm(sptr, ctypes.byref(proj), ctypes.byref(dec), xbuf[in_f].data_ptr(), 2, m,
+                                  ybuf[out_f].data_ptr(), gemm_ws.data_ptr(), gemm_ws.numel())
+        else:  # the decode GEMV; weights are loaded once, so launches may overlap the previous one's tail
+            st = L.sx_linear_ex(sptr, ctypes.byref(proj), ctypes.byref(dec), xbuf[in_f].data_ptr(), 2, m,
+                                ybuf[out_f].data_ptr(), 1)
         if st:
             raise RuntimeError(f"{L.sx_status_name(st).decode()} {L.sx_last_error_detail().decode()} "
                                f"(out {out_f} in {in_f} n {n} rows {m})")
@@ -226,8 +232,7 @@ def main():
             for p in projs:
                 launch(in_f, out_f, n, m, p)
         graphs.append((g, len(projs), alg_bytes(in_f, out_f, n, m) * len(projs)))
-        chunks = -(-m // 16)
-        launches_per_step += len(projs) * chunks
+        launches_per_step += len(projs) * (2 if m >= GEMM_ROWS else 1)  # GEMM: prep + MMA kernel
         bytes_per_step += alg_bytes(in_f, out_f, n, m) * len(projs)
     torch.cuda.synchronize()
 
@@ -327,6 +332,8 @@ def main():
 
     if not args.no_moe:
         out["moe"] = moe_bench(sx, _lib, torch, args, stream, sptr)
+        if world == 1:
+            out["moe_prefill"] = prefill_bench(sx, torch, args, stream, tf_peak)
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline()
@@ -415,6 +422,54 @@ def moe_bench(sx, _lib, torch, args, stream, sptr):
     return res
 
 
+def prefill_bench(sx, torch, args, stream, tf_peak):
+    """BASELINE configs[3] on one GPU: the configs[2] layer in prefill, 8192 tokens of bf16 N(0,1)
+    hidden states, routing skewed by a Zipf(1.1) bias log(r_e^-1.1 / sum) over a seeded rank
+    permutation added to the logits; router + routed experts through the tensor-core path.
+    Roofline: tensor, F = 2*T*k*3*H*I + 2*T*H*E flops per layer (the routed GEMMs and the router)
+    over the measured dense bf16 peak; the expert weights are decoded inside the GEMMs."""
+    E, D, I, k, T = 512, 2048, 512, 10, 8192
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(77)
+    parts = []
+    for (i_f, o_f) in ((D, I), (D, I), (I, D)):
+        tr = torch.randint(-32768, 32768, (E, i_f // 16, o_f // 16, 32), dtype=torch.int16, device="cuda", generator=gen)
+        su = (torch.randint(0, 2, (E, i_f), device="cuda", generator=gen).half() * 2 - 1) * 0.05
+        sv = torch.randint(0, 2, (E, o_f), device="cuda", generator=gen).half() * 2 - 1
+        parts.append(sx.Proj(tr, su, sv))
+    bank = sx.Bank(*parts)
+    dec = sx.Decode(sx.Codebook.MCG, 16)
+    wr = (torch.randn((D, E), device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+    ranks = torch.randperm(E, generator=torch.Generator().manual_seed(5)).float() + 1.0
+    zb = (ranks ** -1.1)
+    bias = torch.log(zb / zb.sum()).cuda()
+    x = torch.randn((T, D), device="cuda", generator=gen).to(torch.bfloat16)
+    ws = torch.empty(sx._lib.load().sx_moe_workspace_bytes(ctypes.byref(bank.c()), T, k), dtype=torch.uint8, device="cuda")
+
+    def layer():
+        logits = (x @ wr).float() + bias
+        inds, scores = sx.router_topk(logits, k)
+        return sx.moe(x, bank, inds, scores, dec, workspace=ws)
+
+    for _ in range(max(3, args.warmup)):
+        layer()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(3, args.steps)
+    e0.record(stream)
+    for _ in range(reps):
+        layer()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    flops = 2.0 * T * k * 3 * D * I + 2.0 * T * D * E
+    inds, _ = sx.router_topk((x @ wr).float() + bias, k)
+    counts = torch.bincount(inds.flatten().long(), minlength=E)
+    return {"tokens": T, "tokens_per_s": round(T / (ms * 1e-3), 1), "ms_per_layer": round(ms, 3),
+            "tflops": round(flops / (ms * 1e-3) / 1e12, 1), "tensor_frac_of_measured": round(flops / (ms * 1e-3) / 1e12 / tf_peak, 4),
+            "max_rows_per_expert": int(counts.max()), "active_experts": int((counts > 0).sum())}
+
+
 def run_profile(args):
     """ncu case: the 4096x14336 K2 (n32) M=1 projection (config 1's rate, the sweep's largest
     shape) over 12 distinct weight copies (176 MB > L2), or one MoE decode layer (T=8)."""
@@ -424,6 +479,27 @@ def run_profile(args):
 
     torch.cuda.set_device(0)
     dec = sx.Decode(sx.Codebook.MCG, 16)
+    if args.profile == "prefill":
+        class A:  # the prefill layer as in the bench, warmup + steps layers
+            warmup, steps = args.warmup, args.steps
+        prefill_bench(sx, torch, A, torch.cuda.current_stream(), 1618.5)
+        torch.cuda.synchronize()
+        assert sx.device_error() == 0
+        print("profile case done", flush=True)
+        return
+    if args.profile == "gemm":
+        in_f, out_f, n, copies, rows = 14336, 4096, 32, 4, 1024
+        tr = torch.randint(-32768, 32768, (copies, in_f // 16, out_f // 16, n), dtype=torch.int16, device="cuda")
+        su = (torch.randint(0, 2, (copies, in_f), device="cuda").half() * 2 - 1) * 0.05
+        sv = torch.randint(0, 2, (copies, out_f), device="cuda").half() * 2 - 1
+        projs = [sx.Proj(tr[c], su[c], sv[c]) for c in range(copies)]
+        x = torch.randn((rows, in_f), device="cuda").to(torch.bfloat16)
+        for i in range(args.warmup + args.steps):
+            sx.linear_gemm(x, projs[i % copies], dec)
+        torch.cuda.synchronize()
+        assert sx.device_error() == 0
+        print("profile case done", flush=True)
+        return
     if args.profile == "gemv":
         in_f, out_f, n, copies = 14336, 4096, 32, 12
         tr = torch.randint(-32768, 32768, (copies, in_f // 16, out_f // 16, n), dtype=torch.int16, device="cuda")

@@ -216,7 +216,9 @@ EpWs ep_ws_layout(const sx_bank* bank, int world, int cap, int K, int esz) {
     w.recv_scores = off; off = up(off + places * K * sizeof(float));
     w.part_send = off; off = up(off + places * D * sizeof(float));
     w.part_recv = off; off = up(off + places * D * sizeof(float));
-    w.moe_bytes = sx_moe_workspace_bytes(bank, (int32_t)places, K);
+    // a rank receives about rows_cap * K valid slots (every rank's rows_cap rows, K slots each,
+    // spread over the world): that, not the places' sentinel-padded slots, picks its expert path
+    w.moe_bytes = moe_workspace_bytes(bank, (int32_t)places, K, (long long)cap * K);
     w.moe = off; off = up(off + w.moe_bytes);
     w.total = off;
     return w;
@@ -375,7 +377,7 @@ sx_status sx_ep_moe(sx_ep* ep, sx_stream stream, const sx_bank* local_bank, int3
     float* part_send = reinterpret_cast<float*>(ws + L.part_send);
     st = moe_impl(stream, local_bank, dec, ws + L.recv_x, dtype, (int32_t)places,
                   reinterpret_cast<const uint32_t*>(ws + L.recv_inds), reinterpret_cast<const float*>(ws + L.recv_scores),
-                  topk, nullptr, nullptr, clamp_limit, nullptr, ws + L.moe, L.moe_bytes, part_send);
+                  topk, nullptr, nullptr, clamp_limit, nullptr, ws + L.moe, L.moe_bytes, part_send, (long long)C * topk);
     if (st) return st;
 
     // 5. combine: partials back to the rows' owners

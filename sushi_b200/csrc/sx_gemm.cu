@@ -10,7 +10,8 @@
 namespace sx {
 
 template <int KIND>
-cudaError_t gemm_dispatch(const CUtensorMap& pmap, const GemmArgs& a, int n, int items, int S, cudaStream_t stream);
+cudaError_t gemm_dispatch(const CUtensorMap& pmap, const GemmArgs& a, int n, int rt, int items, int S,
+                          cudaStream_t stream);
 
 // P[r][kb*128 + i] = f16(H128(f16(x[r]) * suh)) for one (row, 128-input block) per warp: the
 // reference's prepareInput (src/exl3/expert_exl3.zig:490-501).
@@ -56,13 +57,13 @@ cudaError_t prep_map(CUtensorMap* m, const uint16_t* P, int rows, int in) {
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-cudaError_t gemm_launch(int kind, const CUtensorMap& pmap, const GemmArgs& a, int n, int items, int S,
+cudaError_t gemm_launch(int kind, const CUtensorMap& pmap, const GemmArgs& a, int n, int rt, int items, int S,
                         cudaStream_t stream) {
     switch (kind) {
-        case K_MCG: return gemm_dispatch<K_MCG>(pmap, a, n, items, S, stream);
-        case K_MUL1: return gemm_dispatch<K_MUL1>(pmap, a, n, items, S, stream);
-        case K_HASH: return gemm_dispatch<K_HASH>(pmap, a, n, items, S, stream);
-        case K_PAIR1: return gemm_dispatch<K_PAIR1>(pmap, a, n, items, S, stream);
+        case K_MCG: return gemm_dispatch<K_MCG>(pmap, a, n, rt, items, S, stream);
+        case K_MUL1: return gemm_dispatch<K_MUL1>(pmap, a, n, rt, items, S, stream);
+        case K_HASH: return gemm_dispatch<K_HASH>(pmap, a, n, rt, items, S, stream);
+        case K_PAIR1: return gemm_dispatch<K_PAIR1>(pmap, a, n, rt, items, S, stream);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -75,6 +76,18 @@ int gemm_split(long long ctas, int chunks) {
     S = std::min(S, 16);
     S = std::min(S, std::max(1, chunks / 4));
     return std::max(1, S);
+}
+
+bool gemm_rt_rate(int n) { return n == 16 || n == 24 || n == 32 || n == 40 || n == 48 || n == 64; }
+
+// Row tiles per CTA for a dense projection of `rows` rows over `blocks` output blocks: four (each
+// decoded weight chunk feeds four 128-row accumulators) when that still gives every SM a CTA
+// without splitting K and the rate has the kernel, else one.
+int gemm_rt(long long rows, long long units, int blocks, int n) {
+    if (!gemm_rt_rate(n)) return 1;
+    const long long per = 4LL * kGemmRows;
+    if (rows >= per * 3 / 4 && units * ((rows + per - 1) / per) * blocks >= sm_count()) return 4;
+    return 1;
 }
 
 }  // namespace sx
@@ -122,8 +135,9 @@ extern "C" sx_status sx_linear_gemm(sx_stream stream, const sx_proj* proj, const
     a.mode = GEMM_OUT_ACT;
     a.y = y;
     a.ydt = dtype;
-    const int items = (rows + kGemmRows - 1) / kGemmRows;
-    const int S = gemm_split((long long)items * (out / 128), in / kGemmKC);
-    e = gemm_launch(kind, pmap, a, proj->n, items, S, s);
+    const int rt = gemm_rt(rows, 1, out / 128, proj->n);
+    const int items = (rows + kGemmRows * rt - 1) / (kGemmRows * rt);
+    const int S = rt > 1 ? 1 : gemm_split((long long)items * (out / 128), in / kGemmKC);
+    e = gemm_launch(kind, pmap, a, proj->n, rt, items, S, s);
     return cuda_status(e, "gemm launch");
 }

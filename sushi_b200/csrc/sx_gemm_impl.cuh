@@ -5,7 +5,7 @@
 //
 //   D[o][t] = sum_k W[k][o] * P[t][k]      (o: 128 outputs of a block, t: NT rows, k: inputs)
 //
-// * A = the weights, M = 128 outputs: eight decoder warps decode each 64-input chunk's 32 trellis
+// * A = the weights, M = 128 outputs: 16 decoder warps decode each 64-input chunk's 32 trellis
 //   tiles (streamed into shared memory by 1-D bulk copies) into f16 with the reference's
 //   rounding (the f16 sum of the codebook's two halves, or MUL1's f16 fma: the bit-exact inner
 //   weights of sx_dequant_inner) and store them as a K-major, 128-byte-swizzled tile.
@@ -26,7 +26,7 @@
 
 namespace sx {
 
-constexpr int kGemmDecWarps = 8;                        // decoders, then the epilogue
+constexpr int kGemmDecWarps = 16;                       // decoders, then the epilogue
 constexpr int kGemmThreads = (kGemmDecWarps + 2) * 32;  // + producer warp + MMA warp
 constexpr int kGemmKC = 64;                             // inputs per stage (one 128-byte swizzle row)
 constexpr int kGemmRows = 128;                          // NT: rows per CTA tile (the MMA's N)
@@ -61,19 +61,24 @@ struct GemmArgs {
     const float* scores;       // GEMM_OUT_SLOT: [slots]
 };
 
-template <int N, int NT>
+// RT row tiles of NT rows per CTA share each decoded weight chunk: RT accumulators of NT columns
+// in tensor memory (RT * NT <= 512), RT prepared-row tiles per stage.
+template <int N, int NT, int RT>
 struct GemmLayout {
     static constexpr int A_BYTES = 128 * kGemmKC * 2;   // 16 KB
-    static constexpr int B_BYTES = NT * kGemmKC * 2;    // 8 or 16 KB
+    static constexpr int B_TILE = NT * kGemmKC * 2;     // 16 KB per row tile
+    static constexpr int B_BYTES = RT * B_TILE;
     static constexpr int T_BYTES = 4 * 8 * N * 2;       // 32 trellis tiles
-    static constexpr int NST = 4;
+    static constexpr int NST = RT == 1 ? 4 : (RT == 2 ? 3 : 2);
+    static constexpr int TMEM_COLS = NT * RT;
     static constexpr int A_OFF = 0;
     static constexpr int B_OFF = A_OFF + NST * A_BYTES;
     static constexpr int T_OFF = B_OFF + NST * B_BYTES;
     static constexpr int BAR_OFF = (T_OFF + NST * T_BYTES + 15) / 16 * 16;
     static constexpr int TOTAL = BAR_OFF + (3 * NST + 1) * 8 + 16;
-    static constexpr int RED_BYTES = NT * 128 * 4;      // the accumulator in f32, reusing A and B
+    static constexpr int RED_BYTES = NT * 128 * 4;      // one row tile's accumulator in f32, reusing A and B
     static_assert(RED_BYTES <= T_OFF, "accumulator staging fits in the A/B ring");
+    static_assert(TMEM_COLS <= 512, "tensor memory holds 512 columns");
     static constexpr int ALLOC = TOTAL + 1024;          // room to align the base to 1024 bytes
 };
 
@@ -157,7 +162,7 @@ struct GemmItem {
     int e, row0, rows;
 };
 
-__device__ __forceinline__ bool gemm_item(const GemmArgs& a, int w, int NT, GemmItem& it) {
+__device__ __forceinline__ bool gemm_item(const GemmArgs& a, int w, int NT, GemmItem& it) {  // NT: rows per item
     if (a.rows > 0) {
         it.e = 0;
         it.row0 = w * NT;
@@ -172,16 +177,51 @@ __device__ __forceinline__ bool gemm_item(const GemmArgs& a, int w, int NT, Gemm
     return true;
 }
 
-template <int KIND, int N, int NT, bool W16>
+// Rows t0 .. t0+rows-1 of the item from red[t - t0][o] (summed over the cluster's S ranks in rank
+// order when split): H128, svh, the codebook scale, and the store of the launch's mode.
+__device__ __forceinline__ void gemm_store(const GemmArgs& a, const GemmItem& it, float* red, cg::cluster_group& cluster,
+                                           int S, int ob, int t0, int rows) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint16_t* svh = a.svh + (size_t)it.e * a.out;
+    float sv[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) sv[i] = h2f(svh[ob * 128 + lane * 4 + i]) * a.scale;
+    for (int t = warp; t < rows; t += kGemmDecWarps) {
+        const float4 s4 = S > 1 ? cluster_sum4(cluster, red, S, t * 128)
+                                : *reinterpret_cast<const float4*>(red + t * 128 + lane * 4);
+        float v[4] = {s4.x, s4.y, s4.z, s4.w};
+        warp_hadamard128(v);
+        const int row = it.row0 + t0 + t;
+        const size_t o = (size_t)ob * 128 + lane * 4;
+        if (a.mode == GEMM_OUT_ACT) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) store_act(a.y, (size_t)row * a.out + o + i, a.ydt, v[i] * sv[i]);
+        } else if (a.mode == GEMM_OUT_F32) {
+            *reinterpret_cast<float4*>(a.yf + (size_t)row * a.out + o) =
+                make_float4(v[0] * sv[0], v[1] * sv[1], v[2] * sv[2], v[3] * sv[3]);
+        } else {
+            const int slot = a.order[row];
+            const float sc = a.scores[slot];
+            *reinterpret_cast<float4*>(a.yf + (size_t)slot * a.out + o) =
+                make_float4(v[0] * sv[0] * sc, v[1] * sv[1] * sc, v[2] * sv[2] * sc, v[3] * sv[3] * sc);
+        }
+    }
+}
+
+// Named barrier 1 over the decoder warps.
+__device__ __forceinline__ void decoders_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kGemmDecWarps * 32) : "memory"); }
+
+template <int KIND, int N, int NT, int RT, bool W16>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap pmap, GemmArgs a) {
-    using Lay = GemmLayout<N, NT>;
+    using Lay = GemmLayout<N, NT, RT>;
     constexpr int NST = Lay::NST;
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint32_t tmem_slot;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     cg::cluster_group cluster = cg::this_cluster();
     GemmItem it;
-    if (!gemm_item(a, blockIdx.x, NT, it)) return;  // every CTA of a cluster shares blockIdx.x
+    if (!gemm_item(a, blockIdx.x, NT * RT, it)) return;  // every CTA of a cluster shares blockIdx.x
+    const int rt_live = (it.rows + NT - 1) / NT;          // row tiles with rows in them
     const int ob = blockIdx.y;
     const int S = gridDim.z;
     const int split = blockIdx.z;
@@ -206,7 +246,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     }
     if (warp == kGemmDecWarps + 1) {  // the MMA warp owns the tensor memory
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
-                     "n"(NT < 32 ? 32 : NT)
+                     "n"(Lay::TMEM_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -224,7 +264,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
             for (int i = 0; i < ncs; i++) {
                 const int st = i % NST;
                 if (i >= NST && !mbar_wait(&empty[st], ((i / NST) - 1) & 1, DEV_TIMEOUT_EMPTY)) break;
-                mbar_arrive_expect_tx(&full[st], Lay::T_BYTES + Lay::B_BYTES);
+                mbar_arrive_expect_tx(&full[st], Lay::T_BYTES + rt_live * Lay::B_TILE);
                 const int kc = c0 + i;
 #pragma unroll 1
                 for (int r = 0; r < 4; r++) {
@@ -232,7 +272,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                     bulk_g2s(smem + Lay::T_OFF + st * Lay::T_BYTES + r * row_bytes, tr + (tk * OT + (size_t)ob * 8) * N,
                              row_bytes, &full[st]);
                 }
-                tma_load_2d(smem + Lay::B_OFF + st * Lay::B_BYTES, &pmap, kc * kGemmKC, it.row0, &full[st]);
+                for (int r = 0; r < rt_live; r++)
+                    tma_load_2d(smem + Lay::B_OFF + st * Lay::B_BYTES + r * Lay::B_TILE, &pmap, kc * kGemmKC,
+                                it.row0 + r * NT, &full[st]);
             }
         }
     } else if (warp == kGemmDecWarps + 1) {
@@ -247,21 +289,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                 if (ok) {
                     const uint32_t a0 = smem_u32(smem + Lay::A_OFF + st * Lay::A_BYTES);
                     const uint32_t b0 = smem_u32(smem + Lay::B_OFF + st * Lay::B_BYTES);
+                    for (int r = 0; r < rt_live; r++)
 #pragma unroll
-                    for (int kk = 0; kk < kGemmKC / 16; kk++)
-                        tc_mma_f16(tmem, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32), idesc,
-                                   (i > 0 || kk > 0) ? 1u : 0u);
+                        for (int kk = 0; kk < kGemmKC / 16; kk++)
+                            tc_mma_f16(tmem + (uint32_t)(r * NT), smem_desc_sw128(a0 + kk * 32),
+                                       smem_desc_sw128(b0 + r * Lay::B_TILE + kk * 32), idesc, (i > 0 || kk > 0) ? 1u : 0u);
                 }
                 tc_commit(&empty[st]);  // frees the stage once these MMAs have read it
             }
             tc_commit(acc_full);
         }
     } else {
-        // ---------------- decoders: warp w decodes trellis row w/2, output tiles (w%2)*4 .. +3
+        // ---------------- decoders: warp w decodes trellis row w/4, output tiles (w%4)*2 and +1
+        constexpr int TPW = 32 / kGemmDecWarps;  // tiles per warp per stage
         LaneFunnel<N> lf;
         lf.init(lane);
-        const int ti = warp >> 1;
-        const int to0 = (warp & 1) * 4;
+        const int ti = warp / (8 / TPW);
+        const int to0 = (warp % (8 / TPW)) * TPW;
         const int g = lane >> 2, c = lane & 3;
         // this lane's four 32-bit stores in a decoded tile (output tile to, trellis row ti)
         const uint32_t off_lo = sw128_offset(g, ti * 16 + 2 * c);      // out g,   in 2c, 2c+1
@@ -275,7 +319,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                     reinterpret_cast<const uint32_t*>(smem + Lay::T_OFF + st * Lay::T_BYTES) + (ti * 8 + to0) * (N / 2);
                 uint8_t* at = smem + Lay::A_OFF + st * Lay::A_BYTES;
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
+                for (int j = 0; j < TPW; j++) {
                     uint32_t q[8];
                     decode_lane_q<KIND, N, W16>(trow + j * (N / 2), lf, a.dp, q);
                     // output rows (to0 + j)*16 + g and + 8: 8-row groups 2*(to0+j) and 2*(to0+j)+1
@@ -291,61 +335,39 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
             if (lane == 0) mbar_arrive(&decoded[st]);
         }
 
-        // ---------------- epilogue 1: the accumulator to shared memory, red[t][o]
+        // ---------------- epilogue: the accumulator of each row tile to shared memory red[t][o]; then
+        // H128, svh, scale and the store, after summing the cluster's partials when split (RT = 1)
         const bool acc_ok = mbar_wait(acc_full, 0, DEV_TIMEOUT_FULL);
         tc_fence_after();
-        if (warp < 4) {
-            const int o = warp * 32 + lane;
+        for (int r = 0; r < rt_live; r++) {
+            if (warp < 4) {
+                const int o = warp * 32 + lane;
 #pragma unroll 1
-            for (int col = 0; col < NT; col += 32) {
-                float v[32];
-                tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)col, v);
+                for (int col = 0; col < NT; col += 32) {
+                    float v[32];
+                    tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(r * NT + col), v);
 #pragma unroll
-                for (int j = 0; j < 32; j++) red[(col + j) * 128 + o] = acc_ok ? v[j] : 0.0f;
+                    for (int j = 0; j < 32; j++) red[(col + j) * 128 + o] = acc_ok ? v[j] : 0.0f;
+                }
             }
+            if (S > 1) break;  // RT == 1: the cluster's sum follows below, with every thread
+            decoders_sync();
+            gemm_store(a, it, red, cluster, 1, ob, r * NT, min(NT, it.rows - r * NT));
+            decoders_sync();
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == kGemmDecWarps + 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(NT < 32 ? 32 : NT)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(Lay::TMEM_COLS)
                      : "memory");
     }
-
-    // ---------------- epilogue 2: rank 0 sums the cluster's partials, H128, svh, scale, store
-    if (S > 1) cluster.sync();
-    if (split == 0 && warp < kGemmDecWarps) {
-        const uint16_t* svh = a.svh + (size_t)it.e * a.out;
-        float sv[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) sv[i] = h2f(svh[ob * 128 + lane * 4 + i]) * a.scale;
-        for (int t = warp; t < it.rows; t += kGemmDecWarps) {
-            float4 s4;
-            if (S > 1) {
-                s4 = cluster_sum4(cluster, red, S, t * 128);
-            } else {
-                s4 = *reinterpret_cast<const float4*>(red + t * 128 + lane * 4);
-            }
-            float v[4] = {s4.x, s4.y, s4.z, s4.w};
-            warp_hadamard128(v);
-            const int row = it.row0 + t;
-            const size_t o = (size_t)ob * 128 + lane * 4;
-            if (a.mode == GEMM_OUT_ACT) {
-#pragma unroll
-                for (int i = 0; i < 4; i++) store_act(a.y, (size_t)row * a.out + o + i, a.ydt, v[i] * sv[i]);
-            } else if (a.mode == GEMM_OUT_F32) {
-                float4 w4 = make_float4(v[0] * sv[0], v[1] * sv[1], v[2] * sv[2], v[3] * sv[3]);
-                *reinterpret_cast<float4*>(a.yf + (size_t)row * a.out + o) = w4;
-            } else {
-                const int slot = a.order[row];
-                const float sc = a.scores[slot];
-                float4 w4 = make_float4(v[0] * sv[0] * sc, v[1] * sv[1] * sc, v[2] * sv[2] * sc, v[3] * sv[3] * sc);
-                *reinterpret_cast<float4*>(a.yf + (size_t)slot * a.out + o) = w4;
-            }
-        }
+    if (S > 1) {
+        cluster.sync();
+        if (split == 0 && warp < kGemmDecWarps) gemm_store(a, it, red, cluster, S, ob, 0, min(NT, it.rows));
+        cluster.sync();
     }
-    if (S > 1) cluster.sync();
 }
 
 }  // namespace sx

@@ -7,11 +7,12 @@
 
 namespace sx {
 
-template <int KIND, int N>
+template <int KIND, int N, int RT>
 static cudaError_t launch_gemm_t(const CUtensorMap& pmap, const GemmArgs& a, int items, int S, cudaStream_t stream) {
     constexpr int NT = kGemmRows;
-    auto kern = gemm_kernel<KIND, N, NT, false>;
-    const int smem = GemmLayout<N, NT>::ALLOC;
+    if (RT > 1 && S > 1) return cudaErrorInvalidValue;  // split-K launches hold one row tile per CTA
+    auto kern = gemm_kernel<KIND, N, NT, RT, false>;
+    const int smem = GemmLayout<N, NT, RT>::ALLOC;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     if (S > 8) {
@@ -43,10 +44,23 @@ static cudaError_t launch_gemm_t(const CUtensorMap& pmap, const GemmArgs& a, int
     X(24) X(26) X(28) X(30) X(32) X(34) X(36) X(38) X(40) X(42) X(44) X(46) X(48) X(50) X(52) X(54) X(56) X(58) X(60) \
     X(62) X(64)
 
+// Rates with a four-row-tile (RT = 4) kernel: the configs' K1..K4 and PAIR1's common rows; other
+// rates run one row tile per CTA.
+#define SX_GEMM_N_LIST_RT(X) X(16) X(24) X(32) X(40) X(48) X(64)
+
 template <int KIND>
-cudaError_t gemm_dispatch(const CUtensorMap& pmap, const GemmArgs& a, int n, int items, int S, cudaStream_t stream) {
+cudaError_t gemm_dispatch(const CUtensorMap& pmap, const GemmArgs& a, int n, int rt, int items, int S,
+                          cudaStream_t stream) {
 #define SX_CASE(NN) \
-    case NN: return launch_gemm_t<KIND, NN>(pmap, a, items, S, stream);
+    case NN: return launch_gemm_t<KIND, NN, 1>(pmap, a, items, S, stream);
+#define SX_CASE4(NN) \
+    case NN: return launch_gemm_t<KIND, NN, 4>(pmap, a, items, S, stream);
+    if (rt == 4) {
+        switch (n) {
+            SX_GEMM_N_LIST_RT(SX_CASE4)
+            default: return cudaErrorInvalidValue;
+        }
+    }
     if constexpr (KIND == K_PAIR1) {
         switch (n) {
             SX_GEMM_N_LIST_PAIR1(SX_CASE)
@@ -59,6 +73,7 @@ cudaError_t gemm_dispatch(const CUtensorMap& pmap, const GemmArgs& a, int n, int
         }
     }
 #undef SX_CASE
+#undef SX_CASE4
 }
 
 }  // namespace sx

@@ -19,14 +19,19 @@ struct GemmArgs;
 // rows, the split-K choice, and the launch over codebook families and rates.
 cudaError_t prep_map(CUtensorMap* m, const uint16_t* P, int rows, int in);
 int gemm_split(long long ctas, int chunks);
-cudaError_t gemm_launch(int kind, const CUtensorMap& pmap, const GemmArgs& a, int n, int items, int S,
+int gemm_rt(long long rows_per_unit, long long units, int blocks, int n);
+bool gemm_rt_rate(int n);  // rates with four-row-tile tensor-core kernels
+cudaError_t gemm_launch(int kind, const CUtensorMap& pmap, const GemmArgs& a, int n, int rt, int items, int S,
                         cudaStream_t stream);
 
 // sx_moe's body; with `partial` set, the routed k-order sums land there in f32, unrounded and
 // without the shared expert (an expert-parallel rank's share of its peers' tokens), and y is unused.
+// `slots` bounds the routed slots that can be valid (0: rows * topk); it picks the decode chain or
+// the tensor-core path, and moe_workspace_bytes must be asked with the same value.
 sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, const void* x, sx_dtype dtype,
                    int32_t rows, const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
                    const void* shared_gate, int32_t clamp_limit, void* y, void* workspace, size_t workspace_bytes,
-                   float* partial);
+                   float* partial, long long slots);
+size_t moe_workspace_bytes(const sx_bank* bank, int32_t rows, int32_t topk, long long slots);
 
 }  // namespace sx

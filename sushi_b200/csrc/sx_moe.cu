@@ -14,6 +14,10 @@ cudaError_t moe_launch_kind(const MoeArgs& a, int n_gu, int n_d, int S_gu, int S
 namespace {
 
 // ------------------------------------------------------------------ 1. routing metadata
+// One CTA: the slots' expert histogram, a warp scan, and the scatter of slots into expert order.
+// Work items: experts with fewer than big_min rows are cut into chunks of `chunk` rows (list 1,
+// meta[0] items); larger ones into chunks of big_chunk rows (list 2, meta[1] items), so that the
+// tensor-core path can reuse each decoded weight chunk over four row tiles.  meta[2] = slots.
 __global__ void __launch_bounds__(1024) route_prep_kernel(MoeArgs a) {
     extern __shared__ int rp[];
     int* cnt = rp;             // [E]
@@ -27,32 +31,37 @@ __global__ void __launch_bounds__(1024) route_prep_kernel(MoeArgs a) {
         if (e < (uint32_t)a.E) atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
-    // Warp 0 scans: slot offsets, active-expert ranks and work-item ranks (8-row chunks).
     if (tid < 32) {
         const int lane = tid;
         const int per = (a.E + 31) / 32;
         const int e0 = lane * per, e1 = min(a.E, e0 + per);
-        int s_sum = 0, a_sum = 0, w_sum = 0;
+        auto items1 = [&](int c) { return c >= a.big_min ? 0 : (c + a.chunk - 1) / a.chunk; };
+        auto items2 = [&](int c) { return c >= a.big_min ? (c + a.big_chunk - 1) / a.big_chunk : 0; };
+        int s_sum = 0, a_sum = 0, w_sum = 0, v_sum = 0;
         for (int e = e0; e < e1; e++) {
             s_sum += cnt[e];
             a_sum += cnt[e] > 0;
-            w_sum += (cnt[e] + a.chunk - 1) / a.chunk;
+            w_sum += items1(cnt[e]);
+            v_sum += items2(cnt[e]);
         }
-        int s_ex = s_sum, a_ex = a_sum, w_ex = w_sum;
+        int s_ex = s_sum, a_ex = a_sum, w_ex = w_sum, v_ex = v_sum;
 #pragma unroll
         for (int m = 1; m < 32; m <<= 1) {
             const int ts = __shfl_up_sync(0xffffffffu, s_ex, m);
             const int ta = __shfl_up_sync(0xffffffffu, a_ex, m);
             const int tw = __shfl_up_sync(0xffffffffu, w_ex, m);
+            const int tv = __shfl_up_sync(0xffffffffu, v_ex, m);
             if (lane >= m) {
                 s_ex += ts;
                 a_ex += ta;
                 w_ex += tw;
+                v_ex += tv;
             }
         }
         s_ex -= s_sum;
         a_ex -= a_sum;
         w_ex -= w_sum;
+        v_ex -= v_sum;
         for (int e = e0; e < e1; e++) {
             const int c = cnt[e];
             off[e] = s_ex;
@@ -60,16 +69,25 @@ __global__ void __launch_bounds__(1024) route_prep_kernel(MoeArgs a) {
                 a.act_expert[a_ex] = e;
                 a.act_start[a_ex] = s_ex;
                 a.act_count[a_ex] = c;
-                for (int ch = 0; ch < (c + a.chunk - 1) / a.chunk; ch++) {
+                for (int ch = 0; ch < items1(c); ch++) {
                     a.work_act[w_ex + ch] = a_ex;
                     a.work_chunk[w_ex + ch] = ch;
                 }
+                for (int ch = 0; ch < items2(c); ch++) {
+                    a.work_act4[v_ex + ch] = a_ex;
+                    a.work_chunk4[v_ex + ch] = ch;
+                }
                 a_ex++;
-                w_ex += (c + a.chunk - 1) / a.chunk;
+                w_ex += items1(c);
+                v_ex += items2(c);
             }
             s_ex += c;
         }
-        if (lane == 31) a.meta[0] = w_ex;
+        if (lane == 31) {
+            a.meta[0] = w_ex;
+            a.meta[1] = v_ex;
+            a.meta[2] = s_ex;
+        }
     }
     __syncthreads();
     for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;  // reused as cursors
@@ -79,31 +97,48 @@ __global__ void __launch_bounds__(1024) route_prep_kernel(MoeArgs a) {
         if (e < (uint32_t)a.E) {
             const int pos = atomicAdd(&cnt[e], 1);
             a.order[off[e] + pos] = s;
+            a.sorted_e[off[e] + pos] = (int)e;
         }
     }
 }
-
 
 constexpr size_t kAlign = 256;
 size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 struct MoeWs {
-    size_t meta, act_expert, act_start, act_count, work_act, work_chunk, order, hprep, yslot, tg, tu, gf, uf, total;
-    int A_max, W_max, chunk;
+    size_t meta, act_expert, act_start, act_count, work_act, work_chunk, work_act4, work_chunk4, order, sorted_e, hprep,
+        yslot, tg, tu, gf, uf, total;
+    int A_max, W_max, W4_max, chunk, big_min, big_chunk;
     bool gemm;
 };
 
-// More rows than the decode chain serves go through the tensor-core path (the reference's
-// DECODE_ROWS_MAX, src/exl3/expert_exl3_kernels.zig:152).
+// Experts with at least this many routed rows take the four-row-tile kernel (chunks of 512).
+constexpr int kBigRows = 3 * kGemmRows;
+
+// The decode chain serves up to 16 rows (the reference's DECODE_ROWS_MAX,
+// src/exl3/expert_exl3_kernels.zig:152); more rows go through the tensor-core path once the
+// routed slots average at least 16 rows per active expert, so that a 128-row tile is not mostly
+// empty (decode batches of 64 tokens spread over 512 experts stay on the decode chain).
+// `slots` bounds the slots that can be valid (R*K for sx_moe; an expert-parallel rank's share).
 constexpr int kDecodeRowsMax = 16;
 
-MoeWs moe_ws_layout(int E, int R, int K, int D, int I) {
+bool use_gemm(int E, int R, int K, long long slots) {
+    if (R <= kDecodeRowsMax) return false;
+    if (slots <= 0) slots = (long long)R * K;
+    return slots >= 16LL * std::min<long long>(E, slots);
+}
+
+MoeWs moe_ws_layout(int E, int R, int K, int D, int I, int n_gu, int n_d, long long slots = 0) {
     MoeWs w;
     const int RK = R * K;
-    w.gemm = R > kDecodeRowsMax;
+    w.gemm = use_gemm(E, R, K, slots);
+    const bool big = w.gemm && gemm_rt_rate(n_gu) && gemm_rt_rate(n_d);
     w.chunk = w.gemm ? kGemmRows : 8;
+    w.big_min = big ? kBigRows : 0x7FFFFFFF;
+    w.big_chunk = 4 * kGemmRows;
     w.A_max = std::min(E, RK);
     w.W_max = w.A_max + RK / w.chunk + 1;
+    w.W4_max = big ? RK / w.big_chunk + RK / w.big_min + 1 : 0;
     size_t off = 0;
     w.meta = off; off = align_up(off + 16 * sizeof(int));
     w.act_expert = off; off = align_up(off + (size_t)w.A_max * sizeof(int));
@@ -111,7 +146,10 @@ MoeWs moe_ws_layout(int E, int R, int K, int D, int I) {
     w.act_count = off; off = align_up(off + (size_t)w.A_max * sizeof(int));
     w.work_act = off; off = align_up(off + (size_t)w.W_max * sizeof(int));
     w.work_chunk = off; off = align_up(off + (size_t)w.W_max * sizeof(int));
+    w.work_act4 = off; off = align_up(off + (size_t)std::max(1, w.W4_max) * sizeof(int));
+    w.work_chunk4 = off; off = align_up(off + (size_t)std::max(1, w.W4_max) * sizeof(int));
     w.order = off; off = align_up(off + (size_t)RK * sizeof(int));
+    w.sorted_e = off; off = align_up(off + (size_t)RK * sizeof(int));
     w.hprep = off; off = align_up(off + (size_t)RK * I * sizeof(uint16_t));
     w.yslot = off; off = align_up(off + (size_t)RK * D * sizeof(float));
     w.tg = w.tu = w.gf = w.uf = 0;
@@ -145,80 +183,65 @@ __global__ void __launch_bounds__(256) moe_reduce_kernel(MoeArgs a) {
 }
 
 // ------------------------------------------------------------------ tensor-core path
-// Work item w (chunk of kGemmRows sorted positions of one expert) of route_prep's list.
-__device__ __forceinline__ bool chunk_item(const MoeArgs& a, int w, int& e, int& first, int& rows) {
-    if (w >= a.meta[0]) return false;
-    const int ai = a.work_act[w];
-    e = a.act_expert[ai];
-    first = a.act_start[ai] + a.work_chunk[w] * a.chunk;
-    rows = min(a.chunk, a.act_count[ai] - a.work_chunk[w] * a.chunk);
-    return true;
-}
-
 // The gate and up projections' prepared inputs of every sorted position p (slot order[p], token
-// order[p] / K): f16(H128(f16(x) * suh)) per 128-input block, as prepareInput does.  One warp per
-// position and block.
+// order[p] / K, expert sorted_e[p]): f16(H128(f16(x) * suh)) per 128-input block, as
+// prepareInput does.  One warp per position and block; positions past meta[2] return.
 __global__ void __launch_bounds__(256) moe_prep_kernel(MoeArgs a) {
-    int e, first, rows;
-    if (!chunk_item(a, blockIdx.x, e, first, rows)) return;
-    const int kb = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int p = blockIdx.x * 8 + warp;
+    if (p >= a.meta[2]) return;
+    const int e = a.sorted_e[p];
+    const int kb = blockIdx.y;
     const int base = kb * 128 + lane * 4;
     const uint16_t* sg = a.gate_suh + (size_t)e * a.D;
     const uint16_t* su = a.up_suh + (size_t)e * a.D;
-    for (int t = warp; t < rows; t += 8) {
-        const int p = first + t;
-        const int tok = a.order[p] / a.K;
-        float g[4], u[4];
+    const int tok = a.order[p] / a.K;
+    float g[4], u[4];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const float v = round_f16(load_act(a.x, (size_t)tok * a.D + base + i, a.xdt));
-            g[i] = v * h2f(sg[base + i]);
-            u[i] = v * h2f(su[base + i]);
-        }
-        warp_hadamard128(g);
-        warp_hadamard128(u);
-        uint2 hg, hu;
-        hg.x = (uint32_t)f2h(g[0]) | ((uint32_t)f2h(g[1]) << 16);
-        hg.y = (uint32_t)f2h(g[2]) | ((uint32_t)f2h(g[3]) << 16);
-        hu.x = (uint32_t)f2h(u[0]) | ((uint32_t)f2h(u[1]) << 16);
-        hu.y = (uint32_t)f2h(u[2]) | ((uint32_t)f2h(u[3]) << 16);
-        *reinterpret_cast<uint2*>(a.tg + (size_t)p * a.D + base) = hg;
-        *reinterpret_cast<uint2*>(a.tu + (size_t)p * a.D + base) = hu;
+    for (int i = 0; i < 4; i++) {
+        const float v = round_f16(load_act(a.x, (size_t)tok * a.D + base + i, a.xdt));
+        g[i] = v * h2f(sg[base + i]);
+        u[i] = v * h2f(su[base + i]);
     }
+    warp_hadamard128(g);
+    warp_hadamard128(u);
+    uint2 hg, hu;
+    hg.x = (uint32_t)f2h(g[0]) | ((uint32_t)f2h(g[1]) << 16);
+    hg.y = (uint32_t)f2h(g[2]) | ((uint32_t)f2h(g[3]) << 16);
+    hu.x = (uint32_t)f2h(u[0]) | ((uint32_t)f2h(u[1]) << 16);
+    hu.y = (uint32_t)f2h(u[2]) | ((uint32_t)f2h(u[3]) << 16);
+    *reinterpret_cast<uint2*>(a.tg + (size_t)p * a.D + base) = hg;
+    *reinterpret_cast<uint2*>(a.tu + (size_t)p * a.D + base) = hu;
 }
 
 // The reference's mid (expert_exl3_kernels.zig:2243 MID_SOURCE) on the gate and up outputs of
 // every sorted position: SwiGLU in f32 (gate upper-clamped, up clipped when a limit is set), times
 // the down projection's suh, H128, rounded to f16: the down projection's prepared input.
 __global__ void __launch_bounds__(256) moe_mid_kernel(MoeArgs a) {
-    int e, first, rows;
-    if (!chunk_item(a, blockIdx.x, e, first, rows)) return;
-    const int ib = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int o0 = ib * 128 + lane * 4;
+    const int p = blockIdx.x * 8 + warp;
+    if (p >= a.meta[2]) return;
+    const int e = a.sorted_e[p];
+    const int o0 = blockIdx.y * 128 + lane * 4;
     const uint16_t* dsu = a.down_suh + (size_t)e * a.I;
-    for (int t = warp; t < rows; t += 8) {
-        const int p = first + t;
-        const float4 g4 = *reinterpret_cast<const float4*>(a.gf + (size_t)p * a.I + o0);
-        const float4 u4 = *reinterpret_cast<const float4*>(a.uf + (size_t)p * a.I + o0);
-        const float gg[4] = {g4.x, g4.y, g4.z, g4.w}, uu[4] = {u4.x, u4.y, u4.z, u4.w};
-        float h[4];
+    const float4 g4 = *reinterpret_cast<const float4*>(a.gf + (size_t)p * a.I + o0);
+    const float4 u4 = *reinterpret_cast<const float4*>(a.uf + (size_t)p * a.I + o0);
+    const float gg[4] = {g4.x, g4.y, g4.z, g4.w}, uu[4] = {u4.x, u4.y, u4.z, u4.w};
+    float h[4];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            float gv = gg[i], uv = uu[i];
-            if (a.clamp > 0.0f) {
-                gv = fminf(gv, a.clamp);
-                uv = fminf(fmaxf(uv, -a.clamp), a.clamp);
-            }
-            h[i] = gv / (1.0f + expf(-gv)) * uv * h2f(dsu[o0 + i]);
+    for (int i = 0; i < 4; i++) {
+        float gv = gg[i], uv = uu[i];
+        if (a.clamp > 0.0f) {
+            gv = fminf(gv, a.clamp);
+            uv = fminf(fmaxf(uv, -a.clamp), a.clamp);
         }
-        warp_hadamard128(h);
-        uint2 hh;
-        hh.x = (uint32_t)f2h(h[0]) | ((uint32_t)f2h(h[1]) << 16);
-        hh.y = (uint32_t)f2h(h[2]) | ((uint32_t)f2h(h[3]) << 16);
-        *reinterpret_cast<uint2*>(a.hprep + (size_t)p * a.I + o0) = hh;
+        h[i] = gv / (1.0f + expf(-gv)) * uv * h2f(dsu[o0 + i]);
     }
+    warp_hadamard128(h);
+    uint2 hh;
+    hh.x = (uint32_t)f2h(h[0]) | ((uint32_t)f2h(h[1]) << 16);
+    hh.y = (uint32_t)f2h(h[2]) | ((uint32_t)f2h(h[3]) << 16);
+    *reinterpret_cast<uint2*>(a.hprep + (size_t)p * a.I + o0) = hh;
 }
 
 int pick_split(int units, int kb) {
@@ -233,18 +256,19 @@ int pick_split(int units, int kb) {
 
 using namespace sx;
 
-extern "C" size_t sx_moe_workspace_bytes(const sx_bank* bank, int32_t rows, int32_t topk) {
-    if (!bank || rows < 1 || topk < 1) return 0;
-    const int D = bank->gate.in_features, I = bank->gate.out_features;
-    return moe_ws_layout(bank->gate.experts, rows, topk, D, I).total;
-}
-
 namespace sx {
+
+size_t moe_workspace_bytes(const sx_bank* bank, int32_t rows, int32_t topk, long long slots) {
+    if (!bank || rows < 1 || topk < 1) return 0;
+    return moe_ws_layout(bank->gate.experts, rows, topk, bank->gate.in_features, bank->gate.out_features, bank->gate.n,
+                         bank->down.n, slots)
+        .total;
+}
 
 sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, const void* x, sx_dtype dtype,
                    int32_t rows, const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
                    const void* shared_gate, int32_t clamp_limit, void* y, void* workspace, size_t workspace_bytes,
-                   float* partial) {
+                   float* partial, long long slots) {
     if (!bank || !x || !inds || !scores || (!y && !partial)) return SX_ERR_NULL_POINTER;
     if (clamp_limit < 0 || clamp_limit > 128) return SX_ERR_INVALID_CLAMP;
     if (rows < 1 || topk < 1) return SX_ERR_BAD_SHAPE;
@@ -264,7 +288,7 @@ sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, 
     // (an expert-parallel rank's rows carry every slot, most of them other ranks' sentinels)
     if (topk > E && !partial) return SX_ERR_TOPK_EXCEEDS_EXPERTS;
     if (bank->gate.n != bank->up.n) return SX_ERR_TRELLIS_GEOMETRY;  // mixed gate/up rates: not served yet
-    const MoeWs L = moe_ws_layout(E, rows, topk, D, I);
+    const MoeWs L = moe_ws_layout(E, rows, topk, D, I, bank->gate.n, bank->down.n, slots);
     if (!workspace || workspace_bytes < L.total) return SX_ERR_WORKSPACE_TOO_SMALL;
     if (E > 8192) return SX_ERR_BAD_SHAPE;
 
@@ -302,6 +326,11 @@ sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, 
     a.y = y;
     a.partial = partial;
     a.chunk = L.chunk;
+    a.big_min = L.big_min;
+    a.big_chunk = L.big_chunk;
+    a.work_act4 = reinterpret_cast<int*>(ws + L.work_act4);
+    a.work_chunk4 = reinterpret_cast<int*>(ws + L.work_chunk4);
+    a.sorted_e = reinterpret_cast<int*>(ws + L.sorted_e);
 
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     route_prep_kernel<<<1, 1024, 2 * (size_t)E * sizeof(int), s>>>(a);
@@ -317,26 +346,37 @@ sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, 
         a.gf = reinterpret_cast<float*>(ws + L.gf);
         a.uf = reinterpret_cast<float*>(ws + L.uf);
         const int RK = rows * topk;
-        moe_prep_kernel<<<dim3(L.W_max, D / 128), 256, 0, s>>>(a);
+        const dim3 pos_grid((RK + 7) / 8, 1);
+        moe_prep_kernel<<<dim3(pos_grid.x, D / 128), 256, 0, s>>>(a);
         if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "moe prep launch");
         CUtensorMap mg, mu, mh;
         if ((e = prep_map(&mg, a.tg, RK, D)) != cudaSuccess || (e = prep_map(&mu, a.tu, RK, D)) != cudaSuccess ||
             (e = prep_map(&mh, a.hprep, RK, I)) != cudaSuccess)
             return cuda_status(e, "cuTensorMapEncodeTiled");
+        // two launches per projection: list 1 (chunks of 128 rows, one row tile per CTA) and list 2
+        // (chunks of 512 rows of the experts with many rows, four row tiles per CTA)
+        auto both = [&](GemmArgs g, int kind, const CUtensorMap& m, int n, int out_blocks, int chunks) -> cudaError_t {
+            g.meta = a.meta;
+            g.work_act = a.work_act;
+            g.work_chunk = a.work_chunk;
+            const int S = gemm_split((long long)L.A_max * out_blocks, chunks);
+            cudaError_t r = gemm_launch(kind, m, g, n, 1, L.W_max, S, s);
+            if (r != cudaSuccess || L.W4_max == 0) return r;
+            g.meta = a.meta + 1;
+            g.work_act = a.work_act4;
+            g.work_chunk = a.work_chunk4;
+            return gemm_launch(kind, m, g, n, 4, L.W4_max, 1, s);
+        };
         GemmArgs g{};
         g.rows = 0;
-        g.meta = a.meta;
         g.act_expert = a.act_expert;
         g.act_start = a.act_start;
         g.act_count = a.act_count;
-        g.work_act = a.work_act;
-        g.work_chunk = a.work_chunk;
         g.mode = GEMM_OUT_F32;
         g.in = D;
         g.out = I;
         g.dp = a.dp_gu;
         g.scale = a.scale_gu;
-        const int S_gu = gemm_split((long long)L.A_max * (I / 128), D / kGemmKC);
         const struct { const sx_proj* p; float* out; const CUtensorMap* m; } gu[2] = {{&bank->gate, a.gf, &mg},
                                                                                         {&bank->up, a.uf, &mu}};
         for (const auto& q : gu) {
@@ -344,10 +384,10 @@ sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, 
             g.tr_expert = (size_t)(D / 16) * (I / 16) * q.p->n;
             g.svh = q.p->svh;
             g.yf = q.out;
-            if ((e = gemm_launch(kind_gu, *q.m, g, q.p->n, L.W_max, S_gu, s)) != cudaSuccess)
+            if ((e = both(g, kind_gu, *q.m, q.p->n, I / 128, D / kGemmKC)) != cudaSuccess)
                 return cuda_status(e, "moe gate/up gemm launch");
         }
-        moe_mid_kernel<<<dim3(L.W_max, I / 128), 256, 0, s>>>(a);
+        moe_mid_kernel<<<dim3(pos_grid.x, I / 128), 256, 0, s>>>(a);
         if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "moe mid launch");
         g.mode = GEMM_OUT_SLOT;
         g.in = I;
@@ -360,8 +400,7 @@ sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, 
         g.yf = a.yslot;
         g.order = a.order;
         g.scores = a.scores;
-        const int S_d = gemm_split((long long)L.A_max * (D / 128), I / kGemmKC);
-        if ((e = gemm_launch(kind_d, mh, g, bank->down.n, L.W_max, S_d, s)) != cudaSuccess)
+        if ((e = both(g, kind_d, mh, bank->down.n, D / 128, I / kGemmKC)) != cudaSuccess)
             return cuda_status(e, "moe down gemm launch");
         moe_reduce_kernel<<<rows, 256, 0, s>>>(a);
         return cuda_status(cudaGetLastError(), "moe reduce launch");
@@ -382,10 +421,14 @@ sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, 
 
 }  // namespace sx
 
+extern "C" size_t sx_moe_workspace_bytes(const sx_bank* bank, int32_t rows, int32_t topk) {
+    return moe_workspace_bytes(bank, rows, topk, 0);
+}
+
 extern "C" sx_status sx_moe(sx_stream stream, const sx_bank* bank, const sx_decode* dec, const void* x, sx_dtype dtype,
                             int32_t rows, const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
                             const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
                             size_t workspace_bytes) {
     return moe_impl(stream, bank, dec, x, dtype, rows, inds, scores, topk, shared, shared_gate, clamp_limit, y,
-                    workspace, workspace_bytes, nullptr);
+                    workspace, workspace_bytes, nullptr, 0);
 }

@@ -51,6 +51,11 @@ struct MoeArgs {
     void* y;                // [R][D] x dtype
     float* partial;         // [R][D] f32: when set, the k-order sum lands here unrounded (no shared)
     int chunk;              // rows per work item: 8 (decode chain) or kGemmRows (tensor-core path)
+    int big_min;            // experts with this many rows or more go to the second list (INT_MAX: none)
+    int big_chunk;          // rows per work item of the second list (4 row tiles per CTA)
+    int* work_act4;         // second list: [W4_max]
+    int* work_chunk4;
+    int* sorted_e;          // [R*K] the expert of each sorted position
     // tensor-core path (sorted positions p): prepared gate/up inputs, gate/up outputs
     uint16_t* tg;           // [R*K][D] f16
     uint16_t* tu;           // [R*K][D] f16

@@ -50,6 +50,11 @@ def test_gemm_shapes(sx, in_f, out_f, rows):
     _check(sx, in_f, out_f, 32, rows)
 
 
+def test_gemm_four_row_tiles_per_cta(sx):
+    """1024 rows over 74 output blocks: four 128-row accumulators per CTA share each decoded chunk."""
+    _check(sx, 256, 128 * 74, 32, 1024)
+
+
 @pytest.mark.parametrize("n", [16, 24, 32, 40, 48, 64, 96, 128])
 def test_gemm_rates(sx, n):
     _check(sx, 512, 256, n, 40)

@@ -153,3 +153,56 @@ def test_moe_clamped_and_shared(sx):
     with pytest.raises(sx.Exl3Error) as e:
         sx.moe_clamped(xt, b, ii, ww, dec, 129)
     assert e.value.name == "SX_ERR_INVALID_CLAMP"
+
+
+def _zipf_route(seed, T, E, k, s=1.1):
+    """Top-k routes with a Zipf(s) preference over experts, so some experts take several
+    128-row chunks and others none (the prefill config's skew)."""
+    rng = np.random.default_rng(seed)
+    p = 1.0 / np.arange(1, E + 1) ** s
+    p = p[rng.permutation(E)]
+    p /= p.sum()
+    inds = np.stack([rng.choice(E, size=k, replace=False, p=p) for _ in range(T)]).astype(np.int32)
+    wts = (0.05 + rng.random((T, k)) * 0.25).astype(np.float32)
+    return inds, wts
+
+
+@pytest.mark.parametrize("T,E,k,big", [(300, 64, 6, False), (200, 16, 4, False), (700, 16, 4, True)])
+def test_moe_prefill_tensor_core_path(sx, T, E, k, big):
+    """More than 16 rows take the tcgen05 path (prep, gate/up GEMMs, mid, down GEMM, reduce);
+    experts with 384 or more rows take the four-row-tile kernel (`big`)."""
+    D, I = 512, 256
+    bank_np = _bank(T + E, E, D, I, 32, 32)
+    oargs, dec = dec_args(orc.CB_MCG, 16)
+    x = synth.activations(T + 1, T, D)
+    inds, wts = _zipf_route(T, T, E, k)
+    most = np.bincount(inds.ravel(), minlength=E).max()
+    assert most > 128 and (most >= 384) == big  # an expert spans several row tiles
+    xt = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    y = to_f32(sx.moe(xt, _sx_bank(sx, bank_np), torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda(), dec))
+    truth = _truth(bank_np, D, I, 32, 32, oargs, xt.float().cpu().numpy(), inds, wts)
+    assert np.isfinite(y).all()
+    assert max_rel(y, truth) <= MAX_REL_TOL, max_rel(y, truth)
+    assert rel_rms(y, truth) <= REL_RMS_TOL, rel_rms(y, truth)
+    assert sx.device_error() == 0
+
+
+def test_moe_prefill_clamped_gated_shared_and_codebook(sx):
+    E, D, I, k, T = 8, 256, 128, 2, 80
+    bank_np = _bank(15, E, D, I, 24, 40)
+    oargs, dec = dec_args(orc.CB_PAIR1, 16)
+    x = synth.activations(6, T, D) * 4.0
+    inds, wts = _route(16, T, E, k)
+    xt = torch.from_numpy(x).cuda().to(torch.float16)
+    b = _sx_bank(sx, bank_np)
+    ii, ww = torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda()
+    y = to_f32(sx.moe_clamped(xt, b, ii, ww, dec, 2))
+    truth = _truth(bank_np, D, I, 24, 40, oargs, xt.float().cpu().numpy(), inds, wts, limit=2.0)
+    assert max_rel(y, truth) <= MAX_REL_TOL, max_rel(y, truth)
+    shared = torch.randn((T, D), device="cuda").to(torch.float16)
+    gate = torch.randn((T,), device="cuda").to(torch.float16)
+    y2 = to_f32(sx.moe_with_gated_shared(xt, b, ii, ww, dec, shared, gate))
+    base = _truth(bank_np, D, I, 24, 40, oargs, xt.float().cpu().numpy(), inds, wts)
+    sg = 1 / (1 + np.exp(-gate.float().cpu().numpy().astype(np.float64)))
+    want = base + sg[:, None] * shared.float().cpu().numpy()
+    assert max_rel(y2, want) <= MAX_REL_TOL
