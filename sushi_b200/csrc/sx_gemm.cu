@@ -80,15 +80,10 @@ int gemm_split(long long ctas, int chunks) {
 
 bool gemm_rt_rate(int n) { return n == 16 || n == 24 || n == 32 || n == 40 || n == 48 || n == 64; }
 
-// Row tiles per CTA for a dense projection of `rows` rows over `blocks` output blocks: four (each
-// decoded weight chunk feeds four 128-row accumulators) when that still gives every SM a CTA
-// without splitting K and the rate has the kernel, else one.
-int gemm_rt(long long rows, long long units, int blocks, int n) {
-    if (!gemm_rt_rate(n)) return 1;
-    const long long per = 4LL * kGemmRows;
-    if (rows >= per * 3 / 4 && units * ((rows + per - 1) / per) * blocks >= sm_count()) return 4;
-    return 1;
-}
+// Row tiles per CTA for `rows` rows: four (each decoded weight chunk feeds four 128-row
+// accumulators, so the decode work per flop drops fourfold) from 384 rows, for rates that have the
+// kernel; the split over K then fills the SMs.
+int gemm_rt(long long rows, int n) { return gemm_rt_rate(n) && rows >= 3LL * kGemmRows ? 4 : 1; }
 
 }  // namespace sx
 
@@ -135,9 +130,9 @@ extern "C" sx_status sx_linear_gemm(sx_stream stream, const sx_proj* proj, const
     a.mode = GEMM_OUT_ACT;
     a.y = y;
     a.ydt = dtype;
-    const int rt = gemm_rt(rows, 1, out / 128, proj->n);
+    const int rt = gemm_rt(rows, proj->n);
     const int items = (rows + kGemmRows * rt - 1) / (kGemmRows * rt);
-    const int S = rt > 1 ? 1 : gemm_split((long long)items * (out / 128), in / kGemmKC);
+    const int S = gemm_split((long long)items * (out / 128), in / kGemmKC);
     e = gemm_launch(kind, pmap, a, proj->n, rt, items, S, s);
     return cuda_status(e, "gemm launch");
 }

@@ -256,6 +256,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     const uint32_t tmem = tmem_slot;
     const int OT = a.out / 16;
     const uint16_t* tr = a.trellis + (size_t)it.e * a.tr_expert;
+    bool acc_ok = false;  // decoder warps: the accumulator is complete
 
     if (warp == kGemmDecWarps) {
         // ---------------- producer: trellis rows (bulk) and the prepared rows' tile (TMA)
@@ -335,26 +336,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
             if (lane == 0) mbar_arrive(&decoded[st]);
         }
 
-        // ---------------- epilogue: the accumulator of each row tile to shared memory red[t][o]; then
-        // H128, svh, scale and the store, after summing the cluster's partials when split (RT = 1)
-        const bool acc_ok = mbar_wait(acc_full, 0, DEV_TIMEOUT_FULL);
-        tc_fence_after();
-        for (int r = 0; r < rt_live; r++) {
-            if (warp < 4) {
-                const int o = warp * 32 + lane;
+        acc_ok = mbar_wait(acc_full, 0, DEV_TIMEOUT_FULL);
+    }
+
+    // ---------------- epilogue, every thread (the cluster barriers count them all): per row tile,
+    // warps 0..3 move the accumulator to shared memory red[t][o] (tensor-memory lane quadrant =
+    // warp), then rank 0 sums the cluster's partials in rank order (split-K), applies H128, svh and
+    // the scale, and stores; the second barrier keeps every rank's red alive until rank 0 is done.
+    for (int r = 0; r < rt_live; r++) {
+        if (warp < 4) {
+            tc_fence_after();
+            const int o = warp * 32 + lane;
 #pragma unroll 1
-                for (int col = 0; col < NT; col += 32) {
-                    float v[32];
-                    tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(r * NT + col), v);
+            for (int col = 0; col < NT; col += 32) {
+                float v[32];
+                tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(r * NT + col), v);
 #pragma unroll
-                    for (int j = 0; j < 32; j++) red[(col + j) * 128 + o] = acc_ok ? v[j] : 0.0f;
-                }
+                for (int j = 0; j < 32; j++) red[(col + j) * 128 + o] = acc_ok ? v[j] : 0.0f;
             }
-            if (S > 1) break;  // RT == 1: the cluster's sum follows below, with every thread
-            decoders_sync();
-            gemm_store(a, it, red, cluster, 1, ob, r * NT, min(NT, it.rows - r * NT));
-            decoders_sync();
         }
+        if (S > 1) cluster.sync(); else __syncthreads();
+        if (split == 0 && warp < kGemmDecWarps) gemm_store(a, it, red, cluster, S, ob, r * NT, min(NT, it.rows - r * NT));
+        if (S > 1) cluster.sync(); else __syncthreads();
     }
     tc_fence_before();
     __syncthreads();
@@ -362,11 +365,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(Lay::TMEM_COLS)
                      : "memory");
-    }
-    if (S > 1) {
-        cluster.sync();
-        if (split == 0 && warp < kGemmDecWarps) gemm_store(a, it, red, cluster, S, ob, 0, min(NT, it.rows));
-        cluster.sync();
     }
 }
 

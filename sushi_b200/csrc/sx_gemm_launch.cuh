@@ -10,7 +10,6 @@ namespace sx {
 template <int KIND, int N, int RT>
 static cudaError_t launch_gemm_t(const CUtensorMap& pmap, const GemmArgs& a, int items, int S, cudaStream_t stream) {
     constexpr int NT = kGemmRows;
-    if (RT > 1 && S > 1) return cudaErrorInvalidValue;  // split-K launches hold one row tile per CTA
     auto kern = gemm_kernel<KIND, N, NT, RT, false>;
     const int smem = GemmLayout<N, NT, RT>::ALLOC;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

@@ -19,7 +19,7 @@ struct GemmArgs;
 // rows, the split-K choice, and the launch over codebook families and rates.
 cudaError_t prep_map(CUtensorMap* m, const uint16_t* P, int rows, int in);
 int gemm_split(long long ctas, int chunks);
-int gemm_rt(long long rows_per_unit, long long units, int blocks, int n);
+int gemm_rt(long long rows, int n);
 bool gemm_rt_rate(int n);  // rates with four-row-tile tensor-core kernels
 cudaError_t gemm_launch(int kind, const CUtensorMap& pmap, const GemmArgs& a, int n, int rt, int items, int S,
                         cudaStream_t stream);

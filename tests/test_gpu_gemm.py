@@ -50,9 +50,11 @@ def test_gemm_shapes(sx, in_f, out_f, rows):
     _check(sx, in_f, out_f, 32, rows)
 
 
-def test_gemm_four_row_tiles_per_cta(sx):
-    """1024 rows over 74 output blocks: four 128-row accumulators per CTA share each decoded chunk."""
-    _check(sx, 256, 128 * 74, 32, 1024)
+@pytest.mark.parametrize("in_f,out_f,rows", [(256, 128 * 74, 1024), (2048, 256, 400), (4096, 128, 777)])
+def test_gemm_four_row_tiles_per_cta(sx, in_f, out_f, rows):
+    """From 384 rows, four 128-row accumulators per CTA share each decoded chunk; with few output
+    blocks the input range is also split over a cluster (400 rows: the last tile holds 16)."""
+    _check(sx, in_f, out_f, 32, rows)
 
 
 @pytest.mark.parametrize("n", [16, 24, 32, 40, 48, 64, 96, 128])
