@@ -182,6 +182,37 @@ sx_status sx_moe(sx_stream stream, const sx_bank* bank, const sx_decode* dec, co
                  int32_t rows, const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
                  const void* shared_gate, int32_t clamp_limit, void* y, void* workspace, size_t workspace_bytes);
 
+/* ------------------------------------------------------------------ rate-grouped routed experts
+ * A layer whose experts come in rate groups (`.gN` groups, each with its own gate/up/down rates)
+ * held as one ragged bank per projection: rate_groups.Ragged (src/exl3/rate_groups.zig:23-130).
+ * trellis[p] is projection p's flat U16 storage (gate, up, down), groups back to back and each
+ * expert's tiles contiguous; suh[p] / svh[p] hold one F16 row per expert over all groups; meta is
+ * the reference's table of 8 u32 words per expert (rate_groups.zig:23-25): gate n, up n, down n,
+ * group, the gate/up/down offsets of the expert's tiles in trellis[p] counted in u32 words, and the
+ * expert's index in its group.  meta is HOST memory (the library reads the groups from it at each
+ * call); every other pointer is device memory.  Each group must be a run of consecutive expert ids
+ * with one rate per projection and tiles at a fixed stride (else SX_ERR_GROUP_GEOMETRY); groups
+ * whose gate and up rates differ are refused with SX_ERR_TRELLIS_GEOMETRY. */
+typedef struct sx_ragged {
+    const uint16_t* trellis[3];
+    const uint16_t* suh[3];
+    const uint16_t* svh[3];
+    const uint32_t* meta;     /* host [experts][8] */
+    int32_t experts;
+    int32_t hidden;           /* the gate/up input and down output width, multiple of 128 */
+    int32_t inter;            /* the gate/up output and down input width, multiple of 128 */
+} sx_ragged;
+
+/* The workspace sx_moe_ragged needs (bytes); 0 for a malformed meta table. */
+size_t sx_moe_ragged_workspace_bytes(const sx_ragged* bank, int32_t rows, int32_t topk);
+
+/* root.moeRagged (src/exl3/root.zig:582; rate_groups.moeDecode :1659 / moePrefill :2042): sx_moe
+ * over a rate-grouped layer.  inds are the layer's expert ids; every slot decodes at its expert's
+ * group rates; y as sx_moe (k-order sum, rounding, optional shared / gated shared, clamp). */
+sx_status sx_moe_ragged(sx_stream stream, const sx_ragged* bank, const sx_decode* dec, const void* x, sx_dtype dtype,
+                        int32_t rows, const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
+                        const void* shared_gate, int32_t clamp_limit, void* y, void* workspace, size_t workspace_bytes);
+
 /* ------------------------------------------------------------------ routed experts, no allocation
  * sx_moe for callers that cannot allocate device memory at all.  Some hosts never call cudaMalloc
  * on the path that runs the layer: a caller recording the layer into a CUDA graph (an allocation

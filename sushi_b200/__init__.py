@@ -17,6 +17,7 @@ from .exl3 import (  # noqa: E402
     ExpertParallel,
     LINEAR_WEIGHTS_STATIC,
     Proj,
+    Ragged,
     RouterMode,
     TileOrder,
     decode_codewords,
@@ -27,6 +28,7 @@ from .exl3 import (  # noqa: E402
     linear_grouped,
     moe,
     moe_clamped,
+    moe_ragged,
     moe_with_gated_shared,
     moe_with_shared,
     router_topk,
@@ -36,7 +38,7 @@ from .exl3 import (  # noqa: E402
 )
 
 __all__ = [
-    "Bank", "Codebook", "Decode", "Exl3Error", "ExpertParallel", "LINEAR_WEIGHTS_STATIC", "Proj", "RouterMode", "TileOrder", "decode_codewords",
-    "dequant_inner", "device_error", "linear", "linear_gemm", "linear_grouped", "moe", "moe_clamped", "moe_with_gated_shared",
+    "Bank", "Codebook", "Decode", "Exl3Error", "ExpertParallel", "LINEAR_WEIGHTS_STATIC", "Proj", "Ragged", "RouterMode", "TileOrder", "decode_codewords",
+    "dequant_inner", "device_error", "linear", "linear_gemm", "linear_grouped", "moe", "moe_clamped", "moe_ragged", "moe_with_gated_shared",
     "moe_with_shared", "router_topk", "share_unique_id", "table_info", "table_row",
 ]

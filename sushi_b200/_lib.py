@@ -33,6 +33,18 @@ class SxBank(ctypes.Structure):
     _fields_ = [("gate", SxProj), ("up", SxProj), ("down", SxProj)]
 
 
+class SxRagged(ctypes.Structure):
+    _fields_ = [
+        ("trellis", ctypes.c_void_p * 3),
+        ("suh", ctypes.c_void_p * 3),
+        ("svh", ctypes.c_void_p * 3),
+        ("meta", ctypes.c_void_p),
+        ("experts", ctypes.c_int32),
+        ("hidden", ctypes.c_int32),
+        ("inter", ctypes.c_int32),
+    ]
+
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int32
 _SZ = ctypes.c_size_t
@@ -51,6 +63,9 @@ SIGNATURES = {
     "sx_router_topk": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, ctypes.c_float, _I, _I, _P, _P]),
     "sx_moe_workspace_bytes": (_SZ, [ctypes.POINTER(SxBank), _I, _I]),
     "sx_moe": (_I, [_P, ctypes.POINTER(SxBank), ctypes.POINTER(SxDecode), _P, _I, _I, _P, _P, _I, _P, _P, _I, _P, _P, _SZ]),
+    "sx_moe_ragged_workspace_bytes": (_SZ, [ctypes.POINTER(SxRagged), _I, _I]),
+    "sx_moe_ragged": (_I, [_P, ctypes.POINTER(SxRagged), ctypes.POINTER(SxDecode), _P, _I, _I, _P, _P, _I, _P, _P, _I, _P,
+                           _P, _SZ]),
     "sx_moe_static_scratch": (_I, [_P, ctypes.POINTER(SxBank), ctypes.POINTER(SxDecode), _P, _I, _I, _P, _P, _I, _P, _P, _I, _P]),
     "sx_moe_static_scratch_bytes": (_SZ, []),
     "sx_ep_unique_id": (_I, [_P]),

@@ -27,7 +27,7 @@ __global__ void __launch_bounds__(1024) route_prep_kernel(MoeArgs a) {
     for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
     for (int s = tid; s < RK; s += blockDim.x) {
-        const uint32_t e = a.inds[s];
+        const uint32_t e = a.inds[s] - (uint32_t)a.e_lo;  // ids below the group wrap past E
         if (e < (uint32_t)a.E) atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(1024) route_prep_kernel(MoeArgs a) {
     for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;  // reused as cursors
     __syncthreads();
     for (int s = tid; s < RK; s += blockDim.x) {
-        const uint32_t e = a.inds[s];
+        const uint32_t e = a.inds[s] - (uint32_t)a.e_lo;
         if (e < (uint32_t)a.E) {
             const int pos = atomicAdd(&cnt[e], 1);
             a.order[off[e] + pos] = s;
@@ -128,7 +128,7 @@ bool use_gemm(int E, int R, int K, long long slots) {
     return slots >= 16LL * std::min<long long>(E, slots);
 }
 
-MoeWs moe_ws_layout(int E, int R, int K, int D, int I, int n_gu, int n_d, long long slots = 0) {
+MoeWs moe_ws_layout(int E, int R, int K, int D, int I, int n_gu, int n_d, long long slots = 0, bool with_yslot = true) {
     MoeWs w;
     const int RK = R * K;
     w.gemm = use_gemm(E, R, K, slots);
@@ -151,7 +151,8 @@ MoeWs moe_ws_layout(int E, int R, int K, int D, int I, int n_gu, int n_d, long l
     w.order = off; off = align_up(off + (size_t)RK * sizeof(int));
     w.sorted_e = off; off = align_up(off + (size_t)RK * sizeof(int));
     w.hprep = off; off = align_up(off + (size_t)RK * I * sizeof(uint16_t));
-    w.yslot = off; off = align_up(off + (size_t)RK * D * sizeof(float));
+    w.yslot = off;
+    if (with_yslot) off = align_up(off + (size_t)RK * D * sizeof(float));
     w.tg = w.tu = w.gf = w.uf = 0;
     if (w.gemm) {
         w.tg = off; off = align_up(off + (size_t)RK * D * sizeof(uint16_t));
@@ -258,40 +259,48 @@ using namespace sx;
 
 namespace sx {
 
-size_t moe_workspace_bytes(const sx_bank* bank, int32_t rows, int32_t topk, long long slots) {
-    if (!bank || rows < 1 || topk < 1) return 0;
-    return moe_ws_layout(bank->gate.experts, rows, topk, bank->gate.in_features, bank->gate.out_features, bank->gate.n,
-                         bank->down.n, slots)
-        .total;
+// One rate group of a routed layer: its experts are ids [e_lo, e_lo + bank.experts) of the layer.
+struct MoeGroup {
+    sx_bank bank;
+    int e_lo;
+};
+
+// The valid slots a group can expect: its share of the layer's experts.
+long long group_slots(long long slots, int rows, int topk, int Eg, int Etot) {
+    const long long base = slots > 0 ? slots : (long long)rows * topk;
+    return std::max(1LL, base * Eg / std::max(1, Etot));
 }
 
-sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, const void* x, sx_dtype dtype,
-                   int32_t rows, const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
-                   const void* shared_gate, int32_t clamp_limit, void* y, void* workspace, size_t workspace_bytes,
-                   float* partial, long long slots) {
-    if (!bank || !x || !inds || !scores || (!y && !partial)) return SX_ERR_NULL_POINTER;
-    if (clamp_limit < 0 || clamp_limit > 128) return SX_ERR_INVALID_CLAMP;
-    if (rows < 1 || topk < 1) return SX_ERR_BAD_SHAPE;
-    if (topk > 32) return SX_ERR_TOPK_EXCEEDS_REDUCE_BANK;
-    if (!dtype_ok(dtype)) return SX_ERR_BAD_DTYPE;
-    if (shared_gate && !shared) return SX_ERR_NULL_POINTER;
+size_t yslot_bytes(int rows, int topk, int D) { return align_up((size_t)rows * topk * D * sizeof(float)); }
+
+// Workspace of a layer of groups: the per-slot planes first (every group writes its slots'), then
+// the largest group's own scratch (the groups run one after another on the stream).
+size_t moe_groups_ws(const MoeGroup* g, int ng, int Etot, int rows, int topk, long long slots) {
+    const int D = g[0].bank.gate.in_features, I = g[0].bank.gate.out_features;
+    size_t most = 0;
+    for (int i = 0; i < ng; i++) {
+        const sx_bank& b = g[i].bank;
+        const MoeWs L = moe_ws_layout(b.gate.experts, rows, topk, D, I, b.gate.n, b.down.n,
+                                      group_slots(slots, rows, topk, b.gate.experts, Etot), false);
+        most = std::max(most, L.total);
+    }
+    return yslot_bytes(rows, topk, D) + most;
+}
+
+size_t moe_workspace_bytes(const sx_bank* bank, int32_t rows, int32_t topk, long long slots) {
+    if (!bank || rows < 1 || topk < 1) return 0;
+    const MoeGroup g{*bank, 0};
+    return moe_groups_ws(&g, 1, bank->gate.experts, rows, topk, slots);
+}
+
+// Route metadata and the decode chain or the tensor-core path for one group's slots, into yslot.
+sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_decode* dec, const void* x,
+                    sx_dtype dtype, int32_t rows, const uint32_t* inds, const float* scores, int32_t topk,
+                    int32_t clamp_limit, float* yslot, uint8_t* ws, long long slots) {
     const int E = bank->gate.experts;
     const int D = bank->gate.in_features, I = bank->gate.out_features;
-    // validateClampedProjection for gate, up and down (src/exl3/root.zig:117-135).
     sx_status st;
-    if ((st = check_proj(&bank->gate, E)) || (st = check_proj(&bank->up, E)) || (st = check_proj(&bank->down, E))) return st;
-    if (bank->up.in_features != D || bank->up.out_features != I || bank->down.in_features != I ||
-        bank->down.out_features != D)
-        return SX_ERR_BAD_SHAPE;
-    if (bank->gate.tile_order != SX_TILE_PACK || bank->up.tile_order != SX_TILE_PACK || bank->down.tile_order != SX_TILE_PACK)
-        return SX_ERR_TILE_ORDER_UNSUPPORTED;
-    // (an expert-parallel rank's rows carry every slot, most of them other ranks' sentinels)
-    if (topk > E && !partial) return SX_ERR_TOPK_EXCEEDS_EXPERTS;
-    if (bank->gate.n != bank->up.n) return SX_ERR_TRELLIS_GEOMETRY;  // mixed gate/up rates: not served yet
-    const MoeWs L = moe_ws_layout(E, rows, topk, D, I, bank->gate.n, bank->down.n, slots);
-    if (!workspace || workspace_bytes < L.total) return SX_ERR_WORKSPACE_TOO_SMALL;
-    if (E > 8192) return SX_ERR_BAD_SHAPE;
-
+    const MoeWs L = moe_ws_layout(E, rows, topk, D, I, bank->gate.n, bank->down.n, slots, false);
     MoeArgs a{};
     int kind_gu, kind_d;
     if ((st = resolve_decode(dec, bank->gate.n, &kind_gu, &a.dp_gu))) return st;
@@ -311,7 +320,6 @@ sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, 
     a.scale_gu = kind_scale(kind_gu);
     a.scale_down = kind_scale(kind_d);
     a.clamp = (float)clamp_limit;
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
     a.meta = reinterpret_cast<int*>(ws + L.meta);
     a.act_expert = reinterpret_cast<int*>(ws + L.act_expert);
     a.act_start = reinterpret_cast<int*>(ws + L.act_start);
@@ -320,11 +328,8 @@ sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, 
     a.work_chunk = reinterpret_cast<int*>(ws + L.work_chunk);
     a.order = reinterpret_cast<int*>(ws + L.order);
     a.hprep = reinterpret_cast<uint16_t*>(ws + L.hprep);
-    a.yslot = reinterpret_cast<float*>(ws + L.yslot);
-    a.shared = shared;
-    a.shared_gate = shared_gate;
-    a.y = y;
-    a.partial = partial;
+    a.yslot = yslot;
+    a.e_lo = e_lo;
     a.chunk = L.chunk;
     a.big_min = L.big_min;
     a.big_chunk = L.big_chunk;
@@ -402,8 +407,7 @@ sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, 
         g.scores = a.scores;
         if ((e = both(g, kind_d, mh, bank->down.n, D / 128, I / kGemmKC)) != cudaSuccess)
             return cuda_status(e, "moe down gemm launch");
-        moe_reduce_kernel<<<rows, 256, 0, s>>>(a);
-        return cuda_status(cudaGetLastError(), "moe reduce launch");
+        return SX_OK;
     }
     const int S_gu = pick_split(L.A_max * (I / 128), D / 128);
     const int S_d = pick_split(L.A_max * (D / 128), I / 128);
@@ -415,8 +419,78 @@ sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, 
         default: return SX_ERR_CODEBOOK_UNSUPPORTED;
     }
     if (e != cudaSuccess) return cuda_status(e, "moe pair/down launch");
-    moe_reduce_kernel<<<rows, 256, 0, s>>>(a);
+    return SX_OK;
+}
+
+// A routed layer of groups: every group's chain into the per-slot planes, then the k-order reduce
+// over all slots (rounding, shared expert; or an expert-parallel rank's f32 partial).
+sx_status moe_run(sx_stream stream, const MoeGroup* groups, int ng, int Etot, const sx_decode* dec, const void* x,
+                  sx_dtype dtype, int32_t rows, const uint32_t* inds, const float* scores, int32_t topk,
+                  const void* shared, const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
+                  size_t workspace_bytes, float* partial, long long slots) {
+    if (!x || !inds || !scores || (!y && !partial)) return SX_ERR_NULL_POINTER;
+    if (clamp_limit < 0 || clamp_limit > 128) return SX_ERR_INVALID_CLAMP;
+    if (rows < 1 || topk < 1) return SX_ERR_BAD_SHAPE;
+    if (topk > 32) return SX_ERR_TOPK_EXCEEDS_REDUCE_BANK;
+    if (!dtype_ok(dtype)) return SX_ERR_BAD_DTYPE;
+    if (shared_gate && !shared) return SX_ERR_NULL_POINTER;
+    // (an expert-parallel rank's rows carry every slot, most of them other ranks' sentinels)
+    if (topk > Etot && !partial) return SX_ERR_TOPK_EXCEEDS_EXPERTS;
+    if (Etot > 8192) return SX_ERR_BAD_SHAPE;
+    const int D = groups[0].bank.gate.in_features, I = groups[0].bank.gate.out_features;
+    for (int i = 0; i < ng; i++) {
+        // validateClampedProjection for gate, up and down (src/exl3/root.zig:117-135).
+        const sx_bank* bank = &groups[i].bank;
+        const int E = bank->gate.experts;
+        sx_status st;
+        if ((st = check_proj(&bank->gate, E)) || (st = check_proj(&bank->up, E)) || (st = check_proj(&bank->down, E)))
+            return st;
+        if (bank->gate.in_features != D || bank->gate.out_features != I || bank->up.in_features != D ||
+            bank->up.out_features != I || bank->down.in_features != I || bank->down.out_features != D)
+            return SX_ERR_BAD_SHAPE;
+        if (bank->gate.tile_order != SX_TILE_PACK || bank->up.tile_order != SX_TILE_PACK ||
+            bank->down.tile_order != SX_TILE_PACK)
+            return SX_ERR_TILE_ORDER_UNSUPPORTED;
+        if (bank->gate.n != bank->up.n) return SX_ERR_TRELLIS_GEOMETRY;  // mixed gate/up rates: not served yet
+        int kind;
+        DecParams dp;
+        if ((st = resolve_decode(dec, bank->gate.n, &kind, &dp)) || (st = resolve_decode(dec, bank->down.n, &kind, &dp)))
+            return st;
+    }
+    if (!workspace || workspace_bytes < moe_groups_ws(groups, ng, Etot, rows, topk, slots))
+        return SX_ERR_WORKSPACE_TOO_SMALL;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    float* yslot = reinterpret_cast<float*>(ws);
+    uint8_t* scratch = ws + yslot_bytes(rows, topk, D);
+    for (int i = 0; i < ng; i++) {
+        const sx_status st = moe_group(stream, &groups[i].bank, groups[i].e_lo, dec, x, dtype, rows, inds, scores, topk,
+                                       clamp_limit, yslot, scratch,
+                                       group_slots(slots, rows, topk, groups[i].bank.gate.experts, Etot));
+        if (st) return st;
+    }
+    MoeArgs r{};
+    r.inds = inds;
+    r.K = topk;
+    r.D = D;
+    r.E = Etot;
+    r.xdt = dtype;
+    r.yslot = yslot;
+    r.shared = shared;
+    r.shared_gate = shared_gate;
+    r.y = y;
+    r.partial = partial;
+    moe_reduce_kernel<<<rows, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(r);
     return cuda_status(cudaGetLastError(), "moe reduce launch");
+}
+
+sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, const void* x, sx_dtype dtype,
+                   int32_t rows, const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
+                   const void* shared_gate, int32_t clamp_limit, void* y, void* workspace, size_t workspace_bytes,
+                   float* partial, long long slots) {
+    if (!bank) return SX_ERR_NULL_POINTER;
+    const MoeGroup g{*bank, 0};
+    return moe_run(stream, &g, 1, bank->gate.experts, dec, x, dtype, rows, inds, scores, topk, shared, shared_gate,
+                   clamp_limit, y, workspace, workspace_bytes, partial, slots);
 }
 
 }  // namespace sx
@@ -431,4 +505,72 @@ extern "C" sx_status sx_moe(sx_stream stream, const sx_bank* bank, const sx_deco
                             size_t workspace_bytes) {
     return moe_impl(stream, bank, dec, x, dtype, rows, inds, scores, topk, shared, shared_gate, clamp_limit, y,
                     workspace, workspace_bytes, nullptr, 0);
+}
+
+namespace sx {
+namespace {
+
+constexpr int kMetaWords = 8;  // rate_groups.META_WORDS (src/exl3/rate_groups.zig:25)
+constexpr int kMaxGroups = 32;  // layout.max_groups (src/exl3/layout.zig:4)
+
+// The groups of a ragged layer from its host meta table: runs of consecutive experts with one group
+// id, one rate per projection, and tiles at the stride of that rate.
+sx_status ragged_groups(const sx_ragged* rb, MoeGroup* out, int* ng) {
+    if (!rb || !rb->meta) return SX_ERR_NULL_POINTER;
+    if (rb->experts < 1 || rb->hidden <= 0 || rb->inter <= 0 || rb->hidden % 128 || rb->inter % 128)
+        return SX_ERR_BAD_SHAPE;
+    for (int p = 0; p < 3; p++)
+        if (!rb->trellis[p] || !rb->suh[p] || !rb->svh[p]) return SX_ERR_NULL_POINTER;
+    const uint64_t tiles = (uint64_t)(rb->hidden / 16) * (rb->inter / 16);
+    int n = 0;
+    for (int e = 0; e < rb->experts;) {
+        const uint32_t* m = rb->meta + (size_t)e * kMetaWords;
+        if (n == kMaxGroups || m[7] != 0) return SX_ERR_GROUP_GEOMETRY;
+        int len = 1;
+        for (; e + len < rb->experts; len++) {
+            const uint32_t* q = rb->meta + (size_t)(e + len) * kMetaWords;
+            if (q[3] != m[3]) break;
+            if (q[0] != m[0] || q[1] != m[1] || q[2] != m[2] || q[7] != (uint32_t)len) return SX_ERR_GROUP_GEOMETRY;
+            for (int p = 0; p < 3; p++)
+                if ((uint64_t)q[4 + p] != (uint64_t)m[4 + p] + (uint64_t)len * tiles * m[p] / 2) return SX_ERR_GROUP_GEOMETRY;
+        }
+        MoeGroup& g = out[n++];
+        g.e_lo = e;
+        sx_proj* pr[3] = {&g.bank.gate, &g.bank.up, &g.bank.down};
+        for (int p = 0; p < 3; p++) {
+            pr[p]->trellis = rb->trellis[p] + (size_t)m[4 + p] * 2;
+            pr[p]->suh = rb->suh[p] + (size_t)e * (p == 2 ? rb->inter : rb->hidden);
+            pr[p]->svh = rb->svh[p] + (size_t)e * (p == 2 ? rb->hidden : rb->inter);
+            pr[p]->experts = len;
+            pr[p]->in_features = p == 2 ? rb->inter : rb->hidden;
+            pr[p]->out_features = p == 2 ? rb->hidden : rb->inter;
+            pr[p]->n = (int32_t)m[p];
+            pr[p]->tile_order = SX_TILE_PACK;
+        }
+        e += len;
+    }
+    *ng = n;
+    return SX_OK;
+}
+
+}  // namespace
+}  // namespace sx
+
+extern "C" size_t sx_moe_ragged_workspace_bytes(const sx_ragged* bank, int32_t rows, int32_t topk) {
+    MoeGroup g[kMaxGroups];
+    int ng = 0;
+    if (rows < 1 || topk < 1 || ragged_groups(bank, g, &ng) != SX_OK) return 0;
+    return moe_groups_ws(g, ng, bank->experts, rows, topk, 0);
+}
+
+extern "C" sx_status sx_moe_ragged(sx_stream stream, const sx_ragged* bank, const sx_decode* dec, const void* x,
+                                   sx_dtype dtype, int32_t rows, const uint32_t* inds, const float* scores, int32_t topk,
+                                   const void* shared, const void* shared_gate, int32_t clamp_limit, void* y,
+                                   void* workspace, size_t workspace_bytes) {
+    MoeGroup g[kMaxGroups];
+    int ng = 0;
+    const sx_status st = ragged_groups(bank, g, &ng);
+    if (st) return st;
+    return moe_run(stream, g, ng, bank->experts, dec, x, dtype, rows, inds, scores, topk, shared, shared_gate,
+                   clamp_limit, y, workspace, workspace_bytes, nullptr, 0);
 }

@@ -27,6 +27,7 @@ struct MoeArgs {
     const void* x;          // [R][D]
     int xdt;
     int R, K, D, I, E;
+    int e_lo;               // the group's first expert id: slot ids in [e_lo, e_lo + E) are this launch's
     const uint32_t* inds;   // [R*K]
     const float* scores;    // [R*K]
     const uint16_t* gate_tr; const uint16_t* gate_suh; const uint16_t* gate_svh;

@@ -18,6 +18,8 @@ import enum
 from dataclasses import dataclass
 from typing import Optional
 
+import numpy as np
+
 import torch
 
 from . import _lib
@@ -292,6 +294,77 @@ def moe(x, bank: Bank, inds, scores, dec: Decode, shared=None, shared_gate=None,
                         sc.data_ptr(), topk, None if sh is None else sh.data_ptr(),
                         None if sg is None else sg.data_ptr(), int(clamp_limit), y.data_ptr(), ws.data_ptr(),
                         ws.numel()))
+    return y.reshape(shape)
+
+
+class Ragged:
+    """rate_groups.Ragged (src/exl3/rate_groups.zig:23-130): a layer of rate groups held as one flat
+    trellis per projection, scales concatenated over all experts, and the 8-word per-expert meta
+    table (gate/up/down n, group, tile offsets in u32 words, index in group).  `from_banks` builds it
+    from the groups' Banks in order, as Ragged.init does; expert ids run over the groups in order."""
+
+    def __init__(self, trellis, suh, svh, meta, hidden, inter):
+        self.trellis, self.suh, self.svh = list(trellis), list(suh), list(svh)
+        self.meta = meta.astype(np.uint32).reshape(-1, 8)  # host table
+        self.hidden, self.inter = int(hidden), int(inter)
+        self.experts = self.meta.shape[0]
+
+    @classmethod
+    def from_banks(cls, banks):
+        hidden = banks[0].gate.trellis.shape[1] * 16
+        inter = banks[0].gate.trellis.shape[2] * 16
+        tiles = (hidden // 16) * (inter // 16)
+        meta, words = [], [0, 0, 0]
+        for g, b in enumerate(banks):
+            projs = (b.gate, b.up, b.down)
+            rates = [int(p.trellis.shape[3]) for p in projs]
+            E = int(b.gate.trellis.shape[0])
+            for local in range(E):
+                meta.append(rates + [g] + [words[p] + local * tiles * rates[p] // 2 for p in range(3)] + [local])
+            for p in range(3):
+                words[p] += E * tiles * rates[p] // 2
+        flat = [torch.cat([(b.gate, b.up, b.down)[p].trellis.reshape(-1) for b in banks]) for p in range(3)]
+        suh = [torch.cat([(b.gate, b.up, b.down)[p].suh.reshape(-1) for b in banks]) for p in range(3)]
+        svh = [torch.cat([(b.gate, b.up, b.down)[p].svh.reshape(-1) for b in banks]) for p in range(3)]
+        return cls(flat, suh, svh, np.array(meta, np.uint32), hidden, inter)
+
+    def c(self):
+        r = _lib.SxRagged()
+        for p in range(3):
+            r.trellis[p] = self.trellis[p].data_ptr()
+            r.suh[p] = self.suh[p].data_ptr()
+            r.svh[p] = self.svh[p].data_ptr()
+        r.meta = self.meta.ctypes.data
+        r.experts, r.hidden, r.inter = self.experts, self.hidden, self.inter
+        return r
+
+
+def moe_ragged(x, ragged: Ragged, inds, scores, dec: Decode, shared=None, shared_gate=None, clamp_limit=0,
+               workspace=None):
+    """root.moeRagged: routed SwiGLU experts over a rate-grouped layer; returns x's shape and dtype."""
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1]).contiguous()
+    rows = x2.shape[0]
+    ix = inds.reshape(rows, -1).to(torch.int32).contiguous()
+    sc = scores.reshape(rows, -1).float().contiguous()
+    topk = ix.shape[1]
+    if sc.shape != ix.shape:
+        raise Exl3Error(1)
+    if x2.dtype not in _DT:
+        raise Exl3Error(2)
+    r = ragged.c()
+    need = lib().sx_moe_ragged_workspace_bytes(ctypes.byref(r), rows, topk)
+    if need == 0:
+        raise Exl3Error(19)
+    ws = workspace if workspace is not None else _workspace(need, x.device)
+    y = torch.empty_like(x2)
+    d = dec.c()
+    sh = None if shared is None else shared.reshape(rows, -1).to(x2.dtype).contiguous()
+    sg = None if shared_gate is None else shared_gate.reshape(rows).to(x2.dtype).contiguous()
+    _check(lib().sx_moe_ragged(_stream(), ctypes.byref(r), ctypes.byref(d), x2.data_ptr(), _DT[x2.dtype], rows,
+                               ix.data_ptr(), sc.data_ptr(), topk, None if sh is None else sh.data_ptr(),
+                               None if sg is None else sg.data_ptr(), int(clamp_limit), y.data_ptr(), ws.data_ptr(),
+                               ws.numel()))
     return y.reshape(shape)
 
 

@@ -131,3 +131,56 @@ def test_router_declines_before_launch(L):
     assert L.sx_status_name(st).decode() == "SX_ERR_ROUTER_DECLINED"
     st = L.sx_router_topk(None, FAKE, FAKE, 1, 64, 8, 2, 1, 1.0, 3, 1, FAKE, FAKE)  # 64 % 3 != 0
     assert L.sx_status_name(st).decode() == "SX_ERR_ROUTER_DECLINED"
+
+
+class SxRaggedMeta:
+    """A host meta table for sx_ragged (8 u32 words per expert)."""
+
+    def __init__(self, rows):
+        import numpy as np
+
+        self.arr = np.ascontiguousarray(np.array(rows, np.uint32))
+
+
+def _ragged(meta_rows, experts=None, hidden=256, inter=128):
+    m = SxRaggedMeta(meta_rows)
+    r = _lib.SxRagged()
+    for p in range(3):
+        r.trellis[p] = FAKE
+        r.suh[p] = FAKE
+        r.svh[p] = FAKE
+    r.meta = m.arr.ctypes.data
+    r.experts = len(meta_rows) if experts is None else experts
+    r.hidden, r.inter = hidden, inter
+    return r, m
+
+
+def test_ragged_meta_admission(L):
+    """sx_moe_ragged reads the groups from the host meta table before any device work: groups must
+    be runs of experts with one rate per projection and tiles at the rate's stride."""
+    tiles = (256 // 16) * (128 // 16)
+    good = [[16, 16, 32, 0, e * tiles * 16 // 2, e * tiles * 16 // 2, e * tiles * 32 // 2, e] for e in range(2)]
+    good += [[32, 32, 32, 1, 2 * tiles * 8 + e * tiles * 16, 2 * tiles * 8 + e * tiles * 16,
+              2 * tiles * 16 + e * tiles * 16, e] for e in range(3)]
+    r, keep = _ragged(good)
+    assert L.sx_moe_ragged_workspace_bytes(ctypes.byref(r), 4, 2) > 0
+    bad_stride = [row[:] for row in good]
+    bad_stride[1][4] += 2
+    bad_rate = [row[:] for row in good]
+    bad_rate[3][2] = 48
+    bad_local = [row[:] for row in good]
+    bad_local[2][7] = 1
+    for rows in (bad_stride, bad_rate, bad_local):
+        r, keep = _ragged(rows)
+        assert L.sx_moe_ragged_workspace_bytes(ctypes.byref(r), 4, 2) == 0
+        st = L.sx_moe_ragged(None, ctypes.byref(r), ctypes.byref(_dec()), FAKE, 2, 4, FAKE, FAKE, 2, None, None, 0,
+                             FAKE, FAKE, 1 << 30)
+        assert L.sx_status_name(st).decode() == "SX_ERR_GROUP_GEOMETRY"
+    mixed = [row[:] for row in good]
+    for row in mixed[:2]:
+        row[1] = 24  # up rate differs from gate within the group
+        row[5] = row[7] * tiles * 24 // 2
+    r, keep = _ragged(mixed)
+    st = L.sx_moe_ragged(None, ctypes.byref(r), ctypes.byref(_dec()), FAKE, 2, 4, FAKE, FAKE, 2, None, None, 0, FAKE,
+                         FAKE, 1 << 30)
+    assert L.sx_status_name(st).decode() == "SX_ERR_TRELLIS_GEOMETRY"

@@ -206,3 +206,36 @@ def test_moe_prefill_clamped_gated_shared_and_codebook(sx):
     sg = 1 / (1 + np.exp(-gate.float().cpu().numpy().astype(np.float64)))
     want = base + sg[:, None] * shared.float().cpu().numpy()
     assert max_rel(y2, want) <= MAX_REL_TOL
+
+
+@pytest.mark.parametrize("T,cb,w", [(5, orc.CB_MCG, 16), (200, orc.CB_MCG, 16), (7, orc.CB_SPEC1, 15)])
+def test_moe_ragged_rate_groups(sx, T, cb, w):
+    """rate_groups.Ragged: two rate groups (K1 n=16 and K2 n=32, as the DeepSeek config's routed
+    experts) in one layer; every slot decodes at its expert's group rate.  T=5/7: decode chain per
+    group; T=200: the tensor-core path per group."""
+    D, I, k = 256, 128, 4
+    E0, E1 = 6, 10
+    g0 = _bank(400 + T, E0, D, I, 16, 16)
+    g1 = _bank(500 + T, E1, D, I, 32, 32)
+    oargs, dec = dec_args(cb, w)
+    rb = sx.Ragged.from_banks([_sx_bank(sx, g0), _sx_bank(sx, g1)])
+    x = synth.activations(T + 9, T, D)
+    inds, wts = _route(T + 3, T, E0 + E1, k)
+    xt = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    y = to_f32(sx.moe_ragged(xt, rb, torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda(), dec))
+    torch.cuda.synchronize()
+    assert sx.device_error() == 0
+    xf = xt.float().cpu().numpy()
+    truth = np.zeros((T, D))
+    dense = {}
+    for r in range(T):
+        for j in range(k):
+            e = int(inds[r, j])
+            bank_np, loc, n = (g0, e, 16) if e < E0 else (g1, e - E0, 32)
+            if e not in dense:
+                dense[e] = tuple(orc.decode_dense(p[0][loc], p[1][loc], p[2][loc], a, b, n, *oargs)
+                                 for p, a, b in zip(bank_np, (D, D, I), (I, I, D)))
+            truth[r] += wts[r, j] * orc.expert_truth(dense[e], xf[r])
+    assert np.isfinite(y).all()
+    assert max_rel(y, truth) <= MAX_REL_TOL, max_rel(y, truth)
+    assert rel_rms(y, truth) <= REL_RMS_TOL, rel_rms(y, truth)
