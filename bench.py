@@ -334,6 +334,7 @@ def main():
         out["moe"] = moe_bench(sx, _lib, torch, args, stream, sptr)
         if world == 1:
             out["moe_prefill"] = prefill_bench(sx, torch, args, stream, tf_peak)
+            out["ffn_stack_deepseek"] = deepseek_bench(sx, torch, args, stream, tf_peak)
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline()
@@ -468,6 +469,91 @@ def prefill_bench(sx, torch, args, stream, tf_peak):
     return {"tokens": T, "tokens_per_s": round(T / (ms * 1e-3), 1), "ms_per_layer": round(ms, 3),
             "tflops": round(flops / (ms * 1e-3) / 1e12, 1), "tensor_frac_of_measured": round(flops / (ms * 1e-3) / 1e12 / tf_peak, 4),
             "max_rows_per_expert": int(counts.max()), "active_experts": int((counts > 0).sum())}
+
+
+def deepseek_bench(sx, torch, args, stream, tf_peak):
+    """BASELINE configs[4] on one GPU: a DeepSeek-style FFN stack of 16 layers, hidden 7168, 256
+    routed experts of 2048 + one shared expert of 2048, top-8 sigmoid routing with a bias
+    (renormalised, x2.5).  Routed experts are STQ SPEC1 (window 15) in two rate groups, K1 (n16,
+    64 experts) and K2 (n32, 192 experts): 1.75 bits per weight on average; the group an expert
+    falls in is fixed by its id range, which is how a rate-grouped pack orders experts.  The shared
+    expert is K4 (n64), run as a one-expert layer through sx_moe.  Each layer: router, shared expert,
+    rate-grouped routed layer (sx_moe_ragged) with the shared output added, residual add.  Decode
+    batches T = 1, 8, 64 (CUDA graph of the 16 layers) and prefill T = 4096.  Random trellis words,
+    sign-only scales (the decode cost does not depend on the values); 39 GB of routed weights."""
+    H, I, E, k, L = 7168, 2048, 256, 8, 16
+    groups = ((64, 16), (192, 32))
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(4242)
+
+    def proj(experts, i_f, o_f, n):
+        tr = torch.randint(-32768, 32768, (experts, i_f // 16, o_f // 16, n), dtype=torch.int16, device="cuda",
+                           generator=gen)
+        su = (torch.randint(0, 2, (experts, i_f), device="cuda", generator=gen).half() * 2 - 1) * 0.02
+        sv = torch.randint(0, 2, (experts, o_f), device="cuda", generator=gen).half() * 2 - 1
+        return sx.Proj(tr, su, sv)
+
+    layers = []
+    for _ in range(L):
+        banks = [sx.Bank(proj(e, H, I, n), proj(e, H, I, n), proj(e, I, H, n)) for e, n in groups]
+        shared = sx.Bank(proj(1, H, I, 64), proj(1, H, I, 64), proj(1, I, H, 64))
+        wr = (torch.randn((H, E), device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+        bias = torch.randn((E,), device="cuda", generator=gen) * 0.1
+        rb = sx.Ragged.from_banks(banks)
+        del banks
+        layers.append((rb, shared, wr, bias))
+    dec = sx.Decode(sx.Codebook.SPEC1, 15, 1)  # spec1-w15: the table with rows at n = 16..128
+    res = {"layers": L, "routed_bits_per_weight": 1.75, "routed_gb": round(sum(
+        sum(t.numel() * 2 for t in rb.trellis) for rb, _, _, _ in layers) / 1e9, 2)}
+    one = torch.zeros((1, 1), dtype=torch.int32, device="cuda")
+    for T in (1, 8, 64, 4096):
+        x0 = torch.randn((T, H), device="cuda", generator=gen).to(torch.bfloat16)
+        ws = torch.empty(max(sx._lib.load().sx_moe_ragged_workspace_bytes(ctypes.byref(layers[0][0].c()), T, k),
+                             sx._lib.load().sx_moe_workspace_bytes(ctypes.byref(layers[0][1].c()), T, 1)),
+                         dtype=torch.uint8, device="cuda")
+        ones_i, ones_s = one.expand(T, 1).contiguous(), torch.ones((T, 1), device="cuda")
+
+        def stack():
+            x = x0
+            for rb, shared, wr, bias in layers:
+                inds, scores = sx.router_topk((x @ wr).float(), k, sx.RouterMode.SIGMOID_BIAS, bias, route_norm=True,
+                                              route_scale=2.5)
+                sh = sx.moe(x, shared, ones_i, ones_s, dec, workspace=ws)
+                x = x + sx.moe_ragged(x, rb, inds, scores, dec, shared=sh, workspace=ws)
+            return x
+
+        for _ in range(2):
+            stack()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        rounds = max(2, args.steps)
+        if T <= 64:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                stack()
+            g.replay()
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(rounds):
+                g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            del g
+        else:
+            e0.record(stream)
+            for _ in range(rounds):
+                stack()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / rounds
+        flops = 2.0 * T * L * (k + 1) * 3 * H * I
+        res[f"T{T}"] = {"tokens_per_s": round(T / (ms * 1e-3), 1), "ms_per_stack": round(ms, 3),
+                        "tflops": round(flops / (ms * 1e-3) / 1e12, 1)}
+        del ws
+    assert sx.device_error() == 0
+    del layers
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_profile(args):

@@ -177,7 +177,9 @@ size_t sx_moe_workspace_bytes(const sx_bank* bank, int32_t rows, int32_t topk);
  * clamped SwiGLU, src/exl3/root.zig:96-125; 1..128, else SX_ERR_INVALID_CLAMP).  When `shared`
  * ([rows, hidden], x's dtype) is given it is added to every row; with `shared_gate` ([rows] x's
  * dtype logits) it is added as sigmoid(gate) * shared (moeWithGatedShared).  topk <= 32.
- * `workspace` holds at least sx_moe_workspace_bytes(bank, rows, topk). */
+ * `workspace` holds at least sx_moe_workspace_bytes(bank, rows, topk).  Layers the tensor-core path
+ * serves (more than 16 rows averaging 16 or more per routed expert) need x and the workspace
+ * 16-byte aligned and the gate/up suh 8-byte aligned (else SX_ERR_BAD_SHAPE). */
 sx_status sx_moe(sx_stream stream, const sx_bank* bank, const sx_decode* dec, const void* x, sx_dtype dtype,
                  int32_t rows, const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
                  const void* shared_gate, int32_t clamp_limit, void* y, void* workspace, size_t workspace_bytes);

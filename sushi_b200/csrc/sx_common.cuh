@@ -108,6 +108,21 @@ __device__ __forceinline__ float load_act(const void* p, size_t i, int dt) {
     return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
 }
 
+// Four consecutive elements from element i (a multiple of 4) of an activation row whose rows start
+// 16-byte aligned: one 8- or 16-byte load.
+__device__ __forceinline__ void load_act4(const void* p, size_t i, int dt, float (&v)[4]) {
+    if (dt == 0) {
+        const float4 t = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+        v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
+        return;
+    }
+    const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p) + i);
+    const uint16_t h[4] = {(uint16_t)u.x, (uint16_t)(u.x >> 16), (uint16_t)u.y, (uint16_t)(u.y >> 16)};
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+        v[k] = dt == 1 ? __half2float(__ushort_as_half(h[k])) : __bfloat162float(__ushort_as_bfloat16(h[k]));
+}
+
 __device__ __forceinline__ void store_act(void* p, size_t i, int dt, float v) {
     if (dt == 0) static_cast<float*>(p)[i] = v;
     else if (dt == 1) static_cast<__half*>(p)[i] = __float2half_rn(v);

@@ -220,9 +220,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     cg::cluster_group cluster = cg::this_cluster();
     GemmItem it;
-    if (!gemm_item(a, blockIdx.x, NT * RT, it)) return;  // every CTA of a cluster shares blockIdx.x
+    // Grid x = output block, y = row item: the output blocks of one row item launch together, so
+    // their shared prepared-row tiles come from HBM once and from L2 after.
+    if (!gemm_item(a, blockIdx.y, NT * RT, it)) return;  // every CTA of a cluster shares blockIdx.y
     const int rt_live = (it.rows + NT - 1) / NT;          // row tiles with rows in them
-    const int ob = blockIdx.y;
+    const int ob = blockIdx.x;
     const int S = gridDim.z;
     const int split = blockIdx.z;
     const int KC = a.in / kGemmKC;  // chunks of 64 inputs

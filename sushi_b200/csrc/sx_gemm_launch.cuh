@@ -19,7 +19,7 @@ static cudaError_t launch_gemm_t(const CUtensorMap& pmap, const GemmArgs& a, int
         if (e != cudaSuccess) return e;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(items, a.out / 128, S);
+    cfg.gridDim = dim3(a.out / 128, items, S);
     cfg.blockDim = dim3(kGemmThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;

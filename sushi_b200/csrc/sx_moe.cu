@@ -26,9 +26,14 @@ __global__ void __launch_bounds__(1024) route_prep_kernel(MoeArgs a) {
     const int RK = a.R * a.K;
     for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
-    for (int s = tid; s < RK; s += blockDim.x) {
-        const uint32_t e = a.inds[s] - (uint32_t)a.e_lo;  // ids below the group wrap past E
-        if (e < (uint32_t)a.E) atomicAdd(&cnt[e], 1);
+    // Warp-aggregated counting: lanes holding the same expert add once (a hot expert would
+    // otherwise serialise thousands of atomics on one shared-memory word).
+    for (int s0 = tid - (tid & 31); s0 < RK; s0 += blockDim.x) {
+        const int s = s0 + (tid & 31);
+        const uint32_t e = s < RK ? a.inds[s] - (uint32_t)a.e_lo : 0xFFFFFFFFu;  // ids below the group wrap past E
+        const bool valid = e < (uint32_t)a.E;
+        const unsigned peers = __match_any_sync(0xffffffffu, valid ? e : 0xFFFFFFFFu);
+        if (valid && (tid & 31) == __ffs(peers) - 1) atomicAdd(&cnt[e], __popc(peers));
     }
     __syncthreads();
     if (tid < 32) {
@@ -92,10 +97,18 @@ __global__ void __launch_bounds__(1024) route_prep_kernel(MoeArgs a) {
     __syncthreads();
     for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;  // reused as cursors
     __syncthreads();
-    for (int s = tid; s < RK; s += blockDim.x) {
-        const uint32_t e = a.inds[s] - (uint32_t)a.e_lo;
-        if (e < (uint32_t)a.E) {
-            const int pos = atomicAdd(&cnt[e], 1);
+    for (int s0 = tid - (tid & 31); s0 < RK; s0 += blockDim.x) {
+        const int lane = tid & 31;
+        const int s = s0 + lane;
+        const uint32_t e = s < RK ? a.inds[s] - (uint32_t)a.e_lo : 0xFFFFFFFFu;
+        const bool valid = e < (uint32_t)a.E;
+        const unsigned peers = __match_any_sync(0xffffffffu, valid ? e : 0xFFFFFFFFu);
+        const int leader = __ffs(peers) - 1;
+        int base = 0;
+        if (valid && lane == leader) base = atomicAdd(&cnt[e], __popc(peers));
+        base = __shfl_sync(0xffffffffu, base, leader);
+        if (valid) {
+            const int pos = base + __popc(peers & ((1u << lane) - 1u));
             a.order[off[e] + pos] = s;
             a.sorted_e[off[e] + pos] = (int)e;
         }
@@ -166,20 +179,36 @@ MoeWs moe_ws_layout(int E, int R, int K, int D, int I, int n_gu, int n_d, long l
 
 __global__ void __launch_bounds__(256) moe_reduce_kernel(MoeArgs a) {
     const int r = blockIdx.x;
-    for (int d = threadIdx.x; d < a.D; d += blockDim.x) {
-        float acc = 0.0f;
-        for (int k = 0; k < a.K; k++) {
-            const int slot = r * a.K + k;
-            if (a.inds[slot] < (uint32_t)a.E) acc += a.yslot[(size_t)slot * a.D + d];
+    __shared__ int live[32];  // the row's slots with an expert of the layer, in k order
+    __shared__ int nlive;
+    if (threadIdx.x == 0) {
+        int c = 0;
+        for (int k = 0; k < a.K; k++)
+            if (a.inds[r * a.K + k] < (uint32_t)a.E) live[c++] = r * a.K + k;
+        nlive = c;
+    }
+    __syncthreads();
+    const int nl = nlive;
+    for (int d = threadIdx.x * 4; d < a.D; d += blockDim.x * 4) {
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int j = 0; j < nl; j++) {
+            const float4 v = *reinterpret_cast<const float4*>(a.yslot + (size_t)live[j] * a.D + d);
+            acc[0] += v.x;
+            acc[1] += v.y;
+            acc[2] += v.z;
+            acc[3] += v.w;
         }
         if (a.partial) {  // an expert-parallel rank's share: combined and rounded by the token's owner
-            a.partial[(size_t)r * a.D + d] = acc;
+            *reinterpret_cast<float4*>(a.partial + (size_t)r * a.D + d) = make_float4(acc[0], acc[1], acc[2], acc[3]);
             continue;
         }
         // The routed sum is rounded to the output dtype before a shared expert is added
         // (docs/engine-exl3-experts.md "Streamed serial decode"; src/exl3/root.zig:56-92).
-        const float y = routed_finish(acc, a.xdt, a.shared, a.shared_gate, (size_t)r * a.D + d, r);
-        store_act(a.y, (size_t)r * a.D + d, a.xdt, y);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float y = routed_finish(acc[i], a.xdt, a.shared, a.shared_gate, (size_t)r * a.D + d + i, r);
+            store_act(a.y, (size_t)r * a.D + d + i, a.xdt, y);
+        }
     }
 }
 
@@ -197,12 +226,18 @@ __global__ void __launch_bounds__(256) moe_prep_kernel(MoeArgs a) {
     const uint16_t* sg = a.gate_suh + (size_t)e * a.D;
     const uint16_t* su = a.up_suh + (size_t)e * a.D;
     const int tok = a.order[p] / a.K;
+    float xv[4];
+    load_act4(a.x, (size_t)tok * a.D + base, a.xdt, xv);
+    const uint2 sgv = *reinterpret_cast<const uint2*>(sg + base);
+    const uint2 suv = *reinterpret_cast<const uint2*>(su + base);
+    const uint16_t sgh[4] = {(uint16_t)sgv.x, (uint16_t)(sgv.x >> 16), (uint16_t)sgv.y, (uint16_t)(sgv.y >> 16)};
+    const uint16_t suh4[4] = {(uint16_t)suv.x, (uint16_t)(suv.x >> 16), (uint16_t)suv.y, (uint16_t)(suv.y >> 16)};
     float g[4], u[4];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        const float v = round_f16(load_act(a.x, (size_t)tok * a.D + base + i, a.xdt));
-        g[i] = v * h2f(sg[base + i]);
-        u[i] = v * h2f(su[base + i]);
+        const float v = round_f16(xv[i]);
+        g[i] = v * h2f(sgh[i]);
+        u[i] = v * h2f(suh4[i]);
     }
     warp_hadamard128(g);
     warp_hadamard128(u);
@@ -345,7 +380,10 @@ sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_de
         // Tensor-core path (kernels.moePrefill, src/exl3/expert_exl3_kernels.zig:2861): prepared
         // gate/up inputs per sorted position, the gate and up GEMMs, the mid, the down GEMM into the
         // per-slot planes; the same k-order reduce as the decode chain.
-        if (reinterpret_cast<uintptr_t>(ws) % 16) return SX_ERR_BAD_SHAPE;
+        // the prep kernel reads x rows and the suh rows as vectors; TMA reads the workspace
+        if (reinterpret_cast<uintptr_t>(ws) % 16 || reinterpret_cast<uintptr_t>(x) % 16 ||
+            reinterpret_cast<uintptr_t>(bank->gate.suh) % 8 || reinterpret_cast<uintptr_t>(bank->up.suh) % 8)
+            return SX_ERR_BAD_SHAPE;
         a.tg = reinterpret_cast<uint16_t*>(ws + L.tg);
         a.tu = reinterpret_cast<uint16_t*>(ws + L.tu);
         a.gf = reinterpret_cast<float*>(ws + L.gf);

@@ -10,6 +10,10 @@ template <typename Kern>
 static cudaError_t launch_clustered(Kern kern, dim3 grid, int S, size_t smem, cudaStream_t stream, const MoeArgs& a) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
+    if (S > 8) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kThreads, 1, 1);
@@ -25,9 +29,18 @@ static cudaError_t launch_clustered(Kern kern, dim3 grid, int S, size_t smem, cu
     return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
+// The split grows until a CTA's input slice fits in shared memory (wide hidden sizes: 7168).
+template <int N, int NP>
+static int fit_split(int S, int KB) {
+    S = S < KB ? S : KB;
+    while (S < 16 && S < KB && core_layout<N, NP, 1>((KB + S - 1) / S).total > 200 * 1024) S++;
+    return S;
+}
+
 template <int KIND, int N>
 static cudaError_t launch_pair_t(const MoeArgs& a, int S, int W_max, cudaStream_t stream) {
     const int KB = a.D / 128;
+    S = fit_split<N, 2>(S, KB);
     const CoreLayout L = core_layout<N, 2, 1>((KB + S - 1) / S);
     return launch_clustered(moe_pair_kernel<KIND, N>, dim3(W_max, a.I / 128, S), S, L.total, stream, a);
 }
@@ -35,6 +48,7 @@ static cudaError_t launch_pair_t(const MoeArgs& a, int S, int W_max, cudaStream_
 template <int KIND, int N>
 static cudaError_t launch_down_t(const MoeArgs& a, int S, int W_max, cudaStream_t stream) {
     const int KB = a.I / 128;
+    S = fit_split<N, 1>(S, KB);
     const CoreLayout L = core_layout<N, 1, 1>((KB + S - 1) / S);
     return launch_clustered(moe_down_kernel<KIND, N>, dim3(W_max, a.D / 128, S), S, L.total, stream, a);
 }

@@ -239,3 +239,18 @@ def test_moe_ragged_rate_groups(sx, T, cb, w):
     assert np.isfinite(y).all()
     assert max_rel(y, truth) <= MAX_REL_TOL, max_rel(y, truth)
     assert rel_rms(y, truth) <= REL_RMS_TOL, rel_rms(y, truth)
+
+
+def test_moe_wide_hidden_decode_chain(sx):
+    """A wide hidden size (7168, the DeepSeek config's) with few active experts: the decode chain's
+    k split grows until each CTA's prepared input slice fits in shared memory."""
+    E, D, I, k, T = 4, 7168, 256, 2, 1
+    bank_np = _bank(71, E, D, I, 32, 32)
+    oargs, dec = dec_args(orc.CB_MCG, 16)
+    x = synth.activations(72, T, D)
+    inds, wts = _route(73, T, E, k)
+    xt = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    y = to_f32(sx.moe(xt, _sx_bank(sx, bank_np), torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda(), dec))
+    truth = _truth(bank_np, D, I, 32, 32, oargs, xt.float().cpu().numpy(), inds, wts)
+    assert max_rel(y, truth) <= MAX_REL_TOL, max_rel(y, truth)
+    assert sx.device_error() == 0
