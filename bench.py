@@ -13,8 +13,15 @@ metric: compressed-HBM GB/s of the GEMVs (algorithmic bytes: trellis + suh + svh
 launch) over the device time of the step, graph-replayed with inputs resident in HBM.  e2e: the
 same bytes over the time of the same projections called one by one through the C ABI with the
 activations copied from pinned host memory and the outputs copied back, inside the timed region.
-At N > 1 every rank runs its own sweep (the GEMV does not shard: replicas), value sums the ranks'
-bytes over the slowest rank's time.  The MoE decode layer rides along as "moe".
+Rows from 16 go through the tensor-core projection (sx_linear_gemm); fewer through the decode
+GEMV (sx_linear_ex with static weights).  At N > 1 every rank runs its own sweep (the projections
+do not shard: replicas), value sums the ranks' bytes over the slowest rank's time.  roofline: the
+headline launch (4096x14336 K2 M=1 gemv_kernel) against the measured HBM copy bandwidth.
+
+Riding along: "moe" (configs[2]: the 512-expert decode layer, T = 1/8/64 tokens per rank; expert
+parallel over the ranks at N > 1), and at N = 1 "moe_prefill" (configs[3]: 8192 tokens, Zipf
+routing, tensor-core path) and "ffn_stack_deepseek" (configs[4]: 16 layers, rate-grouped K1/K2
+routed experts, T = 1/8/64/4096).
 
 --impl reference times the reference's CPU decode + matmul (`format.project`,
 src/exl3/expert_exl3.zig:546; Zig is not installed, so its C++ restatement in oracle/) on the
@@ -40,12 +47,20 @@ RATES = [32, 48, 64]
 ROWS = [1, 2, 4, 8, 16, 64]
 L2_BYTES = 126 * 1024 * 1024
 GEMM_ROWS = 16  # sweep rows at or above this go through the tensor-core projection
+GEMV_HEADLINE_TRAFFIC = 14_783_232  # DRAM bytes per headline GEMV launch, ncu (profiles/gemv_kernel_4096x14336_k2_m1.md)
 METRIC = "EXL3 GEMV compressed-HBM GB/s (% peak); MoE layer tokens/s at 1/2/4/8 B200"
 UNIT = "GB/s"
 
 
 def alg_bytes(in_f, out_f, n, m):
     return in_f * out_f * n // 128 + 2 * (in_f + out_f) + 2 * m * in_f + 2 * m * out_f
+
+
+def sweep_config(world):
+    """The workload both arms report on (the reference arm times a bounded sample of it)."""
+    return {"workload": "gemv_sweep (BASELINE configs[1])", "shapes_out_x_in": ["2048x7168", "7168x2048", "4096x14336"],
+            "n": RATES, "rows": ROWS, "codebook": "mcg", "window": 16,
+            "l2": "ring of distinct weight copies > 2x L2 per (shape, rate)", "parallelism": f"replicas x{world}"}
 
 
 def measured_peaks():
@@ -144,10 +159,10 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "u16 trellis -> f32 accumulate", "data": "synthetic (seeded random trellis words)",
-        "config": {"workload": "gemv_sweep_m1_sample", "shapes_out_x_in": ["2048x7168", "7168x2048", "4096x14336"],
-                   "n": RATES, "rows": 1},
+        "config": sweep_config(world),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": "9 projections per step: every sweep shape at n=32/48/64, M=1 (format.project restated in C++, OpenMP)"},
+                         "sample": "each step: the sweep's 9 (shape, rate) projections at M = 1 (rows cost the CPU "
+                                   "path proportionally; format.project restated in C++, OpenMP over output tiles)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -316,12 +331,16 @@ def main():
         "warmup": args.warmup, "ms_per_step": round(kernel_ms, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "u16 trellis (K=2/3/4) decoded to f16, bf16 activations, f32 accumulate",
         "data": "synthetic (seeded random trellis words, sign-only scales; bf16 N(0,1) activations)",
-        "config": {"workload": "gemv_sweep (BASELINE configs[1])", "shapes_out_x_in": ["2048x7168", "7168x2048", "4096x14336"],
-                   "n": RATES, "rows": ROWS, "codebook": "mcg", "window": 16,
-                   "l2": "ring of distinct weight copies > 2x L2 per (shape, rate)", "parallelism": f"replicas x{world}"},
-        "roofline": {"bound": "hbm", "achieved": round(bytes_per_step / (kernel_ms * 1e-3) / 1e9, 2), "peak": hbm_peak,
-                     "unit": "GB/s", "frac": round(bytes_per_step / (kernel_ms * 1e-3) / 1e9 / hbm_peak, 4),
-                     "traffic": None, "peak_kind": peak_kind, "kernel": "sx::gemv_kernel (per-GPU)"},
+        "config": sweep_config(world),
+        # The dominant kernel at the metric's headline config: gemv_kernel on 4096x14336 K2 M=1;
+        # achieved = its algorithmic bytes per launch over its average launch time in this run's
+        # timed graphs; traffic = DRAM bytes read + written per launch from one ncu capture of the
+        # same launch (profiles/gemv_kernel_4096x14336_k2_m1.md).
+        "roofline": {"bound": "hbm", "achieved": headline, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(headline / hbm_peak, 4) if headline else None, "traffic": GEMV_HEADLINE_TRAFFIC,
+                     "algorithmic_bytes_per_launch": alg_bytes(14336, 4096, 32, 1), "peak_kind": peak_kind,
+                     "kernel": "sx::gemv_kernel<MCG,32,1,W16> 4096x14336 M=1"},
+        "sweep_gbs": round(bytes_per_step / (kernel_ms * 1e-3) / 1e9, 2),
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),

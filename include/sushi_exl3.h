@@ -111,6 +111,16 @@ sx_status sx_dequant_inner(sx_stream stream, const sx_proj* proj, int32_t expert
  * (src/exl3/expert_exl3.zig:361-369). */
 sx_status sx_decode_codewords(sx_stream stream, int32_t n, const sx_decode* dec, uint32_t* out32);
 
+/* Converts trellis tiles between the pack order [E, IT, OT, n] and the pair-major order
+ * [E, OT/2, IT, 2, n] (layout.tileMajor / tileMajorInverse, src/exl3/layout.zig:141-160;
+ * `trellis_pm` tensors, docs/pack-format.md "tile order").  The projection kernels read the pack
+ * order; a host that loads pair-major packs converts each routed trellis once after loading.
+ * src and dst are device buffers of experts*in/16*out/16*n halfwords that must not overlap
+ * (SX_ERR_BAD_SHAPE) unless the orders are equal. */
+sx_status sx_tile_order_convert(sx_stream stream, const uint16_t* src, uint16_t* dst, int32_t experts,
+                                int32_t in_features, int32_t out_features, int32_t n, int32_t from_order,
+                                int32_t to_order);
+
 /* ------------------------------------------------------------------ dense linears
  * y = x . W for `rows` rows through the one-bank projection `proj` (experts == 1):
  * linear.linear (src/exl3/linear.zig:27-35), trunk.matmul (src/exl3/trunk.zig:53).

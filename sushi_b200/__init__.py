@@ -35,10 +35,11 @@ from .exl3 import (  # noqa: E402
     share_unique_id,
     table_info,
     table_row,
+    tile_order_convert,
 )
 
 __all__ = [
     "Bank", "Codebook", "Decode", "Exl3Error", "ExpertParallel", "LINEAR_WEIGHTS_STATIC", "Proj", "Ragged", "RouterMode", "TileOrder", "decode_codewords",
     "dequant_inner", "device_error", "linear", "linear_gemm", "linear_grouped", "moe", "moe_clamped", "moe_ragged", "moe_with_gated_shared",
-    "moe_with_shared", "router_topk", "share_unique_id", "table_info", "table_row",
+    "moe_with_shared", "router_topk", "share_unique_id", "table_info", "table_row", "tile_order_convert",
 ]

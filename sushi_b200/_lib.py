@@ -55,6 +55,7 @@ SIGNATURES = {
     "sx_version": (ctypes.c_char_p, []),
     "sx_dequant_inner": (_I, [_P, ctypes.POINTER(SxProj), _I, ctypes.POINTER(SxDecode), _P]),
     "sx_decode_codewords": (_I, [_P, _I, ctypes.POINTER(SxDecode), _P]),
+    "sx_tile_order_convert": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I]),
     "sx_linear": (_I, [_P, ctypes.POINTER(SxProj), ctypes.POINTER(SxDecode), _P, _I, _I, _P]),
     "sx_linear_ex": (_I, [_P, ctypes.POINTER(SxProj), ctypes.POINTER(SxDecode), _P, _I, _I, _P, ctypes.c_uint32]),
     "sx_linear_gemm_workspace_bytes": (_SZ, [ctypes.POINTER(SxProj), _I]),

@@ -6,8 +6,8 @@
 //   2. ep_gather (one CTA per (list place, d)): copies the listed row of x into the send block of
 //      d, with its slots as d-local expert ids (other ranks' slots and unused places carry the
 //      sentinel id 0xFFFFFFFF, which the expert chain skips) and scores.
-//   3. dispatch: all-to-all of the fixed-size blocks (rows_cap rows per peer) as grouped
-//      ncclSend/ncclRecv; this rank's own block is a device-to-device copy.
+//   3. dispatch: all-to-alls of the fixed-size blocks (rows_cap rows per peer; rows, slot ids and
+//      scores) as one group of ncclSend/ncclRecv; this rank's own blocks are device copies.
 //   4. the local expert chain (moe_impl) over the world*rows_cap received rows, writing each row's
 //      k-order f32 sum over its slots here (the partial) instead of a rounded output.
 //   5. combine: all-to-all of the partials back to the rows' owners.
@@ -226,22 +226,36 @@ EpWs ep_ws_layout(const sx_bank* bank, int world, int cap, int K, int esz) {
 
 size_t dtype_size(int dt) { return dt == SX_DT_F32 ? 4 : 2; }
 
-// One all-to-all of `bytes` per peer: block p of `send` goes to rank p, block p of `recv` comes
-// from rank p; the own block is a device copy.
-sx_status all_to_all(const sx_ep* ep, const void* send, void* recv, size_t bytes, cudaStream_t s) {
+// All-to-alls of several buffers in one NCCL group: for each (send, recv, bytes), block p of send
+// goes to rank p and block p of recv comes from rank p; the own blocks are device copies.
+struct A2A {
+    const void* send;
+    void* recv;
+    size_t bytes;
+};
+
+sx_status all_to_all(const sx_ep* ep, const A2A* bufs, int nb, cudaStream_t s) {
     const NcclApi& n = nccl();
-    const uint8_t* sb = static_cast<const uint8_t*>(send);
-    uint8_t* rb = static_cast<uint8_t*>(recv);
-    cudaError_t ce = cudaMemcpyAsync(rb + (size_t)ep->rank * bytes, sb + (size_t)ep->rank * bytes, bytes,
-                                     cudaMemcpyDeviceToDevice, s);
-    if (ce != cudaSuccess) return cuda_status(ce, "ep own block copy");
+    for (int b = 0; b < nb; b++) {
+        const uint8_t* sb = static_cast<const uint8_t*>(bufs[b].send);
+        uint8_t* rb = static_cast<uint8_t*>(bufs[b].recv);
+        const size_t bytes = bufs[b].bytes;
+        const cudaError_t ce = cudaMemcpyAsync(rb + (size_t)ep->rank * bytes, sb + (size_t)ep->rank * bytes, bytes,
+                                               cudaMemcpyDeviceToDevice, s);
+        if (ce != cudaSuccess) return cuda_status(ce, "ep own block copy");
+    }
     if (ep->world == 1) return SX_OK;
     sx_status st = nccl_status(n.group_start(), "ncclGroupStart");
     if (st) return st;
-    for (int p = 0; p < ep->world && !st; p++) {
-        if (p == ep->rank) continue;
-        st = nccl_status(n.send(sb + (size_t)p * bytes, bytes, ncclUint8, p, ep->comm, s), "ncclSend");
-        if (!st) st = nccl_status(n.recv(rb + (size_t)p * bytes, bytes, ncclUint8, p, ep->comm, s), "ncclRecv");
+    for (int b = 0; b < nb && !st; b++) {
+        const uint8_t* sb = static_cast<const uint8_t*>(bufs[b].send);
+        uint8_t* rb = static_cast<uint8_t*>(bufs[b].recv);
+        const size_t bytes = bufs[b].bytes;
+        for (int p = 0; p < ep->world && !st; p++) {
+            if (p == ep->rank) continue;
+            st = nccl_status(n.send(sb + (size_t)p * bytes, bytes, ncclUint8, p, ep->comm, s), "ncclSend");
+            if (!st) st = nccl_status(n.recv(rb + (size_t)p * bytes, bytes, ncclUint8, p, ep->comm, s), "ncclRecv");
+        }
     }
     const sx_status end = nccl_status(n.group_end(), "ncclGroupEnd");
     return st ? st : end;
@@ -367,11 +381,12 @@ sx_status sx_ep_moe(sx_ep* ep, sx_stream stream, const sx_bank* local_bank, int3
     ep_gather_kernel<<<dim3(C, G), 128, 0, s>>>(a);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "ep gather launch");
 
-    // 3. dispatch
+    // 3. dispatch: rows, slot ids and scores in one NCCL group
     sx_status st;
-    if ((st = all_to_all(ep, ws + L.send_x, ws + L.recv_x, (size_t)C * D * esz, s))) return st;
-    if ((st = all_to_all(ep, ws + L.send_inds, ws + L.recv_inds, (size_t)C * topk * 4, s))) return st;
-    if ((st = all_to_all(ep, ws + L.send_scores, ws + L.recv_scores, (size_t)C * topk * 4, s))) return st;
+    const A2A dispatch[3] = {{ws + L.send_x, ws + L.recv_x, (size_t)C * D * esz},
+                             {ws + L.send_inds, ws + L.recv_inds, (size_t)C * topk * 4},
+                             {ws + L.send_scores, ws + L.recv_scores, (size_t)C * topk * 4}};
+    if ((st = all_to_all(ep, dispatch, 3, s))) return st;
 
     // 4. the local experts over every received row, partials in f32
     float* part_send = reinterpret_cast<float*>(ws + L.part_send);
@@ -381,7 +396,8 @@ sx_status sx_ep_moe(sx_ep* ep, sx_stream stream, const sx_bank* local_bank, int3
     if (st) return st;
 
     // 5. combine: partials back to the rows' owners
-    if ((st = all_to_all(ep, part_send, ws + L.part_recv, (size_t)C * D * sizeof(float), s))) return st;
+    const A2A combine[1] = {{part_send, ws + L.part_recv, (size_t)C * D * sizeof(float)}};
+    if ((st = all_to_all(ep, combine, 1, s))) return st;
 
     // 6. rank-order sum, rounding, shared expert
     if (rows == 0) return SX_OK;

@@ -284,6 +284,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         // ---------------- MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f16_m128(NT);
+            constexpr uint32_t idesc2 = idesc_f16_m128(2 * NT);  // N = 256
             bool ok = true;
             for (int i = 0; i < ncs; i++) {
                 const int st = i % NST;
@@ -292,11 +293,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                 if (ok) {
                     const uint32_t a0 = smem_u32(smem + Lay::A_OFF + st * Lay::A_BYTES);
                     const uint32_t b0 = smem_u32(smem + Lay::B_OFF + st * Lay::B_BYTES);
-                    for (int r = 0; r < rt_live; r++)
+                    // Row tiles go two at a time as one N = 256 MMA where both are live (their
+                    // prepared-row tiles and accumulators sit back to back): half the A reads
+                    // from shared memory per flop of N = 128 MMAs.
+                    for (int r = 0; r < rt_live; r += 2) {
+                        const bool pair = r + 1 < rt_live;
+                        const uint32_t id = pair ? idesc2 : idesc;
 #pragma unroll
                         for (int kk = 0; kk < kGemmKC / 16; kk++)
                             tc_mma_f16(tmem + (uint32_t)(r * NT), smem_desc_sw128(a0 + kk * 32),
-                                       smem_desc_sw128(b0 + r * Lay::B_TILE + kk * 32), idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                                       smem_desc_sw128(b0 + r * Lay::B_TILE + kk * 32), id, (i > 0 || kk > 0) ? 1u : 0u);
+                    }
                 }
                 tc_commit(&empty[st]);  // frees the stage once these MMAs have read it
             }

@@ -223,6 +223,25 @@ def dequant_inner(proj: Proj, expert: int, dec: Decode):
     return out
 
 
+def tile_order_convert(trellis, to_order: "TileOrder", from_order: "TileOrder" = None):
+    """layout.tileMajor / tileMajorInverse on the device: a [E, IT, OT, n] pack-order trellis to the
+    pair-major order (stored as [E, OT/2, IT, 2, n]) or back; returns a new tensor."""
+    from_order = TileOrder.PACK if from_order is None else TileOrder(from_order)
+    t = trellis.contiguous()
+    if t.dim() == 4:
+        E, IT, OT, n = t.shape
+    elif t.dim() == 5:
+        E, P, IT, two, n = t.shape
+        OT = 2 * P
+    else:
+        raise Exl3Error(1)
+    out_shape = (E, OT // 2, IT, 2, n) if TileOrder(to_order) == TileOrder.PAIR_MAJOR else (E, IT, OT, n)
+    dst = torch.empty(out_shape, dtype=t.dtype, device=t.device)
+    _check(lib().sx_tile_order_convert(_stream(), t.data_ptr(), dst.data_ptr(), E, IT * 16, OT * 16, n, int(from_order),
+                                       int(to_order)))
+    return dst
+
+
 def decode_codewords(n: int, dec: Decode, device="cuda"):
     """Every codeword's decode at rate n (int32: weight bits low, PAIR1's partner high)."""
     out = torch.empty(65536, dtype=torch.int32, device=device)

@@ -112,3 +112,24 @@ def test_refusals_are_named(sx):
         sx.dequant_inner(p16, 0, sx.Decode(sx.Codebook.PAIR1, 16, None))
     assert e.value.name == "SX_ERR_CODEBOOK_TABLE_RATE_MISSING"
     assert sx.device_error() == 0
+
+
+@pytest.mark.parametrize("n,E,in_f,out_f", [(32, 2, 256, 384), (18, 1, 128, 256), (64, 3, 384, 128)])
+def test_tile_order_round_trip(n, E, in_f, out_f):
+    """sx_tile_order_convert: pack order -> pair-major is layout.tileMajor (src/exl3/layout.zig:141),
+    restated here in numpy, and pair-major -> pack undoes it bit for bit."""
+    import sushi_b200 as sx
+
+    rng = np.random.default_rng(n + E)
+    src = rng.integers(0, 1 << 16, size=(E, in_f // 16, out_f // 16, n), dtype=np.uint16)
+    IT, OT = in_f // 16, out_f // 16
+    want = np.empty((E, OT // 2, IT, 2, n), np.uint16)
+    for pair in range(OT // 2):
+        for tk in range(IT):
+            for o in range(2):
+                want[:, pair, tk, o] = src[:, tk, pair * 2 + o]
+    t = torch.from_numpy(src.view(np.int16)).cuda()
+    pm = sx.tile_order_convert(t, sx.TileOrder.PAIR_MAJOR)
+    np.testing.assert_array_equal(pm.cpu().numpy().view(np.uint16), want)
+    back = sx.tile_order_convert(pm, sx.TileOrder.PACK, sx.TileOrder.PAIR_MAJOR)
+    np.testing.assert_array_equal(back.cpu().numpy().view(np.uint16), src)
