@@ -75,7 +75,7 @@ struct GemmLayout {
     static constexpr int B_OFF = A_OFF + NST * A_BYTES;
     static constexpr int T_OFF = B_OFF + NST * B_BYTES;
     static constexpr int BAR_OFF = (T_OFF + NST * T_BYTES + 15) / 16 * 16;
-    static constexpr int TOTAL = BAR_OFF + (3 * NST + 1) * 8 + 16;
+    static constexpr int TOTAL = BAR_OFF + (4 * NST + 1) * 8 + 16;
     static constexpr int RED_BYTES = NT * 128 * 4;      // one row tile's accumulator in f32, reusing A and B
     static_assert(RED_BYTES <= T_OFF, "accumulator staging fits in the A/B ring");
     static_assert(TMEM_COLS <= 512, "tensor memory holds 512 columns");
@@ -231,15 +231,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     const int c0 = (int)(((long long)split * KC) / S);
     const int ncs = (int)(((long long)(split + 1) * KC) / S) - c0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lay::BAR_OFF);
-    uint64_t* decoded = full + NST;
+    // tfull: a stage's trellis rows landed (the decoders start); bfull: its prepared-row tiles
+    // landed (the MMA needs them); separate so the decode overlaps the larger row-tile copies.
+    uint64_t* tfull = reinterpret_cast<uint64_t*>(smem + Lay::BAR_OFF);
+    uint64_t* bfull = tfull + NST;
+    uint64_t* decoded = bfull + NST;
     uint64_t* empty = decoded + NST;
     uint64_t* acc_full = empty + NST;
     float* red = reinterpret_cast<float*>(smem);  // [NT][128], after the main loop
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < NST; i++) {
-            mbar_init(&full[i], 1);
+            mbar_init(&tfull[i], 1);
+            mbar_init(&bfull[i], 1);
             mbar_init(&decoded[i], kGemmDecWarps);
             mbar_init(&empty[i], 1);
         }
@@ -267,17 +271,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
             for (int i = 0; i < ncs; i++) {
                 const int st = i % NST;
                 if (i >= NST && !mbar_wait(&empty[st], ((i / NST) - 1) & 1, DEV_TIMEOUT_EMPTY)) break;
-                mbar_arrive_expect_tx(&full[st], Lay::T_BYTES + rt_live * Lay::B_TILE);
+                mbar_arrive_expect_tx(&tfull[st], Lay::T_BYTES);
                 const int kc = c0 + i;
 #pragma unroll 1
                 for (int r = 0; r < 4; r++) {
                     const size_t tk = (size_t)kc * 4 + r;
                     bulk_g2s(smem + Lay::T_OFF + st * Lay::T_BYTES + r * row_bytes, tr + (tk * OT + (size_t)ob * 8) * N,
-                             row_bytes, &full[st]);
+                             row_bytes, &tfull[st]);
                 }
+                mbar_arrive_expect_tx(&bfull[st], rt_live * Lay::B_TILE);
                 for (int r = 0; r < rt_live; r++)
                     tma_load_2d(smem + Lay::B_OFF + st * Lay::B_BYTES + r * Lay::B_TILE, &pmap, kc * kGemmKC,
-                                it.row0 + r * NT, &full[st]);
+                                it.row0 + r * NT, &bfull[st]);
             }
         }
     } else if (warp == kGemmDecWarps + 1) {
@@ -289,6 +294,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
             for (int i = 0; i < ncs; i++) {
                 const int st = i % NST;
                 if (ok) ok = mbar_wait(&decoded[st], (i / NST) & 1, DEV_TIMEOUT_FULL);
+                if (ok) ok = mbar_wait(&bfull[st], (i / NST) & 1, DEV_TIMEOUT_FULL);
                 tc_fence_after();
                 if (ok) {
                     const uint32_t a0 = smem_u32(smem + Lay::A_OFF + st * Lay::A_BYTES);
@@ -323,7 +329,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         bool ok = true;
         for (int i = 0; i < ncs; i++) {
             const int st = i % NST;
-            if (ok) ok = mbar_wait(&full[st], (i / NST) & 1, DEV_TIMEOUT_FULL);
+            if (ok) ok = mbar_wait(&tfull[st], (i / NST) & 1, DEV_TIMEOUT_FULL);
             if (ok) {
                 const uint32_t* trow =
                     reinterpret_cast<const uint32_t*>(smem + Lay::T_OFF + st * Lay::T_BYTES) + (ti * 8 + to0) * (N / 2);

@@ -22,13 +22,14 @@ namespace sx {
 template <int KIND, int NB, bool W16>
 cudaError_t dispatch_n(const GemvArgs& a, int n, int groups, cudaStream_t stream);
 
-// Consumer warps of the GEMV: 16, each decoding 4 of a stage's 64 tiles (more warps in flight to
-// hide the decode chain's latency than 8 warps x 8 tiles).
-constexpr int kGemvCW = 16;
+// Consumer warps of the GEMV: 8, each owning one output tile across a stage's 8 input-tile rows,
+// at three CTAs per SM for up to 8 rows (measured on B200: faster than 16 warps at two CTAs per
+// SM on every sweep shape).
+constexpr int kGemvCW = 8;
 constexpr int kGemvThreads = (kGemvCW + 1) * 32;
 
 template <int KIND, int N, int NB, bool W16>
-__global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) gemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 3 : 2) gemv_kernel(GemvArgs a) {
     constexpr int CW = kGemvCW;
     extern __shared__ __align__(128) uint8_t smem[];
     cg::cluster_group cluster = cg::this_cluster();
