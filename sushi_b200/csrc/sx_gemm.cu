@@ -11,7 +11,7 @@ namespace sx {
 
 template <int KIND>
 cudaError_t gemm_dispatch(const CUtensorMap& pmap, const GemmArgs& a, int n, int rt, int items, int S,
-                          cudaStream_t stream);
+                          cudaStream_t stream, bool pair);
 
 // P[r][kb*128 + i] = f16(H128(f16(x[r]) * suh)) for one (row, 128-input block) per warp: the
 // reference's prepareInput (src/exl3/expert_exl3.zig:490-501).
@@ -58,12 +58,12 @@ cudaError_t prep_map(CUtensorMap* m, const uint16_t* P, int rows, int in) {
 }
 
 cudaError_t gemm_launch(int kind, const CUtensorMap& pmap, const GemmArgs& a, int n, int rt, int items, int S,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, bool pair) {
     switch (kind) {
-        case K_MCG: return gemm_dispatch<K_MCG>(pmap, a, n, rt, items, S, stream);
-        case K_MUL1: return gemm_dispatch<K_MUL1>(pmap, a, n, rt, items, S, stream);
-        case K_HASH: return gemm_dispatch<K_HASH>(pmap, a, n, rt, items, S, stream);
-        case K_PAIR1: return gemm_dispatch<K_PAIR1>(pmap, a, n, rt, items, S, stream);
+        case K_MCG: return gemm_dispatch<K_MCG>(pmap, a, n, rt, items, S, stream, pair);
+        case K_MUL1: return gemm_dispatch<K_MUL1>(pmap, a, n, rt, items, S, stream, pair);
+        case K_HASH: return gemm_dispatch<K_HASH>(pmap, a, n, rt, items, S, stream, pair);
+        case K_PAIR1: return gemm_dispatch<K_PAIR1>(pmap, a, n, rt, items, S, stream, pair);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -133,6 +133,6 @@ extern "C" sx_status sx_linear_gemm(sx_stream stream, const sx_proj* proj, const
     const int rt = gemm_rt(rows, proj->n);
     const int items = (rows + kGemmRows * rt - 1) / (kGemmRows * rt);
     const int S = gemm_split((long long)items * (out / 128), in / kGemmKC);
-    e = gemm_launch(kind, pmap, a, proj->n, rt, items, S, s);
+    e = gemm_launch(kind, pmap, a, proj->n, rt, items, S, s, false);
     return cuda_status(e, "gemm launch");
 }

@@ -63,22 +63,25 @@ struct GemmArgs {
 
 // RT row tiles of NT rows per CTA share each decoded weight chunk: RT accumulators of NT columns
 // in tensor memory (RT * NT <= 512), RT prepared-row tiles per stage.
-template <int N, int NT, int RT>
+// PAIR: a CTA pair (cta_group::2) shares the four row tiles; each CTA holds half of each 256-row
+// block's prepared rows, so it loads two 16 KB tiles per stage and the ring is four deep.
+template <int N, int NT, int RT, bool PAIR = false>
 struct GemmLayout {
     static constexpr int A_BYTES = 128 * kGemmKC * 2;   // 16 KB
     static constexpr int B_TILE = NT * kGemmKC * 2;     // 16 KB per row tile
-    static constexpr int B_BYTES = RT * B_TILE;
+    static constexpr int B_BYTES = (PAIR ? RT / 2 : RT) * B_TILE;
     static constexpr int T_BYTES = 4 * 8 * N * 2;       // 32 trellis tiles
-    static constexpr int NST = RT == 1 ? 4 : (RT == 2 ? 3 : 2);
+    static constexpr int NST = PAIR ? 4 : (RT == 1 ? 4 : (RT == 2 ? 3 : 2));
     static constexpr int TMEM_COLS = NT * RT;
     static constexpr int A_OFF = 0;
     static constexpr int B_OFF = A_OFF + NST * A_BYTES;
     static constexpr int T_OFF = B_OFF + NST * B_BYTES;
     static constexpr int BAR_OFF = (T_OFF + NST * T_BYTES + 15) / 16 * 16;
-    static constexpr int TOTAL = BAR_OFF + (4 * NST + 1) * 8 + 16;
+    static constexpr int TOTAL = BAR_OFF + (5 * NST + 1) * 8 + 16;
     static constexpr int RED_BYTES = NT * 128 * 4;      // one row tile's accumulator in f32, reusing A and B
     static_assert(RED_BYTES <= T_OFF, "accumulator staging fits in the A/B ring");
     static_assert(TMEM_COLS <= 512, "tensor memory holds 512 columns");
+    static_assert(!PAIR || RT == 4, "the pair kernel holds two 256-row blocks");
     static constexpr int ALLOC = TOTAL + 1024;          // room to align the base to 1024 bytes
 };
 
@@ -111,6 +114,64 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uin
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
         ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
+}
+
+// M = 256 over a CTA pair (cta_group::2): each CTA supplies 128 rows of A and half of B's N rows.
+__host__ __device__ constexpr uint32_t idesc_f16_m256(int nt) {
+    return (1u << 4) | ((uint32_t)(nt >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma2_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Completion of this thread's pair MMAs, arriving on the barrier at the same offset in both CTAs.
+__device__ __forceinline__ void tc_commit2(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"((uint16_t)3)
+        : "memory");
+}
+
+// Arrive (release at cluster scope) on the barrier at the same offset in cluster CTA `rank`.
+__device__ __forceinline__ void mbar_arrive_remote(uint64_t* bar, uint32_t rank) {
+    asm volatile(
+        "{\n\t.reg .b32 ra;\n\t"
+        "mapa.shared::cluster.u32 ra, %0, %1;\n\t"
+        "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [ra];\n\t}" ::"r"(smem_u32(bar)),
+        "r"(rank)
+        : "memory");
+}
+
+// mbar_wait with acquire at cluster scope (arrivals from the peer CTA).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int code) {
+    auto try_once = [&]() {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+        return ok != 0;
+    };
+    if (try_once()) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 0;; i++) {
+        if (try_once()) return true;
+        if ((i & 255u) == 255u && global_timer_ns() - t0 > kWaitLimitNs) {
+            latch_error(code);
+            return false;
+        }
+    }
 }
 
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
@@ -211,9 +272,9 @@ __device__ __forceinline__ void gemm_store(const GemmArgs& a, const GemmItem& it
 // Named barrier 1 over the decoder warps.
 __device__ __forceinline__ void decoders_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kGemmDecWarps * 32) : "memory"); }
 
-template <int KIND, int N, int NT, int RT, bool W16>
+template <int KIND, int N, int NT, int RT, bool W16, bool PAIR>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap pmap, GemmArgs a) {
-    using Lay = GemmLayout<N, NT, RT>;
+    using Lay = GemmLayout<N, NT, RT, PAIR>;
     constexpr int NST = Lay::NST;
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint32_t tmem_slot;
@@ -238,7 +299,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     uint64_t* decoded = bfull + NST;
     uint64_t* empty = decoded + NST;
     uint64_t* acc_full = empty + NST;
+    uint64_t* peer_ready = acc_full + 1;  // PAIR, leader: the peer's stage is decoded and loaded
     float* red = reinterpret_cast<float*>(smem);  // [NT][128], after the main loop
+    const uint32_t rank = PAIR ? cluster.block_rank() : 0;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < NST; i++) {
@@ -246,18 +309,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
             mbar_init(&bfull[i], 1);
             mbar_init(&decoded[i], kGemmDecWarps);
             mbar_init(&empty[i], 1);
+            mbar_init(&peer_ready[i], 1);
         }
         mbar_init(acc_full, 1);
         fence_mbar_init();
     }
-    if (warp == kGemmDecWarps + 1) {  // the MMA warp owns the tensor memory
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
-                     "n"(Lay::TMEM_COLS)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    if (warp == kGemmDecWarps + 1) {  // the MMA warp owns the tensor memory (both CTAs of a pair)
+        if constexpr (PAIR) {
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                         "n"(Lay::TMEM_COLS)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
+                         "n"(Lay::TMEM_COLS)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        }
     }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) cluster.sync();  // the peer's barriers exist before any remote arrival
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
     const int OT = a.out / 16;
@@ -279,41 +351,74 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                     bulk_g2s(smem + Lay::T_OFF + st * Lay::T_BYTES + r * row_bytes, tr + (tk * OT + (size_t)ob * 8) * N,
                              row_bytes, &tfull[st]);
                 }
-                mbar_arrive_expect_tx(&bfull[st], rt_live * Lay::B_TILE);
-                for (int r = 0; r < rt_live; r++)
-                    tma_load_2d(smem + Lay::B_OFF + st * Lay::B_BYTES + r * Lay::B_TILE, &pmap, kc * kGemmKC,
-                                it.row0 + r * NT, &bfull[st]);
+                if constexpr (PAIR) {
+                    // this CTA's half (128 rows) of each live 256-row block
+                    const int nb = (it.rows + 2 * NT - 1) / (2 * NT);
+                    mbar_arrive_expect_tx(&bfull[st], nb * Lay::B_TILE);
+                    for (int j = 0; j < nb; j++)
+                        tma_load_2d(smem + Lay::B_OFF + st * Lay::B_BYTES + j * Lay::B_TILE, &pmap, kc * kGemmKC,
+                                    it.row0 + j * 2 * NT + (int)rank * NT, &bfull[st]);
+                } else {
+                    mbar_arrive_expect_tx(&bfull[st], rt_live * Lay::B_TILE);
+                    for (int r = 0; r < rt_live; r++)
+                        tma_load_2d(smem + Lay::B_OFF + st * Lay::B_BYTES + r * Lay::B_TILE, &pmap, kc * kGemmKC,
+                                    it.row0 + r * NT, &bfull[st]);
+                }
             }
         }
     } else if (warp == kGemmDecWarps + 1) {
-        // ---------------- MMA issuer
-        if (lane == 0) {
+        // ---------------- MMA issuer (a pair's leader; the peer forwards its readiness)
+        if (lane == 0 && PAIR && rank == 1) {
+            for (int i = 0; i < ncs; i++) {
+                const int st = i % NST;
+                mbar_wait(&decoded[st], (i / NST) & 1, DEV_TIMEOUT_FULL);
+                mbar_wait(&bfull[st], (i / NST) & 1, DEV_TIMEOUT_FULL);
+                mbar_arrive_remote(&peer_ready[st], 0);  // arrives even after a timeout: the leader moves on
+            }
+        } else if (lane == 0) {
             constexpr uint32_t idesc = idesc_f16_m128(NT);
-            constexpr uint32_t idesc2 = idesc_f16_m128(2 * NT);  // N = 256
+            constexpr uint32_t idesc2 = idesc_f16_m128(2 * NT);   // N = 256
+            constexpr uint32_t idescp = idesc_f16_m256(2 * NT);   // pair: M = 256, N = 256
+            const int nb = (it.rows + 2 * NT - 1) / (2 * NT);
             bool ok = true;
             for (int i = 0; i < ncs; i++) {
                 const int st = i % NST;
                 if (ok) ok = mbar_wait(&decoded[st], (i / NST) & 1, DEV_TIMEOUT_FULL);
                 if (ok) ok = mbar_wait(&bfull[st], (i / NST) & 1, DEV_TIMEOUT_FULL);
+                if (PAIR && ok) ok = mbar_wait_cluster(&peer_ready[st], (i / NST) & 1, DEV_TIMEOUT_FULL);
                 tc_fence_after();
                 if (ok) {
                     const uint32_t a0 = smem_u32(smem + Lay::A_OFF + st * Lay::A_BYTES);
                     const uint32_t b0 = smem_u32(smem + Lay::B_OFF + st * Lay::B_BYTES);
-                    // Row tiles go two at a time as one N = 256 MMA where both are live (their
-                    // prepared-row tiles and accumulators sit back to back): half the A reads
-                    // from shared memory per flop of N = 128 MMAs.
-                    for (int r = 0; r < rt_live; r += 2) {
-                        const bool pair = r + 1 < rt_live;
-                        const uint32_t id = pair ? idesc2 : idesc;
+                    if constexpr (PAIR) {
+                        // block j: columns j*256.. of both CTAs' accumulators; rows 0..127 of N from
+                        // this CTA's tile j, 128..255 from the peer's
+                        for (int j = 0; j < nb; j++)
 #pragma unroll
-                        for (int kk = 0; kk < kGemmKC / 16; kk++)
-                            tc_mma_f16(tmem + (uint32_t)(r * NT), smem_desc_sw128(a0 + kk * 32),
-                                       smem_desc_sw128(b0 + r * Lay::B_TILE + kk * 32), id, (i > 0 || kk > 0) ? 1u : 0u);
+                            for (int kk = 0; kk < kGemmKC / 16; kk++)
+                                tc_mma2_f16(tmem + (uint32_t)(j * 2 * NT), smem_desc_sw128(a0 + kk * 32),
+                                            smem_desc_sw128(b0 + j * Lay::B_TILE + kk * 32), idescp,
+                                            (i > 0 || kk > 0) ? 1u : 0u);
+                    } else {
+                        // Row tiles go two at a time as one N = 256 MMA where both are live (their
+                        // prepared-row tiles and accumulators sit back to back): half the A reads
+                        // from shared memory per flop of N = 128 MMAs.
+                        for (int r = 0; r < rt_live; r += 2) {
+                            const bool pair = r + 1 < rt_live;
+                            const uint32_t id = pair ? idesc2 : idesc;
+#pragma unroll
+                            for (int kk = 0; kk < kGemmKC / 16; kk++)
+                                tc_mma_f16(tmem + (uint32_t)(r * NT), smem_desc_sw128(a0 + kk * 32),
+                                           smem_desc_sw128(b0 + r * Lay::B_TILE + kk * 32), id,
+                                           (i > 0 || kk > 0) ? 1u : 0u);
+                        }
                     }
                 }
-                tc_commit(&empty[st]);  // frees the stage once these MMAs have read it
+                if constexpr (PAIR) tc_commit2(&empty[st]);  // frees the stage in both CTAs
+                else tc_commit(&empty[st]);
             }
-            tc_commit(acc_full);
+            if constexpr (PAIR) tc_commit2(acc_full);
+            else tc_commit(acc_full);
         }
     } else {
         // ---------------- decoders: warp w decodes trellis row w/4, output tiles (w%4)*2 and +1
@@ -375,11 +480,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         if (S > 1) cluster.sync(); else __syncthreads();
     }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) cluster.sync();  // both CTAs are done with the pair's MMAs and tensor memory
+    else __syncthreads();
     if (warp == kGemmDecWarps + 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(Lay::TMEM_COLS)
-                     : "memory");
+        if constexpr (PAIR)
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(Lay::TMEM_COLS)
+                         : "memory");
+        else
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(Lay::TMEM_COLS)
+                         : "memory");
     }
 }
 

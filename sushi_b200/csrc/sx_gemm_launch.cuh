@@ -7,11 +7,12 @@
 
 namespace sx {
 
-template <int KIND, int N, int RT>
+template <int KIND, int N, int RT, bool PAIR = false>
 static cudaError_t launch_gemm_t(const CUtensorMap& pmap, const GemmArgs& a, int items, int S, cudaStream_t stream) {
     constexpr int NT = kGemmRows;
-    auto kern = gemm_kernel<KIND, N, NT, RT, false>;
-    const int smem = GemmLayout<N, NT, RT>::ALLOC;
+    if (PAIR && (S != 1 || (a.out / 128) % 2)) return cudaErrorInvalidValue;  // pairs: no split, even blocks
+    auto kern = gemm_kernel<KIND, N, NT, RT, false, PAIR>;
+    const int smem = GemmLayout<N, NT, RT, PAIR>::ALLOC;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     if (S > 8) {
@@ -25,7 +26,7 @@ static cudaError_t launch_gemm_t(const CUtensorMap& pmap, const GemmArgs& a, int
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.x = PAIR ? 2 : 1;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = S;
     cfg.attrs = attr;
@@ -49,11 +50,12 @@ static cudaError_t launch_gemm_t(const CUtensorMap& pmap, const GemmArgs& a, int
 
 template <int KIND>
 cudaError_t gemm_dispatch(const CUtensorMap& pmap, const GemmArgs& a, int n, int rt, int items, int S,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, bool pair) {
 #define SX_CASE(NN) \
     case NN: return launch_gemm_t<KIND, NN, 1>(pmap, a, items, S, stream);
 #define SX_CASE4(NN) \
-    case NN: return launch_gemm_t<KIND, NN, 4>(pmap, a, items, S, stream);
+    case NN: return pair ? launch_gemm_t<KIND, NN, 4, true>(pmap, a, items, S, stream) \
+                         : launch_gemm_t<KIND, NN, 4>(pmap, a, items, S, stream);
     if (rt == 4) {
         switch (n) {
             SX_GEMM_N_LIST_RT(SX_CASE4)

@@ -21,8 +21,9 @@ cudaError_t prep_map(CUtensorMap* m, const uint16_t* P, int rows, int in);
 int gemm_split(long long ctas, int chunks);
 int gemm_rt(long long rows, int n);
 bool gemm_rt_rate(int n);  // rates with four-row-tile tensor-core kernels
+// pair: the CTA-pair (cta_group::2) kernel for rt == 4 (no split, an even count of output blocks).
 cudaError_t gemm_launch(int kind, const CUtensorMap& pmap, const GemmArgs& a, int n, int rt, int items, int S,
-                        cudaStream_t stream);
+                        cudaStream_t stream, bool pair = false);
 
 // sx_moe's body; with `partial` set, the routed k-order sums land there in f32, unrounded and
 // without the shared expert (an expert-parallel rank's share of its peers' tokens), and y is unused.

@@ -408,7 +408,7 @@ sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_de
             g.meta = a.meta + 1;
             g.work_act = a.work_act4;
             g.work_chunk = a.work_chunk4;
-            return gemm_launch(kind, m, g, n, 4, L.W4_max, 1, s);
+            return gemm_launch(kind, m, g, n, 4, L.W4_max, 1, s, out_blocks % 2 == 0);
         };
         GemmArgs g{};
         g.rows = 0;
