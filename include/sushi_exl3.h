@@ -304,6 +304,12 @@ sx_status sx_ep_info(const sx_ep* ep, int32_t* world, int32_t* rank);
  * (0 = none) and clears it; synchronises `stream` first. */
 int32_t sx_device_error(sx_stream stream);
 
+/* Failure-detection self-test: launches one kernel whose bounded wait nothing satisfies (an
+ * mbarrier no thread arrives at).  The wait gives up after limit_ms (1..2000) and latches code 3,
+ * which the next sx_device_error returns; the context stays usable.  No reference counterpart: it
+ * checks the timeout path every kernel here relies on, without faulting or hanging the GPU. */
+sx_status sx_selftest_wait_timeout(sx_stream stream, int32_t limit_ms);
+
 /* Detail of the last SX_ERR_CUDA or SX_ERR_NCCL this thread got: the failing call's error and where
  * ("cudaLaunchKernelEx gemv: cudaErrorInvalidValue"); "" when there is none. */
 const char* sx_last_error_detail(void);

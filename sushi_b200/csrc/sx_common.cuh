@@ -15,6 +15,7 @@ enum DeviceError : int {
     DEV_OK = 0,
     DEV_TIMEOUT_FULL = 1,     // a consumer waited too long for a stage's bytes
     DEV_TIMEOUT_EMPTY = 2,    // the producer waited too long for a stage to drain
+    DEV_TIMEOUT_SELFTEST = 3, // sx_selftest_wait_timeout's wait gave up, as it is meant to
 };
 
 extern __device__ int g_device_error;
@@ -65,12 +66,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // every later block- and cluster-wide barrier, so no thread is left waiting.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code,
+                                          uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (uint32_t i = 0;; i++) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255u) == 255u && global_timer_ns() - t0 > kWaitLimitNs) {
+        if ((i & 255u) == 255u && global_timer_ns() - t0 > limit_ns) {
             latch_error(code);
             return false;
         }

@@ -5,6 +5,7 @@
 // tensorCorePerm place.  Used by the bit-exact parity tests and by callers that want the dense
 // inner matrix (the reference's trunk_gemm decode-once arm, src/exl3/trunk_gemm.zig).
 #include "sx_decode.cuh"
+#include "sx_internal.h"
 #include "sx_kernels.h"
 
 namespace sx {
@@ -110,3 +111,27 @@ cudaError_t launch_decode_codewords(int kind, int n, uint32_t wmask, uint32_t mu
 }
 
 }  // namespace sx
+
+namespace sx {
+namespace {
+
+// A wait nothing will satisfy: one thread waits on a fresh mbarrier (expected arrivals 1, none
+// made) through the same bounded wait every kernel uses, gives up after limit_ns and latches
+// DEV_TIMEOUT_SELFTEST.
+__global__ void wait_selftest_kernel(uint64_t limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        mbar_wait(&bar, 0, DEV_TIMEOUT_SELFTEST, limit_ns);
+    }
+}
+
+}  // namespace
+}  // namespace sx
+
+extern "C" sx_status sx_selftest_wait_timeout(sx_stream stream, int32_t limit_ms) {
+    if (limit_ms < 1 || limit_ms > 2000) return SX_ERR_BAD_SHAPE;
+    sx::wait_selftest_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>((uint64_t)limit_ms * 1000000ull);
+    return sx::cuda_status(cudaGetLastError(), "selftest launch");
+}

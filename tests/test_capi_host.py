@@ -184,3 +184,8 @@ def test_ragged_meta_admission(L):
     st = L.sx_moe_ragged(None, ctypes.byref(r), ctypes.byref(_dec()), FAKE, 2, 4, FAKE, FAKE, 2, None, None, 0, FAKE,
                          FAKE, 1 << 30)
     assert L.sx_status_name(st).decode() == "SX_ERR_TRELLIS_GEOMETRY"
+
+
+def test_selftest_limit_is_checked_before_launch(L):
+    for bad in (0, -5, 2001):
+        assert L.sx_status_name(L.sx_selftest_wait_timeout(None, bad)).decode() == "SX_ERR_BAD_SHAPE"

@@ -7,6 +7,9 @@ codebook, as the reference holds every Metal reader to the host decode over all 
 (firstPair1PairMismatch, :361-369).
 """
 
+import ctypes
+import time
+
 import numpy as np
 import pytest
 
@@ -133,3 +136,24 @@ def test_tile_order_round_trip(n, E, in_f, out_f):
     np.testing.assert_array_equal(pm.cpu().numpy().view(np.uint16), want)
     back = sx.tile_order_convert(pm, sx.TileOrder.PACK, sx.TileOrder.PAIR_MAJOR)
     np.testing.assert_array_equal(back.cpu().numpy().view(np.uint16), src)
+
+
+def test_bounded_wait_gives_up_and_the_context_stays_usable():
+    """The failure-detection path: a kernel waits on a barrier nothing arrives at; the bounded wait
+    gives up after its limit, latches code 3 (sx_device_error), and later work runs normally."""
+    import sushi_b200 as sx
+    from sushi_b200 import _lib
+
+    L = _lib.load()
+    assert sx.device_error() == 0
+    t0 = time.perf_counter()
+    assert L.sx_selftest_wait_timeout(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), 20) == 0
+    assert sx.device_error() == 3  # synchronises, reads and clears the latch
+    assert time.perf_counter() - t0 < 5.0
+    assert sx.device_error() == 0
+    tr, su, sv = random_pack(5, 256, 128, 32)
+    _, dec = dec_args(orc.CB_MCG, 16)
+    proj = sx.Proj(dev(tr, torch), dev(su, torch), dev(sv, torch))
+    y = sx.linear(torch.ones((1, 256), device="cuda", dtype=torch.bfloat16), proj, dec)
+    torch.cuda.synchronize()
+    assert torch.isfinite(y.float()).all() and sx.device_error() == 0
