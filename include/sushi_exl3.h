@@ -155,6 +155,14 @@ size_t sx_linear_gemm_workspace_bytes(const sx_proj* proj, int32_t rows);
 sx_status sx_linear_gemm(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x, sx_dtype dtype,
                          int32_t rows, void* y, void* workspace, size_t workspace_bytes);
 
+/* linear.linearShared (src/exl3/linear.zig:144-247): up to 4 linears that read the same rows,
+ * stacked along the output into one bank (trellis [1, in/16, out/16, n], svh [1, out]) with one suh
+ * row per linear (suh [count, in]); linear s owns columns cols[s]..cols[s+1] (host array of
+ * count+1 bounds, multiples of 128, cols[0] = 0, cols[count] = out).  One launch (per 16 rows)
+ * writes ys[s] [rows, cols[s+1]-cols[s]] in x's dtype. */
+sx_status sx_linear_shared(sx_stream stream, const sx_proj* proj, const int32_t* cols, int32_t count,
+                           const sx_decode* dec, const void* x, sx_dtype dtype, int32_t rows, void* const* ys);
+
 /* linear.linearGrouped (src/exl3/linear.zig:38-54): x [G, rows, in] through the G-bank proj
  * (experts == G, bank g serves x[g]) into y [G, rows, out]. */
 sx_status sx_linear_grouped(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x,

@@ -100,12 +100,13 @@ int sm_count() {
 }
 
 sx_status linear_impl(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x, sx_dtype dtype,
-                      int32_t rows, void* y, int groups, uint32_t flags) {
+                      int32_t rows, void* y, int groups, uint32_t flags, const int32_t* cols = nullptr,
+                      int32_t count = 0, void* const* ys = nullptr) {
     if (flags & ~(uint32_t)SX_LINEAR_WEIGHTS_STATIC) return SX_ERR_BAD_SHAPE;
     sx_status st = check_proj(proj, groups);
     if (st) return st;
     if (proj->tile_order != SX_TILE_PACK) return SX_ERR_TILE_ORDER_UNSUPPORTED;
-    if (!x || !y) return SX_ERR_NULL_POINTER;
+    if (!x || (!y && !count)) return SX_ERR_NULL_POINTER;
     if (!dtype_ok(dtype)) return SX_ERR_BAD_DTYPE;
     if (rows < 1) return SX_ERR_BAD_SHAPE;
     int kind;
@@ -136,6 +137,12 @@ sx_status linear_impl(sx_stream stream, const sx_proj* proj, const sx_decode* de
         a.mask1 = dp.mask1;
         a.rot = dp.rot;
         a.out_scale = kind_scale(kind);
+        a.nseg = count;
+        for (int i = 0; i < count; i++) {
+            a.seg_end[i] = cols[i + 1] / 128;
+            a.ywidth[i] = cols[i + 1] - cols[i];
+            a.ys[i] = static_cast<uint8_t*>(ys[i]) + (size_t)r0 * a.ywidth[i] * esz;
+        }
         // A later 16-row chunk follows this call's own launch, which writes only y.
         a.pdl = (flags & SX_LINEAR_WEIGHTS_STATIC) || r0 > 0;
         cudaError_t e = launch_gemv(a, kind, proj->n, groups, s);
@@ -240,6 +247,18 @@ sx_status sx_linear(sx_stream stream, const sx_proj* proj, const sx_decode* dec,
                     int32_t rows, void* y) {
     if (proj && proj->experts != 1) return SX_ERR_BAD_SHAPE;
     return linear_impl(stream, proj, dec, x, dtype, rows, y, 1, 0);
+}
+
+sx_status sx_linear_shared(sx_stream stream, const sx_proj* proj, const int32_t* cols, int32_t count,
+                           const sx_decode* dec, const void* x, sx_dtype dtype, int32_t rows, void* const* ys) {
+    if (!proj || !cols || !ys) return SX_ERR_NULL_POINTER;
+    if (proj->experts != 1 || count < 1 || count > 4) return SX_ERR_BAD_SHAPE;
+    if (cols[0] != 0 || cols[count] != proj->out_features) return SX_ERR_BAD_SHAPE;
+    for (int i = 0; i < count; i++) {
+        if (cols[i + 1] <= cols[i] || cols[i + 1] % 128) return SX_ERR_BAD_SHAPE;
+        if (!ys[i]) return SX_ERR_NULL_POINTER;
+    }
+    return linear_impl(stream, proj, dec, x, dtype, rows, nullptr, 1, 0, cols, count, ys);
 }
 
 sx_status sx_linear_ex(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x, sx_dtype dtype,

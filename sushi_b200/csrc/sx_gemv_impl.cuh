@@ -45,7 +45,9 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 3 : 2) gemv_kernel(Gem
     const CoreSmem s = core_smem<N, 1, NB>(smem, kbl_max, mg);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int OT = a.out / 16;
-    const uint16_t* suh = a.suh + (size_t)g * a.in;
+    int seg = 0;  // the stacked linear this output block belongs to
+    while (seg + 1 < a.nseg && ob >= a.seg_end[seg]) seg++;
+    const uint16_t* suh = a.suh + (size_t)(g + seg) * a.in;
     const uint16_t* svh = a.svh + (size_t)g * a.out;
 
     core_init_barriers<N, 1, CW>(s);
@@ -91,11 +93,17 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 3 : 2) gemv_kernel(Gem
             const float4 t = cluster_sum4(cluster, s.red, S, m * 128);
             float v[4] = {t.x, t.y, t.z, t.w};
             warp_hadamard128(v);
-            const size_t yoff = (size_t)g * a.y_group_stride + (size_t)m * a.out + (size_t)ob * 128 + lane * 4;
+            void* yp = a.y;
+            size_t yoff = (size_t)g * a.y_group_stride + (size_t)m * a.out + (size_t)ob * 128 + lane * 4;
+            if (a.nseg > 0) {
+                const int first = seg ? a.seg_end[seg - 1] : 0;
+                yp = a.ys[seg];
+                yoff = (size_t)m * a.ywidth[seg] + (size_t)(ob - first) * 128 + lane * 4;
+            }
 #pragma unroll
             for (int i = 0; i < 4; i++) {
                 const int o = ob * 128 + lane * 4 + i;
-                store_act(a.y, yoff + i, a.xdt, v[i] * a.out_scale * h2f(svh[o]));
+                store_act(yp, yoff + i, a.xdt, v[i] * a.out_scale * h2f(svh[o]));
             }
         }
     }

@@ -20,6 +20,12 @@ struct GemvArgs {
     uint32_t wmask, mult, mask0, mask1, rot;
     float out_scale;
     int pdl;                   // host side: launch with programmatic stream serialisation
+    // Stacked linears sharing the input (nseg > 0): output blocks [seg_end[s-1], seg_end[s]) are
+    // linear s, prepared with suh row s and written to ys[s] ([rows][ywidth[s]] in x's dtype).
+    int nseg;
+    int seg_end[4];
+    void* ys[4];
+    int ywidth[4];
 };
 
 cudaError_t launch_gemv(const GemvArgs& a, int kind, int n, int groups, cudaStream_t stream);

@@ -198,6 +198,24 @@ def linear_gemm(x, proj: Proj, dec: Decode, workspace=None):
     return y
 
 
+def linear_shared(x, proj: Proj, cols, dec: Decode):
+    """linear.linearShared: the linears stacked along the output of `proj` (suh holds one row per
+    linear) over the same rows x [rows, in]; linear s owns columns cols[s]..cols[s+1].  Returns the
+    list of [rows, cols[s+1]-cols[s]] outputs in x's dtype."""
+    if x.dim() != 2 or not x.is_contiguous():
+        raise Exl3Error(1)
+    if x.dtype not in _DT:
+        raise Exl3Error(2)
+    count = len(cols) - 1
+    outs = [torch.empty((x.shape[0], cols[i + 1] - cols[i]), dtype=x.dtype, device=x.device) for i in range(count)]
+    c = (ctypes.c_int32 * len(cols))(*cols)
+    ys = (ctypes.c_void_p * count)(*[o.data_ptr() for o in outs])
+    p, d = proj.c(), dec.c()
+    _check(lib().sx_linear_shared(_stream(), ctypes.byref(p), c, count, ctypes.byref(d), x.data_ptr(), _DT[x.dtype],
+                                  x.shape[0], ys))
+    return outs
+
+
 def linear_grouped(x, proj: Proj, dec: Decode):
     """linear.linearGrouped: x [G, rows, in] through the G-bank proj (bank g serves x[g]) -> [G, rows, out]."""
     if x.dim() != 3 or not x.is_contiguous():

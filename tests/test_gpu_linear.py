@@ -138,3 +138,25 @@ def test_linear_static_weights_overlap_matches(sx, rows):
         outs.append(a.clone())
     assert torch.equal(outs[0], outs[1])
     assert torch.isfinite(outs[0].float()).all()
+
+
+@pytest.mark.parametrize("rows,cols", [(1, [0, 128, 384, 512]), (5, [0, 256, 512]), (20, [0, 128, 256, 384, 512])])
+def test_linear_shared_stacked_outputs(sx, rows, cols):
+    """linear.linearShared: linears stacked along the output with one suh row each; linear s's
+    truth is the dense twin with suh row s, columns cols[s]..cols[s+1]."""
+    in_f, out_f, n = 384, 512, 32
+    count = len(cols) - 1
+    tr, su0, sv = random_pack(33, in_f, out_f, n)
+    rng = np.random.default_rng(4)
+    suh = np.stack([su0] + [(su0.view(np.float16) * rng.choice([-1.0, 1.0], size=in_f).astype(np.float16)).view(np.uint16)
+                            for _ in range(count - 1)])
+    _, dec = dec_args(orc.CB_MCG, 16)
+    proj = sx.Proj(dev(tr, torch), dev(suh, torch), dev(sv, torch))
+    xt, xv = _x(9, rows, in_f, torch.bfloat16)
+    outs = sx.linear_shared(xt, proj, cols, dec)
+    for s in range(count):
+        W = orc.decode_dense(tr, suh[s], sv, in_f, out_f, n, orc.CB_MCG, 16)[:, cols[s]:cols[s + 1]]
+        truth = orc.matvec_f64(W, xv)
+        y = to_f32(outs[s])
+        assert y.shape == (rows, cols[s + 1] - cols[s])
+        assert max_rel(y, truth) <= MAX_REL_TOL, (s, max_rel(y, truth))
