@@ -163,6 +163,19 @@ sx_status sx_linear_gemm(sx_stream stream, const sx_proj* proj, const sx_decode*
 sx_status sx_linear_shared(sx_stream stream, const sx_proj* proj, const int32_t* cols, int32_t count,
                            const sx_decode* dec, const void* x, sx_dtype dtype, int32_t rows, void* const* ys);
 
+/* linear.linearSharedNormed (src/exl3/linear.zig:269-290; project_rows.zig:394-456, 908-919): as
+ * sx_linear_shared, with linear 0's rows leaving RMS-normed in the same launch:
+ *   ys[0][r][c] = T( w[c] * T( o[r][c] * rsqrt(sum_c' o[r][c']^2 / cols[1] + eps) ) )
+ * where o is linear 0's finished output in x's dtype T and w = norm_w [cols[1]] in that dtype (MLX's
+ * fast rms_norm on the finished row).  rows 1..16, out <= 4096, eps >= 0 (else SX_ERR_BAD_SHAPE).
+ * workspace: sx_linear_shared_normed_workspace_bytes(proj) bytes, 16-byte aligned, ZEROED before
+ * its first use; every call leaves it zeroed again.  Calls that may run at the same time (other
+ * streams) need their own workspace. */
+size_t sx_linear_shared_normed_workspace_bytes(const sx_proj* proj);
+sx_status sx_linear_shared_normed(sx_stream stream, const sx_proj* proj, const int32_t* cols, int32_t count,
+                                  const sx_decode* dec, const void* x, sx_dtype dtype, int32_t rows, void* const* ys,
+                                  const void* norm_w, float eps, void* workspace, size_t workspace_bytes);
+
 /* linear.linearGrouped (src/exl3/linear.zig:38-54): x [G, rows, in] through the G-bank proj
  * (experts == G, bank g serves x[g]) into y [G, rows, out]. */
 sx_status sx_linear_grouped(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x,

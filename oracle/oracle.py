@@ -373,6 +373,14 @@ def expert_truth(dense, x, limit=0.0):
     return matvec_f64(dense[2], act)
 
 
+def rms_norm_truth(y, w, eps):
+    """MLX's rms_norm of each row, as the normed stacked finish applies it to a linear's finished
+    output (src/exl3/project_rows.zig:394-456): y * rsqrt(mean(y^2) + eps) * w, in f64."""
+    y = np.asarray(y, np.float64)
+    inv = 1.0 / np.sqrt(np.mean(y * y, axis=-1, keepdims=True) + eps)
+    return y * inv * np.asarray(w, np.float64)
+
+
 def router_truth(logits, k, mode="softmax", bias=None, renorm=True, scale=1.0, n_group=0, topk_group=0):
     """Top-k routing (src/moe_router.zig:16-65 chain semantics with the fused kernel's lowest-id
     tie break, :130-150; sigmoid_bias and its group limit :200-290).  Returns (inds, weights)."""

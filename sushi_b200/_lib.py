@@ -61,6 +61,9 @@ SIGNATURES = {
     "sx_linear_gemm_workspace_bytes": (_SZ, [ctypes.POINTER(SxProj), _I]),
     "sx_linear_gemm": (_I, [_P, ctypes.POINTER(SxProj), ctypes.POINTER(SxDecode), _P, _I, _I, _P, _P, _SZ]),
     "sx_linear_shared": (_I, [_P, ctypes.POINTER(SxProj), _P, _I, ctypes.POINTER(SxDecode), _P, _I, _I, _P]),
+    "sx_linear_shared_normed_workspace_bytes": (_SZ, [ctypes.POINTER(SxProj)]),
+    "sx_linear_shared_normed": (_I, [_P, ctypes.POINTER(SxProj), _P, _I, ctypes.POINTER(SxDecode), _P, _I, _I, _P, _P,
+                                     ctypes.c_float, _P, _SZ]),
     "sx_linear_grouped": (_I, [_P, ctypes.POINTER(SxProj), ctypes.POINTER(SxDecode), _P, _I, _I, _P]),
     "sx_router_topk": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, ctypes.c_float, _I, _I, _P, _P]),
     "sx_moe_workspace_bytes": (_SZ, [ctypes.POINTER(SxBank), _I, _I]),

@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 
@@ -99,9 +100,13 @@ int sm_count() {
     return cached;
 }
 
+// sx_linear_shared_normed's workspace: the block counter, then [16 rows][out/128 blocks] f32 sums.
+constexpr size_t kNormHeader = 16;
+
 sx_status linear_impl(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x, sx_dtype dtype,
                       int32_t rows, void* y, int groups, uint32_t flags, const int32_t* cols = nullptr,
-                      int32_t count = 0, void* const* ys = nullptr) {
+                      int32_t count = 0, void* const* ys = nullptr, const void* norm_w = nullptr,
+                      float norm_eps = 0.0f, void* norm_ws = nullptr) {
     if (flags & ~(uint32_t)SX_LINEAR_WEIGHTS_STATIC) return SX_ERR_BAD_SHAPE;
     sx_status st = check_proj(proj, groups);
     if (st) return st;
@@ -143,6 +148,10 @@ sx_status linear_impl(sx_stream stream, const sx_proj* proj, const sx_decode* de
             a.ywidth[i] = cols[i + 1] - cols[i];
             a.ys[i] = static_cast<uint8_t*>(ys[i]) + (size_t)r0 * a.ywidth[i] * esz;
         }
+        a.norm_w = norm_w;
+        a.norm_eps = norm_eps;
+        a.norm_count = static_cast<unsigned*>(norm_ws);
+        a.norm_ssq = norm_ws ? reinterpret_cast<float*>(static_cast<uint8_t*>(norm_ws) + kNormHeader) : nullptr;
         // A later 16-row chunk follows this call's own launch, which writes only y.
         a.pdl = (flags & SX_LINEAR_WEIGHTS_STATIC) || r0 > 0;
         cudaError_t e = launch_gemv(a, kind, proj->n, groups, s);
@@ -259,6 +268,31 @@ sx_status sx_linear_shared(sx_stream stream, const sx_proj* proj, const int32_t*
         if (!ys[i]) return SX_ERR_NULL_POINTER;
     }
     return linear_impl(stream, proj, dec, x, dtype, rows, nullptr, 1, 0, cols, count, ys);
+}
+
+size_t sx_linear_shared_normed_workspace_bytes(const sx_proj* proj) {
+    if (!proj || proj->out_features < 128) return 0;
+    return kNormHeader + (size_t)16 * (proj->out_features / 128) * sizeof(float);
+}
+
+sx_status sx_linear_shared_normed(sx_stream stream, const sx_proj* proj, const int32_t* cols, int32_t count,
+                                  const sx_decode* dec, const void* x, sx_dtype dtype, int32_t rows, void* const* ys,
+                                  const void* norm_w, float eps, void* workspace, size_t workspace_bytes) {
+    if (!proj || !cols || !ys || !norm_w) return SX_ERR_NULL_POINTER;
+    if (proj->experts != 1 || count < 1 || count > 4) return SX_ERR_BAD_SHAPE;
+    if (cols[0] != 0 || cols[count] != proj->out_features) return SX_ERR_BAD_SHAPE;
+    for (int i = 0; i < count; i++) {
+        if (cols[i + 1] <= cols[i] || cols[i + 1] % 128) return SX_ERR_BAD_SHAPE;
+        if (!ys[i]) return SX_ERR_NULL_POINTER;
+    }
+    // One launch (<= 16 rows) and an output the reference's one-threadgroup finish covers
+    // (project_rows.zig:914-919: out <= 4096).
+    if (rows > 16 || proj->out_features > 4096) return SX_ERR_BAD_SHAPE;
+    if (!(eps >= 0.0f) || !std::isfinite(eps)) return SX_ERR_BAD_SHAPE;
+    if (!workspace) return SX_ERR_NULL_POINTER;
+    if (workspace_bytes < sx_linear_shared_normed_workspace_bytes(proj)) return SX_ERR_WORKSPACE_TOO_SMALL;
+    if (reinterpret_cast<uintptr_t>(workspace) % 16) return SX_ERR_BAD_SHAPE;
+    return linear_impl(stream, proj, dec, x, dtype, rows, nullptr, 1, 0, cols, count, ys, norm_w, eps, workspace);
 }
 
 sx_status sx_linear_ex(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x, sx_dtype dtype,

@@ -125,6 +125,20 @@ __device__ __forceinline__ void load_act4(const void* p, size_t i, int dt, float
         v[k] = dt == 1 ? __half2float(__ushort_as_half(h[k])) : __bfloat162float(__ushort_as_bfloat16(h[k]));
 }
 
+// v rounded to an activation dtype and back.
+__device__ __forceinline__ float round_act(float v, int dt) {
+    if (dt == 0) return v;
+    if (dt == 1) return __half2float(__float2half_rn(v));
+    return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+// load_act past L1: for values another CTA of the same grid wrote (after a fence).
+__device__ __forceinline__ float load_act_cg(const void* p, size_t i, int dt) {
+    if (dt == 0) return __ldcg(static_cast<const float*>(p) + i);
+    const unsigned short h = __ldcg(static_cast<const unsigned short*>(p) + i);
+    return dt == 1 ? __half2float(__ushort_as_half(h)) : __bfloat162float(__ushort_as_bfloat16(h));
+}
+
 __device__ __forceinline__ void store_act(void* p, size_t i, int dt, float v) {
     if (dt == 0) static_cast<float*>(p)[i] = v;
     else if (dt == 1) static_cast<__half*>(p)[i] = __float2half_rn(v);

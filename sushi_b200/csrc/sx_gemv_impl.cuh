@@ -28,6 +28,36 @@ cudaError_t dispatch_n(const GemvArgs& a, int n, int groups, cudaStream_t stream
 constexpr int kGemvCW = 8;
 constexpr int kGemvThreads = (kGemvCW + 1) * 32;
 
+// The RMS norm of the first linear of a stacked launch (project_rows.zig:394-456's finish, MLX's
+// rms_norm on the finished row): called by every thread of each rank-0 CTA of linear 0 once its
+// rows and sums of squares are written and fenced.  The block that counts itself last reads the
+// whole segment's sums (fixed order), and rewrites the segment's rows as
+// w[c] * T(o[c] * rsqrt(sum / cols + eps)).  No block waits on another.
+// `flag` is a word of the CTA's shared memory that nothing reads any more.
+__device__ __forceinline__ void gemv_norm_last(const GemvArgs& a, int lane, int warp, int* flag) {
+    const int blocks = a.seg_end[0];
+    if (threadIdx.x == 0) *flag = atomicAdd(a.norm_count, 1u) == (unsigned)(blocks - 1);
+    __syncthreads();
+    if (!*flag) return;
+    __threadfence();
+    const int cols = blocks * 128;
+    const int nw = blockDim.x >> 5;
+    for (int m = warp; m < a.rows; m += nw) {
+        float ss = 0.0f;
+        for (int b = lane; b < blocks; b += 32) ss += __ldcg(a.norm_ssq + m * blocks + b);
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
+        const float inv = __frsqrt_rn(ss / (float)cols + a.norm_eps);
+        void* yr = static_cast<uint8_t*>(a.ys[0]) + (size_t)m * cols * (a.xdt == 0 ? 4 : 2);
+        for (int c = lane; c < cols; c += 32) {
+            const float t = round_act(load_act_cg(yr, c, a.xdt) * inv, a.xdt);
+            store_act(yr, c, a.xdt, load_act(a.norm_w, c, a.xdt) * t);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *a.norm_count = 0u;  // ready for the next launch on the stream
+}
+
 template <int KIND, int N, int NB, bool W16>
 __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 3 : 2) gemv_kernel(GemvArgs a) {
     constexpr int CW = kGemvCW;
@@ -87,6 +117,7 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 3 : 2) gemv_kernel(Gem
     }
 
     // rank 0 sums the cluster's partials over DSMEM and finishes
+    const bool normed = a.norm_w != nullptr && seg == 0;
     cluster.sync();
     if (split == 0 && warp < CW) {
         for (int m = warp; m < a.rows; m += CW) {
@@ -100,14 +131,28 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 3 : 2) gemv_kernel(Gem
                 yp = a.ys[seg];
                 yoff = (size_t)m * a.ywidth[seg] + (size_t)(ob - first) * 128 + lane * 4;
             }
+            float ss = 0.0f;
 #pragma unroll
             for (int i = 0; i < 4; i++) {
                 const int o = ob * 128 + lane * 4 + i;
-                store_act(yp, yoff + i, a.xdt, v[i] * a.out_scale * h2f(svh[o]));
+                const float f = v[i] * a.out_scale * h2f(svh[o]);
+                if (normed) {
+                    const float r = round_act(f, a.xdt);
+                    ss = fmaf(r, r, ss);
+                }
+                store_act(yp, yoff + i, a.xdt, f);
+            }
+            if (normed) {
+#pragma unroll
+                for (int d = 16; d > 0; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
+                if (lane == 0) a.norm_ssq[m * a.seg_end[0] + ob] = ss;
             }
         }
+        if (normed) __threadfence();  // this block's rows and sums before its count below
     }
     cluster.sync();
+    // After that sync no peer reads this CTA's shared memory: its first word serves as a flag.
+    if (normed && split == 0) gemv_norm_last(a, lane, warp, reinterpret_cast<int*>(smem));
 }
 
 // The split-K cluster size for a launch: the largest S <= 16 (and <= the input blocks) whose

@@ -26,6 +26,14 @@ struct GemvArgs {
     int seg_end[4];
     void* ys[4];
     int ywidth[4];
+    // RMS-normed first linear (norm_w != nullptr, one bank, rows <= 16): the finish leaves linear
+    // 0's row as w * T(o * rsqrt(mean(o^2) + eps)), o its finished values in x's dtype T.  Each
+    // output block of linear 0 writes its rows' sums of squares to norm_ssq[row][block]; the last
+    // block to count itself in norm_count (left at 0 again) applies the norm.
+    const void* norm_w;
+    float norm_eps;
+    float* norm_ssq;
+    unsigned* norm_count;
 };
 
 cudaError_t launch_gemv(const GemvArgs& a, int kind, int n, int groups, cudaStream_t stream);

@@ -98,7 +98,8 @@ class Proj:
             raise Exl3Error(1)
         return t.shape[0], t.shape[1] * 16, t.shape[2] * 16, t.shape[3]
 
-    def c(self):
+    def c(self, suh_rows: int = 1):
+        """The C struct; `suh_rows` suh rows per bank (stacked linears carry one per linear)."""
         experts, in_f, out_f, n = self.dims()
         for a in (self.trellis, self.suh, self.svh):
             if not a.is_cuda or not a.is_contiguous():
@@ -106,7 +107,7 @@ class Proj:
         if self.trellis.dtype not in (torch.uint16, torch.int16) or self.suh.dtype not in (torch.float16, torch.uint16, torch.int16) \
                 or self.svh.dtype not in (torch.float16, torch.uint16, torch.int16):
             raise Exl3Error(2)
-        if self.suh.numel() != experts * in_f or self.svh.numel() != experts * out_f:
+        if self.suh.numel() != experts * in_f * suh_rows or self.svh.numel() != experts * out_f:
             raise Exl3Error(1)
         return _lib.SxProj(self.trellis.data_ptr(), self.suh.data_ptr(), self.svh.data_ptr(), experts, in_f, out_f, n,
                            int(self.tile_order))
@@ -210,10 +211,41 @@ def linear_shared(x, proj: Proj, cols, dec: Decode):
     outs = [torch.empty((x.shape[0], cols[i + 1] - cols[i]), dtype=x.dtype, device=x.device) for i in range(count)]
     c = (ctypes.c_int32 * len(cols))(*cols)
     ys = (ctypes.c_void_p * count)(*[o.data_ptr() for o in outs])
-    p, d = proj.c(), dec.c()
+    p, d = proj.c(count), dec.c()
     _check(lib().sx_linear_shared(_stream(), ctypes.byref(p), c, count, ctypes.byref(d), x.data_ptr(), _DT[x.dtype],
                                   x.shape[0], ys))
     return outs
+
+
+def linear_shared_normed(x, proj: Proj, cols, dec: Decode, norm_w, eps: float, workspace=None):
+    """linear.linearSharedNormed: linear_shared whose first linear leaves RMS-normed with weight
+    norm_w [cols[1]] (x's dtype) and epsilon eps, in the same launch.  rows 1..16, out <= 4096.
+    `workspace` (optional): a zeroed uint8 device tensor of
+    linear_shared_normed_workspace_bytes(proj) bytes, reused across calls on one stream (each call
+    leaves it zeroed)."""
+    if x.dim() != 2 or not x.is_contiguous():
+        raise Exl3Error(1)
+    if x.dtype not in _DT:
+        raise Exl3Error(2)
+    if norm_w.dtype != x.dtype or not norm_w.is_contiguous() or norm_w.numel() != cols[1]:
+        raise Exl3Error(1)
+    count = len(cols) - 1
+    p, d = proj.c(count), dec.c()
+    need = lib().sx_linear_shared_normed_workspace_bytes(ctypes.byref(p))
+    if workspace is None:
+        workspace = torch.zeros(need, dtype=torch.uint8, device=x.device)
+    outs = [torch.empty((x.shape[0], cols[i + 1] - cols[i]), dtype=x.dtype, device=x.device) for i in range(count)]
+    c = (ctypes.c_int32 * len(cols))(*cols)
+    ys = (ctypes.c_void_p * count)(*[o.data_ptr() for o in outs])
+    _check(lib().sx_linear_shared_normed(_stream(), ctypes.byref(p), c, count, ctypes.byref(d), x.data_ptr(),
+                                         _DT[x.dtype], x.shape[0], ys, norm_w.data_ptr(), float(eps),
+                                         workspace.data_ptr(), workspace.numel()))
+    return outs
+
+
+def linear_shared_normed_workspace_bytes(proj: Proj) -> int:
+    p = proj.c(proj.suh.numel() // max(1, proj.dims()[1]))
+    return lib().sx_linear_shared_normed_workspace_bytes(ctypes.byref(p))
 
 
 def linear_grouped(x, proj: Proj, dec: Decode):

@@ -189,3 +189,32 @@ def test_ragged_meta_admission(L):
 def test_selftest_limit_is_checked_before_launch(L):
     for bad in (0, -5, 2001):
         assert L.sx_status_name(L.sx_selftest_wait_timeout(None, bad)).decode() == "SX_ERR_BAD_SHAPE"
+
+
+def test_linear_shared_normed_admission(L):
+    """linearSharedNormed serves one bank, <= 16 rows, out <= 4096 (project_rows.zig:914-919) and
+    needs its counter workspace; each refusal comes before any launch."""
+    cols = (ctypes.c_int32 * 3)(0, 128, 256)
+    ys = (ctypes.c_void_p * 2)(FAKE, FAKE)
+    p = _proj(in_f=256, out_f=256)
+    need = L.sx_linear_shared_normed_workspace_bytes(ctypes.byref(p))
+    assert need == 16 + 16 * 2 * 4
+
+    def call(proj=p, rows=1, w=FAKE, eps=1e-6, ws=FAKE, wsb=need, c=cols, count=2):
+        st = L.sx_linear_shared_normed(None, ctypes.byref(proj), c, count, ctypes.byref(_dec()), FAKE, 2, rows, ys, w,
+                                       eps, ws, wsb)
+        return L.sx_status_name(st).decode()
+
+    assert call(rows=17) == "SX_ERR_BAD_SHAPE"
+    assert call(w=None) == "SX_ERR_NULL_POINTER"
+    assert call(ws=None) == "SX_ERR_NULL_POINTER"
+    assert call(wsb=need - 1) == "SX_ERR_WORKSPACE_TOO_SMALL"
+    assert call(ws=FAKE + 8) == "SX_ERR_BAD_SHAPE"
+    assert call(eps=-1.0) == "SX_ERR_BAD_SHAPE"
+    assert call(eps=float("nan")) == "SX_ERR_BAD_SHAPE"
+    assert call(proj=_proj(in_f=256, out_f=256, experts=2)) == "SX_ERR_BAD_SHAPE"
+    wide = _proj(in_f=256, out_f=4224)
+    wcols = (ctypes.c_int32 * 2)(0, 4224)
+    assert call(proj=wide, c=wcols, count=1, wsb=1 << 20) == "SX_ERR_BAD_SHAPE"
+    bad = (ctypes.c_int32 * 3)(0, 100, 256)
+    assert call(c=bad) == "SX_ERR_BAD_SHAPE"

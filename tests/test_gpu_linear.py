@@ -160,3 +160,57 @@ def test_linear_shared_stacked_outputs(sx, rows, cols):
         y = to_f32(outs[s])
         assert y.shape == (rows, cols[s + 1] - cols[s])
         assert max_rel(y, truth) <= MAX_REL_TOL, (s, max_rel(y, truth))
+
+
+@pytest.mark.parametrize(
+    "in_f,cols,rows,dtype",
+    [
+        (384, [0, 256, 512], 1, torch.bfloat16),
+        (384, [0, 512], 3, torch.float16),
+        (1024, [0, 1536, 2048], 9, torch.bfloat16),
+        (512, [0, 128, 384, 640], 16, torch.float32),
+    ],
+)
+def test_linear_shared_normed_first_linear(sx, in_f, cols, rows, dtype):
+    """linear.linearSharedNormed: linear 0 leaves as MLX's rms_norm of its finished row
+    (src/exl3/project_rows.zig:394-456) in the same launch; the other linears are linear_shared's
+    bytes.  Bars: the f64 truth of the normed row (1e-2), the unfused composition (linear_shared,
+    then the norm in f32 with the same roundings) to one output rounding, and a second call on
+    the same workspace gives the same bytes and leaves the workspace zeroed."""
+    out_f, n = cols[-1], 32
+    count = len(cols) - 1
+    tr, su0, sv = random_pack(41, in_f, out_f, n)
+    rng = np.random.default_rng(7)
+    suh = np.stack([su0] + [(su0.view(np.float16) * rng.choice([-1.0, 1.0], size=in_f).astype(np.float16)).view(np.uint16)
+                            for _ in range(count - 1)])
+    _, dec = dec_args(orc.CB_MCG, 16)
+    proj = sx.Proj(dev(tr, torch), dev(suh, torch), dev(sv, torch))
+    xt, xv = _x(12, rows, in_f, dtype)
+    w = torch.from_numpy(rng.uniform(0.5, 1.5, size=cols[1]).astype(np.float32)).cuda().to(dtype)
+    eps = 1e-6
+    ws = torch.zeros(sx.linear_shared_normed_workspace_bytes(proj), dtype=torch.uint8, device="cuda")
+    outs = sx.linear_shared_normed(xt, proj, cols, dec, w, eps, workspace=ws)
+    plain = sx.linear_shared(xt, proj, cols, dec)
+    torch.cuda.synchronize()
+    assert int(ws[:16].count_nonzero()) == 0, "the block counter is back at zero"
+    for s in range(1, count):
+        assert torch.equal(outs[s], plain[s]), s
+
+    W0 = orc.decode_dense(tr, suh[0], sv, in_f, out_f, n, orc.CB_MCG, 16)[:, : cols[1]]
+    truth = orc.rms_norm_truth(orc.matvec_f64(W0, xv), to_f32(w), eps)
+    y = to_f32(outs[0])
+    assert y.shape == (rows, cols[1])
+    assert max_rel(y, truth) <= MAX_REL_TOL, max_rel(y, truth)
+
+    o = plain[0].float()
+    inv = torch.rsqrt((o * o).mean(dim=-1, keepdim=True) + eps)
+    want = (w.float() * (o * inv).to(dtype).float()).to(dtype).float()
+    # two output roundings apart at most (the sums' order and rsqrt may differ in the last bit)
+    rtol = {torch.bfloat16: 2.0**-6, torch.float16: 2.0**-9, torch.float32: 2.0**-18}[dtype]
+    assert torch.allclose(outs[0].float(), want, rtol=rtol, atol=0.0)
+
+    again = sx.linear_shared_normed(xt, proj, cols, dec, w, eps, workspace=ws)
+    torch.cuda.synchronize()
+    for s in range(count):
+        assert torch.equal(again[s], outs[s]), s
+    assert int(ws[:16].count_nonzero()) == 0
