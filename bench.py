@@ -351,9 +351,8 @@ def main():
 
     if not args.no_moe:
         out["moe"] = moe_bench(sx, _lib, torch, args, stream, sptr)
-        if world == 1:
-            out["moe_prefill"] = prefill_bench(sx, torch, args, stream, tf_peak)
-            out["ffn_stack_deepseek"] = deepseek_bench(sx, torch, args, stream, tf_peak)
+        out["moe_prefill"] = prefill_bench(sx, torch, args, stream, tf_peak)
+        out["ffn_stack_deepseek"] = deepseek_bench(sx, torch, args, stream, tf_peak)
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline()
@@ -364,10 +363,24 @@ def main():
         print(json.dumps(out), flush=True)
 
 
+def qwen_shared(sx, torch, gen, D, I):
+    """The configs[2] layer's shared expert (one SwiGLU expert of intermediate I, K2 n32, replicated
+    on every rank) and its bf16 gate vector [D, 1]: the layer adds sigmoid(x . wg) * shared(x)
+    (moeWithGatedShared)."""
+    parts = []
+    for (i_f, o_f) in ((D, I), (D, I), (I, D)):
+        tr = torch.randint(-32768, 32768, (1, i_f // 16, o_f // 16, 32), dtype=torch.int16, device="cuda", generator=gen)
+        su = (torch.randint(0, 2, (1, i_f), device="cuda", generator=gen).half() * 2 - 1) * 0.05
+        sv = torch.randint(0, 2, (1, o_f), device="cuda", generator=gen).half() * 2 - 1
+        parts.append(sx.Proj(tr, su, sv))
+    wg = (torch.randn((D, 1), device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+    return sx.Bank(*parts), wg
+
+
 def moe_bench(sx, _lib, torch, args, stream, sptr):
     """hidden 2048, 512 experts of 512, top-10, K2 (n32) MCG random banks,
-    softmax router over fp32 logits from a bf16 2048x512 matrix; tokens/s of router + routed
-    experts for T tokens per rank.  One GPU: sx_moe over the whole bank.  N GPUs: expert parallel
+    softmax router over fp32 logits from a bf16 2048x512 matrix, one sigmoid-gated shared expert of
+    512; tokens/s of router + shared expert + routed experts for T tokens per rank.  One GPU: sx_moe over the whole bank.  N GPUs: expert parallel
     (sx_ep_moe), rank g holding experts [g*512/N, (g+1)*512/N), every rank routing its own T tokens
     (weak scaling: N*T tokens per step); tokens/s = N*T over the slowest rank's layer time.  Each
     measurement replays a CUDA graph of layers over a ring of distinct bank copies (> 2x L2)."""
@@ -394,17 +407,22 @@ def moe_bench(sx, _lib, torch, args, stream, sptr):
     ep = sx.ExpertParallel.from_process_group() if world > 1 else None
     res = {"experts_per_rank": El, "ranks": world, "copies": copies, "scaling": "weak (T tokens per rank)"}
     rgen = torch.Generator(device="cuda")
-    rgen.manual_seed(7)  # the router is replicated: same weights on every rank
+    rgen.manual_seed(7)  # the router and the shared expert are replicated: same weights on every rank
     wr = (torch.randn((D, E), device="cuda", generator=rgen) * 0.02).to(torch.bfloat16)
+    shared, wg = qwen_shared(sx, torch, rgen, D, I)
     for T in (1, 8, 64):
         x = torch.randn((T, D), device="cuda", generator=gen).to(torch.bfloat16)
+        one_i = torch.zeros((T, 1), dtype=torch.int32, device="cuda")
+        one_s = torch.ones((T, 1), device="cuda")
 
         def layer(c):
             logits = (x @ wr).float()
             inds, scores = sx.router_topk(logits, k)
+            sh = sx.moe(x, shared, one_i, one_s, dec)
+            gate = x @ wg
             if ep is None:
-                return sx.moe(x, banks[c % copies], inds, scores, dec)
-            return ep.moe(x, banks[c % copies], E, inds, scores, dec, rows_cap=T)
+                return sx.moe(x, banks[c % copies], inds, scores, dec, shared=sh, shared_gate=gate)
+            return ep.moe(x, banks[c % copies], E, inds, scores, dec, rows_cap=T, shared=sh, shared_gate=gate)
 
         for i in range(max(3, args.warmup)):
             layer(i)
@@ -443,36 +461,61 @@ def moe_bench(sx, _lib, torch, args, stream, sptr):
 
 
 def prefill_bench(sx, torch, args, stream, tf_peak):
-    """BASELINE configs[3] on one GPU: the configs[2] layer in prefill, 8192 tokens of bf16 N(0,1)
-    hidden states, routing skewed by a Zipf(1.1) bias log(r_e^-1.1 / sum) over a seeded rank
-    permutation added to the logits; router + routed experts through the tensor-core path.
-    Roofline: tensor, F = 2*T*k*3*H*I + 2*T*H*E flops per layer (the routed GEMMs and the router)
-    over the measured dense bf16 peak; the expert weights are decoded inside the GEMMs."""
+    """the configs[2] layer in prefill, 8192 tokens of bf16 N(0,1) hidden
+    states per rank, routing skewed by a Zipf(1.1) bias log(r_e^-1.1 / sum) over a seeded rank
+    permutation added to the logits; router + gated shared expert + routed experts through the
+    tensor-core path.  One GPU: sx_moe over the whole bank.  N GPUs: expert parallel (sx_ep_moe,
+    rows_cap = 8192), rank g holding experts [g*512/N, (g+1)*512/N) and routing its own 8192 tokens
+    (weak scaling); the Zipf bias is the same on every rank, so the hot experts' owners carry more
+    rows.  Roofline: tensor, F = 2*T*k*3*H*I + 2*T*3*H*I + 2*T*H*E flops per rank (routed GEMMs,
+    shared expert, router) over the measured dense bf16 peak; weights are decoded inside the GEMMs."""
+    import torch.distributed as dist
+
+    world, rank, _ = dist_env()
     E, D, I, k, T = 512, 2048, 512, 10, 8192
+    El = E // world
     gen = torch.Generator(device="cuda")
-    gen.manual_seed(77)
+    gen.manual_seed(77 + rank)
     parts = []
     for (i_f, o_f) in ((D, I), (D, I), (I, D)):
-        tr = torch.randint(-32768, 32768, (E, i_f // 16, o_f // 16, 32), dtype=torch.int16, device="cuda", generator=gen)
-        su = (torch.randint(0, 2, (E, i_f), device="cuda", generator=gen).half() * 2 - 1) * 0.05
-        sv = torch.randint(0, 2, (E, o_f), device="cuda", generator=gen).half() * 2 - 1
+        tr = torch.randint(-32768, 32768, (El, i_f // 16, o_f // 16, 32), dtype=torch.int16, device="cuda", generator=gen)
+        su = (torch.randint(0, 2, (El, i_f), device="cuda", generator=gen).half() * 2 - 1) * 0.05
+        sv = torch.randint(0, 2, (El, o_f), device="cuda", generator=gen).half() * 2 - 1
         parts.append(sx.Proj(tr, su, sv))
     bank = sx.Bank(*parts)
     dec = sx.Decode(sx.Codebook.MCG, 16)
-    wr = (torch.randn((D, E), device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+    rgen = torch.Generator(device="cuda")
+    rgen.manual_seed(78)  # router and shared expert: replicated
+    wr = (torch.randn((D, E), device="cuda", generator=rgen) * 0.02).to(torch.bfloat16)
+    shared, wg = qwen_shared(sx, torch, rgen, D, I)
     ranks = torch.randperm(E, generator=torch.Generator().manual_seed(5)).float() + 1.0
     zb = (ranks ** -1.1)
     bias = torch.log(zb / zb.sum()).cuda()
     x = torch.randn((T, D), device="cuda", generator=gen).to(torch.bfloat16)
-    ws = torch.empty(sx._lib.load().sx_moe_workspace_bytes(ctypes.byref(bank.c()), T, k), dtype=torch.uint8, device="cuda")
+    one_i = torch.zeros((T, 1), dtype=torch.int32, device="cuda")
+    one_s = torch.ones((T, 1), device="cuda")
+    L = sx._lib.load()
+    ws_sh = torch.empty(L.sx_moe_workspace_bytes(ctypes.byref(shared.c()), T, 1), dtype=torch.uint8, device="cuda")
+    ep = sx.ExpertParallel.from_process_group() if world > 1 else None
+    if ep is None:
+        ws = torch.empty(L.sx_moe_workspace_bytes(ctypes.byref(bank.c()), T, k), dtype=torch.uint8, device="cuda")
+    else:
+        ws = torch.empty(ep.workspace_bytes(bank, T, k), dtype=torch.uint8, device="cuda")
 
     def layer():
         logits = (x @ wr).float() + bias
         inds, scores = sx.router_topk(logits, k)
-        return sx.moe(x, bank, inds, scores, dec, workspace=ws)
+        sh = sx.moe(x, shared, one_i, one_s, dec, workspace=ws_sh)
+        gate = x @ wg
+        if ep is None:
+            return sx.moe(x, bank, inds, scores, dec, shared=sh, shared_gate=gate, workspace=ws)
+        return ep.moe(x, bank, E, inds, scores, dec, rows_cap=T, shared=sh, shared_gate=gate, workspace=ws)
 
     for _ in range(max(3, args.warmup)):
         layer()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     reps = max(3, args.steps)
@@ -482,53 +525,79 @@ def prefill_bench(sx, torch, args, stream, tf_peak):
     e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
-    flops = 2.0 * T * k * 3 * D * I + 2.0 * T * D * E
+    if world > 1:
+        tt = torch.tensor([ms], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    flops = world * (2.0 * T * k * 3 * D * I + 2.0 * T * 3 * D * I + 2.0 * T * D * E)
     inds, _ = sx.router_topk((x @ wr).float() + bias, k)
     counts = torch.bincount(inds.flatten().long(), minlength=E)
-    return {"tokens": T, "tokens_per_s": round(T / (ms * 1e-3), 1), "ms_per_layer": round(ms, 3),
-            "tflops": round(flops / (ms * 1e-3) / 1e12, 1), "tensor_frac_of_measured": round(flops / (ms * 1e-3) / 1e12 / tf_peak, 4),
-            "max_rows_per_expert": int(counts.max()), "active_experts": int((counts > 0).sum())}
+    res = {"tokens": world * T, "tokens_per_rank": T, "ranks": world, "tokens_per_s": round(world * T / (ms * 1e-3), 1),
+           "ms_per_layer": round(ms, 3), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+           "tensor_frac_of_measured": round(flops / (ms * 1e-3) / 1e12 / (world * tf_peak), 4),
+           "max_rows_per_expert_rank0_tokens": int(counts.max()), "active_experts": int((counts > 0).sum())}
+    if ep is not None:
+        torch.cuda.synchronize()
+        ep.destroy()
+    del ws
+    torch.cuda.empty_cache()
+    return res
 
 
 def deepseek_bench(sx, torch, args, stream, tf_peak):
-    """BASELINE configs[4] on one GPU: a DeepSeek-style FFN stack of 16 layers, hidden 7168, 256
-    routed experts of 2048 + one shared expert of 2048, top-8 sigmoid routing with a bias
-    (renormalised, x2.5).  Routed experts are STQ SPEC1 (window 15) in two rate groups, K1 (n16,
-    64 experts) and K2 (n32, 192 experts): 1.75 bits per weight on average; the group an expert
-    falls in is fixed by its id range, which is how a rate-grouped pack orders experts.  The shared
-    expert is K4 (n64), run as a one-expert layer through sx_moe.  Each layer: router, shared expert,
-    rate-grouped routed layer (sx_moe_ragged) with the shared output added, residual add.  Decode
-    batches T = 1, 8, 64 (CUDA graph of the 16 layers) and prefill T = 4096.  Random trellis words,
-    sign-only scales (the decode cost does not depend on the values); 39 GB of routed weights."""
-    H, I, E, k, L = 7168, 2048, 256, 8, 16
-    groups = ((64, 16), (192, 32))
-    gen = torch.Generator(device="cuda")
-    gen.manual_seed(4242)
+    """a DeepSeek-style FFN stack of 16 layers, hidden 7168, 256 routed
+    experts of 2048 + one shared expert of 2048, top-8 sigmoid routing with a bias (renormalised,
+    x2.5).  Routed experts are STQ SPEC1 (window 15) in two rate groups, K1 (n16, experts 0..63) and
+    K2 (n32, experts 64..255): 1.75 bits per weight on average; the group an expert falls in is
+    fixed by its id range, which is how a rate-grouped pack orders experts.  The shared expert is K4
+    (n64), run as a one-expert layer through sx_moe.  Each layer: router, shared expert,
+    rate-grouped routed layer with the shared output added, residual add.  One GPU: sx_moe_ragged
+    over all 256 experts.  N GPUs: expert parallel (sx_ep_moe_ragged), rank g holding experts
+    [g*256/N, (g+1)*256/N) as its own rate groups, every rank running the stack on its own T tokens
+    (weak scaling); router and shared expert replicated.  Decode batches T = 1, 8, 64 (CUDA graph of
+    the 16 layers) and prefill T = 4096.  Random trellis words, sign-only scales (the decode cost
+    does not depend on the values); 39 GB of routed weights over the world."""
+    import torch.distributed as dist
 
-    def proj(experts, i_f, o_f, n):
+    world, rank, _ = dist_env()
+    H, I, E, k, L = 7168, 2048, 256, 8, 16
+    K1 = 64  # experts [0, 64) are K1 (n16), the rest K2 (n32)
+    El = E // world
+    e0, e1 = rank * El, (rank + 1) * El
+    groups = [(b - a, n) for a, b, n in ((e0, min(e1, K1), 16), (max(e0, K1), e1, 32)) if b > a]
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(4242 + rank)
+    rgen = torch.Generator(device="cuda")
+    rgen.manual_seed(4243)  # router and shared expert: replicated
+
+    def proj(g, experts, i_f, o_f, n):
         tr = torch.randint(-32768, 32768, (experts, i_f // 16, o_f // 16, n), dtype=torch.int16, device="cuda",
-                           generator=gen)
-        su = (torch.randint(0, 2, (experts, i_f), device="cuda", generator=gen).half() * 2 - 1) * 0.02
-        sv = torch.randint(0, 2, (experts, o_f), device="cuda", generator=gen).half() * 2 - 1
+                           generator=g)
+        su = (torch.randint(0, 2, (experts, i_f), device="cuda", generator=g).half() * 2 - 1) * 0.02
+        sv = torch.randint(0, 2, (experts, o_f), device="cuda", generator=g).half() * 2 - 1
         return sx.Proj(tr, su, sv)
 
     layers = []
     for _ in range(L):
-        banks = [sx.Bank(proj(e, H, I, n), proj(e, H, I, n), proj(e, I, H, n)) for e, n in groups]
-        shared = sx.Bank(proj(1, H, I, 64), proj(1, H, I, 64), proj(1, I, H, 64))
-        wr = (torch.randn((H, E), device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
-        bias = torch.randn((E,), device="cuda", generator=gen) * 0.1
+        banks = [sx.Bank(proj(gen, e, H, I, n), proj(gen, e, H, I, n), proj(gen, e, I, H, n)) for e, n in groups]
+        shared = sx.Bank(proj(rgen, 1, H, I, 64), proj(rgen, 1, H, I, 64), proj(rgen, 1, I, H, 64))
+        wr = (torch.randn((H, E), device="cuda", generator=rgen) * 0.02).to(torch.bfloat16)
+        bias = torch.randn((E,), device="cuda", generator=rgen) * 0.1
         rb = sx.Ragged.from_banks(banks)
         del banks
         layers.append((rb, shared, wr, bias))
     dec = sx.Decode(sx.Codebook.SPEC1, 15, 1)  # spec1-w15: the table with rows at n = 16..128
-    res = {"layers": L, "routed_bits_per_weight": 1.75, "routed_gb": round(sum(
-        sum(t.numel() * 2 for t in rb.trellis) for rb, _, _, _ in layers) / 1e9, 2)}
+    ep = sx.ExpertParallel.from_process_group() if world > 1 else None
+    routed_gb = sum(sum(t.numel() * 2 for t in rb.trellis) for rb, _, _, _ in layers) / 1e9
+    res = {"layers": L, "ranks": world, "routed_bits_per_weight": 1.75, "routed_gb_rank0": round(routed_gb, 2),
+           "scaling": "weak (T tokens per rank)" if world > 1 else "one GPU"}
     one = torch.zeros((1, 1), dtype=torch.int32, device="cuda")
+    Lib = sx._lib.load()
     for T in (1, 8, 64, 4096):
         x0 = torch.randn((T, H), device="cuda", generator=gen).to(torch.bfloat16)
-        ws = torch.empty(max(sx._lib.load().sx_moe_ragged_workspace_bytes(ctypes.byref(layers[0][0].c()), T, k),
-                             sx._lib.load().sx_moe_workspace_bytes(ctypes.byref(layers[0][1].c()), T, 1)),
+        routed_ws = (ep.workspace_bytes(layers[0][0], T, k) if ep is not None else
+                     Lib.sx_moe_ragged_workspace_bytes(ctypes.byref(layers[0][0].c()), T, k))
+        ws = torch.empty(max(routed_ws, Lib.sx_moe_workspace_bytes(ctypes.byref(layers[0][1].c()), T, 1)),
                          dtype=torch.uint8, device="cuda")
         ones_i, ones_s = one.expand(T, 1).contiguous(), torch.ones((T, 1), device="cuda")
 
@@ -538,13 +607,19 @@ def deepseek_bench(sx, torch, args, stream, tf_peak):
                 inds, scores = sx.router_topk((x @ wr).float(), k, sx.RouterMode.SIGMOID_BIAS, bias, route_norm=True,
                                               route_scale=2.5)
                 sh = sx.moe(x, shared, ones_i, ones_s, dec, workspace=ws)
-                x = x + sx.moe_ragged(x, rb, inds, scores, dec, shared=sh, workspace=ws)
+                if ep is None:
+                    x = x + sx.moe_ragged(x, rb, inds, scores, dec, shared=sh, workspace=ws)
+                else:
+                    x = x + ep.moe(x, rb, E, inds, scores, dec, rows_cap=T, shared=sh, workspace=ws)
             return x
 
         for _ in range(2):
             stack()
         torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0_, e1_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         rounds = max(2, args.steps)
         if T <= 64:
             g = torch.cuda.CUDAGraph()
@@ -552,24 +627,34 @@ def deepseek_bench(sx, torch, args, stream, tf_peak):
                 stack()
             g.replay()
             torch.cuda.synchronize()
-            e0.record(stream)
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            e0_.record(stream)
             for _ in range(rounds):
                 g.replay()
-            e1.record(stream)
+            e1_.record(stream)
             torch.cuda.synchronize()
             del g
         else:
-            e0.record(stream)
+            e0_.record(stream)
             for _ in range(rounds):
                 stack()
-            e1.record(stream)
+            e1_.record(stream)
             torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / rounds
-        flops = 2.0 * T * L * (k + 1) * 3 * H * I
-        res[f"T{T}"] = {"tokens_per_s": round(T / (ms * 1e-3), 1), "ms_per_stack": round(ms, 3),
+        ms = e0_.elapsed_time(e1_) / rounds
+        if world > 1:
+            tt = torch.tensor([ms], device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms = float(tt.item())
+        flops = world * 2.0 * T * L * (k + 1) * 3 * H * I
+        res[f"T{T}"] = {"tokens_per_s": round(world * T / (ms * 1e-3), 1), "ms_per_stack": round(ms, 3),
                         "tflops": round(flops / (ms * 1e-3) / 1e12, 1)}
         del ws
     assert sx.device_error() == 0
+    if ep is not None:
+        torch.cuda.synchronize()
+        ep.destroy()
     del layers
     torch.cuda.empty_cache()
     return res

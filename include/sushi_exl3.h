@@ -316,6 +316,18 @@ sx_status sx_ep_moe(sx_ep* ep, sx_stream stream, const sx_bank* local_bank, int3
                     const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
                     const void* shared_gate, int32_t clamp_limit, void* y, void* workspace, size_t workspace_bytes);
 
+/* sx_ep_moe over a rate-grouped local layer (rate_groups.Ragged, src/exl3/rate_groups.zig:23-130;
+ * root.moeRagged, src/exl3/root.zig:582): `local` holds this rank's experts_total/world experts
+ * (local->experts), in rate groups as sx_moe_ragged takes them; everything else as sx_ep_moe.
+ * Ranks may hold different rates (a rank's experts are a contiguous id range of the layer). */
+size_t sx_ep_ragged_workspace_bytes(const sx_ep* ep, const sx_ragged* local, int32_t rows_cap, int32_t topk,
+                                    sx_dtype dtype);
+sx_status sx_ep_moe_ragged(sx_ep* ep, sx_stream stream, const sx_ragged* local, int32_t experts_total,
+                           const sx_decode* dec, const void* x, sx_dtype dtype, int32_t rows, int32_t rows_cap,
+                           const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
+                           const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
+                           size_t workspace_bytes);
+
 /* The communicator's world size and rank (either pointer may be null). */
 sx_status sx_ep_info(const sx_ep* ep, int32_t* world, int32_t* rank);
 

@@ -201,9 +201,10 @@ struct EpWs {
     size_t moe_bytes;
 };
 
-EpWs ep_ws_layout(const sx_bank* bank, int world, int cap, int K, int esz) {
+// The layout for a local layer of `ng` rate groups (one for a uniform bank) over El experts.
+EpWs ep_ws_layout(const MoeGroup* g, int ng, int El, int world, int cap, int K, int esz) {
     EpWs w{};
-    const int D = bank->gate.in_features;
+    const int D = g[0].bank.gate.in_features;
     const size_t places = (size_t)world * cap;
     size_t off = 0;
     w.list = off; off = up(off + places * sizeof(int));
@@ -218,7 +219,7 @@ EpWs ep_ws_layout(const sx_bank* bank, int world, int cap, int K, int esz) {
     w.part_recv = off; off = up(off + places * D * sizeof(float));
     // a rank receives about rows_cap * K valid slots (every rank's rows_cap rows, K slots each,
     // spread over the world): that, not the places' sentinel-padded slots, picks its expert path
-    w.moe_bytes = moe_workspace_bytes(bank, (int32_t)places, K, (long long)cap * K);
+    w.moe_bytes = moe_groups_ws(g, ng, El, (int32_t)places, K, (long long)cap * K);
     w.moe = off; off = up(off + w.moe_bytes);
     w.total = off;
     return w;
@@ -326,28 +327,43 @@ sx_status sx_ep_info(const sx_ep* ep, int32_t* world, int32_t* rank) {
 size_t sx_ep_workspace_bytes(const sx_ep* ep, const sx_bank* local_bank, int32_t rows_cap, int32_t topk,
                              sx_dtype dtype) {
     if (!ep || !local_bank || rows_cap < 1 || topk < 1 || !dtype_ok(dtype)) return 0;
-    return ep_ws_layout(local_bank, ep->world, rows_cap, topk, (int)dtype_size(dtype)).total;
+    const MoeGroup g{*local_bank, 0};
+    return ep_ws_layout(&g, 1, local_bank->gate.experts, ep->world, rows_cap, topk, (int)dtype_size(dtype)).total;
 }
 
-sx_status sx_ep_moe(sx_ep* ep, sx_stream stream, const sx_bank* local_bank, int32_t experts_total,
-                    const sx_decode* dec, const void* x, sx_dtype dtype, int32_t rows, int32_t rows_cap,
-                    const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
-                    const void* shared_gate, int32_t clamp_limit, void* y, void* workspace, size_t workspace_bytes) {
-    if (!ep || !local_bank) return SX_ERR_NULL_POINTER;
+size_t sx_ep_ragged_workspace_bytes(const sx_ep* ep, const sx_ragged* local, int32_t rows_cap, int32_t topk,
+                                    sx_dtype dtype) {
+    if (!ep || !local || rows_cap < 1 || topk < 1 || !dtype_ok(dtype)) return 0;
+    MoeGroup g[kMaxGroups];
+    int ng = 0;
+    if (ragged_groups(local, g, &ng) != SX_OK) return 0;
+    return ep_ws_layout(g, ng, local->experts, ep->world, rows_cap, topk, (int)dtype_size(dtype)).total;
+}
+
+}  // extern "C"
+
+namespace sx {
+namespace {
+
+// sx_ep_moe over the local layer's rate groups (one group for a uniform bank) of El experts.
+sx_status ep_moe_groups(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int ng, int El, int32_t experts_total,
+                        const sx_decode* dec, const void* x, sx_dtype dtype, int32_t rows, int32_t rows_cap,
+                        const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
+                        const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
+                        size_t workspace_bytes) {
     if (rows > 0 && (!x || !inds || !scores || !y)) return SX_ERR_NULL_POINTER;
     if (shared_gate && !shared) return SX_ERR_NULL_POINTER;
     if (rows < 0 || rows_cap < 1 || rows > rows_cap || topk < 1) return SX_ERR_BAD_SHAPE;
     if (topk > 32) return SX_ERR_TOPK_EXCEEDS_REDUCE_BANK;
     if (!dtype_ok(dtype)) return SX_ERR_BAD_DTYPE;
     if (clamp_limit < 0 || clamp_limit > 128) return SX_ERR_INVALID_CLAMP;
-    const int El = local_bank->gate.experts;
     if (El < 1 || (long long)El * ep->world != experts_total) return SX_ERR_BAD_SHAPE;
     if (topk > experts_total) return SX_ERR_TOPK_EXCEEDS_EXPERTS;
-    const int D = local_bank->gate.in_features;
+    const int D = groups[0].bank.gate.in_features;
     if (D % 128) return SX_ERR_BAD_SHAPE;
     if (reinterpret_cast<uintptr_t>(x) % 16) return SX_ERR_BAD_SHAPE;  // rows move as 16-byte vectors
     const int esz = (int)dtype_size(dtype);
-    const EpWs L = ep_ws_layout(local_bank, ep->world, rows_cap, topk, esz);
+    const EpWs L = ep_ws_layout(groups, ng, El, ep->world, rows_cap, topk, esz);
     if (!workspace || workspace_bytes < L.total) return SX_ERR_WORKSPACE_TOO_SMALL;
     if (!nccl().ok) return nccl_missing();
 
@@ -390,9 +406,9 @@ sx_status sx_ep_moe(sx_ep* ep, sx_stream stream, const sx_bank* local_bank, int3
 
     // 4. the local experts over every received row, partials in f32
     float* part_send = reinterpret_cast<float*>(ws + L.part_send);
-    st = moe_impl(stream, local_bank, dec, ws + L.recv_x, dtype, (int32_t)places,
-                  reinterpret_cast<const uint32_t*>(ws + L.recv_inds), reinterpret_cast<const float*>(ws + L.recv_scores),
-                  topk, nullptr, nullptr, clamp_limit, nullptr, ws + L.moe, L.moe_bytes, part_send, (long long)C * topk);
+    st = moe_run(stream, groups, ng, El, dec, ws + L.recv_x, dtype, (int32_t)places,
+                 reinterpret_cast<const uint32_t*>(ws + L.recv_inds), reinterpret_cast<const float*>(ws + L.recv_scores),
+                 topk, nullptr, nullptr, clamp_limit, nullptr, ws + L.moe, L.moe_bytes, part_send, (long long)C * topk);
     if (st) return st;
 
     // 5. combine: partials back to the rows' owners
@@ -414,6 +430,35 @@ sx_status sx_ep_moe(sx_ep* ep, sx_stream stream, const sx_bank* local_bank, int3
     c.xdt = dtype;
     ep_combine_kernel<<<rows, 256, 0, s>>>(c);
     return cuda_status(cudaGetLastError(), "ep combine launch");
+}
+
+}  // namespace
+}  // namespace sx
+
+extern "C" {
+
+sx_status sx_ep_moe(sx_ep* ep, sx_stream stream, const sx_bank* local_bank, int32_t experts_total,
+                    const sx_decode* dec, const void* x, sx_dtype dtype, int32_t rows, int32_t rows_cap,
+                    const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
+                    const void* shared_gate, int32_t clamp_limit, void* y, void* workspace, size_t workspace_bytes) {
+    if (!ep || !local_bank) return SX_ERR_NULL_POINTER;
+    const MoeGroup g{*local_bank, 0};
+    return ep_moe_groups(ep, stream, &g, 1, local_bank->gate.experts, experts_total, dec, x, dtype, rows, rows_cap,
+                         inds, scores, topk, shared, shared_gate, clamp_limit, y, workspace, workspace_bytes);
+}
+
+sx_status sx_ep_moe_ragged(sx_ep* ep, sx_stream stream, const sx_ragged* local, int32_t experts_total,
+                           const sx_decode* dec, const void* x, sx_dtype dtype, int32_t rows, int32_t rows_cap,
+                           const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
+                           const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
+                           size_t workspace_bytes) {
+    if (!ep || !local) return SX_ERR_NULL_POINTER;
+    MoeGroup g[kMaxGroups];
+    int ng = 0;
+    const sx_status st = ragged_groups(local, g, &ng);
+    if (st) return st;
+    return ep_moe_groups(ep, stream, g, ng, local->experts, experts_total, dec, x, dtype, rows, rows_cap, inds, scores,
+                         topk, shared, shared_gate, clamp_limit, y, workspace, workspace_bytes);
 }
 
 }  // extern "C"

@@ -35,4 +35,20 @@ sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, 
                    float* partial, long long slots);
 size_t moe_workspace_bytes(const sx_bank* bank, int32_t rows, int32_t topk, long long slots);
 
+// One rate group of a routed layer: its experts are ids [e_lo, e_lo + bank.experts) of the layer.
+struct MoeGroup {
+    sx_bank bank;
+    int e_lo;
+};
+constexpr int kMaxGroups = 32;  // layout.max_groups (src/exl3/layout.zig:4)
+
+// moe_impl over the rate groups of a layer of Etot experts (sx_moe_ragged's body).
+sx_status moe_run(sx_stream stream, const MoeGroup* groups, int ng, int Etot, const sx_decode* dec, const void* x,
+                  sx_dtype dtype, int32_t rows, const uint32_t* inds, const float* scores, int32_t topk,
+                  const void* shared, const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
+                  size_t workspace_bytes, float* partial, long long slots);
+size_t moe_groups_ws(const MoeGroup* g, int ng, int Etot, int rows, int topk, long long slots);
+// The groups of a ragged layer (at most kMaxGroups) from its host meta table.
+sx_status ragged_groups(const sx_ragged* rb, MoeGroup* out, int* ng);
+
 }  // namespace sx

@@ -294,12 +294,6 @@ using namespace sx;
 
 namespace sx {
 
-// One rate group of a routed layer: its experts are ids [e_lo, e_lo + bank.experts) of the layer.
-struct MoeGroup {
-    sx_bank bank;
-    int e_lo;
-};
-
 // The valid slots a group can expect: its share of the layer's experts.
 long long group_slots(long long slots, int rows, int topk, int Eg, int Etot) {
     const long long base = slots > 0 ? slots : (long long)rows * topk;
@@ -546,10 +540,8 @@ extern "C" sx_status sx_moe(sx_stream stream, const sx_bank* bank, const sx_deco
 }
 
 namespace sx {
-namespace {
 
 constexpr int kMetaWords = 8;  // rate_groups.META_WORDS (src/exl3/rate_groups.zig:25)
-constexpr int kMaxGroups = 32;  // layout.max_groups (src/exl3/layout.zig:4)
 
 // The groups of a ragged layer from its host meta table: runs of consecutive experts with one group
 // id, one rate per projection, and tiles at the stride of that rate.
@@ -591,7 +583,6 @@ sx_status ragged_groups(const sx_ragged* rb, MoeGroup* out, int* ng) {
     return SX_OK;
 }
 
-}  // namespace
 }  // namespace sx
 
 extern "C" size_t sx_moe_ragged_workspace_bytes(const sx_ragged* bank, int32_t rows, int32_t topk) {

@@ -491,13 +491,17 @@ class ExpertParallel:
 
         return cls(share_unique_id(group), dist.get_world_size(group), dist.get_rank(group))
 
-    def workspace_bytes(self, local_bank: "Bank", rows_cap: int, topk: int, dtype=torch.bfloat16) -> int:
+    def workspace_bytes(self, local_bank, rows_cap: int, topk: int, dtype=torch.bfloat16) -> int:
+        """Workspace bytes for a local Bank (sx_ep_workspace_bytes) or Ragged layer
+        (sx_ep_ragged_workspace_bytes)."""
         b = local_bank.c()
-        return int(lib().sx_ep_workspace_bytes(self._h, ctypes.byref(b), int(rows_cap), int(topk), _DT[dtype]))
+        fn = lib().sx_ep_ragged_workspace_bytes if isinstance(local_bank, Ragged) else lib().sx_ep_workspace_bytes
+        return int(fn(self._h, ctypes.byref(b), int(rows_cap), int(topk), _DT[dtype]))
 
-    def moe(self, x, local_bank: "Bank", experts_total: int, inds, scores, dec: Decode, rows_cap: int,
+    def moe(self, x, local_bank, experts_total: int, inds, scores, dec: Decode, rows_cap: int,
             shared=None, shared_gate=None, clamp_limit=0, workspace=None):
-        """sx_ep_moe: this rank's rows x [rows, D] with GLOBAL expert ids inds [rows, K]; every rank
+        """sx_ep_moe (local_bank a Bank) or sx_ep_moe_ragged (a Ragged layer of this rank's
+        experts): this rank's rows x [rows, D] with GLOBAL expert ids inds [rows, K]; every rank
         calls it with the same rows_cap, K, experts_total and dtype.  Returns y [rows, D]."""
         x2 = x.reshape(-1, x.shape[-1]).contiguous()
         rows = x2.shape[0]
@@ -508,8 +512,11 @@ class ExpertParallel:
         topk = ix.shape[1]
         if sc.shape != ix.shape:
             raise Exl3Error(1)
+        ragged = isinstance(local_bank, Ragged)
         b = local_bank.c()
         need = self.workspace_bytes(local_bank, rows_cap, topk, x2.dtype)
+        if need == 0 and ragged:
+            raise Exl3Error(19)
         if workspace is None:
             if self._ws is None or self._ws.numel() < need:
                 self._ws = torch.empty(max(need, 1), dtype=torch.uint8, device=x2.device)
@@ -520,10 +527,11 @@ class ExpertParallel:
         d = dec.c()
         sh = None if shared is None else shared.reshape(rows, -1).to(x2.dtype).contiguous()
         sg = None if shared_gate is None else shared_gate.reshape(rows).to(x2.dtype).contiguous()
-        _check(lib().sx_ep_moe(self._h, _stream(), ctypes.byref(b), int(experts_total), ctypes.byref(d), x2.data_ptr(),
-                               _DT[x2.dtype], rows, int(rows_cap), ix.data_ptr(), sc.data_ptr(), topk,
-                               None if sh is None else sh.data_ptr(), None if sg is None else sg.data_ptr(),
-                               int(clamp_limit), y.data_ptr(), ws.data_ptr(), ws.numel()))
+        fn = lib().sx_ep_moe_ragged if ragged else lib().sx_ep_moe
+        _check(fn(self._h, _stream(), ctypes.byref(b), int(experts_total), ctypes.byref(d), x2.data_ptr(),
+                  _DT[x2.dtype], rows, int(rows_cap), ix.data_ptr(), sc.data_ptr(), topk,
+                  None if sh is None else sh.data_ptr(), None if sg is None else sg.data_ptr(),
+                  int(clamp_limit), y.data_ptr(), ws.data_ptr(), ws.numel()))
         return y.reshape(x.shape)
 
     def destroy(self):

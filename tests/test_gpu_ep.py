@@ -111,6 +111,47 @@ def test_ep_refusals(sx):
         ep.destroy()
 
 
+def _ragged_np(seed, D, I):
+    """A two-rate layer as the DeepSeek config's routed experts: 6 experts at K1 (n16), 10 at K2."""
+    return [(_bank_np(seed, 6, D, I, 16), 16), (_bank_np(seed + 10, 10, D, I, 32), 32)]
+
+
+def _ragged_slice(sx, groups, e0, e1):
+    """The Ragged layer of experts [e0, e1) of a grouped layer (groups cut at the range's ends)."""
+    banks, lo = [], 0
+    for bank_np, _ in groups:
+        E = bank_np[0][0].shape[0]
+        a, b = max(e0, lo), min(e1, lo + E)
+        if a < b:
+            banks.append(_bank(sx, bank_np, a - lo, b - lo))
+        lo += E
+    return sx.Ragged.from_banks(banks)
+
+
+@pytest.mark.parametrize("T", [3, 40])
+def test_ep_ragged_world1_is_bit_identical_to_moe_ragged(sx, T):
+    """sx_ep_moe_ragged over a world of one: the same bits as sx_moe_ragged (T=40 takes the
+    decode chain per group in both)."""
+    D, I, k = 256, 128, 4
+    groups = _ragged_np(300 + T, D, I)
+    _, dec = dec_args(orc.CB_SPEC1, 15)  # spec1-w15: the table with K1 rows
+    rb = _ragged_slice(sx, groups, 0, 16)
+    xt = torch.from_numpy(synth.activations(T + 1, T, D)).cuda().to(torch.bfloat16)
+    inds, wts = _route(T + 2, T, 16, k)
+    ii, ww = torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda()
+    shared = torch.randn((T, D), device="cuda").to(torch.bfloat16)
+    ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0)
+    try:
+        for kw in ({}, {"shared": shared}):
+            want = sx.moe_ragged(xt, rb, ii, ww, dec, **kw)
+            got = ep.moe(xt, rb, 16, ii, ww, dec, rows_cap=T, **kw)
+            torch.cuda.synchronize()
+            assert torch.equal(want, got), kw
+        assert sx.device_error() == 0
+    finally:
+        ep.destroy()
+
+
 # ------------------------------------------------------------------ two GPUs
 def _rank_main(rank, world, port, out_dir):
     import torch.distributed as dist
@@ -173,3 +214,52 @@ def test_ep_two_gpus_match_single_gpu(tmp_path):
                 truth[r] += wts[r, j] * orc.expert_truth(dense, x[r])
         assert max_rel(got, truth) <= MAX_REL_TOL
         assert rel_rms(got, truth) <= REL_RMS_TOL
+
+
+def _ragged_rank_main(rank, world, port, out_dir):
+    import torch.distributed as dist
+
+    import sushi_b200 as sx
+
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        D, I, k, T = 256, 128, 4, 9 + 4 * rank
+        groups = _ragged_np(777, D, I)
+        _, dec = dec_args(orc.CB_MCG, 16)
+        El = 16 // world
+        local = _ragged_slice(sx, groups, rank * El, (rank + 1) * El)  # rank 0: K1 and K2 experts; rank 1: K2
+        full = _ragged_slice(sx, groups, 0, 16)
+        xt = torch.from_numpy(synth.activations(80 + rank, T, D)).cuda().to(torch.bfloat16)
+        inds, wts = _route(90 + rank, T, 16, k)
+        ii, ww = torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda()
+        ep = sx.ExpertParallel.from_process_group()
+        got = to_f32(ep.moe(xt, local, 16, ii, ww, dec, rows_cap=16))
+        torch.cuda.synchronize()
+        ep.destroy()
+        want = to_f32(sx.moe_ragged(xt, full, ii, ww, dec))
+        np.save(os.path.join(out_dir, f"got{rank}.npy"), got)
+        np.save(os.path.join(out_dir, f"want{rank}.npy"), want)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_ragged_two_gpus_match_single_gpu(tmp_path):
+    """A rate-grouped layer split over two GPUs whose local layers differ (rank 0 holds K1 and K2
+    experts, rank 1 only K2): each rank's rows match sx_moe_ragged over the full layer to the last
+    bf16 bit (rank-order versus k-order sums)."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.start_processes(_ragged_rank_main, args=(2, port, str(tmp_path)), nprocs=2, start_method="spawn", join=True)
+    for rank in range(2):
+        got = np.load(tmp_path / f"got{rank}.npy")
+        want = np.load(tmp_path / f"want{rank}.npy")
+        assert np.isfinite(got).all()
+        assert np.abs(got - want).max() <= 2 ** -7 * np.abs(want).max(), rank
