@@ -14,6 +14,8 @@
 
 #include <cooperative_groups.h>
 
+#include <type_traits>
+
 #include "sx_decode.cuh"
 
 namespace sx {
@@ -34,6 +36,17 @@ struct CoreLayout {
     size_t stages, bfrag, red, bars, total;
 };
 
+// Bytes of one lane's B-fragment entry (four inputs of one row): 16 with each f16 stored twice, as
+// the doubled-k MMA reads it; 8 in the compact form of the two-row-group (9..16 rows) kernels,
+// where the duplicates are made at load time by byte permutes, so that a CTA's input slice for
+// 16 rows takes half the shared memory and two CTAs fit on an SM.
+template <int NB>
+struct BFrag {
+    static constexpr bool COMPACT = NB == 2;
+    static constexpr int BYTES = COMPACT ? 8 : 16;
+    using Entry = std::conditional_t<COMPACT, uint2, uint4>;
+};
+
 // Shared memory of one CTA: the stage ring, the B fragments of kbl_max input blocks per
 // projection (each projection prepares the input with its own suh) for mg rows per 8-row group
 // (mg = min(8, rows); the lanes of later rows read row mg-1's), the NP x (8*NB) x 128 f32
@@ -45,7 +58,7 @@ __host__ __device__ inline CoreLayout core_layout(int kbl_max, int mg = 8) {
     L.stages = off;
     off += (size_t)Ring<N, NP>::NST * Ring<N, NP>::STAGE_BYTES;
     L.bfrag = off;
-    off += (size_t)NP * kbl_max * 8 * NB * mg * 4 * 16;
+    off += (size_t)NP * kbl_max * 8 * NB * mg * 4 * BFrag<NB>::BYTES;
     L.red = off;
     off += (size_t)NP * NB * 8 * 128 * 4;
     L.bars = off;
@@ -56,8 +69,8 @@ __host__ __device__ inline CoreLayout core_layout(int kbl_max, int mg = 8) {
 
 struct CoreSmem {
     uint8_t* stages;
-    uint4* bfrag;          // [NP][kbl_max][8][NB][mg][4]
-    int bfrag_proj_stride; // uint4 elements between projections
+    uint4* bfrag;          // [NP][kbl_max][8][NB][mg][4] entries of BFrag<NB>::BYTES
+    int bfrag_proj_stride; // entries between projections
     int mg;                // fragment rows per 8-row group
     float* red;
     uint64_t* full;
@@ -128,8 +141,20 @@ __device__ __forceinline__ void bfrag_put(uint4* bfrag, int mg, int kbi, int m, 
     const int tk = pos >> 4, r = pos & 15;
     const int c = (r & 7) >> 1;
     const int slot = ((r >> 3) << 1) | (r & 1);
-    uint32_t* dst = reinterpret_cast<uint32_t*>(&bfrag[(((kbi * 8 + tk) * NB + nb) * mg + gg) * 4 + c]);
-    dst[slot] = (uint32_t)h | ((uint32_t)h << 16);
+    const size_t entry = (size_t)((((kbi * 8 + tk) * NB + nb) * mg + gg) * 4 + c);
+    if constexpr (BFrag<NB>::COMPACT) {
+        reinterpret_cast<uint16_t*>(bfrag)[entry * 4 + slot] = h;
+    } else {
+        reinterpret_cast<uint32_t*>(&bfrag[entry])[slot] = (uint32_t)h | ((uint32_t)h << 16);
+    }
+}
+
+// A B-fragment entry as the four doubled-k B registers (inputs 2c, 2c+1, 2c+8, 2c+9, each f16 in
+// both halves).
+__device__ __forceinline__ uint4 bfrag_expand(uint4 v) { return v; }
+__device__ __forceinline__ uint4 bfrag_expand(uint2 u) {
+    return make_uint4(__byte_perm(u.x, 0, 0x1010), __byte_perm(u.x, 0, 0x3232), __byte_perm(u.y, 0, 0x1010),
+                      __byte_perm(u.y, 0, 0x3232));
 }
 
 // Named barrier 1 over the CW consumer warps only.
@@ -177,14 +202,16 @@ __device__ __forceinline__ bool core_consume(const CoreSmem& s, int kbl, const D
                 const uint32_t* base = reinterpret_cast<const uint32_t*>(s.stages + (size_t)st * Ring<N, NP>::STAGE_BYTES +
                                                                          p * Ring<N, NP>::PROJ_BYTES) +
                                        (tr0 * 8 + ot) * TILE_WORDS;
-                const uint4* bf = s.bfrag + p * s.bfrag_proj_stride + (size_t)(i * 8 + tr0) * NB * s.mg * 4 + bf_lane;
+                using BE = typename BFrag<NB>::Entry;
+                const BE* bf = reinterpret_cast<const BE*>(s.bfrag) + p * s.bfrag_proj_stride +
+                               (size_t)(i * 8 + tr0) * NB * s.mg * 4 + bf_lane;
 #pragma unroll
                 for (int j = 0; j < TPW; j++) {
                     uint32_t a1[4], a2[4];
                     decode_lane_mma<KIND, N, W16>(base + j * 8 * TILE_WORDS, lf, dp[p], a1, a2);
 #pragma unroll
                     for (int nb = 0; nb < NB; nb++) {
-                        const uint4 b = bf[(j * NB + nb) * s.mg * 4];
+                        const uint4 b = bfrag_expand(bf[(j * NB + nb) * s.mg * 4]);
                         float(&d)[4] = (j & 1) ? acc2[p][nb] : acc[p][nb];
                         mma16816(d, a1[0], a1[1], a1[2], a1[3], b.x, b.y);
                         mma16816(d, a2[0], a2[1], a2[2], a2[3], b.z, b.w);

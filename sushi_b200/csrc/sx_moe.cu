@@ -13,18 +13,70 @@ cudaError_t moe_launch_kind(const MoeArgs& a, int n_gu, int n_d, int S_gu, int S
 
 namespace {
 
+// A plain (non-cluster) launch with programmatic dependent launch allowed.
+template <typename Kern>
+cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, const MoeArgs& a) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
 // ------------------------------------------------------------------ 1. routing metadata
-// One CTA: the slots' expert histogram, a warp scan, and the scatter of slots into expert order.
-// Work items: experts with fewer than big_min rows are cut into chunks of `chunk` rows (list 1,
-// meta[0] items); larger ones into chunks of big_chunk rows (list 2, meta[1] items), so that the
-// tensor-core path can reuse each decoded weight chunk over four row tiles.  meta[2] = slots.
+// Exclusive block-wide scan of four counters (1024 threads); `tot` receives the block's sums.
+// Every thread of the block calls it.
+__device__ __forceinline__ int4 block_scan4(int4 v, int4* wsum, int4& tot) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int4 inc = v;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+        const int tx = __shfl_up_sync(0xffffffffu, inc.x, m), ty = __shfl_up_sync(0xffffffffu, inc.y, m);
+        const int tz = __shfl_up_sync(0xffffffffu, inc.z, m), tw = __shfl_up_sync(0xffffffffu, inc.w, m);
+        if (lane >= m) inc.x += tx, inc.y += ty, inc.z += tz, inc.w += tw;
+    }
+    if (lane == 31) wsum[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        int4 w = lane < nw ? wsum[lane] : make_int4(0, 0, 0, 0);
+#pragma unroll
+        for (int m = 1; m < 32; m <<= 1) {
+            const int tx = __shfl_up_sync(0xffffffffu, w.x, m), ty = __shfl_up_sync(0xffffffffu, w.y, m);
+            const int tz = __shfl_up_sync(0xffffffffu, w.z, m), tw = __shfl_up_sync(0xffffffffu, w.w, m);
+            if (lane >= m) w.x += tx, w.y += ty, w.z += tz, w.w += tw;
+        }
+        if (lane < nw) wsum[lane] = w;
+    }
+    __syncthreads();
+    const int4 pre = warp > 0 ? wsum[warp - 1] : make_int4(0, 0, 0, 0);
+    tot = wsum[nw - 1];
+    __syncthreads();  // wsum is reused by the next call
+    return make_int4(pre.x + inc.x - v.x, pre.y + inc.y - v.y, pre.z + inc.z - v.z, pre.w + inc.w - v.w);
+}
+
+// One CTA: the slots' expert histogram, a block-wide scan over the experts, and the scatter of
+// slots into expert order.  Work items: experts with fewer than big_min rows are cut into chunks
+// of `chunk` rows (list 1, meta[0] items, one record each: expert, first sorted position, rows);
+// larger ones into chunks of big_chunk rows (list 2, meta[1] items), so that the tensor-core path
+// can reuse each decoded weight chunk over four row tiles.  meta[2] = slots.  With chunk 8 (the
+// decode chain) each list-1 item also lists its rows' slot ids.
 __global__ void __launch_bounds__(1024) route_prep_kernel(MoeArgs a) {
     extern __shared__ int rp[];
     int* cnt = rp;             // [E]
-    int* off = rp + a.E;       // [E]
+    int* off = rp + a.E;       // [E] first sorted position
+    int* wb = rp + 2 * a.E;    // [E] first list-1 item
+    __shared__ int4 wsum[32];
     const int tid = threadIdx.x;
     const int RK = a.R * a.K;
+    grid_launch_dependents();
     for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;
+    grid_dependency_wait();  // the routing comes from the previous kernel
     __syncthreads();
     // Warp-aggregated counting: lanes holding the same expert add once (a hot expert would
     // otherwise serialise thousands of atomics on one shared-memory word).
@@ -36,63 +88,37 @@ __global__ void __launch_bounds__(1024) route_prep_kernel(MoeArgs a) {
         if (valid && (tid & 31) == __ffs(peers) - 1) atomicAdd(&cnt[e], __popc(peers));
     }
     __syncthreads();
-    if (tid < 32) {
-        const int lane = tid;
-        const int per = (a.E + 31) / 32;
-        const int e0 = lane * per, e1 = min(a.E, e0 + per);
-        auto items1 = [&](int c) { return c >= a.big_min ? 0 : (c + a.chunk - 1) / a.chunk; };
-        auto items2 = [&](int c) { return c >= a.big_min ? (c + a.big_chunk - 1) / a.big_chunk : 0; };
-        int s_sum = 0, a_sum = 0, w_sum = 0, v_sum = 0;
-        for (int e = e0; e < e1; e++) {
-            s_sum += cnt[e];
-            a_sum += cnt[e] > 0;
-            w_sum += items1(cnt[e]);
-            v_sum += items2(cnt[e]);
-        }
-        int s_ex = s_sum, a_ex = a_sum, w_ex = w_sum, v_ex = v_sum;
-#pragma unroll
-        for (int m = 1; m < 32; m <<= 1) {
-            const int ts = __shfl_up_sync(0xffffffffu, s_ex, m);
-            const int ta = __shfl_up_sync(0xffffffffu, a_ex, m);
-            const int tw = __shfl_up_sync(0xffffffffu, w_ex, m);
-            const int tv = __shfl_up_sync(0xffffffffu, v_ex, m);
-            if (lane >= m) {
-                s_ex += ts;
-                a_ex += ta;
-                w_ex += tw;
-                v_ex += tv;
+    auto items1 = [&](int c) { return c >= a.big_min ? 0 : (c + a.chunk - 1) / a.chunk; };
+    auto items2 = [&](int c) { return c >= a.big_min ? (c + a.big_chunk - 1) / a.big_chunk : 0; };
+    int4 carry = make_int4(0, 0, 0, 0);  // slots, active experts, list-1 items, list-2 items
+    for (int base = 0; base < a.E; base += blockDim.x) {
+        const int e = base + tid;
+        const int c = e < a.E ? cnt[e] : 0;
+        int4 tot;
+        const int4 ex = block_scan4(make_int4(c, c > 0, items1(c), items2(c)), wsum, tot);
+        if (c > 0) {
+            const int s0 = carry.x + ex.x, ai = carry.y + ex.y, w0 = carry.z + ex.z, v0 = carry.w + ex.w;
+            off[e] = s0;
+            wb[e] = w0;
+            a.act_expert[ai] = e;
+            a.act_start[ai] = s0;
+            a.act_count[ai] = c;
+            for (int ch = 0; ch < items1(c); ch++) {
+                a.work_act[w0 + ch] = ai;
+                a.work_chunk[w0 + ch] = ch;
+                a.work_rec[w0 + ch] = make_int4(e, s0 + ch * a.chunk, min(a.chunk, c - ch * a.chunk), 0);
+            }
+            for (int ch = 0; ch < items2(c); ch++) {
+                a.work_act4[v0 + ch] = ai;
+                a.work_chunk4[v0 + ch] = ch;
             }
         }
-        s_ex -= s_sum;
-        a_ex -= a_sum;
-        w_ex -= w_sum;
-        v_ex -= v_sum;
-        for (int e = e0; e < e1; e++) {
-            const int c = cnt[e];
-            off[e] = s_ex;
-            if (c > 0) {
-                a.act_expert[a_ex] = e;
-                a.act_start[a_ex] = s_ex;
-                a.act_count[a_ex] = c;
-                for (int ch = 0; ch < items1(c); ch++) {
-                    a.work_act[w_ex + ch] = a_ex;
-                    a.work_chunk[w_ex + ch] = ch;
-                }
-                for (int ch = 0; ch < items2(c); ch++) {
-                    a.work_act4[v_ex + ch] = a_ex;
-                    a.work_chunk4[v_ex + ch] = ch;
-                }
-                a_ex++;
-                w_ex += items1(c);
-                v_ex += items2(c);
-            }
-            s_ex += c;
-        }
-        if (lane == 31) {
-            a.meta[0] = w_ex;
-            a.meta[1] = v_ex;
-            a.meta[2] = s_ex;
-        }
+        carry.x += tot.x, carry.y += tot.y, carry.z += tot.z, carry.w += tot.w;
+    }
+    if (tid == 0) {
+        a.meta[0] = carry.z;
+        a.meta[1] = carry.w;
+        a.meta[2] = carry.x;
     }
     __syncthreads();
     for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;  // reused as cursors
@@ -111,6 +137,7 @@ __global__ void __launch_bounds__(1024) route_prep_kernel(MoeArgs a) {
             const int pos = base + __popc(peers & ((1u << lane) - 1u));
             a.order[off[e] + pos] = s;
             a.sorted_e[off[e] + pos] = (int)e;
+            if (a.chunk == 8 && pos < a.big_min) a.work_slots[(wb[e] + pos / 8) * 8 + pos % 8] = s;
         }
     }
 }
@@ -120,7 +147,7 @@ size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 struct MoeWs {
     size_t meta, act_expert, act_start, act_count, work_act, work_chunk, work_act4, work_chunk4, order, sorted_e, hprep,
-        yslot, tg, tu, gf, uf, total;
+        yslot, tg, tu, gf, uf, work_rec, work_slots, total;
     int A_max, W_max, W4_max, chunk, big_min, big_chunk;
     bool gemm;
 };
@@ -159,6 +186,8 @@ MoeWs moe_ws_layout(int E, int R, int K, int D, int I, int n_gu, int n_d, long l
     w.act_count = off; off = align_up(off + (size_t)w.A_max * sizeof(int));
     w.work_act = off; off = align_up(off + (size_t)w.W_max * sizeof(int));
     w.work_chunk = off; off = align_up(off + (size_t)w.W_max * sizeof(int));
+    w.work_rec = off; off = align_up(off + (size_t)w.W_max * sizeof(int4));
+    w.work_slots = off; off = align_up(off + (size_t)(w.gemm ? 1 : w.W_max * 8) * sizeof(int));
     w.work_act4 = off; off = align_up(off + (size_t)std::max(1, w.W4_max) * sizeof(int));
     w.work_chunk4 = off; off = align_up(off + (size_t)std::max(1, w.W4_max) * sizeof(int));
     w.order = off; off = align_up(off + (size_t)RK * sizeof(int));
@@ -177,38 +206,45 @@ MoeWs moe_ws_layout(int E, int R, int K, int D, int I, int n_gu, int n_d, long l
     return w;
 }
 
-__global__ void __launch_bounds__(256) moe_reduce_kernel(MoeArgs a) {
+// Per token and 512-wide block of the output (128 threads, four outputs each): the token's slots
+// in k order summed, rounded, plus the shared expert; or the unrounded f32 partial.
+constexpr int kReduceCols = 512;
+
+__global__ void __launch_bounds__(128) moe_reduce_kernel(MoeArgs a) {
     const int r = blockIdx.x;
     __shared__ int live[32];  // the row's slots with an expert of the layer, in k order
     __shared__ int nlive;
-    if (threadIdx.x == 0) {
-        int c = 0;
-        for (int k = 0; k < a.K; k++)
-            if (a.inds[r * a.K + k] < (uint32_t)a.E) live[c++] = r * a.K + k;
-        nlive = c;
+    grid_launch_dependents();
+    grid_dependency_wait();  // the slots' planes come from the previous kernels
+    if (threadIdx.x < 32) {
+        const int k = threadIdx.x;
+        const bool ok = k < a.K && a.inds[r * a.K + k] < (uint32_t)a.E;
+        const unsigned m = __ballot_sync(0xffffffffu, ok);
+        if (ok) live[__popc(m & ((1u << k) - 1u))] = r * a.K + k;
+        if (k == 0) nlive = __popc(m);
     }
     __syncthreads();
     const int nl = nlive;
-    for (int d = threadIdx.x * 4; d < a.D; d += blockDim.x * 4) {
-        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        for (int j = 0; j < nl; j++) {
-            const float4 v = *reinterpret_cast<const float4*>(a.yslot + (size_t)live[j] * a.D + d);
-            acc[0] += v.x;
-            acc[1] += v.y;
-            acc[2] += v.z;
-            acc[3] += v.w;
-        }
-        if (a.partial) {  // an expert-parallel rank's share: combined and rounded by the token's owner
-            *reinterpret_cast<float4*>(a.partial + (size_t)r * a.D + d) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-            continue;
-        }
-        // The routed sum is rounded to the output dtype before a shared expert is added
-        // (docs/engine-exl3-experts.md "Streamed serial decode"; src/exl3/root.zig:56-92).
+    const int d = blockIdx.y * kReduceCols + threadIdx.x * 4;
+    if (d >= a.D) return;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int j = 0; j < nl; j++) {
+        const float4 v = *reinterpret_cast<const float4*>(a.yslot + (size_t)live[j] * a.D + d);
+        acc[0] += v.x;
+        acc[1] += v.y;
+        acc[2] += v.z;
+        acc[3] += v.w;
+    }
+    if (a.partial) {  // an expert-parallel rank's share: combined and rounded by the token's owner
+        *reinterpret_cast<float4*>(a.partial + (size_t)r * a.D + d) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        return;
+    }
+    // The routed sum is rounded to the output dtype before a shared expert is added
+    // (docs/engine-exl3-experts.md "Streamed serial decode"; src/exl3/root.zig:56-92).
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const float y = routed_finish(acc[i], a.xdt, a.shared, a.shared_gate, (size_t)r * a.D + d + i, r);
-            store_act(a.y, (size_t)r * a.D + d + i, a.xdt, y);
-        }
+    for (int i = 0; i < 4; i++) {
+        const float y = routed_finish(acc[i], a.xdt, a.shared, a.shared_gate, (size_t)r * a.D + d + i, r);
+        store_act(a.y, (size_t)r * a.D + d + i, a.xdt, y);
     }
 }
 
@@ -365,10 +401,14 @@ sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_de
     a.work_act4 = reinterpret_cast<int*>(ws + L.work_act4);
     a.work_chunk4 = reinterpret_cast<int*>(ws + L.work_chunk4);
     a.sorted_e = reinterpret_cast<int*>(ws + L.sorted_e);
+    a.work_rec = reinterpret_cast<int4*>(ws + L.work_rec);
+    a.work_slots = reinterpret_cast<int*>(ws + L.work_slots);
 
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    route_prep_kernel<<<1, 1024, 2 * (size_t)E * sizeof(int), s>>>(a);
-    cudaError_t e = cudaGetLastError();
+    const size_t rp_smem = 3 * (size_t)E * sizeof(int);
+    cudaError_t e = cudaSuccess;
+    if (rp_smem > 48 * 1024) e = cudaFuncSetAttribute(route_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rp_smem);
+    if (e == cudaSuccess) e = launch_pdl(route_prep_kernel, dim3(1), dim3(1024), rp_smem, s, a);
     if (e != cudaSuccess) return cuda_status(e, "route_prep launch");
     if (L.gemm) {
         // Tensor-core path (kernels.moePrefill, src/exl3/expert_exl3_kernels.zig:2861): prepared
@@ -511,8 +551,9 @@ sx_status moe_run(sx_stream stream, const MoeGroup* groups, int ng, int Etot, co
     r.shared_gate = shared_gate;
     r.y = y;
     r.partial = partial;
-    moe_reduce_kernel<<<rows, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(r);
-    return cuda_status(cudaGetLastError(), "moe reduce launch");
+    return cuda_status(launch_pdl(moe_reduce_kernel, dim3(rows, (D + kReduceCols - 1) / kReduceCols), dim3(128), 0,
+                                  reinterpret_cast<cudaStream_t>(stream), r),
+                       "moe reduce launch");
 }
 
 sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, const void* x, sx_dtype dtype,

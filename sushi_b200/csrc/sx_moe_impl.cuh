@@ -3,7 +3,10 @@
 // (src/exl3/expert_exl3_kernels.zig:2683 moeSwigluFused: pair prepare, split-K pair GEMV, fused
 // mid+down GEMV, finish reduce); this chain is:
 //   1. route_prep (one CTA): histogram of the slots' experts, scan, scatter -> slots sorted by
-//      expert, the active experts, and a work list of (active expert, 8-row chunk).
+//      expert, the active experts, and a work list of (active expert, 8-row chunk), one record
+//      and the slot ids per item.
+// The four launch with programmatic dependent launch: each starts its prologue (barriers, shared
+// memory) while its predecessor drains and waits for it before its first global access.
 //   2. moe_pair: per work item and 128-wide block of the intermediate, gate AND up of the expert
 //      for the chunk's rows (NP = 2 core, split-K cluster).  Its rank-0 epilogue does the
 //      reference's mid (:2243 MID_SOURCE): H128, svh, SwiGLU in f32 (gate upper-clamped and up
@@ -57,6 +60,8 @@ struct MoeArgs {
     int* work_act4;         // second list: [W4_max]
     int* work_chunk4;
     int* sorted_e;          // [R*K] the expert of each sorted position
+    int4* work_rec;         // [W_max] list-1 items: expert, first sorted position, rows
+    int* work_slots;        // [W_max][8] decode chain (chunk 8): the slot id of each row of an item
     // tensor-core path (sorted positions p): prepared gate/up inputs, gate/up outputs
     uint16_t* tg;           // [R*K][D] f16
     uint16_t* tu;           // [R*K][D] f16
@@ -97,13 +102,15 @@ struct WorkItem {
     int e, first, rows;
 };
 
+// The item count and the item's record are loaded together (one round of global loads; a record
+// past the count is never used).
 __device__ __forceinline__ bool work_item(const MoeArgs& a, int w, WorkItem& it) {
-    if (w >= a.meta[0]) return false;
-    const int ai = a.work_act[w];
-    const int ch = a.work_chunk[w];
-    it.e = a.act_expert[ai];
-    it.first = a.act_start[ai] + ch * 8;
-    it.rows = min(8, a.act_count[ai] - ch * 8);
+    const int count = a.meta[0];
+    const int4 rec = a.work_rec[w];
+    if (w >= count) return false;
+    it.e = rec.x;
+    it.first = rec.y;
+    it.rows = rec.z;
     return true;
 }
 
@@ -113,8 +120,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_pair_kernel(MoeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int slot_of[8];
     cg::cluster_group cluster = cg::this_cluster();
-    WorkItem it;
-    if (!work_item(a, blockIdx.x, it)) return;  // every CTA of the cluster shares blockIdx.x
     const int ob = blockIdx.y;
     const int S = cluster.dim_blocks().z;
     const int split = blockIdx.z % S;
@@ -126,8 +131,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_pair_kernel(MoeArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int OT = a.I / 16;
     const size_t per = (size_t)(a.D / 16) * OT * N;
-    if (threadIdx.x < 8) slot_of[threadIdx.x] = threadIdx.x < it.rows ? a.order[it.first + threadIdx.x] : 0;
     core_init_barriers<N, 2, kConsumerWarps>(s);
+    grid_launch_dependents();
+    grid_dependency_wait();  // the routing comes from route_prep
+    WorkItem it;
+    if (!work_item(a, blockIdx.x, it)) return;  // every CTA of the cluster shares blockIdx.x
+    if (threadIdx.x < 8) slot_of[threadIdx.x] = threadIdx.x < it.rows ? a.work_slots[blockIdx.x * 8 + threadIdx.x] : 0;
     __syncthreads();
 
     if (warp == kConsumerWarps) {
@@ -196,8 +205,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(MoeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int slot_of[8];
     cg::cluster_group cluster = cg::this_cluster();
-    WorkItem it;
-    if (!work_item(a, blockIdx.x, it)) return;
     const int ob = blockIdx.y;
     const int S = cluster.dim_blocks().z;
     const int split = blockIdx.z % S;
@@ -209,8 +216,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(MoeArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int OT = a.D / 16;
     const size_t per = (size_t)(a.I / 16) * OT * N;
-    if (threadIdx.x < 8) slot_of[threadIdx.x] = threadIdx.x < it.rows ? a.order[it.first + threadIdx.x] : 0;
     core_init_barriers<N, 1, kConsumerWarps>(s);
+    grid_launch_dependents();
+    grid_dependency_wait();  // the prepared rows come from moe_pair
+    WorkItem it;
+    if (!work_item(a, blockIdx.x, it)) return;
+    if (threadIdx.x < 8) slot_of[threadIdx.x] = threadIdx.x < it.rows ? a.work_slots[blockIdx.x * 8 + threadIdx.x] : 0;
     __syncthreads();
 
     if (warp == kConsumerWarps) {
