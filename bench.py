@@ -418,10 +418,10 @@ def moe_bench(sx, _lib, torch, args, stream, sptr):
         def layer(c):
             logits = (x @ wr).float()
             inds, scores = sx.router_topk(logits, k)
-            sh = sx.moe(x, shared, one_i, one_s, dec)
             gate = x @ wg
-            if ep is None:
-                return sx.moe(x, banks[c % copies], inds, scores, dec, shared=sh, shared_gate=gate)
+            if ep is None:  # the shared expert rides the routed launches
+                return sx.moe_folded(x, banks[c % copies], shared, inds, scores, dec, shared_gate=gate)
+            sh = sx.moe(x, shared, one_i, one_s, dec)
             return ep.moe(x, banks[c % copies], E, inds, scores, dec, rows_cap=T, shared=sh, shared_gate=gate)
 
         for i in range(max(3, args.warmup)):
@@ -498,17 +498,19 @@ def prefill_bench(sx, torch, args, stream, tf_peak):
     ws_sh = torch.empty(L.sx_moe_workspace_bytes(ctypes.byref(shared.c()), T, 1), dtype=torch.uint8, device="cuda")
     ep = sx.ExpertParallel.from_process_group() if world > 1 else None
     if ep is None:
-        ws = torch.empty(L.sx_moe_workspace_bytes(ctypes.byref(bank.c()), T, k), dtype=torch.uint8, device="cuda")
+        d = dec.c()
+        ws = torch.empty(L.sx_moe_folded_workspace_bytes(ctypes.byref(bank.c()), ctypes.byref(shared.c()), ctypes.byref(d),
+                                                         None, T, k), dtype=torch.uint8, device="cuda")
     else:
         ws = torch.empty(ep.workspace_bytes(bank, T, k), dtype=torch.uint8, device="cuda")
 
     def layer():
         logits = (x @ wr).float() + bias
         inds, scores = sx.router_topk(logits, k)
-        sh = sx.moe(x, shared, one_i, one_s, dec, workspace=ws_sh)
         gate = x @ wg
         if ep is None:
-            return sx.moe(x, bank, inds, scores, dec, shared=sh, shared_gate=gate, workspace=ws)
+            return sx.moe_folded(x, bank, shared, inds, scores, dec, shared_gate=gate, workspace=ws)
+        sh = sx.moe(x, shared, one_i, one_s, dec, workspace=ws_sh)
         return ep.moe(x, bank, E, inds, scores, dec, rows_cap=T, shared=sh, shared_gate=gate, workspace=ws)
 
     for _ in range(max(3, args.warmup)):
@@ -595,10 +597,13 @@ def deepseek_bench(sx, torch, args, stream, tf_peak):
     Lib = sx._lib.load()
     for T in (1, 8, 64, 4096):
         x0 = torch.randn((T, H), device="cuda", generator=gen).to(torch.bfloat16)
+        d = dec.c()
         routed_ws = (ep.workspace_bytes(layers[0][0], T, k) if ep is not None else
-                     Lib.sx_moe_ragged_workspace_bytes(ctypes.byref(layers[0][0].c()), T, k))
-        ws = torch.empty(max(routed_ws, Lib.sx_moe_workspace_bytes(ctypes.byref(layers[0][1].c()), T, 1)),
-                         dtype=torch.uint8, device="cuda")
+                     Lib.sx_moe_ragged_folded_workspace_bytes(ctypes.byref(layers[0][0].c()),
+                                                              ctypes.byref(layers[0][1].c()), ctypes.byref(d), None, T, k))
+        ws = torch.empty(routed_ws, dtype=torch.uint8, device="cuda")
+        ws_sh = torch.empty(Lib.sx_moe_workspace_bytes(ctypes.byref(layers[0][1].c()), T, 1), dtype=torch.uint8,
+                            device="cuda")
         ones_i, ones_s = one.expand(T, 1).contiguous(), torch.ones((T, 1), device="cuda")
 
         def stack():
@@ -606,10 +611,10 @@ def deepseek_bench(sx, torch, args, stream, tf_peak):
             for rb, shared, wr, bias in layers:
                 inds, scores = sx.router_topk((x @ wr).float(), k, sx.RouterMode.SIGMOID_BIAS, bias, route_norm=True,
                                               route_scale=2.5)
-                sh = sx.moe(x, shared, ones_i, ones_s, dec, workspace=ws)
-                if ep is None:
-                    x = x + sx.moe_ragged(x, rb, inds, scores, dec, shared=sh, workspace=ws)
+                if ep is None:  # the K4 shared expert in the same call as the K1/K2 routed groups
+                    x = x + sx.moe_folded(x, rb, shared, inds, scores, dec, workspace=ws)
                 else:
+                    sh = sx.moe(x, shared, ones_i, ones_s, dec, workspace=ws_sh)
                     x = x + ep.moe(x, rb, E, inds, scores, dec, rows_cap=T, shared=sh, workspace=ws)
             return x
 
@@ -650,7 +655,7 @@ def deepseek_bench(sx, torch, args, stream, tf_peak):
         flops = world * 2.0 * T * L * (k + 1) * 3 * H * I
         res[f"T{T}"] = {"tokens_per_s": round(world * T / (ms * 1e-3), 1), "ms_per_stack": round(ms, 3),
                         "tflops": round(flops / (ms * 1e-3) / 1e12, 1)}
-        del ws
+        del ws, ws_sh
     assert sx.device_error() == 0
     if ep is not None:
         torch.cuda.synchronize()

@@ -246,6 +246,29 @@ sx_status sx_moe_ragged(sx_stream stream, const sx_ragged* bank, const sx_decode
                         int32_t rows, const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
                         const void* shared_gate, int32_t clamp_limit, void* y, void* workspace, size_t workspace_bytes);
 
+/* The routed layer with its shared expert folded in (moe_shared_fold.folded, src/moe_shared_fold.zig:24;
+ * fold_gated.moeGatedSharedFolded, src/exl3/fold_gated.zig:122-160; rate_groups'
+ * moeGatedSharedFolded): y as sx_moe / sx_moe_ragged with `shared` = the shared expert's output
+ * over the same rows, rounded to x's dtype (a one-expert SwiGLU bank, `shared_bank`, experts = 1,
+ * decoded with `shared_dec`, or `dec` when null; the same clamp_limit), optionally sigmoid-gated by
+ * shared_gate [rows].  The shared expert rides the routed decode chain's launches when its rates,
+ * decode and intermediate size match a routed group's; otherwise it runs as its own launches.
+ * Results equal the unfused composition bit for bit.  workspace: the matching
+ * *_folded_workspace_bytes(...). */
+size_t sx_moe_folded_workspace_bytes(const sx_bank* bank, const sx_bank* shared_bank, const sx_decode* dec,
+                                     const sx_decode* shared_dec, int32_t rows, int32_t topk);
+sx_status sx_moe_folded(sx_stream stream, const sx_bank* bank, const sx_bank* shared_bank, const sx_decode* dec,
+                        const sx_decode* shared_dec, const void* x, sx_dtype dtype, int32_t rows, const uint32_t* inds,
+                        const float* scores, int32_t topk, const void* shared_gate, int32_t clamp_limit, void* y,
+                        void* workspace, size_t workspace_bytes);
+size_t sx_moe_ragged_folded_workspace_bytes(const sx_ragged* bank, const sx_bank* shared_bank, const sx_decode* dec,
+                                            const sx_decode* shared_dec, int32_t rows, int32_t topk);
+sx_status sx_moe_ragged_folded(sx_stream stream, const sx_ragged* bank, const sx_bank* shared_bank,
+                               const sx_decode* dec, const sx_decode* shared_dec, const void* x, sx_dtype dtype,
+                               int32_t rows, const uint32_t* inds, const float* scores, int32_t topk,
+                               const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
+                               size_t workspace_bytes);
+
 /* ------------------------------------------------------------------ routed experts, no allocation
  * sx_moe for callers that cannot allocate device memory at all.  Some hosts never call cudaMalloc
  * on the path that runs the layer: a caller recording the layer into a CUDA graph (an allocation

@@ -81,6 +81,12 @@ SIGNATURES = {
     "sx_ep_workspace_bytes": (_SZ, [_P, ctypes.POINTER(SxBank), _I, _I, _I]),
     "sx_ep_moe": (_I, [_P, _P, ctypes.POINTER(SxBank), _I, ctypes.POINTER(SxDecode), _P, _I, _I, _I, _P, _P, _I, _P,
                        _P, _I, _P, _P, _SZ]),
+    "sx_moe_folded_workspace_bytes": (_SZ, [ctypes.POINTER(SxBank), ctypes.POINTER(SxBank), _P, _P, _I, _I]),
+    "sx_moe_folded": (_I, [_P, ctypes.POINTER(SxBank), ctypes.POINTER(SxBank), _P, _P, _P, _I, _I, _P, _P, _I, _P, _I,
+                           _P, _P, _SZ]),
+    "sx_moe_ragged_folded_workspace_bytes": (_SZ, [ctypes.POINTER(SxRagged), ctypes.POINTER(SxBank), _P, _P, _I, _I]),
+    "sx_moe_ragged_folded": (_I, [_P, ctypes.POINTER(SxRagged), ctypes.POINTER(SxBank), _P, _P, _P, _I, _I, _P, _P, _I,
+                                  _P, _I, _P, _P, _SZ]),
     "sx_ep_ragged_workspace_bytes": (_SZ, [_P, ctypes.POINTER(SxRagged), _I, _I, _I]),
     "sx_ep_moe_ragged": (_I, [_P, _P, ctypes.POINTER(SxRagged), _I, ctypes.POINTER(SxDecode), _P, _I, _I, _I, _P, _P,
                               _I, _P, _P, _I, _P, _P, _SZ]),

@@ -187,7 +187,8 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(CombineArgs a) {
             const int p = a.pos[(size_t)r * a.world + g];
             if (p >= 0) acc += a.part[((size_t)g * a.cap + p) * a.D + d];
         }
-        const float y = routed_finish(acc, a.xdt, a.shared, a.shared_gate, (size_t)r * a.D + d, r);
+        const float sh = a.shared ? load_act(a.shared, (size_t)r * a.D + d, a.xdt) : 0.0f;
+        const float y = routed_finish(acc, a.xdt, a.shared != nullptr, sh, a.shared_gate, r);
         store_act(a.y, (size_t)r * a.D + d, a.xdt, y);
     }
 }

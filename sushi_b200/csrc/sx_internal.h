@@ -46,7 +46,8 @@ constexpr int kMaxGroups = 32;  // layout.max_groups (src/exl3/layout.zig:4)
 sx_status moe_run(sx_stream stream, const MoeGroup* groups, int ng, int Etot, const sx_decode* dec, const void* x,
                   sx_dtype dtype, int32_t rows, const uint32_t* inds, const float* scores, int32_t topk,
                   const void* shared, const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
-                  size_t workspace_bytes, float* partial, long long slots);
+                  size_t workspace_bytes, float* partial, long long slots, const sx_bank* sh_bank = nullptr,
+                  const sx_decode* sh_dec = nullptr);
 size_t moe_groups_ws(const MoeGroup* g, int ng, int Etot, int rows, int topk, long long slots);
 // The groups of a ragged layer (at most kMaxGroups) from its host meta table.
 sx_status ragged_groups(const sx_ragged* rb, MoeGroup* out, int* ng);

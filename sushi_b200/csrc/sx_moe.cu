@@ -168,7 +168,9 @@ bool use_gemm(int E, int R, int K, long long slots) {
     return slots >= 16LL * std::min<long long>(E, slots);
 }
 
-MoeWs moe_ws_layout(int E, int R, int K, int D, int I, int n_gu, int n_d, long long slots = 0, bool with_yslot = true) {
+// extra_rows: prepared-input rows past the routed slots (a shared expert's rows riding the chain).
+MoeWs moe_ws_layout(int E, int R, int K, int D, int I, int n_gu, int n_d, long long slots = 0, bool with_yslot = true,
+                    int extra_rows = 0) {
     MoeWs w;
     const int RK = R * K;
     w.gemm = use_gemm(E, R, K, slots);
@@ -192,7 +194,7 @@ MoeWs moe_ws_layout(int E, int R, int K, int D, int I, int n_gu, int n_d, long l
     w.work_chunk4 = off; off = align_up(off + (size_t)std::max(1, w.W4_max) * sizeof(int));
     w.order = off; off = align_up(off + (size_t)RK * sizeof(int));
     w.sorted_e = off; off = align_up(off + (size_t)RK * sizeof(int));
-    w.hprep = off; off = align_up(off + (size_t)RK * I * sizeof(uint16_t));
+    w.hprep = off; off = align_up(off + (size_t)(RK + extra_rows) * I * sizeof(uint16_t));
     w.yslot = off;
     if (with_yslot) off = align_up(off + (size_t)RK * D * sizeof(float));
     w.tg = w.tu = w.gf = w.uf = 0;
@@ -241,9 +243,19 @@ __global__ void __launch_bounds__(128) moe_reduce_kernel(MoeArgs a) {
     }
     // The routed sum is rounded to the output dtype before a shared expert is added
     // (docs/engine-exl3-experts.md "Streamed serial decode"; src/exl3/root.zig:56-92).
+    float sh[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (a.sh_plane) {  // the shared expert's plane, rounded as its own layer output would be
+        const float4 v = *reinterpret_cast<const float4*>(a.yslot + (size_t)(a.sh_slot0 + r) * a.D + d);
+        sh[0] = round_act(v.x, a.xdt), sh[1] = round_act(v.y, a.xdt), sh[2] = round_act(v.z, a.xdt);
+        sh[3] = round_act(v.w, a.xdt);
+    } else if (a.shared) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) sh[i] = load_act(a.shared, (size_t)r * a.D + d + i, a.xdt);
+    }
+    const bool has_sh = a.sh_plane || a.shared;
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        const float y = routed_finish(acc[i], a.xdt, a.shared, a.shared_gate, (size_t)r * a.D + d + i, r);
+        const float y = routed_finish(acc[i], a.xdt, has_sh, sh[i], a.shared_gate, r);
         store_act(a.y, (size_t)r * a.D + d + i, a.xdt, y);
     }
 }
@@ -316,10 +328,42 @@ __global__ void __launch_bounds__(256) moe_mid_kernel(MoeArgs a) {
     *reinterpret_cast<uint2*>(a.hprep + (size_t)p * a.I + o0) = hh;
 }
 
-int pick_split(int units, int kb) {
-    const int want = 2 * sm_count();
-    int S = (want + units - 1) / std::max(units, 1);
-    return std::max(1, std::min(S, std::min(8, kb)));
+void set_shared_ptrs(MoeArgs& a, const sx_bank& sh) {
+    a.sh_gate_tr = sh.gate.trellis; a.sh_gate_suh = sh.gate.suh; a.sh_gate_svh = sh.gate.svh;
+    a.sh_up_tr = sh.up.trellis;     a.sh_up_suh = sh.up.suh;     a.sh_up_svh = sh.up.svh;
+    a.sh_down_tr = sh.down.trellis; a.sh_down_suh = sh.down.suh; a.sh_down_svh = sh.down.svh;
+}
+
+// Every row routed to expert 0 with score 1 (a shared expert through the tensor-core path).
+__global__ void shared_route_kernel(uint32_t* inds, float* scores, int rows) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r < rows) {
+        inds[r] = 0u;
+        scores[r] = 1.0f;
+    }
+}
+
+// The decode chain's split-K cluster size: about four 128-input blocks per CTA.  Measured on B200
+// over the 512-expert layer (hidden 2048, intermediate 512) at 1, 8 and 64 tokens, four blocks per
+// CTA was fastest for both the gate/up kernel (16 blocks: S = 4) and the down kernel (4 blocks:
+// S = 1): fewer blocks pay the cluster reduce more often, more blocks need prepared-input shared
+// memory that leaves one CTA per SM.
+int pick_split(int kb) {
+    constexpr int kBlocksPerCta = 4;
+    return std::max(1, std::min(16, (kb + kBlocksPerCta - 1) / kBlocksPerCta));
+}
+
+// The pair and down launches of the decode chain over `items` work items.
+cudaError_t chain_launch(const MoeArgs& a, int kind, int n_gu, int n_d, int items, cudaStream_t s) {
+    const int S_gu = pick_split(a.D / 128);
+    const int S_d = pick_split(a.I / 128);
+    switch (kind) {
+        case K_MCG: return moe_launch_kind<K_MCG>(a, n_gu, n_d, S_gu, S_d, items, s);
+        case K_MUL1: return moe_launch_kind<K_MUL1>(a, n_gu, n_d, S_gu, S_d, items, s);
+        case K_HASH: return moe_launch_kind<K_HASH>(a, n_gu, n_d, S_gu, S_d, items, s);
+        case K_PAIR1: return moe_launch_kind<K_PAIR1>(a, n_gu, n_d, S_gu, S_d, items, s);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 }  // namespace
@@ -338,18 +382,65 @@ long long group_slots(long long slots, int rows, int topk, int Eg, int Etot) {
 
 size_t yslot_bytes(int rows, int topk, int D) { return align_up((size_t)rows * topk * D * sizeof(float)); }
 
-// Workspace of a layer of groups: the per-slot planes first (every group writes its slots'), then
-// the largest group's own scratch (the groups run one after another on the stream).
-size_t moe_groups_ws(const MoeGroup* g, int ng, int Etot, int rows, int topk, long long slots) {
+bool same_decode(const sx_decode* a, const sx_decode* b) {
+    return a == b || (a && b && a->codebook == b->codebook && a->window_bits == b->window_bits && a->table == b->table);
+}
+
+// How a layer's shared expert runs (moe_shared_fold.folded, src/moe_shared_fold.zig:24; fold_gated,
+// src/exl3/fold_gated.zig:122-160, which serves one to eight rows): up to 16 rows, folded into the
+// decode-chain launches of a routed group with its rates, decode and intermediate size (no launch
+// of its own), else as its own pair and down launches of the chain (no routing pass); more rows
+// through the tensor-core path with a routing of every row to it.  Each is the path a one-expert
+// layer of those rows takes, so the result is the unfused composition's.  Its output is the plane
+// of slots rows*topk + row.
+struct SharedPlan {
+    int mode;   // 0 none, 1 folded into `group`, 2 chain launches of its own, 3 tensor-core path
+    int group;
+};
+
+SharedPlan shared_plan(const MoeGroup* g, int ng, int Etot, int rows, int topk, long long slots, const sx_bank* sh,
+                       const sx_decode* dec, const sx_decode* sh_dec) {
+    if (!sh) return {0, -1};
     const int D = g[0].bank.gate.in_features, I = g[0].bank.gate.out_features;
-    size_t most = 0;
     for (int i = 0; i < ng; i++) {
         const sx_bank& b = g[i].bank;
         const MoeWs L = moe_ws_layout(b.gate.experts, rows, topk, D, I, b.gate.n, b.down.n,
                                       group_slots(slots, rows, topk, b.gate.experts, Etot), false);
+        if (!L.gemm && rows <= kDecodeRowsMax && sh->gate.n == b.gate.n && sh->down.n == b.down.n &&
+            sh->gate.out_features == I && same_decode(dec, sh_dec))
+            return {1, i};
+    }
+    return {rows <= kDecodeRowsMax ? 2 : 3, -1};
+}
+
+size_t shared_fill_bytes(int rows) { return align_up((size_t)rows * (sizeof(uint32_t) + sizeof(float))); }
+
+// Workspace of a layer of groups: the per-slot planes first (every group writes its slots', and a
+// shared expert its rows' past them), then the largest group's own scratch (the groups and the
+// shared expert run one after another on the stream).
+size_t moe_groups_ws(const MoeGroup* g, int ng, int Etot, int rows, int topk, long long slots, const sx_bank* sh,
+                     const sx_decode* dec, const sx_decode* sh_dec) {
+    const int D = g[0].bank.gate.in_features, I = g[0].bank.gate.out_features;
+    const SharedPlan plan = shared_plan(g, ng, Etot, rows, topk, slots, sh, dec, sh_dec);
+    const int extra = sh ? rows : 0;
+    size_t most = 0;
+    for (int i = 0; i < ng; i++) {
+        const sx_bank& b = g[i].bank;
+        const MoeWs L = moe_ws_layout(b.gate.experts, rows, topk, D, I, b.gate.n, b.down.n,
+                                      group_slots(slots, rows, topk, b.gate.experts, Etot), false,
+                                      plan.mode == 1 && plan.group == i ? extra : 0);
         most = std::max(most, L.total);
     }
-    return yslot_bytes(rows, topk, D) + most;
+    if (plan.mode == 2) most = std::max(most, align_up((size_t)(rows * topk + rows) * sh->gate.out_features * 2));
+    if (plan.mode == 3) {
+        const MoeWs L = moe_ws_layout(1, rows, 1, D, sh->gate.out_features, sh->gate.n, sh->down.n, rows, false);
+        most = std::max(most, L.total + shared_fill_bytes(rows));
+    }
+    return yslot_bytes(rows, topk, D) + (sh ? yslot_bytes(rows, 1, D) : 0) + most;
+}
+
+size_t moe_groups_ws(const MoeGroup* g, int ng, int Etot, int rows, int topk, long long slots) {
+    return moe_groups_ws(g, ng, Etot, rows, topk, slots, nullptr, nullptr, nullptr);
 }
 
 size_t moe_workspace_bytes(const sx_bank* bank, int32_t rows, int32_t topk, long long slots) {
@@ -359,13 +450,14 @@ size_t moe_workspace_bytes(const sx_bank* bank, int32_t rows, int32_t topk, long
 }
 
 // Route metadata and the decode chain or the tensor-core path for one group's slots, into yslot.
+// fold: a shared expert riding this group's decode-chain launches (shared_plan mode 1), or null.
 sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_decode* dec, const void* x,
                     sx_dtype dtype, int32_t rows, const uint32_t* inds, const float* scores, int32_t topk,
-                    int32_t clamp_limit, float* yslot, uint8_t* ws, long long slots) {
+                    int32_t clamp_limit, float* yslot, uint8_t* ws, long long slots, const sx_bank* fold = nullptr) {
     const int E = bank->gate.experts;
     const int D = bank->gate.in_features, I = bank->gate.out_features;
     sx_status st;
-    const MoeWs L = moe_ws_layout(E, rows, topk, D, I, bank->gate.n, bank->down.n, slots, false);
+    const MoeWs L = moe_ws_layout(E, rows, topk, D, I, bank->gate.n, bank->down.n, slots, false, fold ? rows : 0);
     MoeArgs a{};
     int kind_gu, kind_d;
     if ((st = resolve_decode(dec, bank->gate.n, &kind_gu, &a.dp_gu))) return st;
@@ -403,6 +495,12 @@ sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_de
     a.sorted_e = reinterpret_cast<int*>(ws + L.sorted_e);
     a.work_rec = reinterpret_cast<int4*>(ws + L.work_rec);
     a.work_slots = reinterpret_cast<int*>(ws + L.work_slots);
+    a.w_routed = L.W_max;
+    if (fold) {
+        a.sh_items = (rows + 7) / 8;
+        a.sh_slot0 = rows * topk;
+        set_shared_ptrs(a, *fold);
+    }
 
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const size_t rp_smem = 3 * (size_t)E * sizeof(int);
@@ -481,17 +579,38 @@ sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_de
             return cuda_status(e, "moe down gemm launch");
         return SX_OK;
     }
-    const int S_gu = pick_split(L.A_max * (I / 128), D / 128);
-    const int S_d = pick_split(L.A_max * (D / 128), I / 128);
-    switch (kind_gu) {
-        case K_MCG: e = moe_launch_kind<K_MCG>(a, bank->gate.n, bank->down.n, S_gu, S_d, L.W_max, s); break;
-        case K_MUL1: e = moe_launch_kind<K_MUL1>(a, bank->gate.n, bank->down.n, S_gu, S_d, L.W_max, s); break;
-        case K_HASH: e = moe_launch_kind<K_HASH>(a, bank->gate.n, bank->down.n, S_gu, S_d, L.W_max, s); break;
-        case K_PAIR1: e = moe_launch_kind<K_PAIR1>(a, bank->gate.n, bank->down.n, S_gu, S_d, L.W_max, s); break;
-        default: return SX_ERR_CODEBOOK_UNSUPPORTED;
-    }
+    e = chain_launch(a, kind_gu, bank->gate.n, bank->down.n, L.W_max + a.sh_items, s);
     if (e != cudaSuccess) return cuda_status(e, "moe pair/down launch");
     return SX_OK;
+}
+
+// A shared expert's own decode-chain launches (shared_plan mode 2): every work item is one of its
+// 8-row chunks; no routing metadata.  hprep holds rows*topk + rows prepared rows.
+sx_status shared_chain(sx_stream stream, const sx_bank* sh, const sx_decode* dec, const void* x, sx_dtype dtype,
+                       int32_t rows, int32_t topk, int32_t clamp_limit, float* yslot, uint8_t* ws) {
+    MoeArgs a{};
+    int kind_gu, kind_d;
+    sx_status st;
+    if ((st = resolve_decode(dec, sh->gate.n, &kind_gu, &a.dp_gu))) return st;
+    if ((st = resolve_decode(dec, sh->down.n, &kind_d, &a.dp_down))) return st;
+    a.x = x;
+    a.xdt = dtype;
+    a.R = rows;
+    a.K = topk;
+    a.D = sh->gate.in_features;
+    a.I = sh->gate.out_features;
+    a.E = 1;
+    a.scale_gu = kind_scale(kind_gu);
+    a.scale_down = kind_scale(kind_d);
+    a.clamp = (float)clamp_limit;
+    a.hprep = reinterpret_cast<uint16_t*>(ws);
+    a.yslot = yslot;
+    a.w_routed = 0;
+    a.sh_items = (rows + 7) / 8;
+    a.sh_slot0 = rows * topk;
+    set_shared_ptrs(a, *sh);
+    const cudaError_t e = chain_launch(a, kind_gu, sh->gate.n, sh->down.n, a.sh_items, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? SX_OK : cuda_status(e, "shared expert pair/down launch");
 }
 
 // A routed layer of groups: every group's chain into the per-slot planes, then the k-order reduce
@@ -499,13 +618,14 @@ sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_de
 sx_status moe_run(sx_stream stream, const MoeGroup* groups, int ng, int Etot, const sx_decode* dec, const void* x,
                   sx_dtype dtype, int32_t rows, const uint32_t* inds, const float* scores, int32_t topk,
                   const void* shared, const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
-                  size_t workspace_bytes, float* partial, long long slots) {
+                  size_t workspace_bytes, float* partial, long long slots, const sx_bank* sh_bank,
+                  const sx_decode* sh_dec) {
     if (!x || !inds || !scores || (!y && !partial)) return SX_ERR_NULL_POINTER;
     if (clamp_limit < 0 || clamp_limit > 128) return SX_ERR_INVALID_CLAMP;
     if (rows < 1 || topk < 1) return SX_ERR_BAD_SHAPE;
     if (topk > 32) return SX_ERR_TOPK_EXCEEDS_REDUCE_BANK;
     if (!dtype_ok(dtype)) return SX_ERR_BAD_DTYPE;
-    if (shared_gate && !shared) return SX_ERR_NULL_POINTER;
+    if (shared_gate && !shared && !sh_bank) return SX_ERR_NULL_POINTER;
     // (an expert-parallel rank's rows carry every slot, most of them other ranks' sentinels)
     if (topk > Etot && !partial) return SX_ERR_TOPK_EXCEEDS_EXPERTS;
     if (Etot > 8192) return SX_ERR_BAD_SHAPE;
@@ -529,15 +649,55 @@ sx_status moe_run(sx_stream stream, const MoeGroup* groups, int ng, int Etot, co
         if ((st = resolve_decode(dec, bank->gate.n, &kind, &dp)) || (st = resolve_decode(dec, bank->down.n, &kind, &dp)))
             return st;
     }
-    if (!workspace || workspace_bytes < moe_groups_ws(groups, ng, Etot, rows, topk, slots))
+    if (sh_bank) {
+        // the shared expert: one SwiGLU expert over the same rows (validateClampedProjection)
+        sx_status st;
+        if (shared || partial) return SX_ERR_BAD_SHAPE;
+        if ((st = check_proj(&sh_bank->gate, 1)) || (st = check_proj(&sh_bank->up, 1)) ||
+            (st = check_proj(&sh_bank->down, 1)))
+            return st;
+        const int Is = sh_bank->gate.out_features;
+        if (sh_bank->gate.in_features != D || sh_bank->up.in_features != D || sh_bank->up.out_features != Is ||
+            sh_bank->down.in_features != Is || sh_bank->down.out_features != D)
+            return SX_ERR_BAD_SHAPE;
+        if (sh_bank->gate.tile_order != SX_TILE_PACK || sh_bank->up.tile_order != SX_TILE_PACK ||
+            sh_bank->down.tile_order != SX_TILE_PACK)
+            return SX_ERR_TILE_ORDER_UNSUPPORTED;
+        if (sh_bank->gate.n != sh_bank->up.n) return SX_ERR_TRELLIS_GEOMETRY;
+        int kind;
+        DecParams dp;
+        if ((st = resolve_decode(sh_dec, sh_bank->gate.n, &kind, &dp)) ||
+            (st = resolve_decode(sh_dec, sh_bank->down.n, &kind, &dp)))
+            return st;
+        if (reinterpret_cast<uintptr_t>(x) % 16) return SX_ERR_BAD_SHAPE;  // the shared plane's rows: 16-byte vectors
+    }
+    if (!workspace || workspace_bytes < moe_groups_ws(groups, ng, Etot, rows, topk, slots, sh_bank, dec, sh_dec))
         return SX_ERR_WORKSPACE_TOO_SMALL;
+    const SharedPlan plan = shared_plan(groups, ng, Etot, rows, topk, slots, sh_bank, dec, sh_dec);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     float* yslot = reinterpret_cast<float*>(ws);
-    uint8_t* scratch = ws + yslot_bytes(rows, topk, D);
+    uint8_t* scratch = ws + yslot_bytes(rows, topk, D) + (sh_bank ? yslot_bytes(rows, 1, D) : 0);
     for (int i = 0; i < ng; i++) {
         const sx_status st = moe_group(stream, &groups[i].bank, groups[i].e_lo, dec, x, dtype, rows, inds, scores, topk,
                                        clamp_limit, yslot, scratch,
-                                       group_slots(slots, rows, topk, groups[i].bank.gate.experts, Etot));
+                                       group_slots(slots, rows, topk, groups[i].bank.gate.experts, Etot),
+                                       plan.mode == 1 && plan.group == i ? sh_bank : nullptr);
+        if (st) return st;
+    }
+    if (plan.mode == 2) {
+        const sx_status st = shared_chain(stream, sh_bank, sh_dec, x, dtype, rows, topk, clamp_limit, yslot, scratch);
+        if (st) return st;
+    } else if (plan.mode == 3) {
+        const MoeWs L = moe_ws_layout(1, rows, 1, D, sh_bank->gate.out_features, sh_bank->gate.n, sh_bank->down.n, rows,
+                                      false);
+        uint32_t* sh_inds = reinterpret_cast<uint32_t*>(scratch + L.total);
+        float* sh_scores = reinterpret_cast<float*>(sh_inds + rows);
+        shared_route_kernel<<<(rows + 255) / 256, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(sh_inds, sh_scores,
+                                                                                                    rows);
+        sx_status st = cuda_status(cudaGetLastError(), "shared route launch");
+        if (!st)
+            st = moe_group(stream, sh_bank, 0, sh_dec, x, dtype, rows, sh_inds, sh_scores, 1, clamp_limit,
+                           yslot + (size_t)rows * topk * D, scratch, rows);
         if (st) return st;
     }
     MoeArgs r{};
@@ -551,6 +711,8 @@ sx_status moe_run(sx_stream stream, const MoeGroup* groups, int ng, int Etot, co
     r.shared_gate = shared_gate;
     r.y = y;
     r.partial = partial;
+    r.sh_plane = sh_bank != nullptr;
+    r.sh_slot0 = rows * topk;
     return cuda_status(launch_pdl(moe_reduce_kernel, dim3(rows, (D + kReduceCols - 1) / kReduceCols), dim3(128), 0,
                                   reinterpret_cast<cudaStream_t>(stream), r),
                        "moe reduce launch");
@@ -563,7 +725,7 @@ sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, 
     if (!bank) return SX_ERR_NULL_POINTER;
     const MoeGroup g{*bank, 0};
     return moe_run(stream, &g, 1, bank->gate.experts, dec, x, dtype, rows, inds, scores, topk, shared, shared_gate,
-                   clamp_limit, y, workspace, workspace_bytes, partial, slots);
+                   clamp_limit, y, workspace, workspace_bytes, partial, slots, nullptr, nullptr);
 }
 
 }  // namespace sx
@@ -642,5 +804,47 @@ extern "C" sx_status sx_moe_ragged(sx_stream stream, const sx_ragged* bank, cons
     const sx_status st = ragged_groups(bank, g, &ng);
     if (st) return st;
     return moe_run(stream, g, ng, bank->experts, dec, x, dtype, rows, inds, scores, topk, shared, shared_gate,
-                   clamp_limit, y, workspace, workspace_bytes, nullptr, 0);
+                   clamp_limit, y, workspace, workspace_bytes, nullptr, 0, nullptr, nullptr);
+}
+
+extern "C" size_t sx_moe_folded_workspace_bytes(const sx_bank* bank, const sx_bank* shared_bank,
+                                                const sx_decode* dec, const sx_decode* shared_dec, int32_t rows,
+                                                int32_t topk) {
+    if (!bank || !shared_bank || rows < 1 || topk < 1) return 0;
+    const MoeGroup g{*bank, 0};
+    return moe_groups_ws(&g, 1, bank->gate.experts, rows, topk, 0, shared_bank, dec, shared_dec ? shared_dec : dec);
+}
+
+extern "C" sx_status sx_moe_folded(sx_stream stream, const sx_bank* bank, const sx_bank* shared_bank,
+                                   const sx_decode* dec, const sx_decode* shared_dec, const void* x, sx_dtype dtype,
+                                   int32_t rows, const uint32_t* inds, const float* scores, int32_t topk,
+                                   const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
+                                   size_t workspace_bytes) {
+    if (!bank || !shared_bank) return SX_ERR_NULL_POINTER;
+    const MoeGroup g{*bank, 0};
+    return moe_run(stream, &g, 1, bank->gate.experts, dec, x, dtype, rows, inds, scores, topk, nullptr, shared_gate,
+                   clamp_limit, y, workspace, workspace_bytes, nullptr, 0, shared_bank, shared_dec ? shared_dec : dec);
+}
+
+extern "C" size_t sx_moe_ragged_folded_workspace_bytes(const sx_ragged* bank, const sx_bank* shared_bank,
+                                                       const sx_decode* dec, const sx_decode* shared_dec, int32_t rows,
+                                                       int32_t topk) {
+    MoeGroup g[kMaxGroups];
+    int ng = 0;
+    if (!shared_bank || rows < 1 || topk < 1 || ragged_groups(bank, g, &ng) != SX_OK) return 0;
+    return moe_groups_ws(g, ng, bank->experts, rows, topk, 0, shared_bank, dec, shared_dec ? shared_dec : dec);
+}
+
+extern "C" sx_status sx_moe_ragged_folded(sx_stream stream, const sx_ragged* bank, const sx_bank* shared_bank,
+                                          const sx_decode* dec, const sx_decode* shared_dec, const void* x,
+                                          sx_dtype dtype, int32_t rows, const uint32_t* inds, const float* scores,
+                                          int32_t topk, const void* shared_gate, int32_t clamp_limit, void* y,
+                                          void* workspace, size_t workspace_bytes) {
+    if (!shared_bank) return SX_ERR_NULL_POINTER;
+    MoeGroup g[kMaxGroups];
+    int ng = 0;
+    const sx_status st = ragged_groups(bank, g, &ng);
+    if (st) return st;
+    return moe_run(stream, g, ng, bank->experts, dec, x, dtype, rows, inds, scores, topk, nullptr, shared_gate,
+                   clamp_limit, y, workspace, workspace_bytes, nullptr, 0, shared_bank, shared_dec ? shared_dec : dec);
 }

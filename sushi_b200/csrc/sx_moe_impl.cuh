@@ -62,6 +62,15 @@ struct MoeArgs {
     int* sorted_e;          // [R*K] the expert of each sorted position
     int4* work_rec;         // [W_max] list-1 items: expert, first sorted position, rows
     int* work_slots;        // [W_max][8] decode chain (chunk 8): the slot id of each row of an item
+    // A shared expert in the decode chain (sh_items > 0): work items w >= w_routed of the pair and
+    // down launches are its 8-row chunks of all R rows, read from the sh_* bank (one expert), with
+    // slot ids sh_slot0 + row (past the routed slots) and score 1.  w_routed = 0: a launch of the
+    // shared expert alone (no routing metadata read).
+    int w_routed, sh_items, sh_slot0;
+    const uint16_t* sh_gate_tr; const uint16_t* sh_gate_suh; const uint16_t* sh_gate_svh;
+    const uint16_t* sh_up_tr;   const uint16_t* sh_up_suh;   const uint16_t* sh_up_svh;
+    const uint16_t* sh_down_tr; const uint16_t* sh_down_suh; const uint16_t* sh_down_svh;
+    int sh_plane;           // reduce: the shared term is the plane of slots sh_slot0 + row, rounded
     // tensor-core path (sorted positions p): prepared gate/up inputs, gate/up outputs
     uint16_t* tg;           // [R*K][D] f16
     uint16_t* tu;           // [R*K][D] f16
@@ -73,12 +82,11 @@ struct MoeArgs {
 // the shared expert added (optionally sigmoid-gated, with MLX's bf16/f16 rounding steps), as
 // moeWithShared / moeWithGatedShared do (src/exl3/root.zig:56-92; moe_shared_fold.folded,
 // src/moe_shared_fold.zig:24).  idx = r * D + d.
-__device__ __forceinline__ float routed_finish(float acc, int xdt, const void* shared, const void* shared_gate, size_t idx,
-                                               int r) {
+// has_sh: a shared term sh (already in the output dtype's values) is added.
+__device__ __forceinline__ float routed_finish(float acc, int xdt, bool has_sh, float sh, const void* shared_gate, int r) {
     float y = acc;
     if (xdt != 0) y = xdt == 1 ? __half2float(__float2half_rn(y)) : __bfloat162float(__float2bfloat16_rn(y));
-    if (shared) {
-        float sh = load_act(shared, idx, xdt);
+    if (has_sh) {
         if (shared_gate) {
             const float gl = load_act(shared_gate, r, xdt);
             float sg = 1.0f / (1.0f + expf(-gl));
@@ -97,21 +105,38 @@ __device__ __forceinline__ float routed_finish(float acc, int xdt, const void* s
     return y;
 }
 
-// Work item -> (expert, first sorted slot, rows of the chunk).
+// Work item -> (expert, first sorted slot, rows of the chunk); shx: a chunk of the shared expert
+// (first = its first row).
 struct WorkItem {
     int e, first, rows;
+    bool shx;
 };
 
 // The item count and the item's record are loaded together (one round of global loads; a record
 // past the count is never used).
 __device__ __forceinline__ bool work_item(const MoeArgs& a, int w, WorkItem& it) {
+    if (w >= a.w_routed) {
+        const int c = w - a.w_routed;
+        if (c >= a.sh_items) return false;
+        it.e = 0;
+        it.first = c * 8;
+        it.rows = min(8, a.R - c * 8);
+        it.shx = true;
+        return true;
+    }
     const int count = a.meta[0];
     const int4 rec = a.work_rec[w];
     if (w >= count) return false;
     it.e = rec.x;
     it.first = rec.y;
     it.rows = rec.z;
+    it.shx = false;
     return true;
+}
+
+// The slot id of row t of a work item.
+__device__ __forceinline__ int work_slot(const MoeArgs& a, int w, const WorkItem& it, int t) {
+    return it.shx ? a.sh_slot0 + it.first + t : a.work_slots[w * 8 + t];
 }
 
 // ------------------------------------------------------------------ 2. gate + up + mid
@@ -136,16 +161,18 @@ __global__ void __launch_bounds__(kThreads, 1) moe_pair_kernel(MoeArgs a) {
     grid_dependency_wait();  // the routing comes from route_prep
     WorkItem it;
     if (!work_item(a, blockIdx.x, it)) return;  // every CTA of the cluster shares blockIdx.x
-    if (threadIdx.x < 8) slot_of[threadIdx.x] = threadIdx.x < it.rows ? a.work_slots[blockIdx.x * 8 + threadIdx.x] : 0;
+    if (threadIdx.x < 8) slot_of[threadIdx.x] = threadIdx.x < it.rows ? work_slot(a, blockIdx.x, it, threadIdx.x) : 0;
     __syncthreads();
 
     if (warp == kConsumerWarps) {
         if (lane == 0) {
-            const uint16_t* const tr[2] = {a.gate_tr + (size_t)it.e * per, a.up_tr + (size_t)it.e * per};
+            const uint16_t* const tr[2] = {it.shx ? a.sh_gate_tr : a.gate_tr + (size_t)it.e * per,
+                                           it.shx ? a.sh_up_tr : a.up_tr + (size_t)it.e * per};
             core_produce<N, 2>(s, tr, OT, ob, kb0, kbl);
         }
     } else {
-        const uint16_t* suh_p[2] = {a.gate_suh + (size_t)it.e * a.D, a.up_suh + (size_t)it.e * a.D};
+        const uint16_t* suh_p[2] = {it.shx ? a.sh_gate_suh : a.gate_suh + (size_t)it.e * a.D,
+                                    it.shx ? a.sh_up_suh : a.up_suh + (size_t)it.e * a.D};
         for (int item = warp; item < 2 * kbl * 8; item += kConsumerWarps) {
             const int p = item / (kbl * 8);
             const int kbi = (item / 8) % kbl;
@@ -153,7 +180,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_pair_kernel(MoeArgs a) {
             const int base = (kb0 + kbi) * 128 + lane * 4;
             float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             if (m < it.rows) {
-                const size_t xoff = (size_t)(slot_of[m] / a.K) * a.D + base;
+                const int row = it.shx ? slot_of[m] - a.sh_slot0 : slot_of[m] / a.K;
+                const size_t xoff = (size_t)row * a.D + base;
 #pragma unroll
                 for (int i = 0; i < 4; i++) v[i] = round_f16(load_act(a.x, xoff + i, a.xdt)) * h2f(suh_p[p][base + i]);
                 warp_hadamard128(v);
@@ -177,9 +205,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_pair_kernel(MoeArgs a) {
         warp_hadamard128(g);
         warp_hadamard128(u);
         float h[4];
-        const uint16_t* gsv = a.gate_svh + (size_t)it.e * a.I;
-        const uint16_t* usv = a.up_svh + (size_t)it.e * a.I;
-        const uint16_t* dsu = a.down_suh + (size_t)it.e * a.I;
+        const uint16_t* gsv = it.shx ? a.sh_gate_svh : a.gate_svh + (size_t)it.e * a.I;
+        const uint16_t* usv = it.shx ? a.sh_up_svh : a.up_svh + (size_t)it.e * a.I;
+        const uint16_t* dsu = it.shx ? a.sh_down_suh : a.down_suh + (size_t)it.e * a.I;
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const int o = ob * 128 + lane * 4 + i;
@@ -221,12 +249,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(MoeArgs a) {
     grid_dependency_wait();  // the prepared rows come from moe_pair
     WorkItem it;
     if (!work_item(a, blockIdx.x, it)) return;
-    if (threadIdx.x < 8) slot_of[threadIdx.x] = threadIdx.x < it.rows ? a.work_slots[blockIdx.x * 8 + threadIdx.x] : 0;
+    if (threadIdx.x < 8) slot_of[threadIdx.x] = threadIdx.x < it.rows ? work_slot(a, blockIdx.x, it, threadIdx.x) : 0;
     __syncthreads();
 
     if (warp == kConsumerWarps) {
         if (lane == 0) {
-            const uint16_t* const tr[1] = {a.down_tr + (size_t)it.e * per};
+            const uint16_t* const tr[1] = {it.shx ? a.sh_down_tr : a.down_tr + (size_t)it.e * per};
             core_produce<N, 1>(s, tr, OT, ob, kb0, kbl);
         }
     } else {
@@ -250,8 +278,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(MoeArgs a) {
         float d[4] = {ds.x, ds.y, ds.z, ds.w};
         warp_hadamard128(d);
         const int slot = slot_of[m];
-        const float sc = a.scores[slot] * a.scale_down;
-        const uint16_t* dsv = a.down_svh + (size_t)it.e * a.D;
+        const float sc = (it.shx ? 1.0f : a.scores[slot]) * a.scale_down;
+        const uint16_t* dsv = it.shx ? a.sh_down_svh : a.down_svh + (size_t)it.e * a.D;
         float* dst = a.yslot + (size_t)slot * a.D + ob * 128 + lane * 4;
 #pragma unroll
         for (int i = 0; i < 4; i++) dst[i] = d[i] * h2f(dsv[ob * 128 + lane * 4 + i]) * sc;

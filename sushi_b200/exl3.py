@@ -437,6 +437,41 @@ def moe_ragged(x, ragged: Ragged, inds, scores, dec: Decode, shared=None, shared
     return y.reshape(shape)
 
 
+def moe_folded(x, bank, shared_bank: Bank, inds, scores, dec: Decode, shared_gate=None, clamp_limit=0,
+               shared_dec: Decode = None, workspace=None):
+    """moe_shared_fold.folded: the routed layer (a Bank, or a Ragged layer) plus its shared expert
+    `shared_bank` (one SwiGLU expert), optionally sigmoid-gated by shared_gate [rows], in one call;
+    the shared expert rides the routed launches where its rates and decode match.  Returns x's
+    shape and dtype; equals moe(..., shared=<the shared expert's own output>, shared_gate=...)."""
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1]).contiguous()
+    rows = x2.shape[0]
+    ix = inds.reshape(rows, -1).to(torch.int32).contiguous()
+    sc = scores.reshape(rows, -1).float().contiguous()
+    topk = ix.shape[1]
+    if sc.shape != ix.shape:
+        raise Exl3Error(1)
+    if x2.dtype not in _DT:
+        raise Exl3Error(2)
+    ragged = isinstance(bank, Ragged)
+    b, shb, d = bank.c(), shared_bank.c(), dec.c()
+    sd = shared_dec.c() if shared_dec is not None else None
+    sdp = ctypes.byref(sd) if sd is not None else None
+    L = lib()
+    wsfn = L.sx_moe_ragged_folded_workspace_bytes if ragged else L.sx_moe_folded_workspace_bytes
+    need = wsfn(ctypes.byref(b), ctypes.byref(shb), ctypes.byref(d), sdp, rows, topk)
+    if need == 0:
+        raise Exl3Error(19 if ragged else 1)
+    ws = workspace if workspace is not None else _workspace(need, x.device)
+    y = torch.empty_like(x2)
+    sg = None if shared_gate is None else shared_gate.reshape(rows).to(x2.dtype).contiguous()
+    fn = L.sx_moe_ragged_folded if ragged else L.sx_moe_folded
+    _check(fn(_stream(), ctypes.byref(b), ctypes.byref(shb), ctypes.byref(d), sdp, x2.data_ptr(), _DT[x2.dtype], rows,
+              ix.data_ptr(), sc.data_ptr(), topk, None if sg is None else sg.data_ptr(), int(clamp_limit), y.data_ptr(),
+              ws.data_ptr(), ws.numel()))
+    return y.reshape(shape)
+
+
 def moe_with_shared(x, bank, inds, scores, dec, shared):
     return moe(x, bank, inds, scores, dec, shared=shared)
 

@@ -218,3 +218,30 @@ def test_linear_shared_normed_admission(L):
     assert call(proj=wide, c=wcols, count=1, wsb=1 << 20) == "SX_ERR_BAD_SHAPE"
     bad = (ctypes.c_int32 * 3)(0, 100, 256)
     assert call(c=bad) == "SX_ERR_BAD_SHAPE"
+
+
+def test_moe_folded_refusals_before_launch(L):
+    """The shared expert of sx_moe_folded is one SwiGLU expert over the layer's hidden size."""
+    g = _lib.SxProj(FAKE, FAKE, FAKE, 8, 256, 128, 32, 0)
+    d = _lib.SxProj(FAKE, FAKE, FAKE, 8, 128, 256, 32, 0)
+    bank = _lib.SxBank(g, g, d)
+    sg = _lib.SxProj(FAKE, FAKE, FAKE, 1, 256, 128, 32, 0)
+    sd = _lib.SxProj(FAKE, FAKE, FAKE, 1, 128, 256, 32, 0)
+    shared = _lib.SxBank(sg, sg, sd)
+    dec = _dec()
+    need = L.sx_moe_folded_workspace_bytes(ctypes.byref(bank), ctypes.byref(shared), ctypes.byref(dec), None, 4, 2)
+    assert need > L.sx_moe_workspace_bytes(ctypes.byref(bank), 4, 2)
+
+    def call(sh=shared, wsb=need):
+        st = L.sx_moe_folded(None, ctypes.byref(bank), ctypes.byref(sh) if sh is not None else None,
+                             ctypes.byref(dec), None, FAKE, 2, 4, FAKE, FAKE, 2, None, 0, FAKE, FAKE, wsb)
+        return L.sx_status_name(st).decode()
+
+    assert call(sh=None) == "SX_ERR_NULL_POINTER"
+    two = _lib.SxBank(_lib.SxProj(FAKE, FAKE, FAKE, 2, 256, 128, 32, 0), _lib.SxProj(FAKE, FAKE, FAKE, 2, 256, 128, 32, 0),
+                      _lib.SxProj(FAKE, FAKE, FAKE, 2, 128, 256, 32, 0))
+    assert call(sh=two) == "SX_ERR_BAD_SHAPE"
+    wide = _lib.SxBank(_lib.SxProj(FAKE, FAKE, FAKE, 1, 512, 128, 32, 0), _lib.SxProj(FAKE, FAKE, FAKE, 1, 512, 128, 32, 0),
+                       _lib.SxProj(FAKE, FAKE, FAKE, 1, 128, 512, 32, 0))
+    assert call(sh=wide) == "SX_ERR_BAD_SHAPE"
+    assert call(wsb=need - 1) == "SX_ERR_WORKSPACE_TOO_SMALL"

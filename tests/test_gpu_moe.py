@@ -254,3 +254,66 @@ def test_moe_wide_hidden_decode_chain(sx):
     truth = _truth(bank_np, D, I, 32, 32, oargs, xt.float().cpu().numpy(), inds, wts)
     assert max_rel(y, truth) <= MAX_REL_TOL, max_rel(y, truth)
     assert sx.device_error() == 0
+
+
+def _unfused(sx, x, bank, shb, inds, wts, dec, gate, shared_dec=None, ragged=False, clamp=0):
+    """The composition sx_moe_folded replaces: the shared expert as its own one-expert layer, its
+    output passed to the routed layer."""
+    T = x.shape[0]
+    one_i = torch.zeros((T, 1), dtype=torch.int32, device="cuda")
+    one_s = torch.ones((T, 1), device="cuda")
+    sh = sx.moe(x, shb, one_i, one_s, shared_dec or dec, clamp_limit=clamp)
+    fn = sx.moe_ragged if ragged else sx.moe
+    return fn(x, bank, inds, wts, dec, shared=sh, shared_gate=gate, clamp_limit=clamp)
+
+
+@pytest.mark.parametrize(
+    "T,n_sh,gated",
+    [(1, 32, True), (5, 32, False), (16, 32, True),  # same rate: folded into the routed launches
+     (3, 64, True),                                    # other rate, <= 16 rows: its own chain launches
+     (40, 32, True),                                   # > 16 rows: tensor-core path
+     (200, 32, True)],                                 # routed layer on the tensor-core path
+)
+def test_moe_folded_equals_unfused(sx, T, n_sh, gated):
+    """moe_shared_fold.folded: the routed layer with its shared expert in one call gives the bits of
+    the unfused composition (the shared expert's own layer output passed as `shared`), in each of
+    the three ways the shared expert runs."""
+    E, D, I, k = (16, 256, 128, 4) if T < 100 else (8, 256, 128, 2)
+    bank_np = _bank(600 + T, E, D, I, 32, 32)
+    sh_np = _bank(700 + T, 1, D, I, n_sh, n_sh)
+    _, dec = dec_args(orc.CB_MCG, 16)
+    b, shb = _sx_bank(sx, bank_np), _sx_bank(sx, sh_np)
+    x = torch.from_numpy(synth.activations(T + 5, T, D)).cuda().to(torch.bfloat16)
+    inds, wts = _route(T + 6, T, E, k)
+    ii, ww = torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda()
+    gate = torch.randn((T,), device="cuda").to(torch.bfloat16) if gated else None
+    want = _unfused(sx, x, b, shb, ii, ww, dec, gate)
+    got = sx.moe_folded(x, b, shb, ii, ww, dec, shared_gate=gate)
+    torch.cuda.synchronize()
+    assert sx.device_error() == 0
+    assert torch.equal(got, want)
+    got2 = sx.moe_folded(x, b, shb, ii, ww, dec, shared_gate=gate, clamp_limit=7)
+    want2 = _unfused(sx, x, b, shb, ii, ww, dec, gate, clamp=7)
+    torch.cuda.synchronize()
+    assert torch.equal(got2, want2)
+
+
+@pytest.mark.parametrize("T", [2, 24])
+def test_moe_ragged_folded_equals_unfused(sx, T):
+    """The DeepSeek shape of the fold: K1/K2 rate groups with a K4 shared expert (SPEC1 w15, whose
+    table has every rate), which runs as its own launches."""
+    D, I, k = 256, 128, 4
+    g0 = _bank(800 + T, 6, D, I, 16, 16)
+    g1 = _bank(900 + T, 10, D, I, 32, 32)
+    sh_np = _bank(950 + T, 1, D, I, 64, 64)
+    _, dec = dec_args(orc.CB_SPEC1, 15)
+    rb = sx.Ragged.from_banks([_sx_bank(sx, g0), _sx_bank(sx, g1)])
+    shb = _sx_bank(sx, sh_np)
+    x = torch.from_numpy(synth.activations(T + 7, T, D)).cuda().to(torch.bfloat16)
+    inds, wts = _route(T + 8, T, 16, k)
+    ii, ww = torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda()
+    want = _unfused(sx, x, rb, shb, ii, ww, dec, None, ragged=True)
+    got = sx.moe_folded(x, rb, shb, ii, ww, dec)
+    torch.cuda.synchronize()
+    assert sx.device_error() == 0
+    assert torch.equal(got, want)
