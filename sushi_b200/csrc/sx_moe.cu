@@ -343,20 +343,33 @@ __global__ void shared_route_kernel(uint32_t* inds, float* scores, int rows) {
     }
 }
 
-// The decode chain's split-K cluster size: about four 128-input blocks per CTA.  Measured on B200
-// over the 512-expert layer (hidden 2048, intermediate 512) at 1, 8 and 64 tokens, four blocks per
-// CTA was fastest for both the gate/up kernel (16 blocks: S = 4) and the down kernel (4 blocks:
-// S = 1): fewer blocks pay the cluster reduce more often, more blocks need prepared-input shared
-// memory that leaves one CTA per SM.
-int pick_split(int kb) {
-    constexpr int kBlocksPerCta = 4;
-    return std::max(1, std::min(16, (kb + kBlocksPerCta - 1) / kBlocksPerCta));
+}  // namespace
+
+int two_per_sm_smem() {
+    static int cached = 0;
+    if (cached <= 0) {
+        int dev = 0, per_sm = 0, reserve = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+        cudaDeviceGetAttribute(&reserve, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+        cached = per_sm > 0 ? per_sm / 2 - reserve : 112 * 1024;
+    }
+    return cached;
+}
+
+namespace {
+
+// The least split-K cluster size of a chain kernel over `units` (work items x output blocks):
+// enough CTAs to give every SM one; fit_split then grows it until two CTAs fit per SM.
+int min_split(long long units) {
+    const long long S = (sm_count() + std::max(1LL, units) - 1) / std::max(1LL, units);
+    return (int)std::max(1LL, std::min(16LL, S));
 }
 
 // The pair and down launches of the decode chain over `items` work items.
-cudaError_t chain_launch(const MoeArgs& a, int kind, int n_gu, int n_d, int items, cudaStream_t s) {
-    const int S_gu = pick_split(a.D / 128);
-    const int S_d = pick_split(a.I / 128);
+cudaError_t chain_launch(const MoeArgs& a, int kind, int n_gu, int n_d, int items, int active, cudaStream_t s) {
+    const int S_gu = min_split((long long)active * (a.I / 128));
+    const int S_d = min_split((long long)active * (a.D / 128));
     switch (kind) {
         case K_MCG: return moe_launch_kind<K_MCG>(a, n_gu, n_d, S_gu, S_d, items, s);
         case K_MUL1: return moe_launch_kind<K_MUL1>(a, n_gu, n_d, S_gu, S_d, items, s);
@@ -579,7 +592,7 @@ sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_de
             return cuda_status(e, "moe down gemm launch");
         return SX_OK;
     }
-    e = chain_launch(a, kind_gu, bank->gate.n, bank->down.n, L.W_max + a.sh_items, s);
+    e = chain_launch(a, kind_gu, bank->gate.n, bank->down.n, L.W_max + a.sh_items, L.A_max + a.sh_items, s);
     if (e != cudaSuccess) return cuda_status(e, "moe pair/down launch");
     return SX_OK;
 }
@@ -609,7 +622,8 @@ sx_status shared_chain(sx_stream stream, const sx_bank* sh, const sx_decode* dec
     a.sh_items = (rows + 7) / 8;
     a.sh_slot0 = rows * topk;
     set_shared_ptrs(a, *sh);
-    const cudaError_t e = chain_launch(a, kind_gu, sh->gate.n, sh->down.n, a.sh_items, reinterpret_cast<cudaStream_t>(stream));
+    const cudaError_t e = chain_launch(a, kind_gu, sh->gate.n, sh->down.n, a.sh_items, a.sh_items,
+                                       reinterpret_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? SX_OK : cuda_status(e, "shared expert pair/down launch");
 }
 

@@ -31,11 +31,19 @@ static cudaError_t launch_clustered(Kern kern, dim3 grid, int S, size_t smem, cu
     return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
-// The split grows until a CTA's input slice fits in shared memory (wide hidden sizes: 7168).
+// Shared memory that lets two CTAs share an SM (per-SM capacity / 2 less the per-block reserve).
+int two_per_sm_smem();
+
+// The split-K cluster size of a chain kernel: the smallest S >= S_min whose CTAs fit two per SM
+// (the chain kernels' registers allow two).  Measured on B200 over S for hidden 2048 / 7168 layers
+// at 1, 8 and 64 tokens: that S was fastest in every case; fewer splits leave one CTA per SM, more
+// pay the cluster reduce and per-CTA start-up more often.  S_min asks for enough CTAs to cover the
+// SMs when few experts are active.
 template <int N, int NP>
 static int fit_split(int S, int KB) {
     S = S < KB ? S : KB;
-    while (S < 16 && S < KB && core_layout<N, NP, 1>((KB + S - 1) / S).total > 200 * 1024) S++;
+    const size_t two = (size_t)two_per_sm_smem();
+    while (S < 16 && S < KB && core_layout<N, NP, 1>((KB + S - 1) / S).total > two) S++;
     return S;
 }
 
