@@ -412,8 +412,6 @@ def moe_bench(sx, _lib, torch, args, stream, sptr):
     shared, wg = qwen_shared(sx, torch, rgen, D, I)
     for T in (1, 8, 64):
         x = torch.randn((T, D), device="cuda", generator=gen).to(torch.bfloat16)
-        one_i = torch.zeros((T, 1), dtype=torch.int32, device="cuda")
-        one_s = torch.ones((T, 1), device="cuda")
 
         def layer(c):
             logits = (x @ wr).float()
@@ -421,8 +419,8 @@ def moe_bench(sx, _lib, torch, args, stream, sptr):
             gate = x @ wg
             if ep is None:  # the shared expert rides the routed launches
                 return sx.moe_folded(x, banks[c % copies], shared, inds, scores, dec, shared_gate=gate)
-            sh = sx.moe(x, shared, one_i, one_s, dec)
-            return ep.moe(x, banks[c % copies], E, inds, scores, dec, rows_cap=T, shared=sh, shared_gate=gate)
+            # expert parallel: the shared expert runs on the side stream during the exchange
+            return ep.moe(x, banks[c % copies], E, inds, scores, dec, rows_cap=T, shared_gate=gate, shared_bank=shared)
 
         for i in range(max(3, args.warmup)):
             layer(i)
@@ -492,17 +490,14 @@ def prefill_bench(sx, torch, args, stream, tf_peak):
     zb = (ranks ** -1.1)
     bias = torch.log(zb / zb.sum()).cuda()
     x = torch.randn((T, D), device="cuda", generator=gen).to(torch.bfloat16)
-    one_i = torch.zeros((T, 1), dtype=torch.int32, device="cuda")
-    one_s = torch.ones((T, 1), device="cuda")
     L = sx._lib.load()
-    ws_sh = torch.empty(L.sx_moe_workspace_bytes(ctypes.byref(shared.c()), T, 1), dtype=torch.uint8, device="cuda")
     ep = sx.ExpertParallel.from_process_group() if world > 1 else None
     if ep is None:
         d = dec.c()
         ws = torch.empty(L.sx_moe_folded_workspace_bytes(ctypes.byref(bank.c()), ctypes.byref(shared.c()), ctypes.byref(d),
                                                          None, T, k), dtype=torch.uint8, device="cuda")
     else:
-        ws = torch.empty(ep.workspace_bytes(bank, T, k), dtype=torch.uint8, device="cuda")
+        ws = torch.empty(ep.workspace_bytes(bank, T, k, shared_bank=shared), dtype=torch.uint8, device="cuda")
 
     def layer():
         logits = (x @ wr).float() + bias
@@ -510,8 +505,7 @@ def prefill_bench(sx, torch, args, stream, tf_peak):
         gate = x @ wg
         if ep is None:
             return sx.moe_folded(x, bank, shared, inds, scores, dec, shared_gate=gate, workspace=ws)
-        sh = sx.moe(x, shared, one_i, one_s, dec, workspace=ws_sh)
-        return ep.moe(x, bank, E, inds, scores, dec, rows_cap=T, shared=sh, shared_gate=gate, workspace=ws)
+        return ep.moe(x, bank, E, inds, scores, dec, rows_cap=T, shared_gate=gate, workspace=ws, shared_bank=shared)
 
     for _ in range(max(3, args.warmup)):
         layer()
@@ -552,8 +546,9 @@ def deepseek_bench(sx, torch, args, stream, tf_peak):
     x2.5).  Routed experts are STQ SPEC1 (window 15) in two rate groups, K1 (n16, experts 0..63) and
     K2 (n32, experts 64..255): 1.75 bits per weight on average; the group an expert falls in is
     fixed by its id range, which is how a rate-grouped pack orders experts.  The shared expert is K4
-    (n64), run as a one-expert layer through sx_moe.  Each layer: router, shared expert,
-    rate-grouped routed layer with the shared output added, residual add.  One GPU: sx_moe_ragged
+    (n64): in the routed call on one GPU (sx_moe_ragged_folded: its own chain launches, no routing
+    pass), on the side stream of the expert-parallel call at N > 1.  Each layer: router, shared
+    expert + rate-grouped routed layer, residual add.  One GPU: sx_moe_ragged
     over all 256 experts.  N GPUs: expert parallel (sx_ep_moe_ragged), rank g holding experts
     [g*256/N, (g+1)*256/N) as its own rate groups, every rank running the stack on its own T tokens
     (weak scaling); router and shared expert replicated.  Decode batches T = 1, 8, 64 (CUDA graph of
@@ -593,18 +588,14 @@ def deepseek_bench(sx, torch, args, stream, tf_peak):
     routed_gb = sum(sum(t.numel() * 2 for t in rb.trellis) for rb, _, _, _ in layers) / 1e9
     res = {"layers": L, "ranks": world, "routed_bits_per_weight": 1.75, "routed_gb_rank0": round(routed_gb, 2),
            "scaling": "weak (T tokens per rank)" if world > 1 else "one GPU"}
-    one = torch.zeros((1, 1), dtype=torch.int32, device="cuda")
     Lib = sx._lib.load()
     for T in (1, 8, 64, 4096):
         x0 = torch.randn((T, H), device="cuda", generator=gen).to(torch.bfloat16)
         d = dec.c()
-        routed_ws = (ep.workspace_bytes(layers[0][0], T, k) if ep is not None else
+        routed_ws = (ep.workspace_bytes(layers[0][0], T, k, shared_bank=layers[0][1]) if ep is not None else
                      Lib.sx_moe_ragged_folded_workspace_bytes(ctypes.byref(layers[0][0].c()),
                                                               ctypes.byref(layers[0][1].c()), ctypes.byref(d), None, T, k))
         ws = torch.empty(routed_ws, dtype=torch.uint8, device="cuda")
-        ws_sh = torch.empty(Lib.sx_moe_workspace_bytes(ctypes.byref(layers[0][1].c()), T, 1), dtype=torch.uint8,
-                            device="cuda")
-        ones_i, ones_s = one.expand(T, 1).contiguous(), torch.ones((T, 1), device="cuda")
 
         def stack():
             x = x0
@@ -613,9 +604,8 @@ def deepseek_bench(sx, torch, args, stream, tf_peak):
                                               route_scale=2.5)
                 if ep is None:  # the K4 shared expert in the same call as the K1/K2 routed groups
                     x = x + sx.moe_folded(x, rb, shared, inds, scores, dec, workspace=ws)
-                else:
-                    sh = sx.moe(x, shared, ones_i, ones_s, dec, workspace=ws_sh)
-                    x = x + ep.moe(x, rb, E, inds, scores, dec, rows_cap=T, shared=sh, workspace=ws)
+                else:  # the shared expert on the side stream while the rows are exchanged
+                    x = x + ep.moe(x, rb, E, inds, scores, dec, rows_cap=T, workspace=ws, shared_bank=shared)
             return x
 
         for _ in range(2):
@@ -655,7 +645,7 @@ def deepseek_bench(sx, torch, args, stream, tf_peak):
         flops = world * 2.0 * T * L * (k + 1) * 3 * H * I
         res[f"T{T}"] = {"tokens_per_s": round(world * T / (ms * 1e-3), 1), "ms_per_stack": round(ms, 3),
                         "tflops": round(flops / (ms * 1e-3) / 1e12, 1)}
-        del ws, ws_sh
+        del ws
     assert sx.device_error() == 0
     if ep is not None:
         torch.cuda.synchronize()

@@ -253,7 +253,9 @@ sx_status sx_moe_ragged(sx_stream stream, const sx_ragged* bank, const sx_decode
  * decoded with `shared_dec`, or `dec` when null; the same clamp_limit), optionally sigmoid-gated by
  * shared_gate [rows].  The shared expert rides the routed decode chain's launches when its rates,
  * decode and intermediate size match a routed group's; otherwise it runs as its own launches.
- * Results equal the unfused composition bit for bit.  workspace: the matching
+ * Each output matches the unfused composition (the same arithmetic per row); where the two take
+ * different k splits for the shared expert's products the f32 sums may differ in their last bit
+ * before rounding.  workspace: the matching
  * *_folded_workspace_bytes(...). */
 size_t sx_moe_folded_workspace_bytes(const sx_bank* bank, const sx_bank* shared_bank, const sx_decode* dec,
                                      const sx_decode* shared_dec, int32_t rows, int32_t topk);
@@ -350,6 +352,27 @@ sx_status sx_ep_moe_ragged(sx_ep* ep, sx_stream stream, const sx_ragged* local, 
                            const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
                            const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
                            size_t workspace_bytes);
+
+/* sx_ep_moe / sx_ep_moe_ragged with the layer's shared expert folded in (moe_shared_fold.folded,
+ * src/moe_shared_fold.zig:24): each rank runs the shared expert (a one-expert `shared_bank`,
+ * replicated on every rank; `shared_dec` or `dec`) over its own rows on the communicator's side
+ * stream, concurrently with the dispatch, the local experts and the combine exchange, and the
+ * combine adds it (rounded, optionally sigmoid-gated by shared_gate [rows]) as sx_moe_folded does.
+ * The caller's stream waits for the side stream before the call returns its work. */
+size_t sx_ep_folded_workspace_bytes(const sx_ep* ep, const sx_bank* local_bank, const sx_bank* shared_bank,
+                                    int32_t rows_cap, int32_t topk, sx_dtype dtype);
+sx_status sx_ep_moe_folded(sx_ep* ep, sx_stream stream, const sx_bank* local_bank, const sx_bank* shared_bank,
+                           int32_t experts_total, const sx_decode* dec, const sx_decode* shared_dec, const void* x,
+                           sx_dtype dtype, int32_t rows, int32_t rows_cap, const uint32_t* inds, const float* scores,
+                           int32_t topk, const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
+                           size_t workspace_bytes);
+size_t sx_ep_ragged_folded_workspace_bytes(const sx_ep* ep, const sx_ragged* local, const sx_bank* shared_bank,
+                                           int32_t rows_cap, int32_t topk, sx_dtype dtype);
+sx_status sx_ep_moe_ragged_folded(sx_ep* ep, sx_stream stream, const sx_ragged* local, const sx_bank* shared_bank,
+                                  int32_t experts_total, const sx_decode* dec, const sx_decode* shared_dec,
+                                  const void* x, sx_dtype dtype, int32_t rows, int32_t rows_cap, const uint32_t* inds,
+                                  const float* scores, int32_t topk, const void* shared_gate, int32_t clamp_limit,
+                                  void* y, void* workspace, size_t workspace_bytes);
 
 /* The communicator's world size and rank (either pointer may be null). */
 sx_status sx_ep_info(const sx_ep* ep, int32_t* world, int32_t* rank);

@@ -90,6 +90,12 @@ SIGNATURES = {
     "sx_ep_ragged_workspace_bytes": (_SZ, [_P, ctypes.POINTER(SxRagged), _I, _I, _I]),
     "sx_ep_moe_ragged": (_I, [_P, _P, ctypes.POINTER(SxRagged), _I, ctypes.POINTER(SxDecode), _P, _I, _I, _I, _P, _P,
                               _I, _P, _P, _I, _P, _P, _SZ]),
+    "sx_ep_folded_workspace_bytes": (_SZ, [_P, ctypes.POINTER(SxBank), ctypes.POINTER(SxBank), _I, _I, _I]),
+    "sx_ep_moe_folded": (_I, [_P, _P, ctypes.POINTER(SxBank), ctypes.POINTER(SxBank), _I, _P, _P, _P, _I, _I, _I, _P,
+                              _P, _I, _P, _I, _P, _P, _SZ]),
+    "sx_ep_ragged_folded_workspace_bytes": (_SZ, [_P, ctypes.POINTER(SxRagged), ctypes.POINTER(SxBank), _I, _I, _I]),
+    "sx_ep_moe_ragged_folded": (_I, [_P, _P, ctypes.POINTER(SxRagged), ctypes.POINTER(SxBank), _I, _P, _P, _P, _I, _I,
+                                     _I, _P, _P, _I, _P, _I, _P, _P, _SZ]),
     "sx_device_error": (_I, [_P]),
     "sx_selftest_wait_timeout": (_I, [_P, _I]),
     "sx_last_error_detail": (ctypes.c_char_p, []),

@@ -26,9 +26,14 @@
 #include "sx_internal.h"
 #include "sx_moe_impl.cuh"
 
+// side: a stream of the communicator's own on which a layer's shared expert runs while the
+// dispatch, the local experts and the combine's exchange run on the caller's stream (fork and
+// join are the events between the two).
 struct sx_ep {
     ncclComm_t comm;
     int world, rank, device;
+    cudaStream_t side;
+    cudaEvent_t fork, join;
 };
 
 namespace sx {
@@ -173,6 +178,7 @@ __global__ void __launch_bounds__(128) ep_gather_kernel(EpArgs a) {
 struct CombineArgs {
     const float* part;       // [world][cap][D]: from rank d, the partials of the rows sent to d
     const int* pos;          // [cap][world]
+    const float* sh_plane;   // [rows][D] f32: the shared expert's output before rounding, or null
     const void* shared;
     const void* shared_gate;
     void* y;
@@ -187,8 +193,9 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(CombineArgs a) {
             const int p = a.pos[(size_t)r * a.world + g];
             if (p >= 0) acc += a.part[((size_t)g * a.cap + p) * a.D + d];
         }
-        const float sh = a.shared ? load_act(a.shared, (size_t)r * a.D + d, a.xdt) : 0.0f;
-        const float y = routed_finish(acc, a.xdt, a.shared != nullptr, sh, a.shared_gate, r);
+        const size_t i = (size_t)r * a.D + d;
+        const float sh = a.sh_plane ? round_act(a.sh_plane[i], a.xdt) : a.shared ? load_act(a.shared, i, a.xdt) : 0.0f;
+        const float y = routed_finish(acc, a.xdt, a.sh_plane || a.shared, sh, a.shared_gate, r);
         store_act(a.y, (size_t)r * a.D + d, a.xdt, y);
     }
 }
@@ -200,10 +207,11 @@ size_t up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 struct EpWs {
     size_t list, pos, send_x, send_inds, send_scores, recv_x, recv_inds, recv_scores, part_send, part_recv, moe, total;
     size_t moe_bytes;
+    size_t sh_plane, sh_scratch;  // the shared expert's plane [cap][D] f32 and scratch (0 bytes without one)
 };
 
 // The layout for a local layer of `ng` rate groups (one for a uniform bank) over El experts.
-EpWs ep_ws_layout(const MoeGroup* g, int ng, int El, int world, int cap, int K, int esz) {
+EpWs ep_ws_layout(const MoeGroup* g, int ng, int El, int world, int cap, int K, int esz, const sx_bank* sh = nullptr) {
     EpWs w{};
     const int D = g[0].bank.gate.in_features;
     const size_t places = (size_t)world * cap;
@@ -222,6 +230,12 @@ EpWs ep_ws_layout(const MoeGroup* g, int ng, int El, int world, int cap, int K, 
     // spread over the world): that, not the places' sentinel-padded slots, picks its expert path
     w.moe_bytes = moe_groups_ws(g, ng, El, (int32_t)places, K, (long long)cap * K);
     w.moe = off; off = up(off + w.moe_bytes);
+    w.sh_plane = w.sh_scratch = off;
+    if (sh) {
+        off = up(off + (size_t)cap * D * sizeof(float));
+        w.sh_scratch = off;
+        off = up(off + shared_expert_ws(sh, cap));
+    }
     w.total = off;
     return w;
 }
@@ -263,6 +277,18 @@ sx_status all_to_all(const sx_ep* ep, const A2A* bufs, int nb, cudaStream_t s) {
     return st ? st : end;
 }
 
+// The side stream and its events (a failed stream sync is not reported: the handle goes anyway).
+void release_side(sx_ep* ep) {
+    if (ep->side) {
+        cudaStreamSynchronize(ep->side);
+        cudaStreamDestroy(ep->side);
+    }
+    if (ep->fork) cudaEventDestroy(ep->fork);
+    if (ep->join) cudaEventDestroy(ep->join);
+    ep->side = nullptr;
+    ep->fork = ep->join = nullptr;
+}
+
 }  // namespace
 }  // namespace sx
 
@@ -295,8 +321,19 @@ sx_status sx_ep_init(const uint8_t id[128], int32_t world, int32_t rank, sx_ep**
     ep->world = world;
     ep->rank = rank;
     cudaGetDevice(&ep->device);
+    ep->side = nullptr;
+    ep->fork = ep->join = nullptr;
+    cudaError_t ce = cudaStreamCreateWithFlags(&ep->side, cudaStreamNonBlocking);
+    if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&ep->fork, cudaEventDisableTiming);
+    if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&ep->join, cudaEventDisableTiming);
+    if (ce != cudaSuccess) {
+        release_side(ep);
+        delete ep;
+        return cuda_status(ce, "expert-parallel side stream");
+    }
     sx_status st = nccl_status(n.comm_init_rank(&ep->comm, world, u, rank), "ncclCommInitRank");
     if (st) {
+        release_side(ep);
         delete ep;
         return st;
     }
@@ -307,6 +344,7 @@ sx_status sx_ep_init(const uint8_t id[128], int32_t world, int32_t rank, sx_ep**
 sx_status sx_ep_destroy(sx_ep* ep) {
     if (!ep) return SX_ERR_NULL_POINTER;
     const sx_status st = nccl_status(nccl().comm_destroy(ep->comm), "ncclCommDestroy");
+    release_side(ep);
     delete ep;
     return st;
 }
@@ -314,6 +352,7 @@ sx_status sx_ep_destroy(sx_ep* ep) {
 sx_status sx_ep_abort(sx_ep* ep) {
     if (!ep) return SX_ERR_NULL_POINTER;
     const sx_status st = nccl_status(nccl().comm_abort(ep->comm), "ncclCommAbort");
+    release_side(ep);
     delete ep;
     return st;
 }
@@ -351,9 +390,10 @@ sx_status ep_moe_groups(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int
                         const sx_decode* dec, const void* x, sx_dtype dtype, int32_t rows, int32_t rows_cap,
                         const uint32_t* inds, const float* scores, int32_t topk, const void* shared,
                         const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
-                        size_t workspace_bytes) {
+                        size_t workspace_bytes, const sx_bank* sh_bank = nullptr, const sx_decode* sh_dec = nullptr) {
     if (rows > 0 && (!x || !inds || !scores || !y)) return SX_ERR_NULL_POINTER;
-    if (shared_gate && !shared) return SX_ERR_NULL_POINTER;
+    if (shared_gate && !shared && !sh_bank) return SX_ERR_NULL_POINTER;
+    if (sh_bank && shared) return SX_ERR_BAD_SHAPE;
     if (rows < 0 || rows_cap < 1 || rows > rows_cap || topk < 1) return SX_ERR_BAD_SHAPE;
     if (topk > 32) return SX_ERR_TOPK_EXCEEDS_REDUCE_BANK;
     if (!dtype_ok(dtype)) return SX_ERR_BAD_DTYPE;
@@ -363,8 +403,12 @@ sx_status ep_moe_groups(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int
     const int D = groups[0].bank.gate.in_features;
     if (D % 128) return SX_ERR_BAD_SHAPE;
     if (reinterpret_cast<uintptr_t>(x) % 16) return SX_ERR_BAD_SHAPE;  // rows move as 16-byte vectors
+    if (sh_bank) {
+        const sx_status st = check_shared_bank(sh_bank, D, sh_dec);
+        if (st) return st;
+    }
     const int esz = (int)dtype_size(dtype);
-    const EpWs L = ep_ws_layout(groups, ng, El, ep->world, rows_cap, topk, esz);
+    const EpWs L = ep_ws_layout(groups, ng, El, ep->world, rows_cap, topk, esz, sh_bank);
     if (!workspace || workspace_bytes < L.total) return SX_ERR_WORKSPACE_TOO_SMALL;
     if (!nccl().ok) return nccl_missing();
 
@@ -372,6 +416,32 @@ sx_status ep_moe_groups(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const int G = ep->world, C = rows_cap;
     const size_t places = (size_t)G * C;
+
+    // 0. the shared expert over this rank's own rows, on the side stream: it needs only x, so it
+    // runs while the rows are exchanged and the experts computed; the combine waits for it.
+    float* sh_plane = sh_bank && rows > 0 ? reinterpret_cast<float*>(ws + L.sh_plane) : nullptr;
+    if (sh_plane) {
+        cudaError_t ce = cudaEventRecord(ep->fork, s);
+        if (ce == cudaSuccess) ce = cudaStreamWaitEvent(ep->side, ep->fork, 0);
+        if (ce != cudaSuccess) return cuda_status(ce, "expert-parallel fork");
+        const sx_status st = shared_expert_run(reinterpret_cast<sx_stream>(ep->side), sh_bank, sh_dec, x, dtype, rows,
+                                               clamp_limit, sh_plane, ws + L.sh_scratch);
+        ce = cudaEventRecord(ep->join, ep->side);
+        if (st || ce != cudaSuccess) {
+            cudaStreamWaitEvent(s, ep->join, 0);
+            return st ? st : cuda_status(ce, "expert-parallel join");
+        }
+    }
+    // Every return below joins the side stream back into the caller's (the combine reads the plane).
+    bool joined = sh_plane == nullptr;
+    auto join = [&](sx_status st) {
+        if (!joined) {
+            const cudaError_t ce = cudaStreamWaitEvent(s, ep->join, 0);
+            joined = true;
+            if (!st && ce != cudaSuccess) st = cuda_status(ce, "expert-parallel join");
+        }
+        return st;
+    };
 
     EpArgs a{};
     a.x = x;
@@ -394,33 +464,35 @@ sx_status ep_moe_groups(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int
     // 1-2. plan and gather this rank's send blocks
     ep_plan_kernel<<<G, 256, 0, s>>>(a);
     cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_status(e, "ep plan launch");
+    if (e != cudaSuccess) return join(cuda_status(e, "ep plan launch"));
     ep_gather_kernel<<<dim3(C, G), 128, 0, s>>>(a);
-    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "ep gather launch");
+    if ((e = cudaGetLastError()) != cudaSuccess) return join(cuda_status(e, "ep gather launch"));
 
     // 3. dispatch: rows, slot ids and scores in one NCCL group
     sx_status st;
     const A2A dispatch[3] = {{ws + L.send_x, ws + L.recv_x, (size_t)C * D * esz},
                              {ws + L.send_inds, ws + L.recv_inds, (size_t)C * topk * 4},
                              {ws + L.send_scores, ws + L.recv_scores, (size_t)C * topk * 4}};
-    if ((st = all_to_all(ep, dispatch, 3, s))) return st;
+    if ((st = all_to_all(ep, dispatch, 3, s))) return join(st);
 
     // 4. the local experts over every received row, partials in f32
     float* part_send = reinterpret_cast<float*>(ws + L.part_send);
     st = moe_run(stream, groups, ng, El, dec, ws + L.recv_x, dtype, (int32_t)places,
                  reinterpret_cast<const uint32_t*>(ws + L.recv_inds), reinterpret_cast<const float*>(ws + L.recv_scores),
                  topk, nullptr, nullptr, clamp_limit, nullptr, ws + L.moe, L.moe_bytes, part_send, (long long)C * topk);
-    if (st) return st;
+    if (st) return join(st);
 
     // 5. combine: partials back to the rows' owners
     const A2A combine[1] = {{part_send, ws + L.part_recv, (size_t)C * D * sizeof(float)}};
-    if ((st = all_to_all(ep, combine, 1, s))) return st;
+    if ((st = all_to_all(ep, combine, 1, s))) return join(st);
 
     // 6. rank-order sum, rounding, shared expert
+    if ((st = join(SX_OK))) return st;
     if (rows == 0) return SX_OK;
     CombineArgs c{};
     c.part = reinterpret_cast<const float*>(ws + L.part_recv);
     c.pos = a.pos;
+    c.sh_plane = sh_plane;
     c.shared = shared;
     c.shared_gate = shared_gate;
     c.y = y;
@@ -460,6 +532,50 @@ sx_status sx_ep_moe_ragged(sx_ep* ep, sx_stream stream, const sx_ragged* local, 
     if (st) return st;
     return ep_moe_groups(ep, stream, g, ng, local->experts, experts_total, dec, x, dtype, rows, rows_cap, inds, scores,
                          topk, shared, shared_gate, clamp_limit, y, workspace, workspace_bytes);
+}
+
+size_t sx_ep_folded_workspace_bytes(const sx_ep* ep, const sx_bank* local_bank, const sx_bank* shared_bank,
+                                    int32_t rows_cap, int32_t topk, sx_dtype dtype) {
+    if (!ep || !local_bank || !shared_bank || rows_cap < 1 || topk < 1 || !dtype_ok(dtype)) return 0;
+    const MoeGroup g{*local_bank, 0};
+    return ep_ws_layout(&g, 1, local_bank->gate.experts, ep->world, rows_cap, topk, (int)dtype_size(dtype), shared_bank)
+        .total;
+}
+
+size_t sx_ep_ragged_folded_workspace_bytes(const sx_ep* ep, const sx_ragged* local, const sx_bank* shared_bank,
+                                           int32_t rows_cap, int32_t topk, sx_dtype dtype) {
+    if (!ep || !local || !shared_bank || rows_cap < 1 || topk < 1 || !dtype_ok(dtype)) return 0;
+    MoeGroup g[kMaxGroups];
+    int ng = 0;
+    if (ragged_groups(local, g, &ng) != SX_OK) return 0;
+    return ep_ws_layout(g, ng, local->experts, ep->world, rows_cap, topk, (int)dtype_size(dtype), shared_bank).total;
+}
+
+sx_status sx_ep_moe_folded(sx_ep* ep, sx_stream stream, const sx_bank* local_bank, const sx_bank* shared_bank,
+                           int32_t experts_total, const sx_decode* dec, const sx_decode* shared_dec, const void* x,
+                           sx_dtype dtype, int32_t rows, int32_t rows_cap, const uint32_t* inds, const float* scores,
+                           int32_t topk, const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
+                           size_t workspace_bytes) {
+    if (!ep || !local_bank || !shared_bank) return SX_ERR_NULL_POINTER;
+    const MoeGroup g{*local_bank, 0};
+    return ep_moe_groups(ep, stream, &g, 1, local_bank->gate.experts, experts_total, dec, x, dtype, rows, rows_cap,
+                         inds, scores, topk, nullptr, shared_gate, clamp_limit, y, workspace, workspace_bytes,
+                         shared_bank, shared_dec ? shared_dec : dec);
+}
+
+sx_status sx_ep_moe_ragged_folded(sx_ep* ep, sx_stream stream, const sx_ragged* local, const sx_bank* shared_bank,
+                                  int32_t experts_total, const sx_decode* dec, const sx_decode* shared_dec,
+                                  const void* x, sx_dtype dtype, int32_t rows, int32_t rows_cap, const uint32_t* inds,
+                                  const float* scores, int32_t topk, const void* shared_gate, int32_t clamp_limit,
+                                  void* y, void* workspace, size_t workspace_bytes) {
+    if (!ep || !local || !shared_bank) return SX_ERR_NULL_POINTER;
+    MoeGroup g[kMaxGroups];
+    int ng = 0;
+    const sx_status st = ragged_groups(local, g, &ng);
+    if (st) return st;
+    return ep_moe_groups(ep, stream, g, ng, local->experts, experts_total, dec, x, dtype, rows, rows_cap, inds, scores,
+                         topk, nullptr, shared_gate, clamp_limit, y, workspace, workspace_bytes, shared_bank,
+                         shared_dec ? shared_dec : dec);
 }
 
 }  // extern "C"

@@ -49,6 +49,12 @@ sx_status moe_run(sx_stream stream, const MoeGroup* groups, int ng, int Etot, co
                   size_t workspace_bytes, float* partial, long long slots, const sx_bank* sh_bank = nullptr,
                   const sx_decode* sh_dec = nullptr);
 size_t moe_groups_ws(const MoeGroup* g, int ng, int Etot, int rows, int topk, long long slots);
+// A layer's shared expert (one SwiGLU expert over hidden size D): its admission, and its output
+// over `rows` rows alone into plane [rows][D] f32 with shared_expert_ws(sh, rows) bytes of scratch.
+sx_status check_shared_bank(const sx_bank* sh, int D, const sx_decode* dec);
+size_t shared_expert_ws(const sx_bank* sh, int rows);
+sx_status shared_expert_run(sx_stream stream, const sx_bank* sh, const sx_decode* dec, const void* x, sx_dtype dtype,
+                            int32_t rows, int32_t clamp_limit, float* plane, uint8_t* scratch);
 // The groups of a ragged layer (at most kMaxGroups) from its host meta table.
 sx_status ragged_groups(const sx_ragged* rb, MoeGroup* out, int* ng);
 

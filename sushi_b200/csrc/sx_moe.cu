@@ -404,8 +404,8 @@ bool same_decode(const sx_decode* a, const sx_decode* b) {
 // decode-chain launches of a routed group with its rates, decode and intermediate size (no launch
 // of its own), else as its own pair and down launches of the chain (no routing pass); more rows
 // through the tensor-core path with a routing of every row to it.  Each is the path a one-expert
-// layer of those rows takes, so the result is the unfused composition's.  Its output is the plane
-// of slots rows*topk + row.
+// layer of those rows takes, so the arithmetic per row is the unfused composition's (its k split
+// may differ).  Its output is the plane of slots rows*topk + row.
 struct SharedPlan {
     int mode;   // 0 none, 1 folded into `group`, 2 chain launches of its own, 3 tensor-core path
     int group;
@@ -627,6 +627,47 @@ sx_status shared_chain(sx_stream stream, const sx_bank* sh, const sx_decode* dec
     return e == cudaSuccess ? SX_OK : cuda_status(e, "shared expert pair/down launch");
 }
 
+// The shared expert of a layer: one SwiGLU expert over the layer's hidden size, rates the
+// decode serves (validateClampedProjection for each projection, src/exl3/root.zig:117-135).
+sx_status check_shared_bank(const sx_bank* sh, int D, const sx_decode* dec) {
+    sx_status st;
+    if (!sh) return SX_ERR_NULL_POINTER;
+    if ((st = check_proj(&sh->gate, 1)) || (st = check_proj(&sh->up, 1)) || (st = check_proj(&sh->down, 1))) return st;
+    const int Is = sh->gate.out_features;
+    if (sh->gate.in_features != D || sh->up.in_features != D || sh->up.out_features != Is ||
+        sh->down.in_features != Is || sh->down.out_features != D)
+        return SX_ERR_BAD_SHAPE;
+    if (sh->gate.tile_order != SX_TILE_PACK || sh->up.tile_order != SX_TILE_PACK || sh->down.tile_order != SX_TILE_PACK)
+        return SX_ERR_TILE_ORDER_UNSUPPORTED;
+    if (sh->gate.n != sh->up.n) return SX_ERR_TRELLIS_GEOMETRY;
+    int kind;
+    DecParams dp;
+    if ((st = resolve_decode(dec, sh->gate.n, &kind, &dp)) || (st = resolve_decode(dec, sh->down.n, &kind, &dp)))
+        return st;
+    return SX_OK;
+}
+
+size_t shared_expert_ws(const sx_bank* sh, int rows) {
+    const int D = sh->gate.in_features, Is = sh->gate.out_features;
+    if (rows <= kDecodeRowsMax) return align_up((size_t)rows * Is * sizeof(uint16_t));
+    return moe_ws_layout(1, rows, 1, D, Is, sh->gate.n, sh->down.n, rows, false).total + shared_fill_bytes(rows);
+}
+
+// The shared expert alone over `rows` rows into plane [rows][D] (f32, before rounding): its own
+// decode-chain launches up to 16 rows, else the tensor-core path with every row routed to it.
+sx_status shared_expert_run(sx_stream stream, const sx_bank* sh, const sx_decode* dec, const void* x, sx_dtype dtype,
+                            int32_t rows, int32_t clamp_limit, float* plane, uint8_t* scratch) {
+    if (rows <= kDecodeRowsMax) return shared_chain(stream, sh, dec, x, dtype, rows, 0, clamp_limit, plane, scratch);
+    const MoeWs L = moe_ws_layout(1, rows, 1, sh->gate.in_features, sh->gate.out_features, sh->gate.n, sh->down.n, rows,
+                                  false);
+    uint32_t* sh_inds = reinterpret_cast<uint32_t*>(scratch + L.total);
+    float* sh_scores = reinterpret_cast<float*>(sh_inds + rows);
+    shared_route_kernel<<<(rows + 255) / 256, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(sh_inds, sh_scores, rows);
+    const sx_status st = cuda_status(cudaGetLastError(), "shared route launch");
+    if (st) return st;
+    return moe_group(stream, sh, 0, dec, x, dtype, rows, sh_inds, sh_scores, 1, clamp_limit, plane, scratch, rows);
+}
+
 // A routed layer of groups: every group's chain into the per-slot planes, then the k-order reduce
 // over all slots (rounding, shared expert; or an expert-parallel rank's f32 partial).
 sx_status moe_run(sx_stream stream, const MoeGroup* groups, int ng, int Etot, const sx_decode* dec, const void* x,
@@ -664,26 +705,9 @@ sx_status moe_run(sx_stream stream, const MoeGroup* groups, int ng, int Etot, co
             return st;
     }
     if (sh_bank) {
-        // the shared expert: one SwiGLU expert over the same rows (validateClampedProjection)
-        sx_status st;
         if (shared || partial) return SX_ERR_BAD_SHAPE;
-        if ((st = check_proj(&sh_bank->gate, 1)) || (st = check_proj(&sh_bank->up, 1)) ||
-            (st = check_proj(&sh_bank->down, 1)))
-            return st;
-        const int Is = sh_bank->gate.out_features;
-        if (sh_bank->gate.in_features != D || sh_bank->up.in_features != D || sh_bank->up.out_features != Is ||
-            sh_bank->down.in_features != Is || sh_bank->down.out_features != D)
-            return SX_ERR_BAD_SHAPE;
-        if (sh_bank->gate.tile_order != SX_TILE_PACK || sh_bank->up.tile_order != SX_TILE_PACK ||
-            sh_bank->down.tile_order != SX_TILE_PACK)
-            return SX_ERR_TILE_ORDER_UNSUPPORTED;
-        if (sh_bank->gate.n != sh_bank->up.n) return SX_ERR_TRELLIS_GEOMETRY;
-        int kind;
-        DecParams dp;
-        if ((st = resolve_decode(sh_dec, sh_bank->gate.n, &kind, &dp)) ||
-            (st = resolve_decode(sh_dec, sh_bank->down.n, &kind, &dp)))
-            return st;
-        if (reinterpret_cast<uintptr_t>(x) % 16) return SX_ERR_BAD_SHAPE;  // the shared plane's rows: 16-byte vectors
+        const sx_status st = check_shared_bank(sh_bank, D, sh_dec);
+        if (st) return st;
     }
     if (!workspace || workspace_bytes < moe_groups_ws(groups, ng, Etot, rows, topk, slots, sh_bank, dec, sh_dec))
         return SX_ERR_WORKSPACE_TOO_SMALL;
@@ -702,16 +726,8 @@ sx_status moe_run(sx_stream stream, const MoeGroup* groups, int ng, int Etot, co
         const sx_status st = shared_chain(stream, sh_bank, sh_dec, x, dtype, rows, topk, clamp_limit, yslot, scratch);
         if (st) return st;
     } else if (plan.mode == 3) {
-        const MoeWs L = moe_ws_layout(1, rows, 1, D, sh_bank->gate.out_features, sh_bank->gate.n, sh_bank->down.n, rows,
-                                      false);
-        uint32_t* sh_inds = reinterpret_cast<uint32_t*>(scratch + L.total);
-        float* sh_scores = reinterpret_cast<float*>(sh_inds + rows);
-        shared_route_kernel<<<(rows + 255) / 256, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(sh_inds, sh_scores,
-                                                                                                    rows);
-        sx_status st = cuda_status(cudaGetLastError(), "shared route launch");
-        if (!st)
-            st = moe_group(stream, sh_bank, 0, sh_dec, x, dtype, rows, sh_inds, sh_scores, 1, clamp_limit,
-                           yslot + (size_t)rows * topk * D, scratch, rows);
+        const sx_status st = shared_expert_run(stream, sh_bank, sh_dec, x, dtype, rows, clamp_limit,
+                                               yslot + (size_t)rows * topk * D, scratch);
         if (st) return st;
     }
     MoeArgs r{};

@@ -442,7 +442,8 @@ def moe_folded(x, bank, shared_bank: Bank, inds, scores, dec: Decode, shared_gat
     """moe_shared_fold.folded: the routed layer (a Bank, or a Ragged layer) plus its shared expert
     `shared_bank` (one SwiGLU expert), optionally sigmoid-gated by shared_gate [rows], in one call;
     the shared expert rides the routed launches where its rates and decode match.  Returns x's
-    shape and dtype; equals moe(..., shared=<the shared expert's own output>, shared_gate=...)."""
+    shape and dtype; the arithmetic of moe(..., shared=<the shared expert's own output>,
+    shared_gate=...), up to the k split of the shared expert's products."""
     shape = x.shape
     x2 = x.reshape(-1, shape[-1]).contiguous()
     rows = x2.shape[0]
@@ -526,18 +527,25 @@ class ExpertParallel:
 
         return cls(share_unique_id(group), dist.get_world_size(group), dist.get_rank(group))
 
-    def workspace_bytes(self, local_bank, rows_cap: int, topk: int, dtype=torch.bfloat16) -> int:
+    def workspace_bytes(self, local_bank, rows_cap: int, topk: int, dtype=torch.bfloat16, shared_bank=None) -> int:
         """Workspace bytes for a local Bank (sx_ep_workspace_bytes) or Ragged layer
-        (sx_ep_ragged_workspace_bytes)."""
+        (sx_ep_ragged_workspace_bytes); with a shared expert, the *_folded_* variants."""
         b = local_bank.c()
-        fn = lib().sx_ep_ragged_workspace_bytes if isinstance(local_bank, Ragged) else lib().sx_ep_workspace_bytes
+        ragged = isinstance(local_bank, Ragged)
+        if shared_bank is not None:
+            sb = shared_bank.c()
+            fn = lib().sx_ep_ragged_folded_workspace_bytes if ragged else lib().sx_ep_folded_workspace_bytes
+            return int(fn(self._h, ctypes.byref(b), ctypes.byref(sb), int(rows_cap), int(topk), _DT[dtype]))
+        fn = lib().sx_ep_ragged_workspace_bytes if ragged else lib().sx_ep_workspace_bytes
         return int(fn(self._h, ctypes.byref(b), int(rows_cap), int(topk), _DT[dtype]))
 
     def moe(self, x, local_bank, experts_total: int, inds, scores, dec: Decode, rows_cap: int,
-            shared=None, shared_gate=None, clamp_limit=0, workspace=None):
+            shared=None, shared_gate=None, clamp_limit=0, workspace=None, shared_bank=None, shared_dec=None):
         """sx_ep_moe (local_bank a Bank) or sx_ep_moe_ragged (a Ragged layer of this rank's
         experts): this rank's rows x [rows, D] with GLOBAL expert ids inds [rows, K]; every rank
-        calls it with the same rows_cap, K, experts_total and dtype.  Returns y [rows, D]."""
+        calls it with the same rows_cap, K, experts_total and dtype.  Returns y [rows, D].  With
+        `shared_bank` (the layer's shared expert, replicated on every rank) the *_folded entries run
+        it over this rank's rows alongside the exchange and add it in the combine."""
         x2 = x.reshape(-1, x.shape[-1]).contiguous()
         rows = x2.shape[0]
         if x2.dtype not in _DT:
@@ -549,7 +557,7 @@ class ExpertParallel:
             raise Exl3Error(1)
         ragged = isinstance(local_bank, Ragged)
         b = local_bank.c()
-        need = self.workspace_bytes(local_bank, rows_cap, topk, x2.dtype)
+        need = self.workspace_bytes(local_bank, rows_cap, topk, x2.dtype, shared_bank)
         if need == 0 and ragged:
             raise Exl3Error(19)
         if workspace is None:
@@ -562,6 +570,15 @@ class ExpertParallel:
         d = dec.c()
         sh = None if shared is None else shared.reshape(rows, -1).to(x2.dtype).contiguous()
         sg = None if shared_gate is None else shared_gate.reshape(rows).to(x2.dtype).contiguous()
+        if shared_bank is not None:
+            sb = shared_bank.c()
+            sd = shared_dec.c() if shared_dec is not None else None
+            fn = lib().sx_ep_moe_ragged_folded if ragged else lib().sx_ep_moe_folded
+            _check(fn(self._h, _stream(), ctypes.byref(b), ctypes.byref(sb), int(experts_total), ctypes.byref(d),
+                      ctypes.byref(sd) if sd is not None else None, x2.data_ptr(), _DT[x2.dtype], rows,
+                      int(rows_cap), ix.data_ptr(), sc.data_ptr(), topk, None if sg is None else sg.data_ptr(),
+                      int(clamp_limit), y.data_ptr(), ws.data_ptr(), ws.numel()))
+            return y.reshape(x.shape)
         fn = lib().sx_ep_moe_ragged if ragged else lib().sx_ep_moe
         _check(fn(self._h, _stream(), ctypes.byref(b), int(experts_total), ctypes.byref(d), x2.data_ptr(),
                   _DT[x2.dtype], rows, int(rows_cap), ix.data_ptr(), sc.data_ptr(), topk,

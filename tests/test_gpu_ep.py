@@ -152,6 +152,35 @@ def test_ep_ragged_world1_is_bit_identical_to_moe_ragged(sx, T):
         ep.destroy()
 
 
+@pytest.mark.parametrize("T", [1, 6, 20])
+def test_ep_folded_world1_equals_unfused(sx, T):
+    """sx_ep_moe_folded over a world of one: the shared expert, run on the side stream over the
+    rank's rows, gives the bits of the unfused composition (its own layer output passed as
+    `shared` to sx_ep_moe), gated and ungated; the caller's stream sees the result."""
+    E, D, I, k = 16, 256, 128, 4
+    bank_np = _bank_np(140 + T, E, D, I, 32)
+    sh_np = _bank_np(150 + T, 1, D, I, 32)
+    _, dec = dec_args(orc.CB_MCG, 16)
+    b, shb = _bank(sx, bank_np), _bank(sx, sh_np)
+    xt = torch.from_numpy(synth.activations(T + 2, T, D)).cuda().to(torch.bfloat16)
+    inds, wts = _route(T + 3, T, E, k)
+    ii, ww = torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda()
+    gate = torch.randn((T,), device="cuda").to(torch.bfloat16)
+    one_i = torch.zeros((T, 1), dtype=torch.int32, device="cuda")
+    one_s = torch.ones((T, 1), device="cuda")
+    ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0)
+    try:
+        for g in (None, gate):
+            sh = sx.moe(xt, shb, one_i, one_s, dec)
+            want = ep.moe(xt, b, E, ii, ww, dec, rows_cap=T, shared=sh, shared_gate=g)
+            got = ep.moe(xt, b, E, ii, ww, dec, rows_cap=T, shared_gate=g, shared_bank=shb)
+            torch.cuda.synchronize()
+            assert torch.equal(want, got), g is None
+        assert sx.device_error() == 0
+    finally:
+        ep.destroy()
+
+
 # ------------------------------------------------------------------ two GPUs
 def _rank_main(rank, world, port, out_dir):
     import torch.distributed as dist

@@ -277,7 +277,7 @@ def _unfused(sx, x, bank, shb, inds, wts, dec, gate, shared_dec=None, ragged=Fal
 def test_moe_folded_equals_unfused(sx, T, n_sh, gated):
     """moe_shared_fold.folded: the routed layer with its shared expert in one call gives the bits of
     the unfused composition (the shared expert's own layer output passed as `shared`), in each of
-    the three ways the shared expert runs."""
+    the three ways the shared expert runs (at these sizes both take the same k split)."""
     E, D, I, k = (16, 256, 128, 4) if T < 100 else (8, 256, 128, 2)
     bank_np = _bank(600 + T, E, D, I, 32, 32)
     sh_np = _bank(700 + T, 1, D, I, n_sh, n_sh)
