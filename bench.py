@@ -410,7 +410,10 @@ def moe_bench(sx, _lib, torch, args, stream, sptr):
     rgen.manual_seed(7)  # the router and the shared expert are replicated: same weights on every rank
     wr = (torch.randn((D, E), device="cuda", generator=rgen) * 0.02).to(torch.bfloat16)
     shared, wg = qwen_shared(sx, torch, rgen, D, I)
-    for T in (1, 8, 64):
+    # T tokens per rank; at N > 1 also 64 / N per rank: the 64-token step split over the ranks
+    # (equal total tokens per step: the strong-scaling point of the expert-parallel layer)
+    Ts = [1, 8, 64] + ([64 // world] if world > 1 and 64 // world not in (1, 8, 64) else [])
+    for T in Ts:
         x = torch.randn((T, D), device="cuda", generator=gen).to(torch.bfloat16)
 
         def layer(c):
@@ -452,6 +455,8 @@ def moe_bench(sx, _lib, torch, args, stream, sptr):
         active = int(torch.unique(inds).numel())
         res[f"T{T}"] = {"tokens_per_s": round(world * T / (ms * 1e-3), 1), "ms_per_layer": round(ms, 4),
                         "tokens_per_rank": T, "active_experts_rank0_tokens": active}
+    if world > 1:
+        res["equal_total_64_tokens"] = f"T{64 // world}"
     if ep is not None:
         torch.cuda.synchronize()
         ep.destroy()

@@ -317,3 +317,34 @@ def test_moe_ragged_folded_equals_unfused(sx, T):
     torch.cuda.synchronize()
     assert sx.device_error() == 0
     assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("T", [1, 9])
+def test_moe_chained_layers_match_synchronised_layers(sx, T):
+    """The decode chain's kernels start early (programmatic dependent launch) and wait for their
+    predecessor before touching global memory: layers whose input is the previous layer's output,
+    issued back to back (routing included), give the bits of the same layers with a device
+    synchronisation between them, with the shared expert folded and not."""
+    E, D, I, k, L = 16, 256, 128, 4, 5
+    banks = [_sx_bank(sx, _bank(1000 + 10 * l, E, D, I, 32, 32)) for l in range(L)]
+    shb = _sx_bank(sx, _bank(1100, 1, D, I, 32, 32))
+    _, dec = dec_args(orc.CB_MCG, 16)
+    wr = torch.randn((D, E), device="cuda") * 0.05
+    x0 = torch.from_numpy(synth.activations(T + 11, T, D)).cuda().to(torch.bfloat16)
+
+    def run(sync, fold):
+        x = x0
+        for l in range(L):
+            inds, scores = sx.router_topk((x.float() @ wr), k)
+            y = (sx.moe_folded(x, banks[l], shb, inds, scores, dec) if fold else sx.moe(x, banks[l], inds, scores, dec))
+            x = (x.float() + y.float()).to(torch.bfloat16)
+            if sync:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        return x
+
+    for fold in (False, True):
+        want = run(True, fold)
+        for _ in range(3):
+            assert torch.equal(run(False, fold), want), fold
+    assert sx.device_error() == 0
