@@ -6,6 +6,9 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "../../include/sushi_exl3.h"
 #include "sx_decode.cuh"
@@ -102,6 +105,25 @@ int sm_count() {
 
 // sx_linear_shared_normed's workspace: the block counter, then [16 rows][out/128 blocks] f32 sums.
 constexpr size_t kNormHeader = 16;
+
+cudaError_t func_attrs(const void* kern, int smem, bool nonportable) {
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, std::pair<int, bool>> done;  // (kernel, device) -> settings
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(mu);
+    auto& d = done[{kern, dev}];
+    if (smem > d.first) {
+        if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) != cudaSuccess) return e;
+        d.first = smem;
+    }
+    if (nonportable && !d.second) {
+        if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1)) != cudaSuccess) return e;
+        d.second = true;
+    }
+    return cudaSuccess;
+}
 
 sx_status linear_impl(sx_stream stream, const sx_proj* proj, const sx_decode* dec, const void* x, sx_dtype dtype,
                       int32_t rows, void* y, int groups, uint32_t flags, const int32_t* cols = nullptr,

@@ -10,6 +10,11 @@
 
 namespace sx {
 
+// A kernel's dynamic shared-memory limit (at least `smem` bytes) and, with `nonportable`, its
+// non-portable cluster sizes, set on the current device once: later calls that ask for no more
+// return without a driver call (host; sx_capi.cu).
+cudaError_t func_attrs(const void* kern, int smem, bool nonportable);
+
 // Codes a kernel latches when a bounded wait gives up (read by sx_device_error).
 enum DeviceError : int {
     DEV_OK = 0,

@@ -13,12 +13,8 @@ static cudaError_t launch_gemm_t(const CUtensorMap& pmap, const GemmArgs& a, int
     if (PAIR && (S != 1 || (a.out / 128) % 2)) return cudaErrorInvalidValue;  // pairs: no split, even blocks
     auto kern = gemm_kernel<KIND, N, NT, RT, false, PAIR>;
     const int smem = GemmLayout<N, NT, RT, PAIR>::ALLOC;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = func_attrs((const void*)kern, smem, S > 8);
     if (e != cudaSuccess) return e;
-    if (S > 8) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        if (e != cudaSuccess) return e;
-    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.out / 128, items, S);
     cfg.blockDim = dim3(kGemmThreads, 1, 1);

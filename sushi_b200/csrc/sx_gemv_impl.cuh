@@ -211,12 +211,8 @@ static cudaError_t launch_gemv_t(const GemvArgs& a, int groups, cudaStream_t str
         remember_split(key, S);
     }
     const CoreLayout L = core_layout<N, 1, NB>((KB + S - 1) / S, mg);
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
+    e = func_attrs((const void*)kern, (int)L.total, S > 8);
     if (e != cudaSuccess) return e;
-    if (S > 8) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        if (e != cudaSuccess) return e;
-    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(OB, S, groups);
     cfg.blockDim = dim3(kGemvThreads, 1, 1);

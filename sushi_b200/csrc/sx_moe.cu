@@ -518,7 +518,7 @@ sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_de
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const size_t rp_smem = 3 * (size_t)E * sizeof(int);
     cudaError_t e = cudaSuccess;
-    if (rp_smem > 48 * 1024) e = cudaFuncSetAttribute(route_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rp_smem);
+    if (rp_smem > 48 * 1024) e = func_attrs((const void*)route_prep_kernel, (int)rp_smem, false);
     if (e == cudaSuccess) e = launch_pdl(route_prep_kernel, dim3(1), dim3(1024), rp_smem, s, a);
     if (e != cudaSuccess) return cuda_status(e, "route_prep launch");
     if (L.gemm) {

@@ -8,12 +8,8 @@ namespace sx {
 
 template <typename Kern>
 static cudaError_t launch_clustered(Kern kern, dim3 grid, int S, size_t smem, cudaStream_t stream, const MoeArgs& a) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const cudaError_t e = func_attrs((const void*)kern, (int)smem, S > 8);
     if (e != cudaSuccess) return e;
-    if (S > 8) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        if (e != cudaSuccess) return e;
-    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kThreads, 1, 1);
