@@ -417,9 +417,13 @@ def moe_bench(sx, _lib, torch, args, stream, sptr):
         x = torch.randn((T, D), device="cuda", generator=gen).to(torch.bfloat16)
 
         def layer(c):
-            logits = (x @ wr).float()
-            inds, scores = sx.router_topk(logits, k)
-            gate = x @ wg
+            # bf16 logits straight into the router; at one token the router launch also computes
+            # the shared expert's gate logit (the reference's softmax_gate, rows == 1 only)
+            if T == 1:
+                inds, scores, gate = sx.router_topk_gate(x @ wr, k, gate=(x, wg))
+            else:
+                inds, scores, _ = sx.router_topk_gate(x @ wr, k)
+                gate = x @ wg
             if ep is None:  # the shared expert rides the routed launches
                 return sx.moe_folded(x, banks[c % copies], shared, inds, scores, dec, shared_gate=gate)
             # expert parallel: the shared expert runs on the side stream during the exchange
@@ -506,7 +510,7 @@ def prefill_bench(sx, torch, args, stream, tf_peak):
 
     def layer():
         logits = (x @ wr).float() + bias
-        inds, scores = sx.router_topk(logits, k)
+        inds, scores, _ = sx.router_topk_gate(logits, k)
         gate = x @ wg
         if ep is None:
             return sx.moe_folded(x, bank, shared, inds, scores, dec, shared_gate=gate, workspace=ws)
@@ -605,8 +609,8 @@ def deepseek_bench(sx, torch, args, stream, tf_peak):
         def stack():
             x = x0
             for rb, shared, wr, bias in layers:
-                inds, scores = sx.router_topk((x @ wr).float(), k, sx.RouterMode.SIGMOID_BIAS, bias, route_norm=True,
-                                              route_scale=2.5)
+                inds, scores, _ = sx.router_topk_gate(x @ wr, k, mode=sx.RouterMode.SIGMOID_BIAS, bias=bias,
+                                                      route_norm=True, route_scale=2.5)
                 if ep is None:  # the K4 shared expert in the same call as the K1/K2 routed groups
                     x = x + sx.moe_folded(x, rb, shared, inds, scores, dec, workspace=ws)
                 else:  # the shared expert on the side stream while the rows are exchanged

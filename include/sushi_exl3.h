@@ -196,6 +196,21 @@ sx_status sx_router_topk(sx_stream stream, const float* logits, const float* bia
                          int32_t k, int32_t mode, int32_t renorm, float scale, int32_t n_group, int32_t topk_group,
                          uint32_t* inds, float* scores);
 
+/* moeRouterTopKGate (src/moe_router.zig:457): sx_router_topk over logits of any activation dtype
+ * (`logits_dtype` F32, F16 or BF16, as the reference admits, :478), and, in the softmax mode, the
+ * reference's softmax_gate: the shared-expert gate's logit x . w computed in the same launch
+ * (gate_x [gate_k] and gate_w [gate_k] of `gate_dtype`, F16 or BF16; gate_logit [1] written in
+ * `gate_dtype`, the `shared_gate` operand of sx_moe / sx_moe_folded).  The dot is summed in the
+ * order of MLX's dot_product that the reference kernel restates (:200-218, :328-332), products
+ * and sums rounded separately.  Pass null gate pointers for no gate; in the sigmoid modes they
+ * are ignored (:471).  Declines (SX_ERR_ROUTER_DECLINED) where the reference does: more than one
+ * row with a gate, gate_k outside 1..16384 or not a multiple of 8, a gate dtype other than F16 and
+ * BF16 (:499-506), and everything sx_router_topk declines. */
+sx_status sx_router_topk_gate(sx_stream stream, const void* logits, sx_dtype logits_dtype, const float* bias,
+                              int32_t rows, int32_t experts, int32_t k, int32_t mode, int32_t renorm, float scale,
+                              int32_t n_group, int32_t topk_group, const void* gate_x, const void* gate_w,
+                              int32_t gate_k, sx_dtype gate_dtype, void* gate_logit, uint32_t* inds, float* scores);
+
 /* ------------------------------------------------------------------ routed experts
  * The workspace sx_moe needs for `rows` rows at top-k `topk` over `bank` (bytes). */
 size_t sx_moe_workspace_bytes(const sx_bank* bank, int32_t rows, int32_t topk);

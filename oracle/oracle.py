@@ -381,6 +381,42 @@ def rms_norm_truth(y, w, eps):
     return y * inv * np.asarray(w, np.float64)
 
 
+def router_gate_logit(x, w):
+    """The softmax_gate router's shared-expert gate logit (src/moe_router.zig:200-218, :328-332),
+    in f32 with the order MLX's dot_product uses as that kernel restates it: virtual group vs of
+    1024 elements; lane l keeps a float4 c over its 8-element chunks at 1024 vs + 8 l + 256 i
+    (i = 0..3; chunks past the end skipped), c[q] += x * w element by element; then
+    c0 + c1 + c2 + c3, a butterfly sum over the 32 lanes (xor 16, 8, 4, 2, 1), and a butterfly
+    over the groups' partials in 16 lanes (xor 8, 4, 2, 1; zeros past the last group).  Products
+    and sums rounded separately.  x and w are the (already rounded) f16/bf16 values as float32;
+    returns the f32 sum (the caller rounds it to the gate dtype)."""
+    x = np.asarray(x, np.float32)
+    w = np.asarray(w, np.float32)
+    gk = x.shape[0]
+    f = np.float32
+
+    def butterfly(vals, widths):
+        v = list(vals)
+        for m in widths:
+            v = [f(v[i] + v[i ^ m]) for i in range(len(v))]
+        return v[0]
+
+    parts = []
+    for vs in range((gk + 1023) // 1024):
+        lanes = []
+        for lane in range(32):
+            c = [f(0.0)] * 4
+            for i in range(0, 32, 8):
+                idx = vs * 1024 + lane * 8 + i * 32
+                if idx + 8 <= gk:
+                    for j in range(8):
+                        c[j & 3] = f(c[j & 3] + f(x[idx + j] * w[idx + j]))
+            lanes.append(f(f(f(c[0] + c[1]) + c[2]) + c[3]))
+        parts.append(butterfly(lanes, (16, 8, 4, 2, 1)))
+    parts = parts + [f(0.0)] * (16 - len(parts))
+    return butterfly(parts, (8, 4, 2, 1))
+
+
 def router_truth(logits, k, mode="softmax", bias=None, renorm=True, scale=1.0, n_group=0, topk_group=0):
     """Top-k routing (src/moe_router.zig:16-65 chain semantics with the fused kernel's lowest-id
     tie break, :130-150; sigmoid_bias and its group limit :200-290).  Returns (inds, weights)."""

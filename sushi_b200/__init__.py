@@ -36,6 +36,7 @@ from .exl3 import (  # noqa: E402
     moe_with_gated_shared,
     moe_with_shared,
     router_topk,
+    router_topk_gate,
     share_unique_id,
     table_info,
     table_row,
@@ -46,5 +47,5 @@ __all__ = [
     "Bank", "Codebook", "Decode", "Exl3Error", "ExpertParallel", "LINEAR_WEIGHTS_STATIC", "Proj", "Ragged", "RouterMode", "TileOrder", "decode_codewords",
     "dequant_inner", "device_error", "linear", "linear_gemm", "linear_grouped", "linear_shared", "linear_shared_normed",
     "linear_shared_normed_workspace_bytes", "moe", "moe_clamped", "moe_folded", "moe_ragged", "moe_with_gated_shared",
-    "moe_with_shared", "router_topk", "share_unique_id", "table_info", "table_row", "tile_order_convert",
+    "moe_with_shared", "router_topk", "router_topk_gate", "share_unique_id", "table_info", "table_row", "tile_order_convert",
 ]

@@ -66,6 +66,8 @@ SIGNATURES = {
                                      ctypes.c_float, _P, _SZ]),
     "sx_linear_grouped": (_I, [_P, ctypes.POINTER(SxProj), ctypes.POINTER(SxDecode), _P, _I, _I, _P]),
     "sx_router_topk": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, ctypes.c_float, _I, _I, _P, _P]),
+    "sx_router_topk_gate": (_I, [_P, _P, _I, _P, _I, _I, _I, _I, _I, ctypes.c_float, _I, _I, _P, _P, _I, _I, _P, _P,
+                                 _P]),
     "sx_moe_workspace_bytes": (_SZ, [ctypes.POINTER(SxBank), _I, _I]),
     "sx_moe": (_I, [_P, ctypes.POINTER(SxBank), ctypes.POINTER(SxDecode), _P, _I, _I, _P, _P, _I, _P, _P, _I, _P, _P, _SZ]),
     "sx_moe_ragged_workspace_bytes": (_SZ, [ctypes.POINTER(SxRagged), _I, _I]),

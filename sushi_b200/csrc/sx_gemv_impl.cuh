@@ -84,6 +84,7 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 3 : 2) gemv_kernel(Gem
     __syncthreads();
     grid_launch_dependents();
 
+    uint16_t svh0[4] = {0, 0, 0, 0};  // the finish's svh values of this lane (rank 0)
     if (warp == CW) {
         // The weights are read-only to the grids around this one, so they stream before the
         // dependency wait (launches with programmatic serialisation only).
@@ -92,9 +93,23 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 3 : 2) gemv_kernel(Gem
             core_produce<N, 1>(s, tr, OT, ob, kb0, kbl);
         }
     } else {
+        // suh and svh are weights too: the warp's first prepare item's four suh values and, in
+        // rank 0, the lane's four svh values of the finish are read before the dependency wait,
+        // so neither read is a round trip after it.
+        const int items = kbl * NB * mg;
+        uint16_t suh0[4] = {0, 0, 0, 0};
+        if (warp < items) {
+            const int base = (kb0 + warp / (NB * mg)) * 128 + lane * 4;
+#pragma unroll
+            for (int i = 0; i < 4; i++) suh0[i] = suh[base + i];
+        }
+        if (split == 0) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) svh0[i] = svh[ob * 128 + lane * 4 + i];
+        }
         grid_dependency_wait();  // x may come from the previous grid
         // prepare: rows x input blocks, one warp per (block, row) of the stored rows
-        for (int item = warp; item < kbl * NB * mg; item += CW) {
+        for (int item = warp; item < items; item += CW) {
             const int kbi = item / (NB * mg);
             const int m = ((item / mg) % NB) * 8 + item % mg;
             const int base = (kb0 + kbi) * 128 + lane * 4;
@@ -102,7 +117,8 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 3 : 2) gemv_kernel(Gem
             if (m < a.rows) {
                 const size_t xoff = (size_t)g * a.x_group_stride + (size_t)m * a.in + base;
 #pragma unroll
-                for (int i = 0; i < 4; i++) v[i] = round_f16(load_act(a.x, xoff + i, a.xdt)) * h2f(suh[base + i]);
+                for (int i = 0; i < 4; i++)
+                    v[i] = round_f16(load_act(a.x, xoff + i, a.xdt)) * h2f(item == warp ? suh0[i] : suh[base + i]);
                 warp_hadamard128(v);
             }
 #pragma unroll
@@ -134,8 +150,7 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 3 : 2) gemv_kernel(Gem
             float ss = 0.0f;
 #pragma unroll
             for (int i = 0; i < 4; i++) {
-                const int o = ob * 128 + lane * 4 + i;
-                const float f = v[i] * a.out_scale * h2f(svh[o]);
+                const float f = v[i] * a.out_scale * h2f(svh0[i]);
                 if (normed) {
                     const float r = round_act(f, a.xdt);
                     ss = fmaf(r, r, ss);
@@ -179,16 +194,16 @@ static cudaError_t launch_gemv_t(const GemvArgs& a, int groups, cudaStream_t str
     int S = cached_split(key);
     cudaError_t e;
     if (S <= 0) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        if (e != cudaSuccess) return e;
         // Fallback when no split is co-resident: the largest one (the most CTAs, the least
-        // shared memory per CTA), which then runs in several waves.
+        // shared memory per CTA), which then runs in several waves.  The kernel's attributes only
+        // ever grow (func_attrs), so a launch of another geometry never meets a shared-memory
+        // limit this search lowered.
         const int s_max = KB < 16 ? KB : 16;
         S = s_max;
         for (int cand = s_max; cand >= 1; cand--) {
             const CoreLayout L = core_layout<N, 1, NB>((KB + cand - 1) / cand, mg);
             if (L.total > 200 * 1024) break;  // smaller splits only need more
-            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
+            e = func_attrs((const void*)kern, (int)L.total, true);
             if (e != cudaSuccess) return e;
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3(OB, cand, groups);

@@ -1,4 +1,5 @@
-// Fused MoE router: moeRouterTopK (src/moe_router.zig:442, kernel text :112-290).
+// Fused MoE router: moeRouterTopK / moeRouterTopKGate (src/moe_router.zig:442, :457; kernel text
+// :112-336).
 //
 // One CTA per row.  Phase 1 writes every expert's selection key (softmax: the logit; sigmoid
 // modes: sigmoid(logit) + bias, with the raw sigmoid kept as the weight) to shared memory.  The
@@ -7,7 +8,9 @@
 // penalty).  Warp 0 then runs k rounds of "max, then mask" whose ties go to the LOWEST expert id,
 // so the pick is a pure function of the keys, and normalises the picked weights: softmax
 // probabilities renormalised over the picks; sigmoid scores divided by their sum (+1e-20) when
-// `renorm` and k > 1, times `scale`.
+// `renorm` and k > 1, times `scale`.  Logits are F32, F16 or BF16.  The softmax_gate mode adds the
+// shared-expert gate's logit, the dot of the row's x with a flat weight vector: warps 1..7 compute
+// it while warp 0 selects.
 #include <cuda_runtime.h>
 #include <math_constants.h>
 
@@ -32,24 +35,59 @@ __device__ __forceinline__ void warp_argmax_lowest(float& v, int& idx) {
     }
 }
 
-__global__ void __launch_bounds__(kRouterThreads) router_kernel(const float* __restrict__ logits,
+// The shared-expert gate's logit (moeRouterTopKGate's `gate`): x . w over gk elements (x and w of
+// dtype dt, F16 or BF16) in the order of MLX's dot_product as the reference kernel restates it
+// (src/moe_router.zig:200-218, :328-332): virtual group vs owns elements [1024 vs, 1024 vs + 1024);
+// lane l accumulates a float4 c over its four 8-element chunks at 1024 vs + 8 l + 256 i (chunks that
+// run past gk are skipped), c[q] += x * w element by element; then c0 + c1 + c2 + c3, a warp sum,
+// and a sum of the groups' partials over 16 lanes (zeros past the last group).  Products and sums
+// are rounded separately (no fused multiply-add).  Called by warps 1..7 (warp w takes groups
+// w-1, w+6, ...); partials land in gp[16].
+__device__ __forceinline__ void router_gate_partials(const void* gx, const void* gw, int gk, int dt, float* gp) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int groups = (gk + 1023) / 1024;
+    for (int vs = warp - 1; vs < groups; vs += kRouterThreads / 32 - 1) {
+        float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int i = 0; i < 32; i += 8) {
+            const int idx = vs * 1024 + lane * 8 + i * 32;
+            if (idx + 8 <= gk) {
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    c[j & 3] = __fadd_rn(c[j & 3], __fmul_rn(load_act(gx, idx + j, dt), load_act(gw, idx + j, dt)));
+            }
+        }
+        float ga = __fadd_rn(__fadd_rn(__fadd_rn(c[0], c[1]), c[2]), c[3]);
+#pragma unroll
+        for (int m = 16; m > 0; m >>= 1) ga = __fadd_rn(ga, __shfl_xor_sync(0xffffffffu, ga, m));
+        if (lane == 0) gp[vs] = ga;
+    }
+}
+
+// Every thread of the block, from warp 0's selection path and the other warps' gate path: a named
+// barrier over the whole block (the two paths reach it from different code).
+__device__ __forceinline__ void router_join() { asm volatile("bar.sync 2, %0;" ::"n"(kRouterThreads) : "memory"); }
+
+__global__ void __launch_bounds__(kRouterThreads) router_kernel(const void* __restrict__ logits, int ldt,
                                                                 const float* __restrict__ bias, int E, int K, int mode,
                                                                 int renorm, float scale, int n_group, int topk_group,
-                                                                uint32_t* __restrict__ inds, float* __restrict__ scores) {
+                                                                uint32_t* __restrict__ inds, float* __restrict__ scores,
+                                                                const void* gx, const void* gw, int gk, int gdt,
+                                                                void* glogit) {
     extern __shared__ float sm[];
     float* key = sm;        // [E]
     float* wraw = sm + E;   // [E] (sigmoid modes)
     __shared__ float red_max[kRouterThreads / 32], red_sum[kRouterThreads / 32];
     __shared__ int sel[32];
     __shared__ float gscore[32];
+    __shared__ float gp[16];
     const int row = blockIdx.x;
-    const float* lg = logits + (size_t)row * E;
+    const size_t lbase = (size_t)row * E;
     const bool sigmoid = mode != SX_ROUTER_SOFTMAX;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
     float lmax = -CUDART_INF_F;
     for (int e = tid; e < E; e += blockDim.x) {
-        const float l = lg[e];
+        const float l = load_act(logits, lbase + e, ldt);
         if (sigmoid) {
             // The two-sided form of MLX's Sigmoid the reference mirrors (src/moe_router.zig:214-219).
             const float sy = 1.0f / (1.0f + expf(fabsf(l)));
@@ -81,7 +119,11 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(const float* __r
         for (int w = 0; w < (int)(blockDim.x / 32); w++) tot += red_sum[w];
         snorm = 1.0f / tot;
     }
-    if (warp != 0) return;
+    if (warp != 0) {
+        if (gk > 0) router_gate_partials(gx, gw, gk, gdt, gp);
+        router_join();  // the gate's partials, for warp 0's final sum
+        return;
+    }
 
     if (mode == SX_ROUTER_SIGMOID_BIAS_GROUPED) {
         const int gsz = E / n_group;
@@ -136,7 +178,7 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(const float* __r
     int myidx = 0;
     if (lane < K) {
         myidx = sel[lane];
-        w = sigmoid ? wraw[myidx] : expf(lg[myidx] - smax) * snorm;
+        w = sigmoid ? wraw[myidx] : expf(load_act(logits, lbase + myidx, ldt) - smax) * snorm;
     }
     float tot = 0.0f;
     for (int j = 0; j < K; j++) tot += __shfl_sync(0xffffffffu, w, j);
@@ -150,17 +192,28 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(const float* __r
         inds[(size_t)row * K + lane] = (uint32_t)myidx;
         scores[(size_t)row * K + lane] = w;
     }
+    router_join();
+    if (gk > 0) {
+        float gt = lane < 16 && lane < (gk + 1023) / 1024 ? gp[lane] : 0.0f;
+#pragma unroll
+        for (int m = 8; m > 0; m >>= 1) gt = __fadd_rn(gt, __shfl_xor_sync(0xffffffffu, gt, m));
+        if (lane == 0) store_act(glogit, row, gdt, gt);
+    }
 }
 
 }  // namespace sx
 
 using namespace sx;
 
-extern "C" sx_status sx_router_topk(sx_stream stream, const float* logits, const float* bias, int32_t rows,
-                                    int32_t experts, int32_t k, int32_t mode, int32_t renorm, float scale,
-                                    int32_t n_group, int32_t topk_group, uint32_t* inds, float* scores) {
+namespace {
+
+sx_status router_launch(sx_stream stream, const void* logits, sx_dtype ldt, const float* bias, int32_t rows,
+                        int32_t experts, int32_t k, int32_t mode, int32_t renorm, float scale, int32_t n_group,
+                        int32_t topk_group, uint32_t* inds, float* scores, const void* gx, const void* gw, int32_t gk,
+                        sx_dtype gdt, void* glogit) {
     if (!logits || !inds || !scores) return SX_ERR_NULL_POINTER;
     if (rows < 1) return SX_ERR_BAD_SHAPE;
+    if (ldt != SX_DT_F32 && ldt != SX_DT_F16 && ldt != SX_DT_BF16) return SX_ERR_ROUTER_DECLINED;
     if (mode < SX_ROUTER_SOFTMAX || mode > SX_ROUTER_SIGMOID_BIAS_GROUPED) return SX_ERR_ROUTER_DECLINED;
     // The reference kernel's admission (src/moe_router.zig:466-490): it declines, the caller keeps its chain.
     if (experts < k || experts > kRouterMaxExperts || k < 1 || k > 32) return SX_ERR_ROUTER_DECLINED;
@@ -172,6 +225,34 @@ extern "C" sx_status sx_router_topk(sx_stream stream, const float* logits, const
     }
     const size_t smem = (size_t)2 * experts * sizeof(float);
     router_kernel<<<rows, kRouterThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
-        logits, bias, experts, k, mode, renorm, scale, n_group, topk_group, inds, scores);
+        logits, (int)ldt, bias, experts, k, mode, renorm, scale, n_group, topk_group, inds, scores, gx, gw, gk,
+        (int)gdt, glogit);
     return cuda_status(cudaGetLastError(), "router launch");
+}
+
+}  // namespace
+
+extern "C" sx_status sx_router_topk(sx_stream stream, const float* logits, const float* bias, int32_t rows,
+                                    int32_t experts, int32_t k, int32_t mode, int32_t renorm, float scale,
+                                    int32_t n_group, int32_t topk_group, uint32_t* inds, float* scores) {
+    return router_launch(stream, logits, SX_DT_F32, bias, rows, experts, k, mode, renorm, scale, n_group, topk_group,
+                         inds, scores, nullptr, nullptr, 0, SX_DT_BF16, nullptr);
+}
+
+extern "C" sx_status sx_router_topk_gate(sx_stream stream, const void* logits, sx_dtype logits_dtype, const float* bias,
+                                         int32_t rows, int32_t experts, int32_t k, int32_t mode, int32_t renorm,
+                                         float scale, int32_t n_group, int32_t topk_group, const void* gate_x,
+                                         const void* gate_w, int32_t gate_k, sx_dtype gate_dtype, void* gate_logit,
+                                         uint32_t* inds, float* scores) {
+    // The gate rides the softmax mode only (src/moe_router.zig:471); the reference's admission of
+    // it (:499-506): one row, 1..16384 elements in whole 8-element chunks, F16 or BF16.
+    const bool gate = mode == SX_ROUTER_SOFTMAX && (gate_x || gate_w || gate_logit);
+    if (gate) {
+        if (!gate_x || !gate_w || !gate_logit) return SX_ERR_NULL_POINTER;
+        if (rows != 1 || gate_k <= 0 || gate_k > 16384 || gate_k % 8 != 0) return SX_ERR_ROUTER_DECLINED;
+        if (gate_dtype != SX_DT_F16 && gate_dtype != SX_DT_BF16) return SX_ERR_ROUTER_DECLINED;
+    }
+    return router_launch(stream, logits, logits_dtype, bias, rows, experts, k, mode, renorm, scale, n_group,
+                         topk_group, inds, scores, gate ? gate_x : nullptr, gate ? gate_w : nullptr, gate ? gate_k : 0,
+                         gate_dtype, gate ? gate_logit : nullptr);
 }

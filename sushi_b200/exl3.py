@@ -327,6 +327,39 @@ def router_topk(logits, k, mode=RouterMode.SOFTMAX, bias=None, route_norm=True, 
     return inds.reshape(shape), scores.reshape(shape)
 
 
+def router_topk_gate(logits, k, gate=None, mode=RouterMode.SOFTMAX, bias=None, route_norm=True, route_scale=1.0,
+                     n_group=0, topk_group=0):
+    """moeRouterTopKGate: router_topk over logits [..., E] of any activation dtype and, in the softmax
+    mode with `gate` = (x [K], w [K]) of one F16/BF16 dtype, the shared-expert gate's logit computed
+    in the same launch (the reference's softmax_gate).  Returns (inds, scores, gate_logit [1] in the
+    gate's dtype, or None without a gate), or None where the reference's kernel declines."""
+    if logits.dtype not in _DT:
+        raise TypeError(f"BadExl3Dtype: router logits dtype {logits.dtype}")
+    lg = logits.reshape(-1, logits.shape[-1]).contiguous()
+    rows, experts = lg.shape
+    inds = torch.empty((rows, k), dtype=torch.int32, device=lg.device)
+    scores = torch.empty((rows, k), dtype=torch.float32, device=lg.device)
+    b = None if bias is None else bias.float().contiguous()
+    gx = gw = glog = None
+    gk, gdt = 0, 2
+    if gate is not None and mode == RouterMode.SOFTMAX:
+        gx, gw = (t.reshape(-1).contiguous() for t in gate)
+        if gx.dtype not in (torch.float16, torch.bfloat16) or gw.dtype != gx.dtype:
+            return None
+        gk, gdt = gx.numel(), _DT[gx.dtype]
+        glog = torch.empty((1,), dtype=gx.dtype, device=lg.device)
+    st = lib().sx_router_topk_gate(_stream(), lg.data_ptr(), _DT[lg.dtype], None if b is None else b.data_ptr(), rows,
+                                   experts, k, int(mode), 1 if route_norm else 0, float(route_scale), n_group,
+                                   topk_group, None if gx is None else gx.data_ptr(),
+                                   None if gw is None else gw.data_ptr(), gk, gdt,
+                                   None if glog is None else glog.data_ptr(), inds.data_ptr(), scores.data_ptr())
+    if st == 12:  # SX_ERR_ROUTER_DECLINED
+        return None
+    _check(st)
+    shape = tuple(logits.shape[:-1]) + (k,)
+    return inds.reshape(shape), scores.reshape(shape), glog
+
+
 _WS_CACHE = {}
 
 

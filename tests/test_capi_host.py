@@ -133,6 +133,34 @@ def test_router_declines_before_launch(L):
     assert L.sx_status_name(st).decode() == "SX_ERR_ROUTER_DECLINED"
 
 
+def test_router_gate_declines_before_launch(L):
+    gate = lambda rows=1, gk=2048, gdt=2, ldt=2: L.sx_status_name(L.sx_router_topk_gate(
+        None, FAKE, ldt, None, rows, 512, 10, 0, 1, 1.0, 0, 0, FAKE, FAKE, gk, gdt, FAKE, FAKE, FAKE)).decode()
+    assert gate(rows=2) == "SX_ERR_ROUTER_DECLINED"  # src/moe_router.zig:503: one row
+    assert gate(gk=12) == "SX_ERR_ROUTER_DECLINED"
+    assert gate(gk=16392) == "SX_ERR_ROUTER_DECLINED"
+    assert gate(gdt=0) == "SX_ERR_ROUTER_DECLINED"  # F32 gate
+    assert gate(ldt=7) == "SX_ERR_ROUTER_DECLINED"  # unknown logits dtype
+    st = L.sx_router_topk_gate(None, FAKE, 2, None, 1, 512, 10, 0, 1, 1.0, 0, 0, FAKE, None, 2048, 2, FAKE, FAKE, FAKE)
+    assert L.sx_status_name(st).decode() == "SX_ERR_NULL_POINTER"
+
+
+def test_router_gate_logit_oracle_is_a_dot():
+    """The restated MLX order is a dot product: within f32 rounding of the f64 sum."""
+    import numpy as np
+
+    from oracle import oracle as orc
+
+    rng = np.random.default_rng(3)
+    for gk in (8, 1032, 2048, 7168):
+        x = rng.standard_normal(gk).astype(np.float32)
+        w = rng.standard_normal(gk).astype(np.float32)
+        got = float(orc.router_gate_logit(x, w))
+        want = float(np.dot(x.astype(np.float64), w.astype(np.float64)))
+        bound = gk * 2.0 ** -23 * float(np.abs(x.astype(np.float64) * w).sum())
+        assert abs(got - want) <= bound
+
+
 class SxRaggedMeta:
     """A host meta table for sx_ragged (8 u32 words per expert)."""
 

@@ -67,6 +67,67 @@ def test_router_declines_like_the_reference(sx):
                           topk_group=1) is None
 
 
+def _gate_case(rng, gk, cancel):
+    x = ((rng.random(gk) - 0.5) * 4.0).astype(np.float32)
+    w = ((rng.random(gk) - 0.5) * 0.4).astype(np.float32)
+    if cancel:  # the reference's test plants large cancelling products (src/moe_router.zig:786-793)
+        for _ in range(3):
+            i, j = rng.integers(0, gk, 2)
+            if i != j:
+                x[i], w[i], x[j], w[j] = 65536.0, 1.0, -65536.0, 1.0
+    return x, w
+
+
+@pytest.mark.parametrize("gk,tdt", [(2048, "bf16"), (7168, "bf16"), (2048, "f16"), (8, "bf16"), (1032, "bf16"),
+                                    (16384, "bf16")])
+def test_router_softmax_gate(sx, gk, tdt):
+    """softmax_gate (moeRouterTopKGate, src/moe_router.zig:457): the gate logit is the oracle's
+    restatement of MLX's dot order to the bit, and inds/scores equal the plain softmax mode's."""
+    dt = torch.bfloat16 if tdt == "bf16" else torch.float16
+    rng = np.random.default_rng(gk + (tdt == "f16"))
+    for trial in range(3):
+        x, w = _gate_case(rng, gk, cancel=trial > 0 and tdt == "bf16")
+        gx, gw = torch.from_numpy(x).cuda().to(dt), torch.from_numpy(w).cuda().to(dt)
+        logits = torch.from_numpy(((rng.random((1, 512)) - 0.5) * 8.0).astype(np.float32)).cuda().to(torch.bfloat16)
+        got = sx.router_topk_gate(logits, 10, gate=(gx, gw))
+        assert got is not None
+        inds, scores, glog = got
+        plain = sx.router_topk(logits.float(), 10)
+        np.testing.assert_array_equal(inds.cpu().numpy(), plain[0].cpu().numpy())
+        np.testing.assert_array_equal(scores.cpu().numpy(), plain[1].cpu().numpy())
+        want = orc.router_gate_logit(gx.float().cpu().numpy(), gw.float().cpu().numpy())
+        want_t = torch.tensor([want], dtype=torch.float32).to(dt)
+        assert glog.dtype == dt
+        assert glog.view(torch.int16).item() == want_t.view(torch.int16).item(), (glog.item(), want)
+
+
+def test_router_logits_in_activation_dtypes(sx):
+    """Logits of F16/BF16 (src/moe_router.zig:478) route exactly as their f32 values do."""
+    rng = np.random.default_rng(5)
+    for dt in (torch.bfloat16, torch.float16):
+        lg = torch.from_numpy(rng.standard_normal((7, 256)).astype(np.float32)).cuda().to(dt)
+        for mode, bias in ((sx.RouterMode.SOFTMAX, None),
+                           (sx.RouterMode.SIGMOID_BIAS, torch.from_numpy(rng.standard_normal(256).astype(np.float32) * 0.1).cuda())):
+            a = sx.router_topk_gate(lg, 8, mode=mode, bias=bias, route_scale=2.5)
+            b = sx.router_topk(lg.float(), 8, mode, bias, route_scale=2.5)
+            assert a[2] is None
+            np.testing.assert_array_equal(a[0].cpu().numpy(), b[0].cpu().numpy())
+            np.testing.assert_array_equal(a[1].cpu().numpy(), b[1].cpu().numpy())
+
+
+def test_router_gate_declines_like_the_reference(sx):
+    lg = torch.zeros((2, 64), device="cuda")
+    g = torch.ones(2048, device="cuda", dtype=torch.bfloat16)
+    assert sx.router_topk_gate(lg, 4, gate=(g, g)) is None  # two rows with a gate
+    assert sx.router_topk_gate(lg[:1], 4, gate=(g[:12], g[:12])) is None  # not whole 8-element chunks
+    big = torch.ones(16392, device="cuda", dtype=torch.bfloat16)
+    assert sx.router_topk_gate(lg[:1], 4, gate=(big, big)) is None
+    assert sx.router_topk_gate(lg[:1], 4, gate=(g.float(), g.float())) is None  # gate dtype
+    # sigmoid modes ignore the gate (src/moe_router.zig:471)
+    r = sx.router_topk_gate(lg, 4, gate=(g, g), mode=sx.RouterMode.SIGMOID_BIAS, bias=torch.zeros(64, device="cuda"))
+    assert r is not None and r[2] is None
+
+
 def _bank(seed, E, D, I, n_gu, n_d):
     g = random_pack(seed, D, I, n_gu, experts=E)
     u = random_pack(seed + 1, D, I, n_gu, experts=E)
