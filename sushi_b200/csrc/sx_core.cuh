@@ -271,7 +271,7 @@ __device__ __forceinline__ void core_reduce(float* red, const float (&acc)[NP][N
 }
 
 // Sum over the cluster's S CTAs, in rank order, of the four floats red[off + 4*lane ..] of each:
-// the loads go out four ranks at a time so distributed shared memory's latency is paid S/4 times.
+// the loads go out eight ranks at a time so distributed shared memory's latency is paid S/8 times.
 __device__ __forceinline__ float4 cluster_sum4(cg::cluster_group& cluster, float* red, int S, int off) {
     const int lane = threadIdx.x & 31;
     float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -282,13 +282,22 @@ __device__ __forceinline__ float4 cluster_sum4(cg::cluster_group& cluster, float
         v.w += t.w;
     };
     int r = 0;
-    for (; r + 4 <= S; r += 4) {
+    for (; r + 8 <= S; r += 8) {
+        float4 t[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++)
+            t[q] = *reinterpret_cast<const float4*>(cluster.map_shared_rank(red, r + q) + off + lane * 4);
+#pragma unroll
+        for (int q = 0; q < 8; q++) add(t[q]);
+    }
+    if (r + 4 <= S) {
         float4 t[4];
 #pragma unroll
         for (int q = 0; q < 4; q++)
             t[q] = *reinterpret_cast<const float4*>(cluster.map_shared_rank(red, r + q) + off + lane * 4);
 #pragma unroll
         for (int q = 0; q < 4; q++) add(t[q]);
+        r += 4;
     }
     for (; r < S; r++) add(*reinterpret_cast<const float4*>(cluster.map_shared_rank(red, r) + off + lane * 4));
     return v;

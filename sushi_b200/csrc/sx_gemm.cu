@@ -3,6 +3,9 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <mutex>
+#include <utility>
+#include <vector>
 
 #include "sx_gemm_impl.cuh"
 #include "sx_internal.h"
@@ -68,8 +71,52 @@ cudaError_t gemm_launch(int kind, const CUtensorMap& pmap, const GemmArgs& a, in
     }
 }
 
+namespace {
+struct CoKey {
+    const void* kern;
+    int clusters, S;
+    bool operator==(const CoKey& o) const { return kern == o.kern && clusters == o.clusters && S == o.S; }
+};
+std::mutex g_co_lock;
+std::vector<std::pair<CoKey, int>> g_co;
+}  // namespace
+
+int gemm_coresident_split(const void* kern, int smem, int threads, dim3 grid_xy, int S) {
+    const int clusters = (int)(grid_xy.x * grid_xy.y);
+    const CoKey key{kern, clusters, S};
+    {
+        std::lock_guard<std::mutex> guard(g_co_lock);
+        for (const auto& e : g_co)
+            if (e.first == key) return e.second;
+    }
+    int best = 1;
+    for (int cand = S; cand > 1; cand--) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(grid_xy.x, grid_xy.y, cand);
+        cfg.blockDim = dim3(threads, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = cand;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int active = 0;
+        if (cudaOccupancyMaxActiveClusters(&active, kern, &cfg) == cudaSuccess && active >= clusters) {
+            best = cand;
+            break;
+        }
+        cudaGetLastError();
+    }
+    std::lock_guard<std::mutex> guard(g_co_lock);
+    g_co.emplace_back(key, best);
+    return best;
+}
+
 // Split-K for `ctas` (row tile, output block) CTAs over `chunks` 64-input chunks: about one wave
-// of one CTA per SM, at most 16 ranks, at least 4 chunks per rank.
+// of one CTA per SM, at most 16 ranks, at least 4 chunks per rank (the launch then lowers it to
+// the largest split whose clusters are all co-resident, gemm_coresident_split).
 int gemm_split(long long ctas, int chunks) {
     const long long want = sm_count();
     int S = (int)std::max(1LL, want / std::max(1LL, ctas));

@@ -71,7 +71,11 @@ struct GemmLayout {
     static constexpr int B_TILE = NT * kGemmKC * 2;     // 16 KB per row tile
     static constexpr int B_BYTES = (PAIR ? RT / 2 : RT) * B_TILE;
     static constexpr int T_BYTES = 4 * 8 * N * 2;       // 32 trellis tiles
-    static constexpr int NST = PAIR ? 4 : (RT == 1 ? 4 : (RT == 2 ? 3 : 2));
+    // One row tile: as many stages as fit in 224 KB (5 or 6; at most 8), since a stage's cycle
+    // (copies, decode, MMA, commit) is longer than its decode and only the ring depth hides it.
+    static constexpr int STAGE1 = 128 * kGemmKC * 2 + NT * kGemmKC * 2 + 4 * 8 * N * 2;
+    static constexpr int NST1 = (223 * 1024) / STAGE1 < 8 ? (223 * 1024) / STAGE1 : 8;
+    static constexpr int NST = PAIR ? 4 : (RT == 1 ? NST1 : (RT == 2 ? 3 : 2));
     static constexpr int TMEM_COLS = NT * RT;
     static constexpr int A_OFF = 0;
     static constexpr int B_OFF = A_OFF + NST * A_BYTES;
@@ -239,15 +243,18 @@ __device__ __forceinline__ bool gemm_item(const GemmArgs& a, int w, int NT, Gemm
 }
 
 // Rows t0 .. t0+rows-1 of the item from red[t - t0][o] (summed over the cluster's S ranks in rank
-// order when split): H128, svh, the codebook scale, and the store of the launch's mode.
+// order when split): H128, svh, the codebook scale, and the store of the launch's mode.  Split-K
+// ranks share the rows: rank `rank` finishes rows t = rank, rank + S, ..., one per decoder warp
+// at a time, so no rank waits through every row's reduction.
 __device__ __forceinline__ void gemm_store(const GemmArgs& a, const GemmItem& it, float* red, cg::cluster_group& cluster,
-                                           int S, int ob, int t0, int rows) {
+                                           int S, int rank, int ob, int t0, int rows) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (rank + warp * S >= rows) return;
     const uint16_t* svh = a.svh + (size_t)it.e * a.out;
     float sv[4];
 #pragma unroll
     for (int i = 0; i < 4; i++) sv[i] = h2f(svh[ob * 128 + lane * 4 + i]) * a.scale;
-    for (int t = warp; t < rows; t += kGemmDecWarps) {
+    for (int t = rank + warp * S; t < rows; t += kGemmDecWarps * S) {
         const float4 s4 = S > 1 ? cluster_sum4(cluster, red, S, t * 128)
                                 : *reinterpret_cast<const float4*>(red + t * 128 + lane * 4);
         float v[4] = {s4.x, s4.y, s4.z, s4.w};
@@ -461,8 +468,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
 
     // ---------------- epilogue, every thread (the cluster barriers count them all): per row tile,
     // warps 0..3 move the accumulator to shared memory red[t][o] (tensor-memory lane quadrant =
-    // warp), then rank 0 sums the cluster's partials in rank order (split-K), applies H128, svh and
-    // the scale, and stores; the second barrier keeps every rank's red alive until rank 0 is done.
+    // warp), then each rank sums its share of the rows over the cluster's partials in rank order
+    // (split-K), applies H128, svh and the scale, and stores; the second barrier keeps every rank's
+    // red alive until every rank is done reading.
     for (int r = 0; r < rt_live; r++) {
         if (warp < 4) {
             tc_fence_after();
@@ -476,7 +484,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
             }
         }
         if (S > 1) cluster.sync(); else __syncthreads();
-        if (split == 0 && warp < kGemmDecWarps) gemm_store(a, it, red, cluster, S, ob, r * NT, min(NT, it.rows - r * NT));
+        if (warp < kGemmDecWarps) gemm_store(a, it, red, cluster, S, split, ob, r * NT, min(NT, it.rows - r * NT));
         if (S > 1) cluster.sync(); else __syncthreads();
     }
     tc_fence_before();

@@ -7,6 +7,10 @@
 
 namespace sx {
 
+// The largest split <= S whose clusters (`clusters` of them, S CTAs each) are all co-resident, so
+// no cluster waits for another to drain (cached per kernel, cluster count and split); 1 if none.
+int gemm_coresident_split(const void* kern, int smem, int threads, dim3 grid_xy, int S);
+
 template <int KIND, int N, int RT, bool PAIR = false>
 static cudaError_t launch_gemm_t(const CUtensorMap& pmap, const GemmArgs& a, int items, int S, cudaStream_t stream) {
     constexpr int NT = kGemmRows;
@@ -15,6 +19,7 @@ static cudaError_t launch_gemm_t(const CUtensorMap& pmap, const GemmArgs& a, int
     const int smem = GemmLayout<N, NT, RT, PAIR>::ALLOC;
     cudaError_t e = func_attrs((const void*)kern, smem, S > 8);
     if (e != cudaSuccess) return e;
+    if (!PAIR && S > 1) S = gemm_coresident_split((const void*)kern, smem, kGemmThreads, dim3(a.out / 128, items), S);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.out / 128, items, S);
     cfg.blockDim = dim3(kGemmThreads, 1, 1);
