@@ -14,6 +14,8 @@
 //     No global scratch.
 #pragma once
 
+#include <algorithm>
+
 #include "sx_core.cuh"
 #include "sx_kernels.h"
 
@@ -183,6 +185,10 @@ struct SplitKey {
 
 int cached_split(const SplitKey& k);
 void remember_split(const SplitKey& k, int S);
+int sm_count();
+
+// Dynamic shared memory that holds the GEMV to two CTAs per SM.
+constexpr int kGemvTwoPerSmSmem = 80 * 1024;
 
 template <int KIND, int N, int NB, bool W16>
 static cudaError_t launch_gemv_t(const GemvArgs& a, int groups, cudaStream_t stream) {
@@ -191,47 +197,79 @@ static cudaError_t launch_gemv_t(const GemvArgs& a, int groups, cudaStream_t str
     const int mg = a.rows < 8 ? a.rows : 8;
     auto kern = gemv_kernel<KIND, N, NB, W16>;
     const SplitKey key{(const void*)kern, a.out, a.in, groups, mg};
-    int S = cached_split(key);
+    int S = cached_split(key);  // split | (two-per-SM floor << 8)
     cudaError_t e;
     if (S <= 0) {
-        // Fallback when no split is co-resident: the largest one (the most CTAs, the least
-        // shared memory per CTA), which then runs in several waves.  The kernel's attributes only
-        // ever grow (func_attrs), so a launch of another geometry never meets a shared-memory
-        // limit this search lowered.
+        // The split and occupancy: among co-resident splits (no cluster waits for another to
+        // drain), at the kernel's natural occupancy and with a shared-memory floor of two CTAs per
+        // SM, the least estimated time of the busiest SM: its CTAs times each CTA's input blocks.
+        // Clusters pack within GPCs, so past one CTA per SM the busiest SM is taken to hold one
+        // CTA more than the even share, up to the occupancy; an SM decodes at about the same rate
+        // with two or three CTAs and at ~0.55 of it with one (measured on B200); of equal estimates
+        // the one with fewer CTAs (fewer partial sums to gather, less per-CTA set-up).  Without any
+        // co-resident split: the largest one (the most CTAs, the least shared memory per CTA),
+        // which then runs in several waves.  The kernel's attributes only ever grow (func_attrs),
+        // so a launch of another geometry never meets a shared-memory limit this search lowered.
         const int s_max = KB < 16 ? KB : 16;
-        S = s_max;
-        for (int cand = s_max; cand >= 1; cand--) {
-            const CoreLayout L = core_layout<N, 1, NB>((KB + cand - 1) / cand, mg);
-            if (L.total > 200 * 1024) break;  // smaller splits only need more
-            e = func_attrs((const void*)kern, (int)L.total, true);
-            if (e != cudaSuccess) return e;
-            cudaLaunchConfig_t cfg = {};
-            cfg.gridDim = dim3(OB, cand, groups);
-            cfg.blockDim = dim3(kGemvThreads, 1, 1);
-            cfg.dynamicSmemBytes = L.total;
-            cudaLaunchAttribute attr[1];
-            attr[0].id = cudaLaunchAttributeClusterDimension;
-            attr[0].val.clusterDim.x = 1;
-            attr[0].val.clusterDim.y = cand;
-            attr[0].val.clusterDim.z = 1;
-            cfg.attrs = attr;
-            cfg.numAttrs = 1;
-            int clusters = 0;
-            if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) == cudaSuccess && clusters >= OB * groups) {
-                S = cand;
-                break;
+        const long long sms = sm_count();
+        long long best_cost = -1, best_ctas = 0;
+        int best = s_max;
+        for (int floor2 = 0; floor2 < 2; floor2++) {
+            for (int cand = s_max; cand >= 1; cand--) {
+                const CoreLayout L = core_layout<N, 1, NB>((KB + cand - 1) / cand, mg);
+                if (L.total > 200 * 1024) break;  // smaller splits only need more
+                const int natural = (int)L.total;
+                const int smem = floor2 && natural < kGemvTwoPerSmSmem ? kGemvTwoPerSmSmem : natural;
+                e = func_attrs((const void*)kern, smem, true);
+                if (e != cudaSuccess) return e;
+                int occ = 0;
+                if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kGemvThreads, smem) != cudaSuccess ||
+                    occ < 1) {
+                    cudaGetLastError();
+                    continue;
+                }
+                if (floor2 && natural >= kGemvTwoPerSmSmem) continue;  // the same launch as without the floor
+                cudaLaunchConfig_t cfg = {};
+                cfg.gridDim = dim3(OB, cand, groups);
+                cfg.blockDim = dim3(kGemvThreads, 1, 1);
+                cfg.dynamicSmemBytes = smem;
+                cudaLaunchAttribute attr[1];
+                attr[0].id = cudaLaunchAttributeClusterDimension;
+                attr[0].val.clusterDim.x = 1;
+                attr[0].val.clusterDim.y = cand;
+                attr[0].val.clusterDim.z = 1;
+                cfg.attrs = attr;
+                cfg.numAttrs = 1;
+                int clusters = 0;
+                if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < OB * groups) {
+                    cudaGetLastError();
+                    continue;
+                }
+                const long long ctas = (long long)OB * cand * groups;
+                const long long even = (ctas + sms - 1) / sms;
+                const long long busiest = ctas <= sms ? 1 : std::min<long long>(occ, even + 1);
+                const long long blocks = (KB + cand - 1) / cand;
+                const long long cost = busiest == 1 ? blocks * 36 : busiest * blocks * 20;
+                if (best_cost < 0 || cost < best_cost || (cost == best_cost && ctas < best_ctas)) {
+                    best_cost = cost;
+                    best_ctas = ctas;
+                    best = cand | (floor2 << 8);
+                }
             }
-            cudaGetLastError();
         }
+        S = best;
         remember_split(key, S);
     }
+    const bool floor2 = (S >> 8) != 0;
+    S &= 0xFF;
     const CoreLayout L = core_layout<N, 1, NB>((KB + S - 1) / S, mg);
-    e = func_attrs((const void*)kern, (int)L.total, S > 8);
+    const int smem = floor2 && (int)L.total < kGemvTwoPerSmSmem ? kGemvTwoPerSmSmem : (int)L.total;
+    e = func_attrs((const void*)kern, smem, S > 8);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(OB, S, groups);
     cfg.blockDim = dim3(kGemvThreads, 1, 1);
-    cfg.dynamicSmemBytes = L.total;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
