@@ -162,11 +162,13 @@ __device__ __forceinline__ void warp_hadamard128(float (&v)[4]) {
     const int lane = threadIdx.x & 31;
 #pragma unroll
     for (int m = 1; m < 32; m <<= 1) {
-        const bool upper = (lane & m) != 0;
+        // upper lanes take other - v, lower lanes v + other: one fma with a lane sign (the
+        // product by +-1 is exact, so the result is the same single rounding of the sum)
+        const float sgn = (lane & m) ? -1.0f : 1.0f;
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const float other = __shfl_xor_sync(0xffffffffu, v[i], m);
-            v[i] = upper ? other - v[i] : v[i] + other;
+            v[i] = fmaf(sgn, v[i], other);
         }
     }
     const float s = 0.08838834764831845f;

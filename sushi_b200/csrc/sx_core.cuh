@@ -149,6 +149,30 @@ __device__ __forceinline__ void bfrag_put(uint4* bfrag, int mg, int kbi, int m, 
     }
 }
 
+// The four prepared values a lane holds (positions 4*lane .. 4*lane+3 of local input block kbi,
+// row m) in two stores: positions 4*lane and +1 fill slots s0 and s0+1 of entry c0, positions +2
+// and +3 the same slots of entry c0+1 (c0 = 2*(lane&1), s0 = 2*((lane>>1)&1); bfrag_put's mapping).
+template <int NB>
+__device__ __forceinline__ void bfrag_put4(uint4* bfrag, int mg, int kbi, int m, int lane, const uint16_t (&h)[4]) {
+    const int nb = m >> 3, gg = m & 7;
+    if (gg >= mg) return;
+    const int tk = lane >> 2;
+    const int c0 = (lane & 1) * 2;
+    const int s0 = ((lane >> 1) & 1) * 2;
+    const size_t entry = (size_t)((((kbi * 8 + tk) * NB + nb) * mg + gg) * 4 + c0);
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+        const uint16_t a = h[2 * q], b = h[2 * q + 1];
+        if constexpr (BFrag<NB>::COMPACT) {
+            reinterpret_cast<uint32_t*>(reinterpret_cast<uint16_t*>(bfrag) + (entry + q) * 4 + s0)[0] =
+                (uint32_t)a | ((uint32_t)b << 16);
+        } else {
+            reinterpret_cast<uint2*>(reinterpret_cast<uint32_t*>(&bfrag[entry + q]) + s0)[0] =
+                make_uint2((uint32_t)a | ((uint32_t)a << 16), (uint32_t)b | ((uint32_t)b << 16));
+        }
+    }
+}
+
 // A B-fragment entry as the four doubled-k B registers (inputs 2c, 2c+1, 2c+8, 2c+9, each f16 in
 // both halves).
 __device__ __forceinline__ uint4 bfrag_expand(uint4 v) { return v; }

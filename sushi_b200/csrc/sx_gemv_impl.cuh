@@ -123,8 +123,8 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 3 : 2) gemv_kernel(Gem
                     v[i] = round_f16(load_act(a.x, xoff + i, a.xdt)) * h2f(item == warp ? suh0[i] : suh[base + i]);
                 warp_hadamard128(v);
             }
-#pragma unroll
-            for (int i = 0; i < 4; i++) bfrag_put<NB>(s.bfrag, mg, kbi, m, lane * 4 + i, f2h(v[i]));
+            const uint16_t h[4] = {f2h(v[0]), f2h(v[1]), f2h(v[2]), f2h(v[3])};
+            bfrag_put4<NB>(s.bfrag, mg, kbi, m, lane, h);
         }
         consumers_sync<CW>();
 

@@ -186,8 +186,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_pair_kernel(MoeArgs a) {
                 for (int i = 0; i < 4; i++) v[i] = round_f16(load_act(a.x, xoff + i, a.xdt)) * h2f(suh_p[p][base + i]);
                 warp_hadamard128(v);
             }
-#pragma unroll
-            for (int i = 0; i < 4; i++) bfrag_put<1>(s.bfrag + p * s.bfrag_proj_stride, 8, kbi, m, lane * 4 + i, f2h(v[i]));
+            const uint16_t h[4] = {f2h(v[0]), f2h(v[1]), f2h(v[2]), f2h(v[3])};
+            bfrag_put4<1>(s.bfrag + p * s.bfrag_proj_stride, 8, kbi, m, lane, h);
         }
         consumers_sync<kConsumerWarps>();
         const DecParams dp[2] = {a.dp_gu, a.dp_gu};
@@ -261,8 +261,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(MoeArgs a) {
         for (int item = warp; item < kbl * 8; item += kConsumerWarps) {
             const int kbi = item / 8, m = item % 8;
             const uint16_t* src = a.hprep + (size_t)slot_of[m] * a.I + (kb0 + kbi) * 128 + lane * 4;
+            uint16_t h[4] = {0, 0, 0, 0};
+            if (m < it.rows) {
 #pragma unroll
-            for (int i = 0; i < 4; i++) bfrag_put<1>(s.bfrag, 8, kbi, m, lane * 4 + i, m < it.rows ? src[i] : (uint16_t)0);
+                for (int i = 0; i < 4; i++) h[i] = src[i];
+            }
+            bfrag_put4<1>(s.bfrag, 8, kbi, m, lane, h);
         }
         consumers_sync<kConsumerWarps>();
         const DecParams dp[1] = {a.dp_down};
