@@ -345,6 +345,18 @@ __global__ void shared_route_kernel(uint32_t* inds, float* scores, int rows) {
 
 }  // namespace
 
+int three_per_sm_smem() {
+    static int cached = 0;
+    if (cached <= 0) {
+        int dev = 0, per_sm = 0, reserve = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+        cudaDeviceGetAttribute(&reserve, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+        cached = per_sm > 0 ? per_sm / 3 - reserve : 74 * 1024;
+    }
+    return cached;
+}
+
 int two_per_sm_smem() {
     static int cached = 0;
     if (cached <= 0) {

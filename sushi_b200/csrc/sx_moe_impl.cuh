@@ -141,7 +141,7 @@ __device__ __forceinline__ int work_slot(const MoeArgs& a, int w, const WorkItem
 
 // ------------------------------------------------------------------ 2. gate + up + mid
 template <int KIND, int N>
-__global__ void __launch_bounds__(kThreads, 1) moe_pair_kernel(MoeArgs a) {
+__global__ void __launch_bounds__(kThreads, 3) moe_pair_kernel(MoeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int slot_of[8];
     cg::cluster_group cluster = cg::this_cluster();
@@ -229,7 +229,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_pair_kernel(MoeArgs a) {
 
 // ------------------------------------------------------------------ 3. down
 template <int KIND, int N>
-__global__ void __launch_bounds__(kThreads, 1) moe_down_kernel(MoeArgs a) {
+__global__ void __launch_bounds__(kThreads, 3) moe_down_kernel(MoeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int slot_of[8];
     cg::cluster_group cluster = cg::this_cluster();

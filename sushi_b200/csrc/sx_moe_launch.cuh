@@ -29,16 +29,24 @@ static cudaError_t launch_clustered(Kern kern, dim3 grid, int S, size_t smem, cu
 
 // Shared memory that lets two CTAs share an SM (per-SM capacity / 2 less the per-block reserve).
 int two_per_sm_smem();
+// The same for three CTAs per SM.
+int three_per_sm_smem();
 
-// The split-K cluster size of a chain kernel: the smallest S >= S_min whose CTAs fit two per SM
-// (the chain kernels' registers allow two).  Measured on B200 over S for hidden 2048 / 7168 layers
-// at 1, 8 and 64 tokens: that S was fastest in every case; fewer splits leave one CTA per SM, more
-// pay the cluster reduce and per-CTA start-up more often.  S_min asks for enough CTAs to cover the
-// SMs when few experts are active.
+// The split-K cluster size of a chain kernel: the smallest S >= S_min whose CTAs fit two per SM.
+// S_min asks for enough CTAs to cover the SMs when few experts are active; then (S_min > 1) the
+// smallest S >= S_min that fits three per SM is taken if any (the chain kernels' registers allow
+// three).  The kernels are compiled for three CTAs per SM (72 registers) either way.  Measured on
+// B200 against two per SM everywhere at 94 registers: the 2048/512 layer 3.5% / 2% / 3% faster
+// at 1 / 8 / 64 tokens, the 16-layer 7168/2048 stack within 1% at 1 token, 6% faster at 8 and 1%
+// at 64; taking three per SM also where S_min = 1 was no faster there and 3% slower on the stack
+// at 64 tokens.  More splits than needed pay the cluster reduce and per-CTA start-up more often.
 template <int N, int NP>
 static int fit_split(int S, int KB) {
     S = S < KB ? S : KB;
-    const size_t two = (size_t)two_per_sm_smem();
+    const size_t three = (size_t)three_per_sm_smem(), two = (size_t)two_per_sm_smem();
+    if (S > 1)
+        for (int c = S; c <= 16 && c <= KB; c++)
+            if (core_layout<N, NP, 1>((KB + c - 1) / c).total <= three) return c;
     while (S < 16 && S < KB && core_layout<N, NP, 1>((KB + S - 1) / S).total > two) S++;
     return S;
 }
