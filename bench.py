@@ -179,6 +179,7 @@ def main():
     ap.add_argument("--no-moe", action="store_true")
     ap.add_argument("--profile", default=None, choices=["gemv", "moe", "gemm", "prefill"],
                     help="a small fixed case for ncu: --warmup launches, then --steps launches, no graphs")
+    ap.add_argument("--profile-tokens", type=int, default=8, help="tokens of the --profile moe layer")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -666,7 +667,8 @@ def deepseek_bench(sx, torch, args, stream, tf_peak):
 
 def run_profile(args):
     """ncu case: the 4096x14336 K2 (n32) M=1 projection (config 1's rate, the sweep's largest
-    shape) over 12 distinct weight copies (176 MB > L2), or one MoE decode layer (T=8)."""
+    shape) over 12 distinct weight copies (176 MB > L2), or the bench's MoE decode layer at
+    --profile-tokens tokens (8 by default)."""
     import torch
 
     import sushi_b200 as sx
@@ -704,7 +706,10 @@ def run_profile(args):
         for i in range(args.warmup + args.steps):
             sx.linear(x, projs[i % copies], dec)
     else:
-        E, D, I, k, T = 512, 2048, 512, 10, 8
+        # the bench's configs[2] layer (moe_bench's `layer`), eagerly: router logits, the router
+        # (with the shared expert's gate logit at one token), the routed experts with the gated
+        # shared expert folded in
+        E, D, I, k, T = 512, 2048, 512, 10, args.profile_tokens
         parts = []
         for (i_f, o_f) in ((D, I), (D, I), (I, D)):
             tr = torch.randint(-32768, 32768, (E, i_f // 16, o_f // 16, 32), dtype=torch.int16, device="cuda")
@@ -712,11 +717,18 @@ def run_profile(args):
             sv = torch.randint(0, 2, (E, o_f), device="cuda").half() * 2 - 1
             parts.append(sx.Proj(tr, su, sv))
         bank = sx.Bank(*parts)
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(7)
+        wr = (torch.randn((D, E), device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+        shared, wg = qwen_shared(sx, torch, gen, D, I)
         x = torch.randn((T, D), device="cuda").to(torch.bfloat16)
-        logits = torch.randn((T, E), device="cuda")
         for i in range(args.warmup + args.steps):
-            inds, scores = sx.router_topk(logits, k)
-            sx.moe(x, bank, inds, scores, dec)
+            if T == 1:
+                inds, scores, gate = sx.router_topk_gate(x @ wr, k, gate=(x, wg))
+            else:
+                inds, scores, _ = sx.router_topk_gate(x @ wr, k)
+                gate = x @ wg
+            sx.moe_folded(x, bank, shared, inds, scores, dec, shared_gate=gate)
     torch.cuda.synchronize()
     assert sx.device_error() == 0
     print("profile case done", flush=True)
