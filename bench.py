@@ -47,7 +47,7 @@ RATES = [32, 48, 64]
 ROWS = [1, 2, 4, 8, 16, 64]
 L2_BYTES = 126 * 1024 * 1024
 GEMM_ROWS = 16  # sweep rows at or above this go through the tensor-core projection
-GEMV_HEADLINE_TRAFFIC = 14_783_232  # DRAM bytes per headline GEMV launch, ncu (profiles/gemv_kernel_4096x14336_k2_m1.md)
+GEMV_HEADLINE_TRAFFIC = 14_794_752  # DRAM bytes per headline GEMV launch, ncu (profiles/gemv_kernel_4096x14336_k2_m1.md, current)
 METRIC = "EXL3 GEMV compressed-HBM GB/s (% peak); MoE layer tokens/s at 1/2/4/8 B200"
 UNIT = "GB/s"
 
