@@ -157,8 +157,10 @@ __global__ void __launch_bounds__(kThreads, 3) moe_pair_kernel(MoeArgs a) {
     const int OT = a.I / 16;
     const size_t per = (size_t)(a.D / 16) * OT * N;
     core_init_barriers<N, 2, kConsumerWarps>(s);
-    grid_launch_dependents();
     grid_dependency_wait();  // the routing comes from route_prep
+    // Dependents may launch only now: every grid before this one has completed, so moe_down
+    // may read the routing (and stream its weights) before its own dependency wait.
+    grid_launch_dependents();
     WorkItem it;
     if (!work_item(a, blockIdx.x, it)) return;  // every CTA of the cluster shares blockIdx.x
     if (threadIdx.x < 8) slot_of[threadIdx.x] = threadIdx.x < it.rows ? work_slot(a, blockIdx.x, it, threadIdx.x) : 0;
@@ -246,9 +248,15 @@ __global__ void __launch_bounds__(kThreads, 3) moe_down_kernel(MoeArgs a) {
     const size_t per = (size_t)(a.I / 16) * OT * N;
     core_init_barriers<N, 1, kConsumerWarps>(s);
     grid_launch_dependents();
-    grid_dependency_wait();  // the prepared rows come from moe_pair
+    // moe_pair (this grid's predecessor) lets it launch only after its own dependency wait, so the
+    // routing (route_prep's, from before moe_pair) is complete here: the work record is read and
+    // the expert's weights stream before this grid's wait, which guards only the prepared rows
+    // (moe_pair's output).  A CTA without work still waits, so this grid completes after moe_pair.
     WorkItem it;
-    if (!work_item(a, blockIdx.x, it)) return;
+    if (!work_item(a, blockIdx.x, it)) {
+        grid_dependency_wait();
+        return;
+    }
     if (threadIdx.x < 8) slot_of[threadIdx.x] = threadIdx.x < it.rows ? work_slot(a, blockIdx.x, it, threadIdx.x) : 0;
     __syncthreads();
 
@@ -258,6 +266,7 @@ __global__ void __launch_bounds__(kThreads, 3) moe_down_kernel(MoeArgs a) {
             core_produce<N, 1>(s, tr, OT, ob, kb0, kbl);
         }
     } else {
+        grid_dependency_wait();  // the prepared rows come from moe_pair
         for (int item = warp; item < kbl * 8; item += kConsumerWarps) {
             const int kbi = item / 8, m = item % 8;
             const uint16_t* src = a.hprep + (size_t)slot_of[m] * a.I + (kb0 + kbi) * 128 + lane * 4;
