@@ -74,7 +74,7 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+    """nvidia-smi clocks and throttle reasons sampled every 50 ms while running."""
 
     def __init__(self, index):
         self.index = index
@@ -88,10 +88,16 @@ class ClockSampler:
              "clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "200", "-i", str(self.index)],
+                ["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "50", "-i", str(self.index)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            # nvidia-smi takes a moment to start: wait for its first line (at most 3 s), then keep
+            # only the lines taken from here on, inside the timed region
+            t_end = time.time() + 3.0
+            while not self.samples and time.time() < t_end:
+                time.sleep(0.005)
+            self.samples.clear()
         except Exception:
             self.proc = None
         return self
