@@ -288,21 +288,22 @@ sx_status sx_moe_ragged_folded(sx_stream stream, const sx_ragged* bank, const sx
 
 /* ------------------------------------------------------------------ routed experts, no allocation
  * sx_moe for callers that cannot allocate device memory at all.  Some hosts never call cudaMalloc
- * on the path that runs the layer: a caller recording the layer into a CUDA graph (an allocation
- * inside stream capture is not allowed), a caller whose allocator bills and owns every device
- * byte (memory admission that a hidden allocation would bypass), or a latency-critical loop that
- * cannot afford the device-wide synchronisation cudaMalloc implies.  They cannot hand sx_moe a
- * workspace either, so this entry point takes none: its scratch is a fixed buffer compiled into
- * the library (sx_moe_static_scratch_bytes(), 8 MiB), held by every GPU that loads the library
- * until the process exits.  No counterpart in the reference, whose MLX host allocates per call.
+ * on the path that runs the layer: a caller whose allocator owns and bills every device byte
+ * (memory admission that a hidden allocation would bypass, an arena sized once at start-up), or a
+ * latency-critical loop that cannot afford the device-wide synchronisation cudaMalloc implies.
+ * They cannot hand sx_moe a workspace either, so this entry point takes none: its scratch is a
+ * fixed buffer compiled into the library (sx_moe_static_scratch_bytes(), 8 MiB), held by every GPU
+ * that loads the library until the process exits.  No counterpart in the reference, whose MLX host
+ * allocates per call.
  *
- * Arguments, semantics and refusals are sx_moe's.  A call whose workspace
- * (sx_moe_workspace_bytes(bank, rows, topk)) exceeds the buffer returns
- * SX_ERR_STATIC_SCRATCH_TOO_SMALL before launching anything.  The first call on a device looks up
- * the buffer's device address (cudaGetSymbolAddress) with that device current; make that first
- * call before any stream capture.  Every call on a device shares the one buffer and the buffer
- * keeps the last call's contents (nothing in it needs to start at zero): calls that overlap on
- * the GPU race, so issue them on one stream or order them. */
+ * Arguments, semantics and refusals are sx_moe's: a malformed call gets sx_moe's own refusal.  A
+ * well-formed call whose workspace (sx_moe_workspace_bytes(bank, rows, topk)) exceeds the buffer
+ * returns SX_ERR_STATIC_SCRATCH_TOO_SMALL before launching anything.  The first call on a device
+ * (per CUDA context) looks up the buffer's device address (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture.  A cudaDeviceReset while the library
+ * is loaded leaves that looked-up address stale: not supported.  Every call on a device shares
+ * the one buffer and the buffer keeps the last call's contents (nothing in it needs to start at
+ * zero): calls that overlap on the GPU race, so issue them on one stream or order them. */
 sx_status sx_moe_static_scratch(sx_stream stream, const sx_bank* bank, const sx_decode* dec, const void* x,
                                 sx_dtype dtype, int32_t rows, const uint32_t* inds, const float* scores, int32_t topk,
                                 const void* shared, const void* shared_gate, int32_t clamp_limit, void* y);
