@@ -47,7 +47,10 @@ RATES = [32, 48, 64]
 ROWS = [1, 2, 4, 8, 16, 64]
 L2_BYTES = 126 * 1024 * 1024
 GEMM_ROWS = 16  # sweep rows at or above this go through the tensor-core projection
-GEMV_HEADLINE_TRAFFIC = 14_794_752  # DRAM bytes per headline GEMV launch, ncu (profiles/gemv_kernel_4096x14336_k2_m1.md, current)
+# DRAM traffic of the headline launch comes from a committed record of one ncu capture, which
+# names the digest of the kernel sources it was taken on; a changed kernel reports no traffic.
+TRAFFIC_RECORD = os.path.join(ROOT, "profiles", "roofline_traffic.txt")
+GEMV_SOURCES = ["sx_gemv_impl.cuh", "sx_core.cuh", "sx_decode.cuh", "sx_common.cuh", "sx_gemv.cu", "sx_gemv_mcg_nb1.cu"]
 METRIC = "EXL3 GEMV compressed-HBM GB/s (% peak); MoE layer tokens/s at 1/2/4/8 B200"
 UNIT = "GB/s"
 
@@ -61,6 +64,56 @@ def sweep_config(world):
     return {"workload": "gemv_sweep (BASELINE configs[1])", "shapes_out_x_in": ["2048x7168", "7168x2048", "4096x14336"],
             "n": RATES, "rows": ROWS, "codebook": "mcg", "window": 16,
             "l2": "ring of distinct weight copies > 2x L2 per (shape, rate)", "parallelism": f"replicas x{world}"}
+
+
+def source_digest(names):
+    """sha256 (16 hex digits) over the named kernel sources, in order (missing names skipped)."""
+    import hashlib
+
+    h = hashlib.sha256()
+    for name in names:
+        path = os.path.join(ROOT, "sushi_b200", "csrc", name)
+        if os.path.exists(path):
+            with open(path, "rb") as f:
+                h.update(name.encode() + b"\0" + f.read())
+    return h.hexdigest()[:16]
+
+
+def recorded_traffic(kernel_key, sources):
+    """(DRAM bytes per launch, provenance) of the kernel's last ncu capture, or (None, why):
+    the record's lines are `key bytes digest command...`; a digest other than the current
+    sources' means the capture was of an older kernel."""
+    digest = source_digest(sources)
+    try:
+        with open(TRAFFIC_RECORD) as f:
+            for line in f:
+                parts = line.split(None, 3)
+                if len(parts) >= 3 and parts[0] == kernel_key:
+                    if parts[2] != digest:
+                        return None, f"stale: captured on sources {parts[2]}, current {digest}"
+                    return int(parts[1]), "ncu dram__bytes_read.sum + dram__bytes_write.sum, one capture: " + (
+                        parts[3].strip() if len(parts) > 3 else "")
+    except OSError:
+        pass
+    return None, f"no capture recorded for sources {digest}"
+
+
+def host_cpu():
+    """(model name, usable host threads) of this machine."""
+    model = "unknown"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    try:
+        cores = len(os.sched_getaffinity(0))
+    except AttributeError:
+        cores = os.cpu_count() or 1
+    return model, cores
 
 
 def measured_peaks():
@@ -143,6 +196,8 @@ def run_reference(args):
     from oracle import oracle as orc
     from oracle import synth
 
+    model, cores = host_cpu()
+    orc.set_num_threads(cores)  # torch.distributed.run sets OMP_NUM_THREADS=1; use every host core
     threads = orc.num_threads()
     packs = []
     for (in_f, out_f) in SHAPES:
@@ -161,12 +216,14 @@ def run_reference(args):
             total += alg_bytes(in_f, out_f, n, 1)
     dt = time.perf_counter() - t0
     value = total / dt / 1e9
+    config = sweep_config(world)
+    config["reference_sample"] = "rows M = 1 of every (shape, rate); the CPU path costs M times the M = 1 time"
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "u16 trellis -> f32 accumulate", "data": "synthetic (seeded random trellis words)",
-        "config": sweep_config(world),
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+        "config": config,
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "cpu_model": model,
                          "sample": "each step: the sweep's 9 (shape, rate) projections at M = 1 (rows cost the CPU "
                                    "path proportionally; format.project restated in C++, OpenMP over output tiles)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -332,6 +389,8 @@ def main():
     for (in_f, out_f, n, m), (g, copies, b), ms in zip(configs, graphs, cfg_ms / args.steps):
         per_config[f"{out_f}x{in_f}_n{n}_m{m}"] = round(b / (ms * 1e-3) / 1e9, 1)
     headline = per_config.get("4096x14336_n32_m1")
+    traffic, traffic_src = recorded_traffic("gemv_kernel<MCG,32,1,W16>:4096x14336:m1", GEMV_SOURCES)
+    dense0 = config0_bench(L, torch, stream, sptr, dec, args, hbm_peak)
 
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -342,9 +401,10 @@ def main():
         # The dominant kernel at the metric's headline config: gemv_kernel on 4096x14336 K2 M=1;
         # achieved = its algorithmic bytes per launch over its average launch time in this run's
         # timed graphs; traffic = DRAM bytes read + written per launch from one ncu capture of the
-        # same launch (profiles/gemv_kernel_4096x14336_k2_m1.md).
+        # same kernel sources (null when the kernel changed since).
         "roofline": {"bound": "hbm", "achieved": headline, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": round(headline / hbm_peak, 4) if headline else None, "traffic": GEMV_HEADLINE_TRAFFIC,
+                     "frac": round(headline / hbm_peak, 4) if headline else None, "traffic": traffic,
+                     "traffic_source": traffic_src,
                      "algorithmic_bytes_per_launch": alg_bytes(14336, 4096, 32, 1), "peak_kind": peak_kind,
                      "kernel": "sx::gemv_kernel<MCG,32,1,W16> 4096x14336 M=1"},
         "sweep_gbs": round(bytes_per_step / (kernel_ms * 1e-3) / 1e9, 2),
@@ -352,12 +412,15 @@ def main():
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
         "headline_4096x14336_k2_m1_gbs": headline,
+        "dense_4096x4096": dense0,
         "per_config_gbs": per_config,
         "wall_ms_per_step": round(total_ms, 3),
     }
 
+    if world > 1:
+        out["ep_parity"] = ep_parity(sx, torch)
     if not args.no_moe:
-        out["moe"] = moe_bench(sx, _lib, torch, args, stream, sptr)
+        out["moe"] = moe_bench(sx, _lib, torch, args, stream, sptr, hbm_peak)
         out["moe_prefill"] = prefill_bench(sx, torch, args, stream, tf_peak)
         out["ffn_stack_deepseek"] = deepseek_bench(sx, torch, args, stream, tf_peak)
 
@@ -368,6 +431,116 @@ def main():
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(out), flush=True)
+
+
+def config0_bench(L, torch, stream, sptr, dec, args, hbm_peak):
+    """one dense 4096x4096 linear at K2 (n32, MCG w16), batch 1, through the
+    decode GEMV; a ring of distinct weight copies (> 2x L2) in a CUDA graph.  Compressed-HBM GB/s
+    on the algorithmic bytes (trellis + suh + svh + x + y) and its fraction of the measured HBM
+    copy bandwidth.  (Its parity, on the quantizer's own pack of that weight, is a GPU test.)"""
+    from sushi_b200 import _lib
+
+    in_f, out_f, n = 4096, 4096, 32
+    size = in_f * out_f * n // 128
+    copies = max(2, -(-2 * L2_BYTES // size))
+    tr = torch.randint(-32768, 32768, (copies, in_f // 16, out_f // 16, n), dtype=torch.int16, device="cuda")
+    su = (torch.randint(0, 2, (copies, in_f), device="cuda").half() * 2 - 1) * 0.05
+    sv = torch.randint(0, 2, (copies, out_f), device="cuda").half() * 2 - 1
+    projs = [_lib.SxProj(tr[c].data_ptr(), su[c].data_ptr(), sv[c].data_ptr(), 1, in_f, out_f, n, 0)
+             for c in range(copies)]
+    x = torch.randn((1, in_f), device="cuda").to(torch.bfloat16)
+    y = torch.empty((1, out_f), device="cuda", dtype=torch.bfloat16)
+
+    def run():
+        for p in projs:
+            st = L.sx_linear_ex(sptr, ctypes.byref(p), ctypes.byref(dec), x.data_ptr(), 2, 1, y.data_ptr(), 1)
+            if st:
+                raise RuntimeError(L.sx_status_name(st).decode())
+
+    run()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        run()
+    for _ in range(max(3, args.warmup)):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(5, args.steps)
+    e0.record(stream)
+    for _ in range(reps):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * copies)
+    del g
+    gbs = alg_bytes(in_f, out_f, n, 1) / (us * 1e-6) / 1e9
+    return {"workload": "configs[0]: 4096x4096 K2 (n32) M=1, decode GEMV", "us_per_launch": round(us, 3),
+            "gbs": round(gbs, 1), "hbm_frac_of_measured": round(gbs / hbm_peak, 4),
+            "algorithmic_bytes_per_launch": alg_bytes(in_f, out_f, n, 1), "copies": copies}
+
+
+def ep_parity(sx, torch):
+    """Expert-parallel correctness at N > 1, outside the timed regions: a seeded 64-expert layer
+    (hidden 512, intermediate 256, K2, top-6, gated shared expert), identical on every rank; each
+    rank routes its own tokens, runs them through the expert-parallel layer holding its eighth,
+    quarter or half of the experts (ExpertParallel.moe, the shared expert on the side stream) and
+    through the single-GPU layer over the whole bank (moe_folded), and compares.  The expert-
+    parallel layer adds the ranks' f32 partials in rank order, the single-GPU one the slots in k
+    order, so a row may differ in the last bf16 bit; the line reports how many rows are
+    bit-identical and the largest difference in units of the output's last place."""
+    import torch.distributed as dist
+
+    world, rank, _ = dist_env()
+    E, D, I, k = 64, 512, 256, 6
+    El = E // world
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(2024)  # the same full bank, router and shared expert on every rank
+
+    def proj(experts, i_f, o_f):
+        tr = torch.randint(-32768, 32768, (experts, i_f // 16, o_f // 16, 32), dtype=torch.int16, device="cuda",
+                           generator=gen)
+        su = (torch.randint(0, 2, (experts, i_f), device="cuda", generator=gen).half() * 2 - 1) * 0.05
+        sv = torch.randint(0, 2, (experts, o_f), device="cuda", generator=gen).half() * 2 - 1
+        return sx.Proj(tr, su, sv)
+
+    full = sx.Bank(proj(E, D, I), proj(E, D, I), proj(E, I, D))
+    shared = sx.Bank(proj(1, D, I), proj(1, D, I), proj(1, I, D))
+    local = sx.Bank(*[sx.Proj(p.trellis[rank * El:(rank + 1) * El], p.suh[rank * El:(rank + 1) * El],
+                              p.svh[rank * El:(rank + 1) * El]) for p in (full.gate, full.up, full.down)])
+    wr = (torch.randn((D, E), device="cuda", generator=gen) * 0.05).to(torch.bfloat16)
+    wg = (torch.randn((D, 1), device="cuda", generator=gen) * 0.05).to(torch.bfloat16)
+    dec = sx.Decode(sx.Codebook.MCG, 16)
+    xg = torch.Generator(device="cuda")
+    xg.manual_seed(3000 + rank)
+    ep = sx.ExpertParallel.from_process_group()
+    rows = same = 0
+    worst = 0.0
+    try:
+        for T, cap in ((1, 1), (5, 8), (37, 40)):
+            x = torch.randn((T, D), device="cuda", generator=xg).to(torch.bfloat16)
+            inds, scores, _ = sx.router_topk_gate(x @ wr, k)
+            gate = x @ wg
+            got = ep.moe(x, local, E, inds, scores, dec, rows_cap=cap, shared_gate=gate, shared_bank=shared)
+            want = sx.moe_folded(x, full, shared, inds, scores, dec, shared_gate=gate)
+            torch.cuda.synchronize()
+            same += int((got == want).all(dim=1).sum())
+            rows += T
+            # difference in units of the bf16 last place of the larger magnitude
+            ulp = torch.maximum(got.float().abs(), want.float().abs()).clamp_min(1e-30)
+            ulp = torch.exp2(torch.floor(torch.log2(ulp)) - 7)
+            worst = max(worst, float(((got.float() - want.float()).abs() / ulp).max()))
+    finally:
+        torch.cuda.synchronize()
+        ep.destroy()
+    t = torch.tensor([float(rows), float(same), worst], device="cuda")
+    mx = t.clone()
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    assert sx.device_error() == 0
+    return {"n": world, "rows": int(t[0]), "bit_identical_rows": int(t[1]), "max_bf16_ulps": float(mx[2]),
+            "within_one_ulp": float(mx[2]) <= 1.0,
+            "case": "64 experts 512/256 K2 top-6 + gated shared expert; 1, 5, 37 tokens per rank"}
 
 
 def qwen_shared(sx, torch, gen, D, I):
@@ -384,7 +557,7 @@ def qwen_shared(sx, torch, gen, D, I):
     return sx.Bank(*parts), wg
 
 
-def moe_bench(sx, _lib, torch, args, stream, sptr):
+def moe_bench(sx, _lib, torch, args, stream, sptr, hbm_peak):
     """hidden 2048, 512 experts of 512, top-10, K2 (n32) MCG random banks,
     softmax router over fp32 logits from a bf16 2048x512 matrix, one sigmoid-gated shared expert of
     512; tokens/s of router + shared expert + routed experts for T tokens per rank.  One GPU: sx_moe over the whole bank.  N GPUs: expert parallel
@@ -464,8 +637,25 @@ def moe_bench(sx, _lib, torch, args, stream, sptr):
         del g
         inds, _ = sx.router_topk((x @ wr).float(), k)
         active = int(torch.unique(inds).numel())
+        # algorithmic HBM bytes of the layer on each rank: the experts it owns that any rank's
+        # tokens touch, the shared expert, the router matrix and gate vector, x and y
+        all_inds = inds.to(torch.int32).contiguous()
+        if world > 1:
+            gathered = torch.empty((world * T, k), dtype=torch.int32, device="cuda")
+            dist.all_gather_into_tensor(gathered, all_inds)
+            all_inds = gathered
+        touched = torch.unique(all_inds)
+        owned = int(((touched >= rank * El) & (touched < (rank + 1) * El)).sum())
+        expert_b = 3 * (D * I * 32 // 128 + 2 * (D + I))
+        rank_bytes = owned * expert_b + expert_b + D * E * 2 + D * 2 + 2 * T * D * 2
+        tot = torch.tensor([float(rank_bytes)], device="cuda")
+        if world > 1:
+            dist.all_reduce(tot)
+        gbs = float(tot.item()) / (ms * 1e-3) / 1e9
         res[f"T{T}"] = {"tokens_per_s": round(world * T / (ms * 1e-3), 1), "ms_per_layer": round(ms, 4),
-                        "tokens_per_rank": T, "active_experts_rank0_tokens": active}
+                        "tokens_per_rank": T, "active_experts_rank0_tokens": active,
+                        "alg_bytes_all_ranks": int(tot.item()), "gbs": round(gbs, 1),
+                        "hbm_frac_of_measured": round(gbs / (world * hbm_peak), 4)}
     if world > 1:
         res["equal_total_64_tokens"] = f"T{64 // world}"
     if ep is not None:
@@ -740,10 +930,58 @@ def run_profile(args):
     print("profile case done", flush=True)
 
 
+def cpu_moe_layer(orc, synth, T, threads):
+    """The reference's CPU path for one configs[2] decode layer of T tokens: routing per
+    moeRoutingChain (softmax, top-10, renormalised; src/moe_router.zig:16-65) over f32 logits,
+    then per (token, slot) the SwiGLU expert of f32_truth.Dense.run (src/exl3/f32_truth.zig:85)
+    with every projection through format.project (decode + matmul, src/exl3/expert_exl3.zig:546),
+    plus the sigmoid-gated shared expert.  Returns seconds per layer."""
+    E, D, I, k, n = 512, 2048, 512, 10, 32
+    rng = np.random.default_rng(31)
+    wr = (rng.standard_normal((D, E)) * 0.02).astype(np.float32)
+    wg = (rng.standard_normal(D) * 0.02).astype(np.float32)
+    x = synth.activations(32, T, D)
+    banks = {}
+
+    def expert(e):
+        if e not in banks:
+            banks[e] = [tuple(a[0] for a in synth.random_bank(7000 + 3 * e + p, 1, i_f, o_f, n))
+                        for p, (i_f, o_f) in enumerate(((D, I), (D, I), (I, D)))]
+        return banks[e]
+
+    def swiglu(e, xr):
+        (gt, gs, gv), (ut, us, uv), (dt, ds, dv) = expert(e)
+        g = orc.project(xr, gt, gs, gv, D, I, n, orc.CB_MCG, 16, threads=threads)[0]
+        u = orc.project(xr, ut, us, uv, D, I, n, orc.CB_MCG, 16, threads=threads)[0]
+        act = (g / (1.0 + np.exp(-g)) * u).astype(np.float32)
+        return orc.project(act, dt, ds, dv, I, D, n, orc.CB_MCG, 16, threads=threads)[0]
+
+    def layer():
+        logits = x @ wr
+        y = np.zeros((T, D), np.float32)
+        for r in range(T):
+            ii, ww = orc.router_truth(logits[r:r + 1], k)
+            for e, w in zip(ii[0], ww[0]):
+                y[r] += np.float32(w) * swiglu(int(e), x[r])
+            y[r] += swiglu(-1, x[r]) / np.float32(1.0 + np.exp(-float(x[r] @ wg)))
+        return y
+
+    layer()  # warm: decodes nothing ahead, but builds the touched experts' packs
+    reps = 3
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        layer()
+    return (time.perf_counter() - t0) / reps
+
+
 def cpu_baseline():
+    """The reference's CPU decode + matmul timed on this host: the headline projection with every
+    host thread and with one, and the configs[2] MoE decode layer at 1 and 8 tokens."""
     from oracle import oracle as orc
     from oracle import synth
 
+    model, cores = host_cpu()
+    orc.set_num_threads(cores)
     in_f, out_f, n = 14336, 4096, 32
     tr, su, sv = synth.random_bank(5, 1, in_f, out_f, n)
     x = synth.activations(5, 1, in_f)
@@ -753,8 +991,20 @@ def cpu_baseline():
     for _ in range(reps):
         orc.project(x, tr[0], su[0], sv[0], in_f, out_f, n, orc.CB_MCG, 16)
     dt = (time.perf_counter() - t0) / reps
-    return {"value": round(alg_bytes(in_f, out_f, n, 1) / dt / 1e9, 3), "unit": UNIT, "cores": orc.num_threads(),
-            "kind": "port", "sample": "4096x14336 K2 M=1 projection x3 (format.project restated in C++, OpenMP over output tiles)"}
+    t0 = time.perf_counter()
+    orc.project_single_thread(x, tr[0], su[0], sv[0], in_f, out_f, n, orc.CB_MCG, 16)
+    dt1 = time.perf_counter() - t0
+    b = alg_bytes(in_f, out_f, n, 1)
+    moe = {}
+    for T in (1, 8):
+        sec = cpu_moe_layer(orc, synth, T, cores)
+        moe[f"T{T}"] = {"tokens_per_s": round(T / sec, 2), "ms_per_layer": round(sec * 1e3, 2)}
+    return {"value": round(b / dt / 1e9, 3), "unit": UNIT, "cores": orc.num_threads(), "kind": "port",
+            "cpu_model": model, "single_thread_gbs": round(b / dt1 / 1e9, 4),
+            "sample": "4096x14336 K2 M=1 projection x3 on every host thread, x1 on one (format.project restated "
+                      "in C++, OpenMP over output tiles)",
+            "moe_decode_layer": dict(moe, workload="configs[2] layer, routed top-10 + gated shared expert, "
+                                                   "every projection through format.project on every host thread")}
 
 
 if __name__ == "__main__":

@@ -61,6 +61,15 @@ def activations(seed, rows, in_f, std=1.0):
     return bf16_round(normal(seed, rows * in_f, std).reshape(rows, in_f))
 
 
+def outlier_activations(seed, rows, in_f, std=1.0):
+    """x [rows, in] as bf16 values: N(0, std) with every channel i where i % 997 == 3 scaled x30,
+    the normed-residual stand-in of the reference's f32 truth (`activations`,
+    src/exl3/f32_truth.zig:42-54)."""
+    x = normal(seed, rows * in_f, std).reshape(rows, in_f)
+    x[:, np.arange(in_f) % 997 == 3] *= 30.0
+    return bf16_round(x)
+
+
 def encode_weight(w, seed, name, n, codebook, window_bits):
     """(trellis, suh, svh, g) for public weight w [in, out] with an identity Hessian."""
     in_f, out_f = w.shape
@@ -94,6 +103,30 @@ def config1_pack(cache_dir=None):
                 return {k: z[k] for k in z.files}
     w = dense_weight(CONFIG1_SEED, 4096, 4096, 0.02)
     trellis, suh, svh, g = encode_weight(w, CONFIG1_SEED, CONFIG1_NAME, 32, orc.CB_MCG, 16)
+    pack = {"trellis": trellis, "suh": suh, "svh": svh, "g": np.float32(g)}
+    if path:
+        os.makedirs(cache_dir, exist_ok=True)
+        np.savez(path, **pack)
+    return pack
+
+
+CONFIG2_SEED = 0xC0F2
+CONFIG2_NAME = "model.layers.0.mlp.up_proj"
+
+
+def config2_pack(cache_dir=None):
+    """BASELINE configs[1]'s encoded weight at the sweep shape 7168x2048 (out x in): W [2048, 7168]
+    ~ N(0, 0.02) bf16 with ceil(1% of 2048) seeded input channels x8 (outlier channels), encoded
+    MCG K2 (n32) at window 12 by the quantizer restatement with an identity Hessian.  Cached as
+    .npz in `cache_dir` when given (about 15 s of encode on 8 cores)."""
+    path = None
+    if cache_dir:
+        path = os.path.join(cache_dir, "config2_mcg_n32_w12_outliers.npz")
+        if os.path.exists(path):
+            with np.load(path) as z:
+                return {k: z[k] for k in z.files}
+    w = dense_weight(CONFIG2_SEED, 2048, 7168, 0.02, outlier_frac=0.01, outlier_scale=8.0)
+    trellis, suh, svh, g = encode_weight(w, CONFIG2_SEED, CONFIG2_NAME, 32, orc.CB_MCG, 12)
     pack = {"trellis": trellis, "suh": suh, "svh": svh, "g": np.float32(g)}
     if path:
         os.makedirs(cache_dir, exist_ok=True)

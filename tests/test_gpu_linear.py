@@ -48,10 +48,21 @@ def _check(sx, tr, su, sv, in_f, out_f, n, cb, w, rows, dtype=None, seed=0):
     return y, truth, xv
 
 
+def _check_reference(y, xv, tr, su, sv, in_f, out_f, n, cb, w):
+    """The fused projection against the reference's CPU projection `format.project` on the same
+    pack and rows: the GEMV's doubled-k products skip the f16 rounding of each weight's half sum
+    that the CPU decode applies, and format.project rounds its inner sums and outputs to f16, so the
+    two agree to the output bar, not bit for bit."""
+    oargs, _ = dec_args(cb, w)
+    ref = orc.project(xv, tr, su, sv, in_f, out_f, n, *oargs)
+    assert max_rel(y, ref) <= MAX_REL_TOL, max_rel(y, ref)
+
+
 @pytest.mark.parametrize("n", [16, 24, 32, 36, 40, 42, 48, 56, 64, 80, 96, 112, 128])
 def test_linear_mcg_every_rate_class(sx, n):
     tr, su, sv = random_pack(n, 256, 384, n)
-    _check(sx, tr, su, sv, 256, 384, n, orc.CB_MCG, 16, rows=1)
+    y, _, xv = _check(sx, tr, su, sv, 256, 384, n, orc.CB_MCG, 16, rows=1)
+    _check_reference(y, xv, tr, su, sv, 256, 384, n, orc.CB_MCG, 16)
 
 
 @pytest.mark.parametrize("rows", [1, 2, 3, 4, 7, 8, 9, 16, 17, 33, 64])
@@ -68,7 +79,8 @@ def test_linear_rows(sx, rows):
 )
 def test_linear_codebooks(sx, cb, w, n):
     tr, su, sv = random_pack(100 + n + cb, 384, 256, n)
-    _check(sx, tr, su, sv, 384, 256, n, cb, w, rows=3)
+    y, _, xv = _check(sx, tr, su, sv, 384, 256, n, cb, w, rows=3)
+    _check_reference(y, xv, tr, su, sv, 384, 256, n, cb, w)
 
 
 @pytest.mark.parametrize("dtype", ["float32", "float16", "bfloat16"])
