@@ -50,7 +50,9 @@ enum {
     SX_ERR_NCCL = 17,                      /* an NCCL call failed (expert-parallel calls) */
     SX_ERR_TILE_ORDER_UNSUPPORTED = 18,    /* error.Exl3TileOrderUnsupported (docs/pack-format.md) */
     SX_ERR_GROUP_GEOMETRY = 19,            /* error.Exl3GroupGeometry (src/exl3/layout.zig:80-95) */
-    SX_ERR_STATIC_SCRATCH_TOO_SMALL = 20   /* the call needs more scratch than sx_moe_static_scratch holds */
+    SX_ERR_STATIC_SCRATCH_TOO_SMALL = 20,  /* the call needs more scratch than sx_moe_static_scratch holds */
+    SX_ERR_PEER_BUFFER_TOO_SMALL = 21,     /* the expert-parallel call needs more peer buffer than is reserved */
+    SX_ERR_PEER_ACCESS = 22                /* a peer's buffer could not be mapped (sx_ep_reserve_peer) */
 };
 
 /* The status's name ("SX_OK", "SX_ERR_BAD_SHAPE", ...); a static string. */
@@ -389,6 +391,33 @@ sx_status sx_ep_moe_ragged_folded(sx_ep* ep, sx_stream stream, const sx_ragged* 
                                   const void* x, sx_dtype dtype, int32_t rows, int32_t rows_cap, const uint32_t* inds,
                                   const float* scores, int32_t topk, const void* shared_gate, int32_t clamp_limit,
                                   void* y, void* workspace, size_t workspace_bytes);
+
+/* ------------------------------------------------------------------ expert parallel over NVLink
+ * With a peer buffer reserved (sx_ep_reserve_peer), every sx_ep_moe* call of the communicator
+ * moves its rows over NVLink peer memory instead of NCCL: each rank's buffer is mapped into every
+ * other rank's address space (CUDA IPC), the dispatch kernel stores each routed row and its slots
+ * straight into the owning rank's buffer and raises a flag there, the owner's expert chain runs
+ * over the rows it received (only those), its reduce kernel stores each row's f32 partial straight
+ * into the token owner's buffer and raises a flag, and the owner's combine waits for the flags and
+ * adds the partials in rank order.  Only routed rows cross NVLink (no fixed-size blocks), nothing
+ * waits on the host, and the calls can be recorded in a CUDA graph after the reservation.  Every
+ * wait is bounded (~2 s); a wait that gives up latches SX_ERR_DEVICE_TIMEOUT's device code
+ * (sx_device_error) and the call's outputs are then undefined.  Results equal the NCCL transport's
+ * bit for bit.  Requires every rank on one node with peer access (NVLink / NVSwitch).  No
+ * reference counterpart. */
+
+/* Peer-buffer bytes a call with these sizes needs (the same on every rank). */
+size_t sx_ep_peer_bytes(const sx_ep* ep, int32_t rows_cap, int32_t hidden, int32_t topk, sx_dtype dtype);
+
+/* Reserves `bytes` of peer buffer on every rank and maps each rank's into every other's (CUDA
+ * IPC handles exchanged over the communicator).  Collective: every rank calls it with the same
+ * bytes, with no sx_ep call of the communicator in flight (it synchronises the device).  A smaller
+ * or equal request than the current reservation does nothing; a larger one replaces it.  bytes = 0
+ * releases the reservation and returns the communicator to the NCCL transport. */
+sx_status sx_ep_reserve_peer(sx_ep* ep, size_t bytes);
+
+/* The reserved peer-buffer bytes (0: the NCCL transport). */
+size_t sx_ep_peer_reserved(const sx_ep* ep);
 
 /* The communicator's world size and rank (either pointer may be null). */
 sx_status sx_ep_info(const sx_ep* ep, int32_t* world, int32_t* rank);

@@ -211,6 +211,8 @@ const char* sx_status_name(sx_status s) {
         case SX_ERR_TILE_ORDER_UNSUPPORTED: return "SX_ERR_TILE_ORDER_UNSUPPORTED";
         case SX_ERR_GROUP_GEOMETRY: return "SX_ERR_GROUP_GEOMETRY";
         case SX_ERR_STATIC_SCRATCH_TOO_SMALL: return "SX_ERR_STATIC_SCRATCH_TOO_SMALL";
+        case SX_ERR_PEER_BUFFER_TOO_SMALL: return "SX_ERR_PEER_BUFFER_TOO_SMALL";
+        case SX_ERR_PEER_ACCESS: return "SX_ERR_PEER_ACCESS";
         default: return "SX_ERR_UNKNOWN";
     }
 }

@@ -21,6 +21,7 @@ enum DeviceError : int {
     DEV_TIMEOUT_FULL = 1,     // a consumer waited too long for a stage's bytes
     DEV_TIMEOUT_EMPTY = 2,    // the producer waited too long for a stage to drain
     DEV_TIMEOUT_SELFTEST = 3, // sx_selftest_wait_timeout's wait gave up, as it is meant to
+    DEV_TIMEOUT_PEER = 4,     // an expert-parallel rank waited too long for a peer's flag
 };
 
 extern __device__ int g_device_error;

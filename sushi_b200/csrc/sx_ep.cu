@@ -26,14 +26,21 @@
 #include "sx_internal.h"
 #include "sx_moe_impl.cuh"
 
+// Peer transport limits: ranks a communicator can map (the flag arrays hold this many words).
+constexpr int kPeerMax = 128;
+
 // side: a stream of the communicator's own on which a layer's shared expert runs while the
 // dispatch, the local experts and the combine's exchange run on the caller's stream (fork and
-// join are the events between the two).
+// join are the events between the two).  peer: this rank's reserved peer buffer (0 bytes: the
+// NCCL transport) and every rank's buffer as mapped here (peer[rank] = own).
 struct sx_ep {
     ncclComm_t comm;
     int world, rank, device;
     cudaStream_t side;
     cudaEvent_t fork, join;
+    uint8_t* own;
+    size_t own_bytes;
+    uint8_t* peer[kPeerMax];
 };
 
 namespace sx {
@@ -51,6 +58,7 @@ struct NcclApi {
     decltype(&ncclGroupEnd) group_end = nullptr;
     decltype(&ncclSend) send = nullptr;
     decltype(&ncclRecv) recv = nullptr;
+    decltype(&ncclAllGather) all_gather = nullptr;
     decltype(&ncclGetErrorString) error_string = nullptr;
     bool ok = false;
     char why[160] = "";
@@ -76,7 +84,7 @@ const NcclApi& nccl() {
         a.ok = bind(h, "ncclGetUniqueId", a.get_unique_id) && bind(h, "ncclCommInitRank", a.comm_init_rank) &&
                bind(h, "ncclCommDestroy", a.comm_destroy) && bind(h, "ncclCommAbort", a.comm_abort) &&
                bind(h, "ncclGroupStart", a.group_start) && bind(h, "ncclGroupEnd", a.group_end) &&
-               bind(h, "ncclSend", a.send) && bind(h, "ncclRecv", a.recv) &&
+               bind(h, "ncclSend", a.send) && bind(h, "ncclRecv", a.recv) && bind(h, "ncclAllGather", a.all_gather) &&
                bind(h, "ncclGetErrorString", a.error_string);
         if (!a.ok) snprintf(a.why, sizeof(a.why), "libnccl.so.2 lacks a needed symbol");
     });
@@ -200,32 +208,266 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(CombineArgs a) {
     }
 }
 
+// ------------------------------------------------------------------ peer transport (NVLink)
+// Every rank's peer buffer has the same layout: a control block of u32 words, then the data
+// regions for the call's sizes (rows_cap C, hidden D, topk K, activation bytes esz):
+//   recv_x   [G][C][D]  rows source rank g stored here (its list for this rank, in order)
+//   recv_ids [G][C][K]  their slots as this rank's local expert ids (kSentinel: another rank's)
+//   recv_sc  [G][C][K]  the slots' scores
+//   part     [G][C][D]  f32: from expert rank g, the partial of this rank's row at place p of the
+//                       list this rank sent to g
+// Control words (zero at reservation; flags only grow):
+//   seq                  the calls this rank has begun (its plan kernel counts them)
+//   disp_flag[g]         the last call whose rows rank g has stored here
+//   comb_flag[g]         the last call whose partials rank g has stored here
+//   recv_cnt[g]          rows rank g stored here in that call
+//   disp_done[g], red_done  this rank's own CTA counters (last CTA signals), reset by that CTA
+constexpr int kCtrlSeq = 0, kCtrlDispFlag = kPeerMax, kCtrlCombFlag = 2 * kPeerMax, kCtrlRecvCnt = 3 * kPeerMax,
+              kCtrlDispDone = 4 * kPeerMax, kCtrlRedDone = 5 * kPeerMax;
+constexpr size_t kCtrlBytes = 16384;
+
+struct PeerLayout {
+    size_t recv_x, recv_ids, recv_sc, part, total;
+};
+
+PeerLayout peer_layout(int G, int C, int D, int K, int esz) {
+    auto up256 = [](size_t v) { return (v + 255) / 256 * 256; };
+    PeerLayout l{};
+    const size_t places = (size_t)G * C;
+    size_t off = kCtrlBytes;
+    l.recv_x = off; off = up256(off + places * D * esz);
+    l.recv_ids = off; off = up256(off + places * K * sizeof(uint32_t));
+    l.recv_sc = off; off = up256(off + places * K * sizeof(float));
+    l.part = off; off = up256(off + places * D * sizeof(float));
+    l.total = off;
+    return l;
+}
+
+struct PeerArgs {
+    uint8_t* base[kPeerMax];  // every rank's buffer as mapped on this device (base[me] = own)
+    PeerLayout lay;
+    int me;
+};
+
+__device__ __forceinline__ uint32_t* ctrl(uint8_t* base) { return reinterpret_cast<uint32_t*>(base); }
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Waits until *flag >= seq (wrap-safe), for at most ~2 s of wall time; on a timeout latches
+// DEV_TIMEOUT_PEER and returns false (the caller goes on: its outputs are undefined, nothing hangs).
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t seq) {
+    if ((int32_t)(ld_acquire_sys(flag) - seq) >= 0) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 0;; i++) {
+        __nanosleep(64);
+        if ((int32_t)(ld_acquire_sys(flag) - seq) >= 0) return true;
+        if ((i & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
+            latch_error(DEV_TIMEOUT_PEER);
+            return false;
+        }
+    }
+}
+
+// The last of `total` CTAs to arrive on `counter` (a word of this rank's own control block)
+// returns true, with every arriving CTA's earlier stores (peer ones included) visible at system
+// scope first; it resets the counter for the next call.  Called by thread 0 after a block barrier
+// that follows every thread's __threadfence_system().
+__device__ __forceinline__ bool last_to_arrive(uint32_t* counter, uint32_t total) {
+    __threadfence_system();
+    const uint32_t prev = atomicAdd(counter, 1u);
+    if (prev + 1 != total) return false;
+    __threadfence_system();
+    *counter = 0;
+    return true;
+}
+
+// Plan for the peer transport: ep_plan_kernel's lists and places, plus the per-destination counts
+// and (block 0) the start of a new call in this rank's control block.
+__global__ void __launch_bounds__(256) ep_peer_plan_kernel(EpArgs a, int* cnt, uint32_t* own_ctrl) {
+    __shared__ int warp_sums[8];
+    const int d = blockIdx.x;
+    if (d == 0 && threadIdx.x == 0) own_ctrl[kCtrlSeq] += 1u;
+    int base = 0;
+    for (int r0 = 0; r0 < a.rows; r0 += 256) {
+        const int r = r0 + threadIdx.x;
+        int flag = 0;
+        if (r < a.rows) {
+            for (int k = 0; k < a.K; k++) {
+                const uint32_t e = a.inds[(size_t)r * a.K + k];
+                if (e < (uint32_t)a.Etot && (int)(e / (uint32_t)a.El) == d) flag = 1;
+            }
+        }
+        int total;
+        const int idx = block_scan_256(flag, warp_sums, &total);
+        if (r < a.rows) {
+            a.pos[(size_t)r * a.world + d] = flag ? base + idx : -1;
+            if (flag) a.list[(size_t)d * a.cap + base + idx] = r;
+        }
+        base += total;
+    }
+    if (threadIdx.x == 0) cnt[d] = base;
+}
+
+// Dispatch (grid: B x G blocks): destination d = blockIdx.y; places i = blockIdx.x, +B, ... below
+// cnt[d]: row list[d][i] of x and its slots (d-local ids, scores) stored into d's recv regions at
+// [me][i].  The last of d's B blocks stores the count and raises d's flag for this rank.
+__global__ void __launch_bounds__(256) ep_peer_dispatch_kernel(EpArgs a, const int* cnt, PeerArgs p) {
+    const int d = blockIdx.y;
+    uint8_t* dst = p.base[d];
+    const uint32_t seq = ctrl(p.base[p.me])[kCtrlSeq];
+    const int n = cnt[d];
+    const size_t row_bytes = (size_t)a.D * a.esz;  // a multiple of 256 (D % 128 == 0)
+    const size_t slot0 = (size_t)p.me * a.cap;
+    uint32_t* ids = reinterpret_cast<uint32_t*>(dst + p.lay.recv_ids);
+    float* sc = reinterpret_cast<float*>(dst + p.lay.recv_sc);
+    for (int i = blockIdx.x; i < n; i += gridDim.x) {
+        const int r = a.list[(size_t)d * a.cap + i];
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.x) + (size_t)r * row_bytes);
+        uint4* out = reinterpret_cast<uint4*>(dst + p.lay.recv_x + (slot0 + i) * row_bytes);
+        for (size_t v = threadIdx.x; v < row_bytes / 16; v += blockDim.x) out[v] = src[v];
+        for (int k = threadIdx.x; k < a.K; k += blockDim.x) {
+            const uint32_t e = a.inds[(size_t)r * a.K + k];
+            const bool here = e < (uint32_t)a.Etot && (int)(e / (uint32_t)a.El) == d;
+            ids[(slot0 + i) * a.K + k] = here ? e - (uint32_t)(d * a.El) : kSentinel;
+            sc[(slot0 + i) * a.K + k] = here ? a.scores[(size_t)r * a.K + k] : 0.0f;
+        }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0 && last_to_arrive(&ctrl(p.base[p.me])[kCtrlDispDone + d], gridDim.x)) {
+        st_relaxed_sys(&ctrl(dst)[kCtrlRecvCnt + p.me], (uint32_t)n);
+        __threadfence_system();
+        st_release_sys(&ctrl(dst)[kCtrlDispFlag + p.me], seq);
+    }
+}
+
+// Every rank's rows for this call have arrived (one block; thread g waits for rank g's flag).
+// The expert chain that follows reads the received rows and counts.
+__global__ void ep_peer_recv_wait_kernel(PeerArgs p, int world) {
+    uint32_t* c = ctrl(p.base[p.me]);
+    const uint32_t seq = c[kCtrlSeq];
+    for (int g = threadIdx.x; g < world; g += blockDim.x) wait_flag(&c[kCtrlDispFlag + g], seq);
+}
+
+// The received rows' partials (grid-stride over (live row, 512-column block) units): the row's
+// slots on this rank summed in k order in f32, stored into the row's owner's part region at
+// [me][i].  The last block raises every rank's combine flag for this rank.
+struct ReducePushArgs {
+    const float* yslot;     // [G*C*K][D] per-slot planes of the local chain
+    const uint32_t* ids;    // [G*C][K] this rank's recv_ids
+    int world, cap, K, D, El;
+};
+
+__global__ void __launch_bounds__(128) ep_peer_reduce_push_kernel(ReducePushArgs a, PeerArgs p) {
+    __shared__ int pre[kPeerMax + 1];
+    uint32_t* c = ctrl(p.base[p.me]);
+    const uint32_t seq = c[kCtrlSeq];
+    if (threadIdx.x == 0) {
+        int acc = 0;
+        for (int g = 0; g < a.world; g++) {
+            pre[g] = acc;
+            acc += min((int)c[kCtrlRecvCnt + g], a.cap);
+        }
+        pre[a.world] = acc;
+    }
+    __syncthreads();
+    const int nb = (a.D + 511) / 512;
+    const long long units = (long long)pre[a.world] * nb;
+    for (long long u = blockIdx.x; u < units; u += gridDim.x) {
+        const int j = (int)(u / nb), cb = (int)(u % nb);
+        int g = 0;
+        while (g + 1 < a.world && pre[g + 1] <= j) g++;
+        const int i = j - pre[g];
+        const size_t place = (size_t)g * a.cap + i;
+        const int d = cb * 512 + threadIdx.x * 4;
+        if (d >= a.D) continue;
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int k = 0; k < a.K; k++) {
+            if (a.ids[place * a.K + k] >= (uint32_t)a.El) continue;
+            const float4 v = *reinterpret_cast<const float4*>(a.yslot + (place * a.K + k) * a.D + d);
+            acc[0] += v.x;
+            acc[1] += v.y;
+            acc[2] += v.z;
+            acc[3] += v.w;
+        }
+        float* dst = reinterpret_cast<float*>(p.base[g] + p.lay.part) + ((size_t)p.me * a.cap + i) * a.D + d;
+        *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0 && last_to_arrive(&c[kCtrlRedDone], gridDim.x)) {
+        for (int g = 0; g < a.world; g++) st_release_sys(&ctrl(p.base[g])[kCtrlCombFlag + p.me], seq);
+    }
+}
+
+// Combine for the peer transport (one block per own row; at least one block): waits for every
+// rank's partials of this call, then as ep_combine_kernel with the partials in this rank's part
+// region ([g][place]).
+__global__ void __launch_bounds__(256) ep_peer_combine_kernel(CombineArgs a, PeerArgs p) {
+    uint32_t* c = ctrl(p.base[p.me]);
+    const uint32_t seq = c[kCtrlSeq];
+    if (threadIdx.x < 32)
+        for (int g = threadIdx.x; g < a.world; g += 32) wait_flag(&c[kCtrlCombFlag + g], seq);
+    __syncthreads();
+    const int r = blockIdx.x;
+    if (r >= a.rows) return;
+    const float* part = reinterpret_cast<const float*>(p.base[p.me] + p.lay.part);
+    for (int d = threadIdx.x; d < a.D; d += blockDim.x) {
+        float acc = 0.0f;
+        for (int g = 0; g < a.world; g++) {
+            const int q = a.pos[(size_t)r * a.world + g];
+            if (q >= 0) acc += __ldcg(part + ((size_t)g * a.cap + q) * a.D + d);  // peers' stores: L2, not L1
+        }
+        const size_t i = (size_t)r * a.D + d;
+        const float sh = a.sh_plane ? round_act(a.sh_plane[i], a.xdt) : a.shared ? load_act(a.shared, i, a.xdt) : 0.0f;
+        const float y = routed_finish(acc, a.xdt, a.sh_plane || a.shared, sh, a.shared_gate, r);
+        store_act(a.y, (size_t)r * a.D + d, a.xdt, y);
+    }
+}
+
 // ------------------------------------------------------------------ workspace
 constexpr size_t kAlign = 256;
 size_t up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 struct EpWs {
-    size_t list, pos, send_x, send_inds, send_scores, recv_x, recv_inds, recv_scores, part_send, part_recv, moe, total;
+    size_t list, pos, cnt, send_x, send_inds, send_scores, recv_x, recv_inds, recv_scores, part_send, part_recv, moe,
+        total;
     size_t moe_bytes;
     size_t sh_plane, sh_scratch;  // the shared expert's plane [cap][D] f32 and scratch (0 bytes without one)
 };
 
-// The layout for a local layer of `ng` rate groups (one for a uniform bank) over El experts.
-EpWs ep_ws_layout(const MoeGroup* g, int ng, int El, int world, int cap, int K, int esz, const sx_bank* sh = nullptr) {
+// The layout for a local layer of `ng` rate groups (one for a uniform bank) over El experts.  With
+// the peer transport (peer) the exchanged blocks live in the peer buffers, not here.
+EpWs ep_ws_layout(const MoeGroup* g, int ng, int El, int world, int cap, int K, int esz, const sx_bank* sh = nullptr,
+                  bool peer = false) {
     EpWs w{};
     const int D = g[0].bank.gate.in_features;
     const size_t places = (size_t)world * cap;
+    const size_t xfer = peer ? 0 : places;  // places of the NCCL transport's own blocks
     size_t off = 0;
     w.list = off; off = up(off + places * sizeof(int));
     w.pos = off; off = up(off + places * sizeof(int));
-    w.send_x = off; off = up(off + places * D * esz);
-    w.send_inds = off; off = up(off + places * K * sizeof(uint32_t));
-    w.send_scores = off; off = up(off + places * K * sizeof(float));
-    w.recv_x = off; off = up(off + places * D * esz);
-    w.recv_inds = off; off = up(off + places * K * sizeof(uint32_t));
-    w.recv_scores = off; off = up(off + places * K * sizeof(float));
-    w.part_send = off; off = up(off + places * D * sizeof(float));
-    w.part_recv = off; off = up(off + places * D * sizeof(float));
+    w.cnt = off; off = up(off + (size_t)world * sizeof(int));
+    w.send_x = off; off = up(off + xfer * D * esz);
+    w.send_inds = off; off = up(off + xfer * K * sizeof(uint32_t));
+    w.send_scores = off; off = up(off + xfer * K * sizeof(float));
+    w.recv_x = off; off = up(off + xfer * D * esz);
+    w.recv_inds = off; off = up(off + xfer * K * sizeof(uint32_t));
+    w.recv_scores = off; off = up(off + xfer * K * sizeof(float));
+    w.part_send = off; off = up(off + xfer * D * sizeof(float));
+    w.part_recv = off; off = up(off + xfer * D * sizeof(float));
     // a rank receives about rows_cap * K valid slots (every rank's rows_cap rows, K slots each,
     // spread over the world): that, not the places' sentinel-padded slots, picks its expert path
     w.moe_bytes = moe_groups_ws(g, ng, El, (int32_t)places, K, (long long)cap * K);
@@ -289,12 +531,127 @@ void release_side(sx_ep* ep) {
     ep->fork = ep->join = nullptr;
 }
 
+// The peer mappings and this rank's buffer (local: every peer has stopped using them once the
+// caller synchronised its streams; the reservation's own barrier precedes a replacement).
+void release_peer(sx_ep* ep) {
+    for (int g = 0; g < kPeerMax; g++) {
+        if (ep->peer[g] && g != ep->rank) cudaIpcCloseMemHandle(ep->peer[g]);
+        ep->peer[g] = nullptr;
+    }
+    if (ep->own) cudaFree(ep->own);
+    ep->own = nullptr;
+    ep->own_bytes = 0;
+}
+
+// Every rank's `bytes`-byte block of `mine` gathered into `all` [world][bytes] on the host, over the
+// communicator (the side stream, synchronised).  Also the reservation's barrier.
+sx_status gather_host(sx_ep* ep, const void* mine, size_t bytes, void* all) {
+    const NcclApi& n = nccl();
+    if (!n.ok) return nccl_missing();
+    uint8_t* dev = nullptr;
+    cudaError_t ce = cudaMalloc(&dev, bytes * (ep->world + 1));
+    if (ce != cudaSuccess) return cuda_status(ce, "peer handle exchange buffer");
+    sx_status st = SX_OK;
+    ce = cudaMemcpy(dev, mine, bytes, cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) st = cuda_status(ce, "peer handle exchange copy");
+    if (!st) st = nccl_status(n.all_gather(dev, dev + bytes, bytes, ncclUint8, ep->comm, ep->side), "ncclAllGather");
+    if (!st && (ce = cudaStreamSynchronize(ep->side)) != cudaSuccess) st = cuda_status(ce, "peer handle exchange sync");
+    if (!st && (ce = cudaMemcpy(all, dev + bytes, bytes * ep->world, cudaMemcpyDeviceToHost)) != cudaSuccess)
+        st = cuda_status(ce, "peer handle exchange copy back");
+    cudaFree(dev);
+    return st;
+}
+
 }  // namespace
 }  // namespace sx
 
 using namespace sx;
 
 extern "C" {
+
+size_t sx_ep_peer_bytes(const sx_ep* ep, int32_t rows_cap, int32_t hidden, int32_t topk, sx_dtype dtype) {
+    if (!ep || rows_cap < 1 || hidden < 128 || hidden % 128 || topk < 1 || !dtype_ok(dtype)) return 0;
+    return peer_layout(ep->world, rows_cap, hidden, topk, (int)dtype_size(dtype)).total;
+}
+
+size_t sx_ep_peer_reserved(const sx_ep* ep) { return ep ? ep->own_bytes : 0; }
+
+sx_status sx_ep_reserve_peer(sx_ep* ep, size_t bytes) {
+    if (!ep) return SX_ERR_NULL_POINTER;
+    if (ep->world > kPeerMax) return SX_ERR_BAD_SHAPE;
+    if (bytes > 0 && bytes <= ep->own_bytes) return SX_OK;
+    if (bytes == 0 && !ep->own) return SX_OK;
+    int dev = -1;
+    cudaGetDevice(&dev);
+    if (dev != ep->device) return SX_ERR_BAD_SHAPE;  // the communicator's device must be current
+    cudaError_t ce = cudaDeviceSynchronize();
+    if (ce != cudaSuccess) return cuda_status(ce, "peer reservation sync");
+    int32_t one = 1;
+    int32_t* all = new (std::nothrow) int32_t[ep->world];
+    if (!all) return SX_ERR_BAD_SHAPE;
+    // every rank has finished with the old buffers before any rank frees its own
+    sx_status st = gather_host(ep, &one, sizeof(one), all);
+    delete[] all;
+    if (st) return st;
+    release_peer(ep);
+    if (bytes == 0) return SX_OK;
+    const size_t size = (bytes + (2u << 20) - 1) / (2u << 20) * (2u << 20);
+    uint8_t* own = nullptr;
+    int32_t ok = 1;
+    cudaIpcMemHandle_t h{};
+    if ((ce = cudaMalloc(&own, size)) != cudaSuccess || (ce = cudaMemset(own, 0, size)) != cudaSuccess ||
+        (ce = cudaDeviceSynchronize()) != cudaSuccess || (ce = cudaIpcGetMemHandle(&h, own)) != cudaSuccess) {
+        note_cuda_error(ce, "peer buffer");
+        ok = 0;
+    }
+    struct Entry {
+        cudaIpcMemHandle_t h;
+        int32_t ok;
+    };
+    Entry mine{h, ok};
+    Entry* ents = new (std::nothrow) Entry[ep->world];
+    if (!ents) {
+        if (own) cudaFree(own);
+        return SX_ERR_BAD_SHAPE;
+    }
+    st = gather_host(ep, &mine, sizeof(mine), ents);
+    bool every = st == SX_OK;
+    for (int g = 0; every && g < ep->world; g++) every = ents[g].ok != 0;
+    ep->own = own;
+    ep->peer[ep->rank] = own;
+    int32_t mapped = every ? 1 : 0;
+    for (int g = 0; mapped && g < ep->world; g++) {
+        if (g == ep->rank) continue;
+        void* p = nullptr;
+        if ((ce = cudaIpcOpenMemHandle(&p, ents[g].h, cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess) {
+            note_cuda_error(ce, "cudaIpcOpenMemHandle");
+            mapped = 0;
+            break;
+        }
+        ep->peer[g] = static_cast<uint8_t*>(p);
+    }
+    delete[] ents;
+    if (st) {
+        release_peer(ep);
+        return st;
+    }
+    // every rank learns whether every rank mapped every peer: all keep the buffers or none does
+    int32_t* agree = new (std::nothrow) int32_t[ep->world];
+    if (!agree) {
+        release_peer(ep);
+        return SX_ERR_BAD_SHAPE;
+    }
+    st = gather_host(ep, &mapped, sizeof(mapped), agree);
+    bool all_mapped = st == SX_OK;
+    for (int g = 0; all_mapped && g < ep->world; g++) all_mapped = agree[g] != 0;
+    delete[] agree;
+    if (!all_mapped) {
+        release_peer(ep);
+        return st ? st : SX_ERR_PEER_ACCESS;
+    }
+    ep->own_bytes = size;
+    return SX_OK;
+}
 
 sx_status sx_ep_unique_id(uint8_t id[128]) {
     if (!id) return SX_ERR_NULL_POINTER;
@@ -316,7 +673,7 @@ sx_status sx_ep_init(const uint8_t id[128], int32_t world, int32_t rank, sx_ep**
     if (!n.ok) return nccl_missing();
     ncclUniqueId u;
     memcpy(&u, id, 128);
-    sx_ep* ep = new (std::nothrow) sx_ep;
+    sx_ep* ep = new (std::nothrow) sx_ep();
     if (!ep) return SX_ERR_BAD_SHAPE;
     ep->world = world;
     ep->rank = rank;
@@ -343,8 +700,9 @@ sx_status sx_ep_init(const uint8_t id[128], int32_t world, int32_t rank, sx_ep**
 
 sx_status sx_ep_destroy(sx_ep* ep) {
     if (!ep) return SX_ERR_NULL_POINTER;
-    const sx_status st = nccl_status(nccl().comm_destroy(ep->comm), "ncclCommDestroy");
     release_side(ep);
+    release_peer(ep);
+    const sx_status st = nccl_status(nccl().comm_destroy(ep->comm), "ncclCommDestroy");
     delete ep;
     return st;
 }
@@ -353,6 +711,7 @@ sx_status sx_ep_abort(sx_ep* ep) {
     if (!ep) return SX_ERR_NULL_POINTER;
     const sx_status st = nccl_status(nccl().comm_abort(ep->comm), "ncclCommAbort");
     release_side(ep);
+    release_peer(ep);
     delete ep;
     return st;
 }
@@ -368,7 +727,9 @@ size_t sx_ep_workspace_bytes(const sx_ep* ep, const sx_bank* local_bank, int32_t
                              sx_dtype dtype) {
     if (!ep || !local_bank || rows_cap < 1 || topk < 1 || !dtype_ok(dtype)) return 0;
     const MoeGroup g{*local_bank, 0};
-    return ep_ws_layout(&g, 1, local_bank->gate.experts, ep->world, rows_cap, topk, (int)dtype_size(dtype)).total;
+    return ep_ws_layout(&g, 1, local_bank->gate.experts, ep->world, rows_cap, topk, (int)dtype_size(dtype), nullptr,
+                        ep->own_bytes > 0)
+        .total;
 }
 
 size_t sx_ep_ragged_workspace_bytes(const sx_ep* ep, const sx_ragged* local, int32_t rows_cap, int32_t topk,
@@ -377,13 +738,73 @@ size_t sx_ep_ragged_workspace_bytes(const sx_ep* ep, const sx_ragged* local, int
     MoeGroup g[kMaxGroups];
     int ng = 0;
     if (ragged_groups(local, g, &ng) != SX_OK) return 0;
-    return ep_ws_layout(g, ng, local->experts, ep->world, rows_cap, topk, (int)dtype_size(dtype)).total;
+    return ep_ws_layout(g, ng, local->experts, ep->world, rows_cap, topk, (int)dtype_size(dtype), nullptr,
+                        ep->own_bytes > 0)
+        .total;
 }
 
 }  // extern "C"
 
 namespace sx {
 namespace {
+
+// The peer transport's call after the admission checks and the shared-expert fork: plan,
+// dispatch into the owners' buffers, wait for every rank's rows, the local chain over the received
+// rows only, reduce + push of the partials into the token owners' buffers, join, combine.
+// `join` joins the side stream into the caller's before the combine (which reads its plane).
+template <typename Join>
+sx_status ep_peer_moe(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int ng, int El, const sx_decode* dec,
+                      const EpArgs& a, const PeerLayout& PL, const EpWs& L, uint8_t* ws, int rows, int topk,
+                      int clamp_limit, const float* sh_plane, const void* shared, const void* shared_gate, void* y,
+                      sx_dtype dtype, Join& join) {
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const int G = ep->world, C = a.cap, D = a.D;
+    const size_t places = (size_t)G * C;
+    PeerArgs pa{};
+    for (int g = 0; g < G; g++) pa.base[g] = ep->peer[g];
+    pa.lay = PL;
+    pa.me = ep->rank;
+    uint8_t* own = ep->own;
+    int* cnt = reinterpret_cast<int*>(ws + L.cnt);
+
+    ep_peer_plan_kernel<<<G, 256, 0, s>>>(a, cnt, reinterpret_cast<uint32_t*>(own));
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_status(e, "ep peer plan launch");
+    const int B = std::max(1, std::min(C, std::max(4, 8 * sm_count() / G)));
+    ep_peer_dispatch_kernel<<<dim3(B, G), 256, 0, s>>>(a, cnt, pa);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "ep peer dispatch launch");
+    ep_peer_recv_wait_kernel<<<1, 128, 0, s>>>(pa, G);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "ep peer wait launch");
+
+    const MoeSegments seg{reinterpret_cast<const int*>(own) + kCtrlRecvCnt, C, G};
+    const uint32_t* ids = reinterpret_cast<const uint32_t*>(own + PL.recv_ids);
+    float* yslot = nullptr;
+    sx_status st = moe_run(stream, groups, ng, El, dec, own + PL.recv_x, dtype, (int32_t)places, ids,
+                           reinterpret_cast<const float*>(own + PL.recv_sc), topk, nullptr, nullptr, clamp_limit,
+                           nullptr, ws + L.moe, L.moe_bytes, nullptr, (long long)C * topk, nullptr, nullptr, &seg,
+                           &yslot);
+    if (st) return st;
+    const ReducePushArgs rp{yslot, ids, G, C, topk, D, El};
+    const long long units = (long long)places * ((D + 511) / 512);
+    const int grid = (int)std::max(1LL, std::min(units, (long long)8 * sm_count()));
+    ep_peer_reduce_push_kernel<<<grid, 128, 0, s>>>(rp, pa);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "ep peer reduce launch");
+
+    if ((st = join(SX_OK))) return st;
+    CombineArgs c{};
+    c.pos = a.pos;
+    c.sh_plane = sh_plane;
+    c.shared = shared;
+    c.shared_gate = shared_gate;
+    c.y = y;
+    c.rows = rows;
+    c.cap = C;
+    c.D = D;
+    c.world = G;
+    c.xdt = dtype;
+    ep_peer_combine_kernel<<<std::max(rows, 1), 256, 0, s>>>(c, pa);
+    return cuda_status(cudaGetLastError(), "ep peer combine launch");
+}
 
 // sx_ep_moe over the local layer's rate groups (one group for a uniform bank) of El experts.
 sx_status ep_moe_groups(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int ng, int El, int32_t experts_total,
@@ -408,9 +829,12 @@ sx_status ep_moe_groups(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int
         if (st) return st;
     }
     const int esz = (int)dtype_size(dtype);
-    const EpWs L = ep_ws_layout(groups, ng, El, ep->world, rows_cap, topk, esz, sh_bank);
+    const bool peer = ep->own_bytes > 0;
+    const EpWs L = ep_ws_layout(groups, ng, El, ep->world, rows_cap, topk, esz, sh_bank, peer);
     if (!workspace || workspace_bytes < L.total) return SX_ERR_WORKSPACE_TOO_SMALL;
-    if (!nccl().ok) return nccl_missing();
+    const PeerLayout PL = peer_layout(ep->world, rows_cap, D, topk, esz);
+    if (peer && ep->own_bytes < PL.total) return SX_ERR_PEER_BUFFER_TOO_SMALL;
+    if (!peer && !nccl().ok) return nccl_missing();
 
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -460,6 +884,9 @@ sx_status ep_moe_groups(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int
     a.send_x = ws + L.send_x;
     a.send_inds = reinterpret_cast<uint32_t*>(ws + L.send_inds);
     a.send_scores = reinterpret_cast<float*>(ws + L.send_scores);
+
+    if (peer) return join(ep_peer_moe(ep, stream, groups, ng, El, dec, a, PL, L, ws, rows, topk, clamp_limit, sh_plane,
+                                      shared, shared_gate, y, dtype, join));
 
     // 1-2. plan and gather this rank's send blocks
     ep_plan_kernel<<<G, 256, 0, s>>>(a);
@@ -538,7 +965,8 @@ size_t sx_ep_folded_workspace_bytes(const sx_ep* ep, const sx_bank* local_bank, 
                                     int32_t rows_cap, int32_t topk, sx_dtype dtype) {
     if (!ep || !local_bank || !shared_bank || rows_cap < 1 || topk < 1 || !dtype_ok(dtype)) return 0;
     const MoeGroup g{*local_bank, 0};
-    return ep_ws_layout(&g, 1, local_bank->gate.experts, ep->world, rows_cap, topk, (int)dtype_size(dtype), shared_bank)
+    return ep_ws_layout(&g, 1, local_bank->gate.experts, ep->world, rows_cap, topk, (int)dtype_size(dtype), shared_bank,
+                        ep->own_bytes > 0)
         .total;
 }
 
@@ -548,7 +976,9 @@ size_t sx_ep_ragged_folded_workspace_bytes(const sx_ep* ep, const sx_ragged* loc
     MoeGroup g[kMaxGroups];
     int ng = 0;
     if (ragged_groups(local, g, &ng) != SX_OK) return 0;
-    return ep_ws_layout(g, ng, local->experts, ep->world, rows_cap, topk, (int)dtype_size(dtype), shared_bank).total;
+    return ep_ws_layout(g, ng, local->experts, ep->world, rows_cap, topk, (int)dtype_size(dtype), shared_bank,
+                        ep->own_bytes > 0)
+        .total;
 }
 
 sx_status sx_ep_moe_folded(sx_ep* ep, sx_stream stream, const sx_bank* local_bank, const sx_bank* shared_bank,

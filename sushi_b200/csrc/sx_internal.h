@@ -42,12 +42,22 @@ struct MoeGroup {
 };
 constexpr int kMaxGroups = 32;  // layout.max_groups (src/exl3/layout.zig:4)
 
-// moe_impl over the rate groups of a layer of Etot experts (sx_moe_ragged's body).
+// An expert-parallel rank's received rows: `n` segments of `cap` places, segment g live in its
+// first cnt[g] places (device counts, read by route_prep after its dependency wait).
+struct MoeSegments {
+    const int* cnt;
+    int cap, n;
+};
+
+// moe_impl over the rate groups of a layer of Etot experts (sx_moe_ragged's body).  seg: only
+// the segments' live places are routed.  yslot_out: no reduce is launched; the per-slot planes
+// (slot s at [s][D] f32, score included, written for the routed slots only) are left for the
+// caller at *yslot_out, the start of the workspace.
 sx_status moe_run(sx_stream stream, const MoeGroup* groups, int ng, int Etot, const sx_decode* dec, const void* x,
                   sx_dtype dtype, int32_t rows, const uint32_t* inds, const float* scores, int32_t topk,
                   const void* shared, const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
                   size_t workspace_bytes, float* partial, long long slots, const sx_bank* sh_bank = nullptr,
-                  const sx_decode* sh_dec = nullptr);
+                  const sx_decode* sh_dec = nullptr, const MoeSegments* seg = nullptr, float** yslot_out = nullptr);
 size_t moe_groups_ws(const MoeGroup* g, int ng, int Etot, int rows, int topk, long long slots);
 // A layer's shared expert (one SwiGLU expert over hidden size D): its admission, and its output
 // over `rows` rows alone into plane [rows][D] f32 with shared_expert_ws(sh, rows) bytes of scratch.

@@ -78,15 +78,28 @@ __global__ void __launch_bounds__(1024) route_prep_kernel(MoeArgs a) {
     for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;
     grid_dependency_wait();  // the routing comes from the previous kernel
     __syncthreads();
+    // The slots to sort, in warp-uniform strides: every slot, or an expert-parallel rank's live
+    // places only (segment by segment).  body(s, in_range) runs on every lane of a warp at once.
+    auto for_slots = [&](auto&& body) {
+        if (!a.seg_cnt) {
+            for (int s0 = tid - (tid & 31); s0 < RK; s0 += blockDim.x) body(s0 + (tid & 31), s0 + (tid & 31) < RK);
+            return;
+        }
+        for (int g = 0; g < a.nseg; g++) {
+            const int live = min(max(a.seg_cnt[g], 0), a.seg_cap) * a.K;
+            const int base = g * a.seg_cap * a.K;
+            for (int s0 = tid - (tid & 31); s0 < live; s0 += blockDim.x)
+                body(base + s0 + (tid & 31), s0 + (tid & 31) < live);
+        }
+    };
     // Warp-aggregated counting: lanes holding the same expert add once (a hot expert would
     // otherwise serialise thousands of atomics on one shared-memory word).
-    for (int s0 = tid - (tid & 31); s0 < RK; s0 += blockDim.x) {
-        const int s = s0 + (tid & 31);
-        const uint32_t e = s < RK ? a.inds[s] - (uint32_t)a.e_lo : 0xFFFFFFFFu;  // ids below the group wrap past E
+    for_slots([&](int s, bool in_range) {
+        const uint32_t e = in_range ? a.inds[s] - (uint32_t)a.e_lo : 0xFFFFFFFFu;  // ids below the group wrap past E
         const bool valid = e < (uint32_t)a.E;
         const unsigned peers = __match_any_sync(0xffffffffu, valid ? e : 0xFFFFFFFFu);
         if (valid && (tid & 31) == __ffs(peers) - 1) atomicAdd(&cnt[e], __popc(peers));
-    }
+    });
     __syncthreads();
     auto items1 = [&](int c) { return c >= a.big_min ? 0 : (c + a.chunk - 1) / a.chunk; };
     auto items2 = [&](int c) { return c >= a.big_min ? (c + a.big_chunk - 1) / a.big_chunk : 0; };
@@ -123,10 +136,9 @@ __global__ void __launch_bounds__(1024) route_prep_kernel(MoeArgs a) {
     __syncthreads();
     for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;  // reused as cursors
     __syncthreads();
-    for (int s0 = tid - (tid & 31); s0 < RK; s0 += blockDim.x) {
+    for_slots([&](int s, bool in_range) {
         const int lane = tid & 31;
-        const int s = s0 + lane;
-        const uint32_t e = s < RK ? a.inds[s] - (uint32_t)a.e_lo : 0xFFFFFFFFu;
+        const uint32_t e = in_range ? a.inds[s] - (uint32_t)a.e_lo : 0xFFFFFFFFu;
         const bool valid = e < (uint32_t)a.E;
         const unsigned peers = __match_any_sync(0xffffffffu, valid ? e : 0xFFFFFFFFu);
         const int leader = __ffs(peers) - 1;
@@ -139,7 +151,7 @@ __global__ void __launch_bounds__(1024) route_prep_kernel(MoeArgs a) {
             a.sorted_e[off[e] + pos] = (int)e;
             if (a.chunk == 8 && pos < a.big_min) a.work_slots[(wb[e] + pos / 8) * 8 + pos % 8] = s;
         }
-    }
+    });
 }
 
 constexpr size_t kAlign = 256;
@@ -478,7 +490,8 @@ size_t moe_workspace_bytes(const sx_bank* bank, int32_t rows, int32_t topk, long
 // fold: a shared expert riding this group's decode-chain launches (shared_plan mode 1), or null.
 sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_decode* dec, const void* x,
                     sx_dtype dtype, int32_t rows, const uint32_t* inds, const float* scores, int32_t topk,
-                    int32_t clamp_limit, float* yslot, uint8_t* ws, long long slots, const sx_bank* fold = nullptr) {
+                    int32_t clamp_limit, float* yslot, uint8_t* ws, long long slots, const sx_bank* fold = nullptr,
+                    const MoeSegments* seg = nullptr) {
     const int E = bank->gate.experts;
     const int D = bank->gate.in_features, I = bank->gate.out_features;
     sx_status st;
@@ -521,6 +534,11 @@ sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_de
     a.work_rec = reinterpret_cast<int4*>(ws + L.work_rec);
     a.work_slots = reinterpret_cast<int*>(ws + L.work_slots);
     a.w_routed = L.W_max;
+    if (seg) {
+        a.seg_cnt = seg->cnt;
+        a.seg_cap = seg->cap;
+        a.nseg = seg->n;
+    }
     if (fold) {
         a.sh_items = (rows + 7) / 8;
         a.sh_slot0 = rows * topk;
@@ -686,15 +704,15 @@ sx_status moe_run(sx_stream stream, const MoeGroup* groups, int ng, int Etot, co
                   sx_dtype dtype, int32_t rows, const uint32_t* inds, const float* scores, int32_t topk,
                   const void* shared, const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
                   size_t workspace_bytes, float* partial, long long slots, const sx_bank* sh_bank,
-                  const sx_decode* sh_dec) {
-    if (!x || !inds || !scores || (!y && !partial)) return SX_ERR_NULL_POINTER;
+                  const sx_decode* sh_dec, const MoeSegments* seg, float** yslot_out) {
+    if (!x || !inds || !scores || (!y && !partial && !yslot_out)) return SX_ERR_NULL_POINTER;
     if (clamp_limit < 0 || clamp_limit > 128) return SX_ERR_INVALID_CLAMP;
     if (rows < 1 || topk < 1) return SX_ERR_BAD_SHAPE;
     if (topk > 32) return SX_ERR_TOPK_EXCEEDS_REDUCE_BANK;
     if (!dtype_ok(dtype)) return SX_ERR_BAD_DTYPE;
     if (shared_gate && !shared && !sh_bank) return SX_ERR_NULL_POINTER;
     // (an expert-parallel rank's rows carry every slot, most of them other ranks' sentinels)
-    if (topk > Etot && !partial) return SX_ERR_TOPK_EXCEEDS_EXPERTS;
+    if (topk > Etot && !partial && !yslot_out) return SX_ERR_TOPK_EXCEEDS_EXPERTS;
     if (Etot > 8192) return SX_ERR_BAD_SHAPE;
     const int D = groups[0].bank.gate.in_features, I = groups[0].bank.gate.out_features;
     for (int i = 0; i < ng; i++) {
@@ -731,8 +749,12 @@ sx_status moe_run(sx_stream stream, const MoeGroup* groups, int ng, int Etot, co
         const sx_status st = moe_group(stream, &groups[i].bank, groups[i].e_lo, dec, x, dtype, rows, inds, scores, topk,
                                        clamp_limit, yslot, scratch,
                                        group_slots(slots, rows, topk, groups[i].bank.gate.experts, Etot),
-                                       plan.mode == 1 && plan.group == i ? sh_bank : nullptr);
+                                       plan.mode == 1 && plan.group == i ? sh_bank : nullptr, seg);
         if (st) return st;
+    }
+    if (yslot_out) {  // the caller reduces the per-slot planes itself
+        *yslot_out = yslot;
+        return SX_OK;
     }
     if (plan.mode == 2) {
         const sx_status st = shared_chain(stream, sh_bank, sh_dec, x, dtype, rows, topk, clamp_limit, yslot, scratch);
@@ -767,7 +789,7 @@ sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, 
     if (!bank) return SX_ERR_NULL_POINTER;
     const MoeGroup g{*bank, 0};
     return moe_run(stream, &g, 1, bank->gate.experts, dec, x, dtype, rows, inds, scores, topk, shared, shared_gate,
-                   clamp_limit, y, workspace, workspace_bytes, partial, slots, nullptr, nullptr);
+                   clamp_limit, y, workspace, workspace_bytes, partial, slots, nullptr, nullptr, nullptr, nullptr);
 }
 
 }  // namespace sx

@@ -76,6 +76,11 @@ struct MoeArgs {
     uint16_t* tu;           // [R*K][D] f16
     float* gf;              // [R*K][I] f32
     float* uf;              // [R*K][I] f32
+    // An expert-parallel rank's received rows (seg_cnt set): R = nseg * seg_cap places, segment g
+    // (the rows source rank g sent) live in its first min(seg_cnt[g], seg_cap) places; route_prep
+    // reads the counts after its dependency wait and skips every other place.
+    const int* seg_cnt;
+    int seg_cap, nseg;
 };
 
 // A token's routed sum `acc` (f32) made into its output value: rounded to the output dtype, then

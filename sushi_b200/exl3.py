@@ -535,17 +535,38 @@ def share_unique_id(group=None) -> bytes:
 class ExpertParallel:
     """An expert-parallel communicator (sx_ep_*): rank `rank` of `world` holds experts
     [rank*E/world, (rank+1)*E/world) of each E-expert layer as a local Bank of E/world experts.
-    Dispatch and combine are NCCL all-to-alls over the GPUs (include/sushi_exl3.h, sx_ep_moe)."""
 
-    def __init__(self, unique_id: bytes, world: int, rank: int):
+    transport "peer" (the default): dispatch and combine store the routed rows and partials straight
+    into the owning ranks' peer buffers over NVLink (sx_ep_reserve_peer; the buffer is reserved, a
+    collective step, the first time a call needs more than is reserved, so every rank must make the
+    same calls); "nccl": fixed-size NCCL all-to-alls."""
+
+    def __init__(self, unique_id: bytes, world: int, rank: int, transport: str = "peer"):
         if len(unique_id) != 128:
             raise Exl3Error(1)
+        if transport not in ("peer", "nccl"):
+            raise ValueError(f"transport {transport!r}")
         self.world, self.rank = int(world), int(rank)
+        self.transport = transport
         buf = (ctypes.c_uint8 * 128).from_buffer_copy(unique_id)
         h = ctypes.c_void_p()
         _check(lib().sx_ep_init(buf, self.world, self.rank, ctypes.byref(h)))
         self._h = h
         self._ws = None
+
+    def reserve(self, rows_cap: int, hidden: int, topk: int, dtype=torch.bfloat16):
+        """Collective: the peer buffers for calls up to these sizes (no-op when already reserved or
+        with the NCCL transport)."""
+        if self.transport != "peer":
+            return
+        need = int(lib().sx_ep_peer_bytes(self._h, int(rows_cap), int(hidden), int(topk), _DT[dtype]))
+        if need == 0:
+            raise Exl3Error(1)
+        if need > int(lib().sx_ep_peer_reserved(self._h)):
+            _check(lib().sx_ep_reserve_peer(self._h, need))
+
+    def peer_reserved(self) -> int:
+        return int(lib().sx_ep_peer_reserved(self._h))
 
     @staticmethod
     def unique_id() -> bytes:
@@ -554,17 +575,19 @@ class ExpertParallel:
         return bytes(buf)
 
     @classmethod
-    def from_process_group(cls, group=None):
+    def from_process_group(cls, group=None, transport: str = "peer"):
         """Every rank of a torch.distributed group joins one communicator (share_unique_id)."""
         import torch.distributed as dist
 
-        return cls(share_unique_id(group), dist.get_world_size(group), dist.get_rank(group))
+        return cls(share_unique_id(group), dist.get_world_size(group), dist.get_rank(group), transport)
 
     def workspace_bytes(self, local_bank, rows_cap: int, topk: int, dtype=torch.bfloat16, shared_bank=None) -> int:
         """Workspace bytes for a local Bank (sx_ep_workspace_bytes) or Ragged layer
-        (sx_ep_ragged_workspace_bytes); with a shared expert, the *_folded_* variants."""
+        (sx_ep_ragged_workspace_bytes); with a shared expert, the *_folded_* variants.  With the
+        peer transport this reserves the peer buffers for these sizes first (collective)."""
         b = local_bank.c()
         ragged = isinstance(local_bank, Ragged)
+        self.reserve(rows_cap, local_bank.hidden if ragged else local_bank.gate.dims()[1], topk, dtype)
         if shared_bank is not None:
             sb = shared_bank.c()
             fn = lib().sx_ep_ragged_folded_workspace_bytes if ragged else lib().sx_ep_folded_workspace_bytes

@@ -1,7 +1,9 @@
-"""Expert-parallel routed layer (sx_ep_moe) on the GPU.
+"""Expert-parallel routed layer (sx_ep_moe) on the GPU, over both transports (NVLink peer buffers,
+the default, and NCCL all-to-alls).
 
 One GPU: a world-1 communicator sends every row to itself, so sx_ep_moe must give the same bits
-as sx_moe (the partial is the same k-order f32 sum; the combine adds it to 0).  Two GPUs (skipped
+as sx_moe (the partial is the same k-order f32 sum; the combine adds it to 0), over either
+transport.  Two GPUs (skipped
 on one): each rank holds half of the experts and its own rows; its output must match the
 single-GPU sx_moe over the full bank within the stated bar (the partials of two ranks are added
 in rank order instead of k order, so a few outputs differ in their last bit) and the f32 truth.
@@ -17,6 +19,8 @@ from oracle import synth
 from tests.helpers import MAX_REL_TOL, REL_RMS_TOL, dec_args, dev, max_rel, rel_rms, random_pack, to_f32
 
 pytestmark = pytest.mark.gpu
+
+TRANSPORTS = ["peer", "nccl"]
 
 torch = pytest.importorskip("torch")
 
@@ -48,7 +52,8 @@ def _route(seed, T, E, k):
 
 
 @pytest.mark.parametrize("T", [1, 6, 19])
-def test_ep_world1_is_bit_identical_to_moe(sx, T):
+@pytest.mark.parametrize("transport", TRANSPORTS)
+def test_ep_world1_is_bit_identical_to_moe(sx, transport, T):
     E, D, I, k = 16, 256, 128, 4
     bank_np = _bank_np(40 + T, E, D, I, 32)
     _, dec = dec_args(orc.CB_MCG, 16)
@@ -58,7 +63,7 @@ def test_ep_world1_is_bit_identical_to_moe(sx, T):
     ii, ww = torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda()
     shared = torch.randn((T, D), device="cuda").to(torch.bfloat16)
     gate = torch.randn((T,), device="cuda").to(torch.bfloat16)
-    ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0)
+    ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0, transport)
     try:
         for kw in ({}, {"shared": shared}, {"shared": shared, "shared_gate": gate}):
             want = sx.moe(xt, b, ii, ww, dec, **kw)
@@ -70,7 +75,8 @@ def test_ep_world1_is_bit_identical_to_moe(sx, T):
         ep.destroy()
 
 
-def test_ep_world1_spare_capacity_and_skipped_ids(sx):
+@pytest.mark.parametrize("transport", TRANSPORTS)
+def test_ep_world1_spare_capacity_and_skipped_ids(sx, transport):
     """rows_cap above rows (unused places carry sentinel slots) and ids >= E (skipped)."""
     E, D, I, k, T = 8, 256, 128, 3, 5
     bank_np = _bank_np(7, E, D, I, 32)
@@ -79,7 +85,7 @@ def test_ep_world1_spare_capacity_and_skipped_ids(sx):
     xt = torch.from_numpy(synth.activations(3, T, D)).cuda().to(torch.float32)
     inds, wts = _route(9, T, E, k)
     inds[1, 2] = E + 5
-    ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0)
+    ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0, transport)
     try:
         got = to_f32(ep.moe(xt, b, E, torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda(), dec, rows_cap=16))
         want = to_f32(sx.moe(xt, b, torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda(), dec))
@@ -89,11 +95,12 @@ def test_ep_world1_spare_capacity_and_skipped_ids(sx):
     assert max_rel(got, want) <= 1e-5
 
 
-def test_ep_refusals(sx):
+@pytest.mark.parametrize("transport", TRANSPORTS)
+def test_ep_refusals(sx, transport):
     E, D, I = 8, 256, 128
     b = _bank(sx, _bank_np(1, E, D, I, 32))
     _, dec = dec_args(orc.CB_MCG, 16)
-    ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0)
+    ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0, transport)
     x = torch.zeros((4, D), device="cuda", dtype=torch.bfloat16)
     ii = torch.zeros((4, 2), device="cuda", dtype=torch.int32)
     ww = torch.zeros((4, 2), device="cuda")
@@ -129,7 +136,8 @@ def _ragged_slice(sx, groups, e0, e1):
 
 
 @pytest.mark.parametrize("T", [3, 40])
-def test_ep_ragged_world1_is_bit_identical_to_moe_ragged(sx, T):
+@pytest.mark.parametrize("transport", TRANSPORTS)
+def test_ep_ragged_world1_is_bit_identical_to_moe_ragged(sx, transport, T):
     """sx_ep_moe_ragged over a world of one: the same bits as sx_moe_ragged (T=40 takes the
     decode chain per group in both)."""
     D, I, k = 256, 128, 4
@@ -140,7 +148,7 @@ def test_ep_ragged_world1_is_bit_identical_to_moe_ragged(sx, T):
     inds, wts = _route(T + 2, T, 16, k)
     ii, ww = torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda()
     shared = torch.randn((T, D), device="cuda").to(torch.bfloat16)
-    ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0)
+    ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0, transport)
     try:
         for kw in ({}, {"shared": shared}):
             want = sx.moe_ragged(xt, rb, ii, ww, dec, **kw)
@@ -153,7 +161,8 @@ def test_ep_ragged_world1_is_bit_identical_to_moe_ragged(sx, T):
 
 
 @pytest.mark.parametrize("T", [1, 6, 20])
-def test_ep_folded_world1_equals_unfused(sx, T):
+@pytest.mark.parametrize("transport", TRANSPORTS)
+def test_ep_folded_world1_equals_unfused(sx, transport, T):
     """sx_ep_moe_folded over a world of one: the shared expert, run on the side stream over the
     rank's rows, gives the bits of the unfused composition (its own layer output passed as
     `shared` to sx_ep_moe), gated and ungated; the caller's stream sees the result."""
@@ -168,7 +177,7 @@ def test_ep_folded_world1_equals_unfused(sx, T):
     gate = torch.randn((T,), device="cuda").to(torch.bfloat16)
     one_i = torch.zeros((T, 1), dtype=torch.int32, device="cuda")
     one_s = torch.ones((T, 1), device="cuda")
-    ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0)
+    ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0, transport)
     try:
         for g in (None, gate):
             sh = sx.moe(xt, shb, one_i, one_s, dec)
@@ -181,8 +190,101 @@ def test_ep_folded_world1_equals_unfused(sx, T):
         ep.destroy()
 
 
+def test_ep_peer_world1_tensor_core_path_matches_nccl(sx):
+    """200 tokens on 16 experts take the tensor-core path; 256 places per rank leave 56 unused ones
+    that the peer transport's routing skips: the peer and NCCL transports give the same bits, and
+    both match sx_moe to its last bit."""
+    E, D, I, k, T = 16, 256, 128, 4, 200
+    bank_np = _bank_np(500, E, D, I, 32)
+    _, dec = dec_args(orc.CB_MCG, 16)
+    b = _bank(sx, bank_np)
+    xt = torch.from_numpy(synth.activations(501, T, D)).cuda().to(torch.bfloat16)
+    inds, wts = _route(502, T, E, k)
+    ii, ww = torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda()
+    gate = torch.randn((T,), device="cuda").to(torch.bfloat16)
+    shb = _bank(sx, _bank_np(503, 1, D, I, 32))
+    outs = {}
+    for transport in TRANSPORTS:
+        ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0, transport)
+        try:
+            outs[transport] = ep.moe(xt, b, E, ii, ww, dec, rows_cap=256, shared_gate=gate, shared_bank=shb)
+            torch.cuda.synchronize()
+        finally:
+            ep.destroy()
+    assert torch.equal(outs["peer"], outs["nccl"])
+    want = to_f32(sx.moe_folded(xt, b, shb, ii, ww, dec, shared_gate=gate))
+    got = to_f32(outs["peer"])
+    assert np.abs(got - want).max() <= 2 ** -7 * np.abs(want).max()
+    assert sx.device_error() == 0
+
+
+def test_ep_peer_world1_graph_replays(sx):
+    """The peer transport recorded in a CUDA graph after a warm call: every replay (each a new call
+    of the communicator, its flags raised anew) gives sx_moe's bits for the inputs of that replay."""
+    E, D, I, k, T = 16, 256, 128, 4, 8
+    bank_np = _bank_np(600, E, D, I, 32)
+    _, dec = dec_args(orc.CB_MCG, 16)
+    b = _bank(sx, bank_np)
+    inds, wts = _route(601, T, E, k)
+    ii, ww = torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda()
+    x = torch.zeros((T, D), device="cuda", dtype=torch.bfloat16)
+    ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0, "peer")
+    stream = torch.cuda.Stream()
+    try:
+        with torch.cuda.stream(stream):
+            ep.moe(x, b, E, ii, ww, dec, rows_cap=T)  # reserves the peer buffer, warms the kernels
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                y = ep.moe(x, b, E, ii, ww, dec, rows_cap=T)
+            for rep in range(3):
+                x.copy_(torch.from_numpy(synth.activations(610 + rep, T, D)).cuda().to(torch.bfloat16))
+                g.replay()
+                want = sx.moe(x, b, ii, ww, dec)
+                torch.cuda.synchronize()
+                assert torch.equal(y, want), rep
+            del g
+        assert sx.device_error() == 0
+    finally:
+        torch.cuda.synchronize()
+        ep.destroy()
+
+
+def test_ep_peer_reservation_grows_and_releases(sx):
+    """A call larger than the reservation grows it (a collective step of the communicator); a
+    reservation of 0 returns the communicator to the NCCL transport; results stay sx_moe's."""
+    from sushi_b200 import _lib
+
+    E, D, I, k = 8, 256, 128, 3
+    bank_np = _bank_np(700, E, D, I, 32)
+    _, dec = dec_args(orc.CB_MCG, 16)
+    b = _bank(sx, bank_np)
+    ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0, "peer")
+    L = _lib.load()
+    try:
+        sizes = []
+        for T in (2, 40):
+            xt = torch.from_numpy(synth.activations(701 + T, T, D)).cuda().to(torch.bfloat16)
+            inds, wts = _route(702 + T, T, E, k)
+            ii, ww = torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda()
+            got = ep.moe(xt, b, E, ii, ww, dec, rows_cap=T)
+            assert torch.equal(got, sx.moe(xt, b, ii, ww, dec)), T
+            sizes.append(ep.peer_reserved())
+        assert 0 < sizes[0] <= sizes[1]
+        assert L.sx_ep_peer_bytes(ep._h, 40, D, k, 2) <= sizes[1]
+        assert L.sx_ep_reserve_peer(ep._h, 0) == 0
+        assert ep.peer_reserved() == 0
+        ep.transport = "nccl"
+        got = ep.moe(xt, b, E, ii, ww, dec, rows_cap=T)
+        assert torch.equal(got, sx.moe(xt, b, ii, ww, dec))
+        assert sx.device_error() == 0
+    finally:
+        torch.cuda.synchronize()
+        ep.destroy()
+
+
 # ------------------------------------------------------------------ two GPUs
-def _rank_main(rank, world, port, out_dir):
+def _rank_main(rank, world, port, out_dir, transport):
     import torch.distributed as dist
 
     import sushi_b200 as sx
@@ -200,7 +302,7 @@ def _rank_main(rank, world, port, out_dir):
         xt = torch.from_numpy(synth.activations(50 + rank, T, D)).cuda().to(torch.bfloat16)
         inds, wts = _route(60 + rank, T, E, k)
         ii, ww = torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda()
-        ep = sx.ExpertParallel.from_process_group()
+        ep = sx.ExpertParallel.from_process_group(transport=transport)
         got = to_f32(ep.moe(xt, local, E, ii, ww, dec, rows_cap=16))
         torch.cuda.synchronize()
         ep.destroy()
@@ -215,7 +317,8 @@ def _rank_main(rank, world, port, out_dir):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_ep_two_gpus_match_single_gpu(tmp_path):
+@pytest.mark.parametrize("transport", TRANSPORTS)
+def test_ep_two_gpus_match_single_gpu(tmp_path, transport):
     import socket
 
     import torch.multiprocessing as mp
@@ -223,7 +326,7 @@ def test_ep_two_gpus_match_single_gpu(tmp_path):
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    mp.start_processes(_rank_main, args=(2, port, str(tmp_path)), nprocs=2, start_method="spawn", join=True)
+    mp.start_processes(_rank_main, args=(2, port, str(tmp_path), transport), nprocs=2, start_method="spawn", join=True)
     E, D, I = 16, 256, 128
     bank_np = _bank_np(123, E, D, I, 32)
     oargs, _ = dec_args(orc.CB_MCG, 16)
@@ -245,7 +348,7 @@ def test_ep_two_gpus_match_single_gpu(tmp_path):
         assert rel_rms(got, truth) <= REL_RMS_TOL
 
 
-def _ragged_rank_main(rank, world, port, out_dir):
+def _ragged_rank_main(rank, world, port, out_dir, transport):
     import torch.distributed as dist
 
     import sushi_b200 as sx
@@ -263,7 +366,7 @@ def _ragged_rank_main(rank, world, port, out_dir):
         xt = torch.from_numpy(synth.activations(80 + rank, T, D)).cuda().to(torch.bfloat16)
         inds, wts = _route(90 + rank, T, 16, k)
         ii, ww = torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda()
-        ep = sx.ExpertParallel.from_process_group()
+        ep = sx.ExpertParallel.from_process_group(transport=transport)
         got = to_f32(ep.moe(xt, local, 16, ii, ww, dec, rows_cap=16))
         torch.cuda.synchronize()
         ep.destroy()
@@ -275,7 +378,8 @@ def _ragged_rank_main(rank, world, port, out_dir):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_ep_ragged_two_gpus_match_single_gpu(tmp_path):
+@pytest.mark.parametrize("transport", TRANSPORTS)
+def test_ep_ragged_two_gpus_match_single_gpu(tmp_path, transport):
     """A rate-grouped layer split over two GPUs whose local layers differ (rank 0 holds K1 and K2
     experts, rank 1 only K2): each rank's rows match sx_moe_ragged over the full layer to the last
     bf16 bit (rank-order versus k-order sums)."""
@@ -286,7 +390,7 @@ def test_ep_ragged_two_gpus_match_single_gpu(tmp_path):
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    mp.start_processes(_ragged_rank_main, args=(2, port, str(tmp_path)), nprocs=2, start_method="spawn", join=True)
+    mp.start_processes(_ragged_rank_main, args=(2, port, str(tmp_path), transport), nprocs=2, start_method="spawn", join=True)
     for rank in range(2):
         got = np.load(tmp_path / f"got{rank}.npy")
         want = np.load(tmp_path / f"want{rank}.npy")
