@@ -422,6 +422,8 @@ def main():
     if not args.no_moe:
         out["moe"] = moe_bench(sx, _lib, torch, args, stream, sptr, hbm_peak)
         out["moe_prefill"] = prefill_bench(sx, torch, args, stream, tf_peak)
+        if world > 1:
+            out["moe_ep"] = ep_efficiency(sx, _lib, torch, args, stream, sptr, hbm_peak, tf_peak, out)
         out["ffn_stack_deepseek"] = deepseek_bench(sx, torch, args, stream, tf_peak)
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -543,6 +545,30 @@ def ep_parity(sx, torch):
             "case": "64 experts 512/256 K2 top-6 + gated shared expert; 1, 5, 37 tokens per rank"}
 
 
+def ep_efficiency(sx, _lib, torch, args, stream, sptr, hbm_peak, tf_peak, out):
+    """The expert-parallel layer's scaling at N > 1, measured in this run: every rank also runs the
+    one-GPU layer over the whole 512-expert bank (a replica, the same kernels as the N = 1 bench),
+    and eff(N) = tokens/s at N / (N x tokens/s of one GPU), weak (T tokens per rank against T on
+    one GPU) and at an equal total (64 decode tokens split over the ranks; 8192 prefill tokens split
+    over the ranks, measured here against 8192 on one GPU)."""
+    world, _, _ = dist_env()
+    one = moe_bench(sx, _lib, torch, args, stream, sptr, hbm_peak, single=True)
+    pre1 = prefill_bench(sx, torch, args, stream, tf_peak, single=True)
+    strong = prefill_bench(sx, torch, args, stream, tf_peak, T=8192 // world)
+    ep, ep_pre = out["moe"], out["moe_prefill"]
+    res = {"ranks": world, "one_gpu": {f"T{T}_tokens_per_s": one[f"T{T}"]["tokens_per_s"] for T in (1, 8, 64)}}
+    res["one_gpu"]["prefill_8192_tokens_per_s"] = pre1["tokens_per_s"]
+    res["decode_weak_eff"] = {f"T{T}": round(ep[f"T{T}"]["tokens_per_s"] / (world * one[f"T{T}"]["tokens_per_s"]), 4)
+                              for T in (1, 8, 64)}
+    t_eq = 64 // world
+    res["decode_equal_total_64_eff"] = round(ep[f"T{t_eq}"]["tokens_per_s"] / (world * one["T64"]["tokens_per_s"]), 4)
+    res["prefill_weak_eff"] = round(ep_pre["tokens_per_s"] / (world * pre1["tokens_per_s"]), 4)
+    res["prefill_equal_total_8192"] = {"tokens_per_rank": strong["tokens_per_rank"],
+                                       "tokens_per_s": strong["tokens_per_s"], "ms_per_layer": strong["ms_per_layer"],
+                                       "eff": round(strong["tokens_per_s"] / (world * pre1["tokens_per_s"]), 4)}
+    return res
+
+
 def qwen_shared(sx, torch, gen, D, I):
     """The configs[2] layer's shared expert (one SwiGLU expert of intermediate I, K2 n32, replicated
     on every rank) and its bf16 gate vector [D, 1]: the layer adds sigmoid(x . wg) * shared(x)
@@ -557,7 +583,7 @@ def qwen_shared(sx, torch, gen, D, I):
     return sx.Bank(*parts), wg
 
 
-def moe_bench(sx, _lib, torch, args, stream, sptr, hbm_peak):
+def moe_bench(sx, _lib, torch, args, stream, sptr, hbm_peak, single=False):
     """hidden 2048, 512 experts of 512, top-10, K2 (n32) MCG random banks,
     softmax router over fp32 logits from a bf16 2048x512 matrix, one sigmoid-gated shared expert of
     512; tokens/s of router + shared expert + routed experts for T tokens per rank.  One GPU: sx_moe over the whole bank.  N GPUs: expert parallel
@@ -567,6 +593,8 @@ def moe_bench(sx, _lib, torch, args, stream, sptr, hbm_peak):
     import torch.distributed as dist
 
     world, rank, _ = dist_env()
+    if single:  # every rank its own one-GPU layer over the whole bank: the efficiency reference
+        world, rank = 1, 0
     E, D, I, k = 512, 2048, 512, 10
     El = E // world
     bank_bytes = El * 3 * (D * I * 32 // 128 + 2 * (D + I))
@@ -593,6 +621,7 @@ def moe_bench(sx, _lib, torch, args, stream, sptr, hbm_peak):
     # T tokens per rank; at N > 1 also 64 / N per rank: the 64-token step split over the ranks
     # (equal total tokens per step: the strong-scaling point of the expert-parallel layer)
     Ts = [1, 8, 64] + ([64 // world] if world > 1 and 64 // world not in (1, 8, 64) else [])
+    real_world = dist_env()[0]
     for T in Ts:
         x = torch.randn((T, D), device="cuda", generator=gen).to(torch.bfloat16)
 
@@ -619,7 +648,7 @@ def moe_bench(sx, _lib, torch, args, stream, sptr, hbm_peak):
                 layer(i)
         g.replay()
         torch.cuda.synchronize()
-        if world > 1:
+        if real_world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -630,7 +659,7 @@ def moe_bench(sx, _lib, torch, args, stream, sptr, hbm_peak):
         e1.record(stream)
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / (rounds * reps)
-        if world > 1:
+        if real_world > 1:  # the slowest rank (with `single`, the slowest replica)
             tt = torch.tensor([ms], device="cuda")
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             ms = float(tt.item())
@@ -664,7 +693,7 @@ def moe_bench(sx, _lib, torch, args, stream, sptr, hbm_peak):
     return res
 
 
-def prefill_bench(sx, torch, args, stream, tf_peak):
+def prefill_bench(sx, torch, args, stream, tf_peak, T=8192, single=False):
     """the configs[2] layer in prefill, 8192 tokens of bf16 N(0,1) hidden
     states per rank, routing skewed by a Zipf(1.1) bias log(r_e^-1.1 / sum) over a seeded rank
     permutation added to the logits; router + gated shared expert + routed experts through the
@@ -676,7 +705,10 @@ def prefill_bench(sx, torch, args, stream, tf_peak):
     import torch.distributed as dist
 
     world, rank, _ = dist_env()
-    E, D, I, k, T = 512, 2048, 512, 10, 8192
+    real_world = world
+    if single:  # every rank its own one-GPU layer over the whole bank: the efficiency reference
+        world, rank = 1, 0
+    E, D, I, k = 512, 2048, 512, 10
     El = E // world
     gen = torch.Generator(device="cuda")
     gen.manual_seed(77 + rank)
@@ -716,7 +748,7 @@ def prefill_bench(sx, torch, args, stream, tf_peak):
     for _ in range(max(3, args.warmup)):
         layer()
     torch.cuda.synchronize()
-    if world > 1:
+    if real_world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -727,7 +759,7 @@ def prefill_bench(sx, torch, args, stream, tf_peak):
     e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
-    if world > 1:
+    if real_world > 1:
         tt = torch.tensor([ms], device="cuda")
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms = float(tt.item())
