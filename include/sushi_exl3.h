@@ -399,8 +399,11 @@ sx_status sx_ep_moe_ragged_folded(sx_ep* ep, sx_stream stream, const sx_ragged* 
  * straight into the owning rank's buffer and raises a flag there, the owner's expert chain runs
  * over the rows it received (only those), its reduce kernel stores each row's f32 partial straight
  * into the token owner's buffer and raises a flag, and the owner's combine waits for the flags and
- * adds the partials in rank order.  Only routed rows cross NVLink (no fixed-size blocks), nothing
- * waits on the host, and the calls can be recorded in a CUDA graph after the reservation.  Every
+ * adds the partials in rank order.  Only routed rows cross NVLink (no fixed-size blocks).  Calls
+ * with rows_cap < 1024 (decode sizes) never wait on the host and can be recorded in a CUDA graph
+ * after the reservation.  Calls with rows_cap >= 1024 (prefill sizes) read the received row and
+ * slot counts back to the host once, after the dispatch, and size the local expert chain's
+ * launches to them: those calls synchronise the host with the stream and cannot be recorded.  Every
  * wait is bounded (~2 s); a wait that gives up latches SX_ERR_DEVICE_TIMEOUT's device code
  * (sx_device_error) and the call's outputs are then undefined.  Results equal the NCCL transport's
  * bit for bit.  Requires every rank on one node with peer access (NVLink / NVSwitch).  No
@@ -418,6 +421,19 @@ sx_status sx_ep_reserve_peer(sx_ep* ep, size_t bytes);
 
 /* The reserved peer-buffer bytes (0: the NCCL transport). */
 size_t sx_ep_peer_reserved(const sx_ep* ep);
+
+/* Phase timing of the communicator's calls (diagnostics; not for calls recorded in a CUDA graph):
+ * with `enable`, every sx_ep_moe* call records CUDA events on its stream at its phase boundaries,
+ * and sx_ep_phase_ms gives the last call's six phase durations in ms (waiting for its end):
+ *   [0] plan + dispatch (peer: the row stores; NCCL: the send blocks' gather)
+ *   [1] peer: waiting for every rank's rows; NCCL: the dispatch all-to-all
+ *   [2] the local experts over the received rows
+ *   [3] peer: the partials' reduce and stores into the owners' buffers; NCCL: the combine all-to-all
+ *   [4] waiting for the shared expert on the side stream
+ *   [5] the combine (peer: including the wait for every rank's partials)
+ * Calls that run past a host-sized read of the received counts include that read in [1]. */
+sx_status sx_ep_phase_timing(sx_ep* ep, int32_t enable);
+sx_status sx_ep_phase_ms(sx_ep* ep, float ms[6]);
 
 /* The communicator's world size and rank (either pointer may be null). */
 sx_status sx_ep_info(const sx_ep* ep, int32_t* world, int32_t* rank);

@@ -83,6 +83,8 @@ SIGNATURES = {
     "sx_ep_peer_bytes": (_SZ, [_P, _I, _I, _I, _I]),
     "sx_ep_reserve_peer": (_I, [_P, _SZ]),
     "sx_ep_peer_reserved": (_SZ, [_P]),
+    "sx_ep_phase_timing": (_I, [_P, _I]),
+    "sx_ep_phase_ms": (_I, [_P, _P]),
     "sx_ep_workspace_bytes": (_SZ, [_P, ctypes.POINTER(SxBank), _I, _I, _I]),
     "sx_ep_moe": (_I, [_P, _P, ctypes.POINTER(SxBank), _I, ctypes.POINTER(SxDecode), _P, _I, _I, _I, _P, _P, _I, _P,
                        _P, _I, _P, _P, _SZ]),

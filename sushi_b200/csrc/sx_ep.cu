@@ -28,6 +28,7 @@
 
 // Peer transport limits: ranks a communicator can map (the flag arrays hold this many words).
 constexpr int kPeerMax = 128;
+constexpr int kEpPhases = 6;  // sx_ep_phase_ms
 
 // side: a stream of the communicator's own on which a layer's shared expert runs while the
 // dispatch, the local experts and the combine's exchange run on the caller's stream (fork and
@@ -41,6 +42,9 @@ struct sx_ep {
     uint8_t* own;
     size_t own_bytes;
     uint8_t* peer[kPeerMax];
+    uint32_t* host_counts;  // pinned: the received rows and slots of a host-sized call
+    cudaEvent_t phase[kEpPhases + 1];  // sx_ep_phase_timing: the last call's phase boundaries
+    bool timing;
 };
 
 namespace sx {
@@ -221,9 +225,14 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(CombineArgs a) {
 //   disp_flag[g]         the last call whose rows rank g has stored here
 //   comb_flag[g]         the last call whose partials rank g has stored here
 //   recv_cnt[g]          rows rank g stored here in that call
+//   recv_slots[g]        the slots of those rows on this rank's experts
 //   disp_done[g], red_done  this rank's own CTA counters (last CTA signals), reset by that CTA
 constexpr int kCtrlSeq = 0, kCtrlDispFlag = kPeerMax, kCtrlCombFlag = 2 * kPeerMax, kCtrlRecvCnt = 3 * kPeerMax,
-              kCtrlDispDone = 4 * kPeerMax, kCtrlRedDone = 5 * kPeerMax;
+              kCtrlRecvSlots = 4 * kPeerMax, kCtrlDispDone = 5 * kPeerMax, kCtrlRedDone = 6 * kPeerMax;
+// From this many rows per rank a call reads the received counts back to the host (one host
+// synchronisation) and sizes the expert chain's launches to the rows and slots it received; below
+// it the launches are sized for every place and the call never waits on the host.
+constexpr int kHostSizedRows = 1024;
 constexpr size_t kCtrlBytes = 16384;
 
 struct PeerLayout {
@@ -295,18 +304,24 @@ __device__ __forceinline__ bool last_to_arrive(uint32_t* counter, uint32_t total
 
 // Plan for the peer transport: ep_plan_kernel's lists and places, plus the per-destination counts
 // and (block 0) the start of a new call in this rank's control block.
+// cnt[d]: rows for destination d; cnt[world + d]: their slots on d's experts.
 __global__ void __launch_bounds__(256) ep_peer_plan_kernel(EpArgs a, int* cnt, uint32_t* own_ctrl) {
     __shared__ int warp_sums[8];
+    __shared__ int slot_sum;
     const int d = blockIdx.x;
     if (d == 0 && threadIdx.x == 0) own_ctrl[kCtrlSeq] += 1u;
-    int base = 0;
+    if (threadIdx.x == 0) slot_sum = 0;
+    int base = 0, slots = 0;
     for (int r0 = 0; r0 < a.rows; r0 += 256) {
         const int r = r0 + threadIdx.x;
         int flag = 0;
         if (r < a.rows) {
             for (int k = 0; k < a.K; k++) {
                 const uint32_t e = a.inds[(size_t)r * a.K + k];
-                if (e < (uint32_t)a.Etot && (int)(e / (uint32_t)a.El) == d) flag = 1;
+                if (e < (uint32_t)a.Etot && (int)(e / (uint32_t)a.El) == d) {
+                    flag = 1;
+                    slots++;
+                }
             }
         }
         int total;
@@ -317,7 +332,12 @@ __global__ void __launch_bounds__(256) ep_peer_plan_kernel(EpArgs a, int* cnt, u
         }
         base += total;
     }
-    if (threadIdx.x == 0) cnt[d] = base;
+    if (slots) atomicAdd(&slot_sum, slots);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        cnt[d] = base;
+        cnt[a.world + d] = slot_sum;
+    }
 }
 
 // Dispatch (grid: B x G blocks): destination d = blockIdx.y; places i = blockIdx.x, +B, ... below
@@ -348,6 +368,7 @@ __global__ void __launch_bounds__(256) ep_peer_dispatch_kernel(EpArgs a, const i
     __syncthreads();
     if (threadIdx.x == 0 && last_to_arrive(&ctrl(p.base[p.me])[kCtrlDispDone + d], gridDim.x)) {
         st_relaxed_sys(&ctrl(dst)[kCtrlRecvCnt + p.me], (uint32_t)n);
+        st_relaxed_sys(&ctrl(dst)[kCtrlRecvSlots + p.me], (uint32_t)cnt[a.world + d]);
         __threadfence_system();
         st_release_sys(&ctrl(dst)[kCtrlDispFlag + p.me], seq);
     }
@@ -459,7 +480,7 @@ EpWs ep_ws_layout(const MoeGroup* g, int ng, int El, int world, int cap, int K, 
     size_t off = 0;
     w.list = off; off = up(off + places * sizeof(int));
     w.pos = off; off = up(off + places * sizeof(int));
-    w.cnt = off; off = up(off + (size_t)world * sizeof(int));
+    w.cnt = off; off = up(off + (size_t)2 * world * sizeof(int));
     w.send_x = off; off = up(off + xfer * D * esz);
     w.send_inds = off; off = up(off + xfer * K * sizeof(uint32_t));
     w.send_scores = off; off = up(off + xfer * K * sizeof(float));
@@ -471,6 +492,9 @@ EpWs ep_ws_layout(const MoeGroup* g, int ng, int El, int world, int cap, int K, 
     // a rank receives about rows_cap * K valid slots (every rank's rows_cap rows, K slots each,
     // spread over the world): that, not the places' sentinel-padded slots, picks its expert path
     w.moe_bytes = moe_groups_ws(g, ng, El, (int32_t)places, K, (long long)cap * K);
+    // a large call sizes its chain to the slots it received, which may pick the tensor-core path
+    if (cap >= kHostSizedRows)
+        w.moe_bytes = std::max(w.moe_bytes, moe_groups_ws(g, ng, El, (int32_t)places, K, (long long)places * K));
     w.moe = off; off = up(off + w.moe_bytes);
     w.sh_plane = w.sh_scratch = off;
     if (sh) {
@@ -539,8 +563,10 @@ void release_peer(sx_ep* ep) {
         ep->peer[g] = nullptr;
     }
     if (ep->own) cudaFree(ep->own);
+    if (ep->host_counts) cudaFreeHost(ep->host_counts);
     ep->own = nullptr;
     ep->own_bytes = 0;
+    ep->host_counts = nullptr;
 }
 
 // Every rank's `bytes`-byte block of `mine` gathered into `all` [world][bytes] on the host, over the
@@ -576,6 +602,32 @@ size_t sx_ep_peer_bytes(const sx_ep* ep, int32_t rows_cap, int32_t hidden, int32
 
 size_t sx_ep_peer_reserved(const sx_ep* ep) { return ep ? ep->own_bytes : 0; }
 
+sx_status sx_ep_phase_timing(sx_ep* ep, int32_t enable) {
+    if (!ep) return SX_ERR_NULL_POINTER;
+    if (enable && !ep->timing) {
+        for (int i = 0; i <= kEpPhases; i++) {
+            const cudaError_t ce = cudaEventCreate(&ep->phase[i]);
+            if (ce != cudaSuccess) {
+                for (int j = 0; j < i; j++) cudaEventDestroy(ep->phase[j]);
+                return cuda_status(ce, "phase timing events");
+            }
+        }
+        ep->timing = true;
+    } else if (!enable && ep->timing) {
+        for (int i = 0; i <= kEpPhases; i++) cudaEventDestroy(ep->phase[i]);
+        ep->timing = false;
+    }
+    return SX_OK;
+}
+
+sx_status sx_ep_phase_ms(sx_ep* ep, float ms[6]) {
+    if (!ep || !ms) return SX_ERR_NULL_POINTER;
+    if (!ep->timing) return SX_ERR_BAD_SHAPE;
+    cudaError_t ce = cudaEventSynchronize(ep->phase[kEpPhases]);
+    for (int i = 0; ce == cudaSuccess && i < kEpPhases; i++) ce = cudaEventElapsedTime(&ms[i], ep->phase[i], ep->phase[i + 1]);
+    return ce == cudaSuccess ? SX_OK : cuda_status(ce, "phase timing");
+}
+
 sx_status sx_ep_reserve_peer(sx_ep* ep, size_t bytes) {
     if (!ep) return SX_ERR_NULL_POINTER;
     if (ep->world > kPeerMax) return SX_ERR_BAD_SHAPE;
@@ -599,7 +651,8 @@ sx_status sx_ep_reserve_peer(sx_ep* ep, size_t bytes) {
     uint8_t* own = nullptr;
     int32_t ok = 1;
     cudaIpcMemHandle_t h{};
-    if ((ce = cudaMalloc(&own, size)) != cudaSuccess || (ce = cudaMemset(own, 0, size)) != cudaSuccess ||
+    if ((ce = cudaMallocHost(&ep->host_counts, 2 * kPeerMax * sizeof(uint32_t))) != cudaSuccess ||
+        (ce = cudaMalloc(&own, size)) != cudaSuccess || (ce = cudaMemset(own, 0, size)) != cudaSuccess ||
         (ce = cudaDeviceSynchronize()) != cudaSuccess || (ce = cudaIpcGetMemHandle(&h, own)) != cudaSuccess) {
         note_cuda_error(ce, "peer buffer");
         ok = 0;
@@ -702,6 +755,7 @@ sx_status sx_ep_destroy(sx_ep* ep) {
     if (!ep) return SX_ERR_NULL_POINTER;
     release_side(ep);
     release_peer(ep);
+    sx_ep_phase_timing(ep, 0);
     const sx_status st = nccl_status(nccl().comm_destroy(ep->comm), "ncclCommDestroy");
     delete ep;
     return st;
@@ -712,6 +766,7 @@ sx_status sx_ep_abort(sx_ep* ep) {
     const sx_status st = nccl_status(nccl().comm_abort(ep->comm), "ncclCommAbort");
     release_side(ep);
     release_peer(ep);
+    sx_ep_phase_timing(ep, 0);
     delete ep;
     return st;
 }
@@ -748,6 +803,11 @@ size_t sx_ep_ragged_workspace_bytes(const sx_ep* ep, const sx_ragged* local, int
 namespace sx {
 namespace {
 
+// Records phase boundary i of the call on `s` when phase timing is on.
+void mark(sx_ep* ep, int i, cudaStream_t s) {
+    if (ep->timing) cudaEventRecord(ep->phase[i], s);
+}
+
 // The peer transport's call after the admission checks and the shared-expert fork: plan,
 // dispatch into the owners' buffers, wait for every rank's rows, the local chain over the received
 // rows only, reduce + push of the partials into the token owners' buffers, join, combine.
@@ -767,30 +827,51 @@ sx_status ep_peer_moe(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int n
     uint8_t* own = ep->own;
     int* cnt = reinterpret_cast<int*>(ws + L.cnt);
 
+    mark(ep, 0, s);
     ep_peer_plan_kernel<<<G, 256, 0, s>>>(a, cnt, reinterpret_cast<uint32_t*>(own));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_status(e, "ep peer plan launch");
     const int B = std::max(1, std::min(C, std::max(4, 8 * sm_count() / G)));
     ep_peer_dispatch_kernel<<<dim3(B, G), 256, 0, s>>>(a, cnt, pa);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "ep peer dispatch launch");
+    mark(ep, 1, s);
     ep_peer_recv_wait_kernel<<<1, 128, 0, s>>>(pa, G);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "ep peer wait launch");
 
-    const MoeSegments seg{reinterpret_cast<const int*>(own) + kCtrlRecvCnt, C, G};
+    // Large calls: the received counts come back to the host, and the chain's launches are sized
+    // to them (the places' bound would launch mostly idle CTAs once rows_cap x world is large).
+    long long live_rows = (long long)places, live_slots = -1;
+    if (C >= kHostSizedRows) {
+        e = cudaMemcpyAsync(ep->host_counts, own + kCtrlRecvCnt * sizeof(uint32_t), 2 * kPeerMax * sizeof(uint32_t),
+                            cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return cuda_status(e, "ep peer received counts");
+        live_rows = live_slots = 0;
+        for (int g = 0; g < G; g++) {
+            live_rows += std::min<long long>(ep->host_counts[g], C);
+            live_slots += ep->host_counts[kPeerMax + g];
+        }
+        live_slots = std::min(live_slots, live_rows * topk);
+    }
+    mark(ep, 2, s);
+    const MoeSegments seg{reinterpret_cast<const int*>(own) + kCtrlRecvCnt, C, G, live_slots};
     const uint32_t* ids = reinterpret_cast<const uint32_t*>(own + PL.recv_ids);
     float* yslot = nullptr;
     sx_status st = moe_run(stream, groups, ng, El, dec, own + PL.recv_x, dtype, (int32_t)places, ids,
                            reinterpret_cast<const float*>(own + PL.recv_sc), topk, nullptr, nullptr, clamp_limit,
-                           nullptr, ws + L.moe, L.moe_bytes, nullptr, (long long)C * topk, nullptr, nullptr, &seg,
-                           &yslot);
+                           nullptr, ws + L.moe, L.moe_bytes, nullptr,
+                           live_slots >= 0 ? live_slots : (long long)C * topk, nullptr, nullptr, &seg, &yslot);
     if (st) return st;
+    mark(ep, 3, s);
     const ReducePushArgs rp{yslot, ids, G, C, topk, D, El};
-    const long long units = (long long)places * ((D + 511) / 512);
+    const long long units = std::max(1LL, live_rows) * ((D + 511) / 512);
     const int grid = (int)std::max(1LL, std::min(units, (long long)8 * sm_count()));
     ep_peer_reduce_push_kernel<<<grid, 128, 0, s>>>(rp, pa);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "ep peer reduce launch");
+    mark(ep, 4, s);
 
     if ((st = join(SX_OK))) return st;
+    mark(ep, 5, s);
     CombineArgs c{};
     c.pos = a.pos;
     c.sh_plane = sh_plane;
@@ -803,7 +884,9 @@ sx_status ep_peer_moe(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int n
     c.world = G;
     c.xdt = dtype;
     ep_peer_combine_kernel<<<std::max(rows, 1), 256, 0, s>>>(c, pa);
-    return cuda_status(cudaGetLastError(), "ep peer combine launch");
+    e = cudaGetLastError();
+    mark(ep, 6, s);
+    return cuda_status(e, "ep peer combine launch");
 }
 
 // sx_ep_moe over the local layer's rate groups (one group for a uniform bank) of El experts.
@@ -889,6 +972,7 @@ sx_status ep_moe_groups(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int
                                       shared, shared_gate, y, dtype, join));
 
     // 1-2. plan and gather this rank's send blocks
+    mark(ep, 0, s);
     ep_plan_kernel<<<G, 256, 0, s>>>(a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return join(cuda_status(e, "ep plan launch"));
@@ -900,7 +984,9 @@ sx_status ep_moe_groups(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int
     const A2A dispatch[3] = {{ws + L.send_x, ws + L.recv_x, (size_t)C * D * esz},
                              {ws + L.send_inds, ws + L.recv_inds, (size_t)C * topk * 4},
                              {ws + L.send_scores, ws + L.recv_scores, (size_t)C * topk * 4}};
+    mark(ep, 1, s);
     if ((st = all_to_all(ep, dispatch, 3, s))) return join(st);
+    mark(ep, 2, s);
 
     // 4. the local experts over every received row, partials in f32
     float* part_send = reinterpret_cast<float*>(ws + L.part_send);
@@ -910,12 +996,18 @@ sx_status ep_moe_groups(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int
     if (st) return join(st);
 
     // 5. combine: partials back to the rows' owners
+    mark(ep, 3, s);
     const A2A combine[1] = {{part_send, ws + L.part_recv, (size_t)C * D * sizeof(float)}};
     if ((st = all_to_all(ep, combine, 1, s))) return join(st);
+    mark(ep, 4, s);
 
     // 6. rank-order sum, rounding, shared expert
     if ((st = join(SX_OK))) return st;
-    if (rows == 0) return SX_OK;
+    mark(ep, 5, s);
+    if (rows == 0) {
+        mark(ep, 6, s);
+        return SX_OK;
+    }
     CombineArgs c{};
     c.part = reinterpret_cast<const float*>(ws + L.part_recv);
     c.pos = a.pos;
@@ -929,7 +1021,9 @@ sx_status ep_moe_groups(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int
     c.world = G;
     c.xdt = dtype;
     ep_combine_kernel<<<rows, 256, 0, s>>>(c);
-    return cuda_status(cudaGetLastError(), "ep combine launch");
+    const cudaError_t ce = cudaGetLastError();
+    mark(ep, 6, s);
+    return cuda_status(ce, "ep combine launch");
 }
 
 }  // namespace

@@ -43,10 +43,12 @@ struct MoeGroup {
 constexpr int kMaxGroups = 32;  // layout.max_groups (src/exl3/layout.zig:4)
 
 // An expert-parallel rank's received rows: `n` segments of `cap` places, segment g live in its
-// first cnt[g] places (device counts, read by route_prep after its dependency wait).
+// first cnt[g] places (device counts, read by route_prep after its dependency wait).  moe_groups_ws
+// must be asked for the worst case (every place live) whichever live_slots a call passes.
 struct MoeSegments {
     const int* cnt;
     int cap, n;
+    long long live_slots;  // the segments' routed slots when the host knows them (sizes the launches), else -1
 };
 
 // moe_impl over the rate groups of a layer of Etot experts (sx_moe_ragged's body).  seg: only

@@ -133,6 +133,8 @@ __global__ void __launch_bounds__(1024) route_prep_kernel(MoeArgs a) {
         a.meta[1] = carry.w;
         a.meta[2] = carry.x;
     }
+    if (a.rcount)  // the folded reduce's arrival counters of this call (after the dependency wait)
+        for (int i = tid; i < a.R * (a.D / 128); i += blockDim.x) a.rcount[i] = 0;
     __syncthreads();
     for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;  // reused as cursors
     __syncthreads();
@@ -159,7 +161,7 @@ size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 struct MoeWs {
     size_t meta, act_expert, act_start, act_count, work_act, work_chunk, work_act4, work_chunk4, order, sorted_e, hprep,
-        yslot, tg, tu, gf, uf, work_rec, work_slots, total;
+        yslot, tg, tu, gf, uf, work_rec, work_slots, rcount, total;
     int A_max, W_max, W4_max, chunk, big_min, big_chunk;
     bool gemm;
 };
@@ -181,10 +183,12 @@ bool use_gemm(int E, int R, int K, long long slots) {
 }
 
 // extra_rows: prepared-input rows past the routed slots (a shared expert's rows riding the chain).
+// bound: the routed slots known to be valid at most (-1: R*K); it sizes the work lists, the
+// sorted positions and the launches that run over them (not the per-slot planes, indexed by slot).
 MoeWs moe_ws_layout(int E, int R, int K, int D, int I, int n_gu, int n_d, long long slots = 0, bool with_yslot = true,
-                    int extra_rows = 0) {
+                    int extra_rows = 0, long long bound = -1) {
     MoeWs w;
-    const int RK = R * K;
+    const int RK = bound >= 0 ? (int)std::min<long long>(bound, (long long)R * K) : R * K;
     w.gemm = use_gemm(E, R, K, slots);
     const bool big = w.gemm && gemm_rt_rate(n_gu) && gemm_rt_rate(n_d);
     w.chunk = w.gemm ? kGemmRows : 8;
@@ -202,13 +206,14 @@ MoeWs moe_ws_layout(int E, int R, int K, int D, int I, int n_gu, int n_d, long l
     w.work_chunk = off; off = align_up(off + (size_t)w.W_max * sizeof(int));
     w.work_rec = off; off = align_up(off + (size_t)w.W_max * sizeof(int4));
     w.work_slots = off; off = align_up(off + (size_t)(w.gemm ? 1 : w.W_max * 8) * sizeof(int));
+    w.rcount = off; off = align_up(off + (size_t)(w.gemm ? 1 : R * ((D + 127) / 128)) * sizeof(int));
     w.work_act4 = off; off = align_up(off + (size_t)std::max(1, w.W4_max) * sizeof(int));
     w.work_chunk4 = off; off = align_up(off + (size_t)std::max(1, w.W4_max) * sizeof(int));
     w.order = off; off = align_up(off + (size_t)RK * sizeof(int));
     w.sorted_e = off; off = align_up(off + (size_t)RK * sizeof(int));
     w.hprep = off; off = align_up(off + (size_t)(RK + extra_rows) * I * sizeof(uint16_t));
     w.yslot = off;
-    if (with_yslot) off = align_up(off + (size_t)RK * D * sizeof(float));
+    if (with_yslot) off = align_up(off + (size_t)R * K * D * sizeof(float));
     w.tg = w.tu = w.gf = w.uf = 0;
     if (w.gemm) {
         w.tg = off; off = align_up(off + (size_t)RK * D * sizeof(uint16_t));
@@ -491,11 +496,12 @@ size_t moe_workspace_bytes(const sx_bank* bank, int32_t rows, int32_t topk, long
 sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_decode* dec, const void* x,
                     sx_dtype dtype, int32_t rows, const uint32_t* inds, const float* scores, int32_t topk,
                     int32_t clamp_limit, float* yslot, uint8_t* ws, long long slots, const sx_bank* fold = nullptr,
-                    const MoeSegments* seg = nullptr) {
+                    const MoeSegments* seg = nullptr, const MoeArgs* reduce = nullptr, bool* reduced = nullptr) {
     const int E = bank->gate.experts;
     const int D = bank->gate.in_features, I = bank->gate.out_features;
     sx_status st;
-    const MoeWs L = moe_ws_layout(E, rows, topk, D, I, bank->gate.n, bank->down.n, slots, false, fold ? rows : 0);
+    const MoeWs L = moe_ws_layout(E, rows, topk, D, I, bank->gate.n, bank->down.n, slots, false, fold ? rows : 0,
+                                  seg ? seg->live_slots : -1);
     MoeArgs a{};
     int kind_gu, kind_d;
     if ((st = resolve_decode(dec, bank->gate.n, &kind_gu, &a.dp_gu))) return st;
@@ -545,6 +551,16 @@ sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_de
         set_shared_ptrs(a, *fold);
     }
 
+    if (reduce && !L.gemm) {  // the layer's reduce rides moe_down (see MoeArgs::rcount)
+        a.rcount = reinterpret_cast<int*>(ws + L.rcount);
+        a.shared = reduce->shared;
+        a.shared_gate = reduce->shared_gate;
+        a.y = reduce->y;
+        a.sh_plane = reduce->sh_plane;
+        a.sh_slot0 = rows * topk;
+        if (reduced) *reduced = true;
+    }
+
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const size_t rp_smem = 3 * (size_t)E * sizeof(int);
     cudaError_t e = cudaSuccess;
@@ -563,7 +579,8 @@ sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_de
         a.tu = reinterpret_cast<uint16_t*>(ws + L.tu);
         a.gf = reinterpret_cast<float*>(ws + L.gf);
         a.uf = reinterpret_cast<float*>(ws + L.uf);
-        const int RK = rows * topk;
+        const int RK = seg && seg->live_slots >= 0 ? (int)std::min<long long>(seg->live_slots, (long long)rows * topk)
+                                                   : rows * topk;  // sorted positions at most
         const dim3 pos_grid((RK + 7) / 8, 1);
         moe_prep_kernel<<<dim3(pos_grid.x, D / 128), 256, 0, s>>>(a);
         if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "moe prep launch");
@@ -745,25 +762,6 @@ sx_status moe_run(sx_stream stream, const MoeGroup* groups, int ng, int Etot, co
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     float* yslot = reinterpret_cast<float*>(ws);
     uint8_t* scratch = ws + yslot_bytes(rows, topk, D) + (sh_bank ? yslot_bytes(rows, 1, D) : 0);
-    for (int i = 0; i < ng; i++) {
-        const sx_status st = moe_group(stream, &groups[i].bank, groups[i].e_lo, dec, x, dtype, rows, inds, scores, topk,
-                                       clamp_limit, yslot, scratch,
-                                       group_slots(slots, rows, topk, groups[i].bank.gate.experts, Etot),
-                                       plan.mode == 1 && plan.group == i ? sh_bank : nullptr, seg);
-        if (st) return st;
-    }
-    if (yslot_out) {  // the caller reduces the per-slot planes itself
-        *yslot_out = yslot;
-        return SX_OK;
-    }
-    if (plan.mode == 2) {
-        const sx_status st = shared_chain(stream, sh_bank, sh_dec, x, dtype, rows, topk, clamp_limit, yslot, scratch);
-        if (st) return st;
-    } else if (plan.mode == 3) {
-        const sx_status st = shared_expert_run(stream, sh_bank, sh_dec, x, dtype, rows, clamp_limit,
-                                               yslot + (size_t)rows * topk * D, scratch);
-        if (st) return st;
-    }
     MoeArgs r{};
     r.inds = inds;
     r.K = topk;
@@ -777,6 +775,32 @@ sx_status moe_run(sx_stream stream, const MoeGroup* groups, int ng, int Etot, co
     r.partial = partial;
     r.sh_plane = sh_bank != nullptr;
     r.sh_slot0 = rows * topk;
+    // One group whose every plane comes from its own decode-chain launches (no shared expert, or
+    // one folded into them): the reduce rides its moe_down.  (Which path the group takes is its
+    // own choice: moe_group says whether it folded.)
+    const bool may_fold = ng == 1 && !partial && !yslot_out && y && (plan.mode == 0 || plan.mode == 1);
+    bool folded = false;
+    for (int i = 0; i < ng; i++) {
+        const sx_status st = moe_group(stream, &groups[i].bank, groups[i].e_lo, dec, x, dtype, rows, inds, scores, topk,
+                                       clamp_limit, yslot, scratch,
+                                       group_slots(slots, rows, topk, groups[i].bank.gate.experts, Etot),
+                                       plan.mode == 1 && plan.group == i ? sh_bank : nullptr, seg,
+                                       may_fold ? &r : nullptr, &folded);
+        if (st) return st;
+    }
+    if (yslot_out) {  // the caller reduces the per-slot planes itself
+        *yslot_out = yslot;
+        return SX_OK;
+    }
+    if (folded) return SX_OK;
+    if (plan.mode == 2) {
+        const sx_status st = shared_chain(stream, sh_bank, sh_dec, x, dtype, rows, topk, clamp_limit, yslot, scratch);
+        if (st) return st;
+    } else if (plan.mode == 3) {
+        const sx_status st = shared_expert_run(stream, sh_bank, sh_dec, x, dtype, rows, clamp_limit,
+                                               yslot + (size_t)rows * topk * D, scratch);
+        if (st) return st;
+    }
     return cuda_status(launch_pdl(moe_reduce_kernel, dim3(rows, (D + kReduceCols - 1) / kReduceCols), dim3(128), 0,
                                   reinterpret_cast<cudaStream_t>(stream), r),
                        "moe reduce launch");

@@ -81,6 +81,11 @@ struct MoeArgs {
     // reads the counts after its dependency wait and skips every other place.
     const int* seg_cnt;
     int seg_cap, nseg;
+    // The reduce folded into moe_down (a one-group decode-chain layer, rounded output): rcount
+    // [R][D/128] arrival counters, zeroed by route_prep; the last of a (token, output block)'s
+    // planes to land (its live routed slots, plus the shared plane when sh_plane) makes that
+    // block of the token's output, as moe_reduce would.
+    int* rcount;
 };
 
 // A token's routed sum `acc` (f32) made into its output value: rounded to the output dtype, then
@@ -108,6 +113,34 @@ __device__ __forceinline__ float routed_finish(float acc, int xdt, bool has_sh, 
         y = y + sh;
     }
     return y;
+}
+
+// moe_reduce's arithmetic for four outputs d..d+3 of token r: the live slots' planes in k order,
+// rounded, plus the shared term (the shared plane rounded, or the caller's shared row), gated.
+// Plane reads bypass L1: other CTAs wrote them during this grid.
+__device__ __forceinline__ void reduce_outputs4(const MoeArgs& a, int r, int d) {
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int k = 0; k < a.K; k++) {
+        if (a.inds[r * a.K + k] >= (uint32_t)a.E) continue;
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(a.yslot + (size_t)(r * a.K + k) * a.D + d));
+        acc[0] += v.x;
+        acc[1] += v.y;
+        acc[2] += v.z;
+        acc[3] += v.w;
+    }
+    float sh[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (a.sh_plane) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(a.yslot + (size_t)(a.sh_slot0 + r) * a.D + d));
+        sh[0] = round_act(v.x, a.xdt), sh[1] = round_act(v.y, a.xdt), sh[2] = round_act(v.z, a.xdt);
+        sh[3] = round_act(v.w, a.xdt);
+    } else if (a.shared) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) sh[i] = load_act(a.shared, (size_t)r * a.D + d + i, a.xdt);
+    }
+    const bool has_sh = a.sh_plane || a.shared;
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+        store_act(a.y, (size_t)r * a.D + d + i, a.xdt, routed_finish(acc[i], a.xdt, has_sh, sh[i], a.shared_gate, r));
 }
 
 // Work item -> (expert, first sorted slot, rows of the chunk); shx: a chunk of the shared expert
@@ -301,6 +334,20 @@ __global__ void __launch_bounds__(kThreads, 3) moe_down_kernel(MoeArgs a) {
         float* dst = a.yslot + (size_t)slot * a.D + ob * 128 + lane * 4;
 #pragma unroll
         for (int i = 0; i < 4; i++) dst[i] = d[i] * h2f(dsv[ob * 128 + lane * 4 + i]) * sc;
+        if (a.rcount) {
+            // the folded reduce: the last plane of (token, output block) to land makes the block
+            const int r = it.shx ? it.first + m : slot / a.K;
+            __threadfence();
+            __syncwarp();
+            const bool live = lane < a.K && a.inds[r * a.K + lane] < (uint32_t)a.E;
+            const int need = __popc(__ballot_sync(0xffffffffu, live)) + (a.sh_plane ? 1 : 0);
+            int last = 0;
+            if (lane == 0) last = atomicAdd(&a.rcount[r * (a.D / 128) + ob], 1) == need - 1;
+            if (__shfl_sync(0xffffffffu, last, 0)) {
+                __threadfence();
+                reduce_outputs4(a, r, ob * 128 + lane * 4);
+            }
+        }
     }
     cluster.sync();
 }

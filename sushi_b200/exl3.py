@@ -568,6 +568,18 @@ class ExpertParallel:
     def peer_reserved(self) -> int:
         return int(lib().sx_ep_peer_reserved(self._h))
 
+    PHASES = ("plan_dispatch", "wait_rows", "local_experts", "reduce_push", "shared_join", "combine")
+
+    def phase_timing(self, enable: bool = True):
+        """sx_ep_phase_timing: CUDA events at each call's phase boundaries (not under graph capture)."""
+        _check(lib().sx_ep_phase_timing(self._h, 1 if enable else 0))
+
+    def phase_ms(self) -> dict:
+        """The last call's phase durations in ms (sx_ep_phase_ms; waits for the call's end)."""
+        out = (ctypes.c_float * 6)()
+        _check(lib().sx_ep_phase_ms(self._h, out))
+        return {name: float(v) for name, v in zip(self.PHASES, out)}
+
     @staticmethod
     def unique_id() -> bytes:
         buf = (ctypes.c_uint8 * 128)()

@@ -218,6 +218,33 @@ def test_ep_peer_world1_tensor_core_path_matches_nccl(sx):
     assert sx.device_error() == 0
 
 
+def test_ep_peer_world1_host_sized_call(sx):
+    """rows_cap >= 1024: the peer transport reads the received counts back and sizes the chain's
+    launches to them (the tensor-core path here); the bits equal the NCCL transport's and sx_moe's
+    to the last bit."""
+    E, D, I, k, T = 16, 256, 128, 4, 1100
+    bank_np = _bank_np(800, E, D, I, 32)
+    _, dec = dec_args(orc.CB_MCG, 16)
+    b = _bank(sx, bank_np)
+    xt = torch.from_numpy(synth.activations(801, T, D)).cuda().to(torch.bfloat16)
+    inds, wts = _route(802, T, E, k)
+    inds[7, 1] = E + 3  # a skipped id
+    ii, ww = torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda()
+    outs = {}
+    for transport in TRANSPORTS:
+        ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0, transport)
+        try:
+            outs[transport] = ep.moe(xt, b, E, ii, ww, dec, rows_cap=1200)
+            torch.cuda.synchronize()
+        finally:
+            ep.destroy()
+    assert torch.equal(outs["peer"], outs["nccl"])
+    want = to_f32(sx.moe(xt, b, ii, ww, dec))
+    got = to_f32(outs["peer"])
+    assert np.abs(got - want).max() <= 2 ** -7 * np.abs(want).max()
+    assert sx.device_error() == 0
+
+
 def test_ep_peer_world1_graph_replays(sx):
     """The peer transport recorded in a CUDA graph after a warm call: every replay (each a new call
     of the communicator, its flags raised anew) gives sx_moe's bits for the inputs of that replay."""
