@@ -813,7 +813,9 @@ def deepseek_bench(sx, torch, args, stream, tf_peak):
     [g*256/N, (g+1)*256/N) as its own rate groups, every rank running the stack on its own T tokens
     (weak scaling); router and shared expert replicated.  Decode batches T = 1, 8, 64 (CUDA graph of
     the 16 layers) and prefill T = 4096.  Random trellis words, sign-only scales (the decode cost
-    does not depend on the values); 39 GB of routed weights over the world."""
+    does not depend on the values); 39 GB of routed weights over the world.  Each layer takes the
+    RMS-normed residual stream as its input (torch's rms_norm, in the timed region), so the stack's
+    activations and routing stay those of a well-scaled model."""
     import torch.distributed as dist
 
     world, rank, _ = dist_env()
@@ -860,16 +862,19 @@ def deepseek_bench(sx, torch, args, stream, tf_peak):
         def stack():
             x = x0
             for rb, shared, wr, bias in layers:
-                inds, scores, _ = sx.router_topk_gate(x @ wr, k, mode=sx.RouterMode.SIGMOID_BIAS, bias=bias,
+                # the block's input norm (a model's post-attention RMSNorm): without it the residual
+                # stream of random-weight SwiGLU layers grows without bound and routes on inf/NaN
+                h = torch.nn.functional.rms_norm(x, (H,))
+                inds, scores, _ = sx.router_topk_gate(h @ wr, k, mode=sx.RouterMode.SIGMOID_BIAS, bias=bias,
                                                       route_norm=True, route_scale=2.5)
                 if ep is None:  # the K4 shared expert in the same call as the K1/K2 routed groups
-                    x = x + sx.moe_folded(x, rb, shared, inds, scores, dec, workspace=ws)
+                    x = x + sx.moe_folded(h, rb, shared, inds, scores, dec, workspace=ws)
                 else:  # the shared expert on the side stream while the rows are exchanged
-                    x = x + ep.moe(x, rb, E, inds, scores, dec, rows_cap=T, workspace=ws, shared_bank=shared)
+                    x = x + ep.moe(h, rb, E, inds, scores, dec, rows_cap=T, workspace=ws, shared_bank=shared)
             return x
 
-        for _ in range(2):
-            stack()
+        finite = bool(torch.isfinite(stack()).all())
+        stack()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -904,7 +909,7 @@ def deepseek_bench(sx, torch, args, stream, tf_peak):
             ms = float(tt.item())
         flops = world * 2.0 * T * L * (k + 1) * 3 * H * I
         res[f"T{T}"] = {"tokens_per_s": round(world * T / (ms * 1e-3), 1), "ms_per_stack": round(ms, 3),
-                        "tflops": round(flops / (ms * 1e-3) / 1e12, 1)}
+                        "tflops": round(flops / (ms * 1e-3) / 1e12, 1), "output_finite": finite}
         if ep is not None and T == 4096:  # the last layer's phases, one eager stack with events on
             ep.phase_timing(True)
             stack()

@@ -415,7 +415,7 @@ __global__ void __launch_bounds__(128) ep_peer_reduce_push_kernel(ReducePushArgs
         const int d = cb * 512 + threadIdx.x * 4;
         if (d >= a.D) continue;
         float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        for (int k = 0; k < a.K; k++) {
+        for (int k = 0; a.yslot && k < a.K; k++) {  // no planes: no expert ran (no slot reached this rank)
             if (a.ids[place * a.K + k] >= (uint32_t)a.El) continue;
             const float4 v = *reinterpret_cast<const float4*>(a.yslot + (place * a.K + k) * a.D + d);
             acc[0] += v.x;
@@ -857,10 +857,12 @@ sx_status ep_peer_moe(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int n
     const MoeSegments seg{reinterpret_cast<const int*>(own) + kCtrlRecvCnt, C, G, live_slots};
     const uint32_t* ids = reinterpret_cast<const uint32_t*>(own + PL.recv_ids);
     float* yslot = nullptr;
-    sx_status st = moe_run(stream, groups, ng, El, dec, own + PL.recv_x, dtype, (int32_t)places, ids,
-                           reinterpret_cast<const float*>(own + PL.recv_sc), topk, nullptr, nullptr, clamp_limit,
-                           nullptr, ws + L.moe, L.moe_bytes, nullptr,
-                           live_slots >= 0 ? live_slots : (long long)C * topk, nullptr, nullptr, &seg, &yslot);
+    sx_status st = SX_OK;
+    if (live_slots != 0)  // a rank no slot reached (skewed routing) has no experts to run
+        st = moe_run(stream, groups, ng, El, dec, own + PL.recv_x, dtype, (int32_t)places, ids,
+                     reinterpret_cast<const float*>(own + PL.recv_sc), topk, nullptr, nullptr, clamp_limit, nullptr,
+                     ws + L.moe, L.moe_bytes, nullptr, live_slots >= 0 ? live_slots : (long long)C * topk, nullptr,
+                     nullptr, &seg, &yslot);
     if (st) return st;
     mark(ep, 3, s);
     const ReducePushArgs rp{yslot, ids, G, C, topk, D, El};

@@ -581,7 +581,7 @@ sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_de
         a.uf = reinterpret_cast<float*>(ws + L.uf);
         const int RK = seg && seg->live_slots >= 0 ? (int)std::min<long long>(seg->live_slots, (long long)rows * topk)
                                                    : rows * topk;  // sorted positions at most
-        const dim3 pos_grid((RK + 7) / 8, 1);
+        const dim3 pos_grid(std::max(1, (RK + 7) / 8), 1);  // positions past meta[2] return
         moe_prep_kernel<<<dim3(pos_grid.x, D / 128), 256, 0, s>>>(a);
         if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "moe prep launch");
         CUtensorMap mg, mu, mh;

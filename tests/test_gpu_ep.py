@@ -245,6 +245,34 @@ def test_ep_peer_world1_host_sized_call(sx):
     assert sx.device_error() == 0
 
 
+@pytest.mark.parametrize("D,I", [(512, 256), (7168, 2048)])
+def test_ep_peer_world1_host_sized_ragged_with_shared(sx, D, I):
+    """A host-sized call (rows_cap >= 1024) over a rate-grouped layer (K1 and K2 SPEC1 groups, the
+    DeepSeek config's routed layout) with a K4 shared expert on the side stream: the peer and NCCL
+    transports give the same bits, and both match the one-GPU folded layer to its last bit."""
+    k, T = 8, 1100
+    groups = [(_bank_np(900 + D, 4, D, I, 16), 16), (_bank_np(910 + D, 12, D, I, 32), 32)]
+    _, dec = dec_args(orc.CB_SPEC1, 15)
+    rb = _ragged_slice(sx, groups, 0, 16)
+    shb = _bank(sx, _bank_np(920 + D, 1, D, I, 64))
+    xt = torch.from_numpy(synth.activations(921, T, D)).cuda().to(torch.bfloat16)
+    inds, wts = _route(922, T, 16, k)
+    ii, ww = torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda()
+    outs = {}
+    for transport in TRANSPORTS:
+        ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0, transport)
+        try:
+            outs[transport] = ep.moe(xt, rb, 16, ii, ww, dec, rows_cap=T, shared_bank=shb)
+            torch.cuda.synchronize()
+        finally:
+            ep.destroy()
+    assert torch.equal(outs["peer"], outs["nccl"])
+    want = to_f32(sx.moe_folded(xt, rb, shb, ii, ww, dec))
+    got = to_f32(outs["peer"])
+    assert np.abs(got - want).max() <= 2 ** -7 * np.abs(want).max()
+    assert sx.device_error() == 0
+
+
 def test_ep_peer_world1_graph_replays(sx):
     """The peer transport recorded in a CUDA graph after a warm call: every replay (each a new call
     of the communicator, its flags raised anew) gives sx_moe's bits for the inputs of that replay."""
