@@ -233,6 +233,11 @@ constexpr int kCtrlSeq = 0, kCtrlDispFlag = kPeerMax, kCtrlCombFlag = 2 * kPeerM
 // synchronisation) and sizes the expert chain's launches to the rows and slots it received; below
 // it the launches are sized for every place and the call never waits on the host.
 constexpr int kHostSizedRows = 1024;
+// Up to this many own rows (the decode chain's row limit) the peer transport runs the layer's
+// shared expert inside the local expert chain's launches (over the rank's own rows, its plane
+// after the routed slots') instead of on the side stream, whose concurrent launches would hold
+// the SMs the exchange's small kernels wait for.
+constexpr int kEpFoldRows = 16;
 constexpr size_t kCtrlBytes = 16384;
 
 struct PeerLayout {
@@ -492,6 +497,9 @@ EpWs ep_ws_layout(const MoeGroup* g, int ng, int El, int world, int cap, int K, 
     // a rank receives about rows_cap * K valid slots (every rank's rows_cap rows, K slots each,
     // spread over the world): that, not the places' sentinel-padded slots, picks its expert path
     w.moe_bytes = moe_groups_ws(g, ng, El, (int32_t)places, K, (long long)cap * K);
+    if (peer && sh && cap <= kEpFoldRows)
+        w.moe_bytes = std::max(w.moe_bytes, moe_groups_ws(g, ng, El, (int32_t)places, K, (long long)cap * K, sh,
+                                                          nullptr, nullptr, cap));
     // a large call sizes its chain to the slots it received, which may pick the tensor-core path
     if (cap >= kHostSizedRows)
         w.moe_bytes = std::max(w.moe_bytes, moe_groups_ws(g, ng, El, (int32_t)places, K, (long long)places * K));
@@ -812,11 +820,12 @@ void mark(sx_ep* ep, int i, cudaStream_t s) {
 // dispatch into the owners' buffers, wait for every rank's rows, the local chain over the received
 // rows only, reduce + push of the partials into the token owners' buffers, join, combine.
 // `join` joins the side stream into the caller's before the combine (which reads its plane).
-template <typename Join>
+template <typename Join, typename Fork>
 sx_status ep_peer_moe(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int ng, int El, const sx_decode* dec,
                       const EpArgs& a, const PeerLayout& PL, const EpWs& L, uint8_t* ws, int rows, int topk,
                       int clamp_limit, const float* sh_plane, const void* shared, const void* shared_gate, void* y,
-                      sx_dtype dtype, Join& join) {
+                      sx_dtype dtype, Join& join, const sx_bank* fold_bank, const sx_decode* fold_dec,
+                      Fork& fork_side) {
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const int G = ep->world, C = a.cap, D = a.D;
     const size_t places = (size_t)G * C;
@@ -834,6 +843,8 @@ sx_status ep_peer_moe(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int n
     const int B = std::max(1, std::min(C, std::max(4, 8 * sm_count() / G)));
     ep_peer_dispatch_kernel<<<dim3(B, G), 256, 0, s>>>(a, cnt, pa);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "ep peer dispatch launch");
+    sx_status st = fork_side();  // the shared expert on the side stream (large calls)
+    if (st) return st;
     mark(ep, 1, s);
     ep_peer_recv_wait_kernel<<<1, 128, 0, s>>>(pa, G);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "ep peer wait launch");
@@ -857,13 +868,16 @@ sx_status ep_peer_moe(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int n
     const MoeSegments seg{reinterpret_cast<const int*>(own) + kCtrlRecvCnt, C, G, live_slots};
     const uint32_t* ids = reinterpret_cast<const uint32_t*>(own + PL.recv_ids);
     float* yslot = nullptr;
-    sx_status st = SX_OK;
-    if (live_slots != 0)  // a rank no slot reached (skewed routing) has no experts to run
+    // the shared expert over this rank's own rows rides the local chain (fold_bank, small calls)
+    const SharedRows own_rows{a.x, rows};
+    const sx_bank* fb = fold_bank && rows > 0 ? fold_bank : nullptr;
+    if (live_slots != 0 || fb)  // a rank no slot reached (skewed routing) has no experts to run
         st = moe_run(stream, groups, ng, El, dec, own + PL.recv_x, dtype, (int32_t)places, ids,
                      reinterpret_cast<const float*>(own + PL.recv_sc), topk, nullptr, nullptr, clamp_limit, nullptr,
-                     ws + L.moe, L.moe_bytes, nullptr, live_slots >= 0 ? live_slots : (long long)C * topk, nullptr,
-                     nullptr, &seg, &yslot);
+                     ws + L.moe, L.moe_bytes, nullptr, live_slots >= 0 ? live_slots : (long long)C * topk, fb,
+                     fold_dec, &seg, &yslot, fb ? &own_rows : nullptr);
     if (st) return st;
+    if (fb) sh_plane = yslot + places * topk * D;
     mark(ep, 3, s);
     const ReducePushArgs rp{yslot, ids, G, C, topk, D, El};
     const long long units = std::max(1LL, live_rows) * ((D + 511) / 512);
@@ -928,23 +942,34 @@ sx_status ep_moe_groups(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int
 
     // 0. the shared expert over this rank's own rows, on the side stream: it needs only x, so it
     // runs while the rows are exchanged and the experts computed; the combine waits for it.
-    float* sh_plane = sh_bank && rows > 0 ? reinterpret_cast<float*>(ws + L.sh_plane) : nullptr;
-    if (sh_plane) {
+    // (the peer transport's small calls fold it into the local expert chain instead)
+    const bool fold_shared = peer && sh_bank && rows_cap <= kEpFoldRows;
+    float* sh_plane = sh_bank && rows > 0 && !fold_shared ? reinterpret_cast<float*>(ws + L.sh_plane) : nullptr;
+    // (the NCCL transport forks it first; the peer transport after its dispatch kernel, so the
+    // exchange's kernels are not queued behind the shared expert's)
+    bool forked = false;
+    auto fork_side = [&]() -> sx_status {
+        if (!sh_plane) return SX_OK;
+        forked = true;
         cudaError_t ce = cudaEventRecord(ep->fork, s);
         if (ce == cudaSuccess) ce = cudaStreamWaitEvent(ep->side, ep->fork, 0);
         if (ce != cudaSuccess) return cuda_status(ce, "expert-parallel fork");
         const sx_status st = shared_expert_run(reinterpret_cast<sx_stream>(ep->side), sh_bank, sh_dec, x, dtype, rows,
                                                clamp_limit, sh_plane, ws + L.sh_scratch);
         ce = cudaEventRecord(ep->join, ep->side);
-        if (st || ce != cudaSuccess) {
-            cudaStreamWaitEvent(s, ep->join, 0);
-            return st ? st : cuda_status(ce, "expert-parallel join");
+        return st ? st : (ce != cudaSuccess ? cuda_status(ce, "expert-parallel join") : SX_OK);
+    };
+    if (!peer) {
+        const sx_status st = fork_side();
+        if (st) {
+            if (forked) cudaStreamWaitEvent(s, ep->join, 0);
+            return st;
         }
     }
     // Every return below joins the side stream back into the caller's (the combine reads the plane).
-    bool joined = sh_plane == nullptr;
+    bool joined = false;
     auto join = [&](sx_status st) {
-        if (!joined) {
+        if (forked && !joined) {
             const cudaError_t ce = cudaStreamWaitEvent(s, ep->join, 0);
             joined = true;
             if (!st && ce != cudaSuccess) st = cuda_status(ce, "expert-parallel join");
@@ -970,8 +995,10 @@ sx_status ep_moe_groups(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int
     a.send_inds = reinterpret_cast<uint32_t*>(ws + L.send_inds);
     a.send_scores = reinterpret_cast<float*>(ws + L.send_scores);
 
-    if (peer) return join(ep_peer_moe(ep, stream, groups, ng, El, dec, a, PL, L, ws, rows, topk, clamp_limit, sh_plane,
-                                      shared, shared_gate, y, dtype, join));
+    if (peer)
+        return join(ep_peer_moe(ep, stream, groups, ng, El, dec, a, PL, L, ws, rows, topk, clamp_limit, sh_plane,
+                                shared, shared_gate, y, dtype, join, fold_shared ? sh_bank : nullptr, sh_dec,
+                                fork_side));
 
     // 1-2. plan and gather this rank's send blocks
     mark(ep, 0, s);

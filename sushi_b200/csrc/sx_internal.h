@@ -51,16 +51,28 @@ struct MoeSegments {
     long long live_slots;  // the segments' routed slots when the host knows them (sizes the launches), else -1
 };
 
+// The rows a layer's shared expert runs over when they are not the routed rows (an expert-parallel
+// rank routes the rows it received, and runs its shared expert over its own).
+struct SharedRows {
+    const void* x;
+    int rows;
+};
+
 // moe_impl over the rate groups of a layer of Etot experts (sx_moe_ragged's body).  seg: only
 // the segments' live places are routed.  yslot_out: no reduce is launched; the per-slot planes
 // (slot s at [s][D] f32, score included, written for the routed slots only) are left for the
-// caller at *yslot_out, the start of the workspace.
+// caller at *yslot_out, the start of the workspace, followed by the shared expert's plane (rows
+// sh_bank runs over, at slot rows*topk + row).  own: the shared expert's rows, if not x's.
 sx_status moe_run(sx_stream stream, const MoeGroup* groups, int ng, int Etot, const sx_decode* dec, const void* x,
                   sx_dtype dtype, int32_t rows, const uint32_t* inds, const float* scores, int32_t topk,
                   const void* shared, const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
                   size_t workspace_bytes, float* partial, long long slots, const sx_bank* sh_bank = nullptr,
-                  const sx_decode* sh_dec = nullptr, const MoeSegments* seg = nullptr, float** yslot_out = nullptr);
+                  const sx_decode* sh_dec = nullptr, const MoeSegments* seg = nullptr, float** yslot_out = nullptr,
+                  const SharedRows* own = nullptr);
 size_t moe_groups_ws(const MoeGroup* g, int ng, int Etot, int rows, int topk, long long slots);
+// With a shared expert over sh_rows rows (its plane follows the routed slots' planes).
+size_t moe_groups_ws(const MoeGroup* g, int ng, int Etot, int rows, int topk, long long slots, const sx_bank* sh,
+                     const sx_decode* dec, const sx_decode* sh_dec, int sh_rows);
 // A layer's shared expert (one SwiGLU expert over hidden size D): its admission, and its output
 // over `rows` rows alone into plane [rows][D] f32 with shared_expert_ws(sh, rows) bytes of scratch.
 sx_status check_shared_bank(const sx_bank* sh, int D, const sx_decode* dec);

@@ -440,19 +440,22 @@ struct SharedPlan {
     int group;
 };
 
+// sh_rows: the rows the shared expert runs over (the routed rows, or an expert-parallel rank's own
+// rows when the routed ones are the rows it received).  any_decode: as if the decodes matched (the
+// workspace query, which is asked without them).
 SharedPlan shared_plan(const MoeGroup* g, int ng, int Etot, int rows, int topk, long long slots, const sx_bank* sh,
-                       const sx_decode* dec, const sx_decode* sh_dec) {
+                       const sx_decode* dec, const sx_decode* sh_dec, int sh_rows, bool any_decode = false) {
     if (!sh) return {0, -1};
     const int D = g[0].bank.gate.in_features, I = g[0].bank.gate.out_features;
     for (int i = 0; i < ng; i++) {
         const sx_bank& b = g[i].bank;
         const MoeWs L = moe_ws_layout(b.gate.experts, rows, topk, D, I, b.gate.n, b.down.n,
                                       group_slots(slots, rows, topk, b.gate.experts, Etot), false);
-        if (!L.gemm && rows <= kDecodeRowsMax && sh->gate.n == b.gate.n && sh->down.n == b.down.n &&
-            sh->gate.out_features == I && same_decode(dec, sh_dec))
+        if (!L.gemm && sh_rows <= kDecodeRowsMax && sh->gate.n == b.gate.n && sh->down.n == b.down.n &&
+            sh->gate.out_features == I && (any_decode || same_decode(dec, sh_dec)))
             return {1, i};
     }
-    return {rows <= kDecodeRowsMax ? 2 : 3, -1};
+    return {sh_rows <= kDecodeRowsMax ? 2 : 3, -1};
 }
 
 size_t shared_fill_bytes(int rows) { return align_up((size_t)rows * (sizeof(uint32_t) + sizeof(float))); }
@@ -461,28 +464,35 @@ size_t shared_fill_bytes(int rows) { return align_up((size_t)rows * (sizeof(uint
 // shared expert its rows' past them), then the largest group's own scratch (the groups and the
 // shared expert run one after another on the stream).
 size_t moe_groups_ws(const MoeGroup* g, int ng, int Etot, int rows, int topk, long long slots, const sx_bank* sh,
-                     const sx_decode* dec, const sx_decode* sh_dec) {
+                     const sx_decode* dec, const sx_decode* sh_dec, int sh_rows) {
     const int D = g[0].bank.gate.in_features, I = g[0].bank.gate.out_features;
-    const SharedPlan plan = shared_plan(g, ng, Etot, rows, topk, slots, sh, dec, sh_dec);
-    const int extra = sh ? rows : 0;
+    // The shared expert's scratch for the plan its rows and rates allow whichever decodes the call
+    // brings: folded (the candidate group's extra prepared rows) and its own chain launches both.
+    const SharedPlan plan = shared_plan(g, ng, Etot, rows, topk, slots, sh, dec, sh_dec, sh_rows, true);
     size_t most = 0;
     for (int i = 0; i < ng; i++) {
         const sx_bank& b = g[i].bank;
         const MoeWs L = moe_ws_layout(b.gate.experts, rows, topk, D, I, b.gate.n, b.down.n,
                                       group_slots(slots, rows, topk, b.gate.experts, Etot), false,
-                                      plan.mode == 1 && plan.group == i ? extra : 0);
+                                      plan.mode == 1 && plan.group == i ? sh_rows : 0);
         most = std::max(most, L.total);
     }
-    if (plan.mode == 2) most = std::max(most, align_up((size_t)(rows * topk + rows) * sh->gate.out_features * 2));
+    if (plan.mode == 1 || plan.mode == 2)
+        most = std::max(most, align_up((size_t)(rows * topk + sh_rows) * sh->gate.out_features * 2));
     if (plan.mode == 3) {
-        const MoeWs L = moe_ws_layout(1, rows, 1, D, sh->gate.out_features, sh->gate.n, sh->down.n, rows, false);
-        most = std::max(most, L.total + shared_fill_bytes(rows));
+        const MoeWs L = moe_ws_layout(1, sh_rows, 1, D, sh->gate.out_features, sh->gate.n, sh->down.n, sh_rows, false);
+        most = std::max(most, L.total + shared_fill_bytes(sh_rows));
     }
-    return yslot_bytes(rows, topk, D) + (sh ? yslot_bytes(rows, 1, D) : 0) + most;
+    return yslot_bytes(rows, topk, D) + (sh ? yslot_bytes(sh_rows, 1, D) : 0) + most;
+}
+
+size_t moe_groups_ws(const MoeGroup* g, int ng, int Etot, int rows, int topk, long long slots, const sx_bank* sh,
+                     const sx_decode* dec, const sx_decode* sh_dec) {
+    return moe_groups_ws(g, ng, Etot, rows, topk, slots, sh, dec, sh_dec, rows);
 }
 
 size_t moe_groups_ws(const MoeGroup* g, int ng, int Etot, int rows, int topk, long long slots) {
-    return moe_groups_ws(g, ng, Etot, rows, topk, slots, nullptr, nullptr, nullptr);
+    return moe_groups_ws(g, ng, Etot, rows, topk, slots, nullptr, nullptr, nullptr, rows);
 }
 
 size_t moe_workspace_bytes(const sx_bank* bank, int32_t rows, int32_t topk, long long slots) {
@@ -496,11 +506,13 @@ size_t moe_workspace_bytes(const sx_bank* bank, int32_t rows, int32_t topk, long
 sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_decode* dec, const void* x,
                     sx_dtype dtype, int32_t rows, const uint32_t* inds, const float* scores, int32_t topk,
                     int32_t clamp_limit, float* yslot, uint8_t* ws, long long slots, const sx_bank* fold = nullptr,
-                    const MoeSegments* seg = nullptr, const MoeArgs* reduce = nullptr, bool* reduced = nullptr) {
+                    const MoeSegments* seg = nullptr, const MoeArgs* reduce = nullptr, bool* reduced = nullptr,
+                    const SharedRows* fold_rows = nullptr) {
     const int E = bank->gate.experts;
     const int D = bank->gate.in_features, I = bank->gate.out_features;
     sx_status st;
-    const MoeWs L = moe_ws_layout(E, rows, topk, D, I, bank->gate.n, bank->down.n, slots, false, fold ? rows : 0,
+    const int sh_rows = fold_rows ? fold_rows->rows : rows;
+    const MoeWs L = moe_ws_layout(E, rows, topk, D, I, bank->gate.n, bank->down.n, slots, false, fold ? sh_rows : 0,
                                   seg ? seg->live_slots : -1);
     MoeArgs a{};
     int kind_gu, kind_d;
@@ -545,8 +557,10 @@ sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_de
         a.seg_cap = seg->cap;
         a.nseg = seg->n;
     }
+    a.sh_x = fold_rows ? fold_rows->x : x;
+    a.sh_rows = sh_rows;
     if (fold) {
-        a.sh_items = (rows + 7) / 8;
+        a.sh_items = (sh_rows + 7) / 8;
         a.sh_slot0 = rows * topk;
         set_shared_ptrs(a, *fold);
     }
@@ -647,7 +661,7 @@ sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_de
 // A shared expert's own decode-chain launches (shared_plan mode 2): every work item is one of its
 // 8-row chunks; no routing metadata.  hprep holds rows*topk + rows prepared rows.
 sx_status shared_chain(sx_stream stream, const sx_bank* sh, const sx_decode* dec, const void* x, sx_dtype dtype,
-                       int32_t rows, int32_t topk, int32_t clamp_limit, float* yslot, uint8_t* ws) {
+                       int32_t rows, int32_t slot0, int32_t clamp_limit, float* yslot, uint8_t* ws) {
     MoeArgs a{};
     int kind_gu, kind_d;
     sx_status st;
@@ -656,10 +670,12 @@ sx_status shared_chain(sx_stream stream, const sx_bank* sh, const sx_decode* dec
     a.x = x;
     a.xdt = dtype;
     a.R = rows;
-    a.K = topk;
+    a.K = 1;
     a.D = sh->gate.in_features;
     a.I = sh->gate.out_features;
     a.E = 1;
+    a.sh_x = x;
+    a.sh_rows = rows;
     a.scale_gu = kind_scale(kind_gu);
     a.scale_down = kind_scale(kind_d);
     a.clamp = (float)clamp_limit;
@@ -667,7 +683,7 @@ sx_status shared_chain(sx_stream stream, const sx_bank* sh, const sx_decode* dec
     a.yslot = yslot;
     a.w_routed = 0;
     a.sh_items = (rows + 7) / 8;
-    a.sh_slot0 = rows * topk;
+    a.sh_slot0 = slot0;
     set_shared_ptrs(a, *sh);
     const cudaError_t e = chain_launch(a, kind_gu, sh->gate.n, sh->down.n, a.sh_items, a.sh_items,
                                        reinterpret_cast<cudaStream_t>(stream));
@@ -721,7 +737,7 @@ sx_status moe_run(sx_stream stream, const MoeGroup* groups, int ng, int Etot, co
                   sx_dtype dtype, int32_t rows, const uint32_t* inds, const float* scores, int32_t topk,
                   const void* shared, const void* shared_gate, int32_t clamp_limit, void* y, void* workspace,
                   size_t workspace_bytes, float* partial, long long slots, const sx_bank* sh_bank,
-                  const sx_decode* sh_dec, const MoeSegments* seg, float** yslot_out) {
+                  const sx_decode* sh_dec, const MoeSegments* seg, float** yslot_out, const SharedRows* own) {
     if (!x || !inds || !scores || (!y && !partial && !yslot_out)) return SX_ERR_NULL_POINTER;
     if (clamp_limit < 0 || clamp_limit > 128) return SX_ERR_INVALID_CLAMP;
     if (rows < 1 || topk < 1) return SX_ERR_BAD_SHAPE;
@@ -756,12 +772,16 @@ sx_status moe_run(sx_stream stream, const MoeGroup* groups, int ng, int Etot, co
         const sx_status st = check_shared_bank(sh_bank, D, sh_dec);
         if (st) return st;
     }
-    if (!workspace || workspace_bytes < moe_groups_ws(groups, ng, Etot, rows, topk, slots, sh_bank, dec, sh_dec))
+    const int sh_rows = own ? own->rows : rows;
+    const void* sh_x = own ? own->x : x;
+    if (sh_bank && sh_rows < 1) return SX_ERR_BAD_SHAPE;
+    if (!workspace ||
+        workspace_bytes < moe_groups_ws(groups, ng, Etot, rows, topk, slots, sh_bank, dec, sh_dec, sh_rows))
         return SX_ERR_WORKSPACE_TOO_SMALL;
-    const SharedPlan plan = shared_plan(groups, ng, Etot, rows, topk, slots, sh_bank, dec, sh_dec);
+    const SharedPlan plan = shared_plan(groups, ng, Etot, rows, topk, slots, sh_bank, dec, sh_dec, sh_rows);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     float* yslot = reinterpret_cast<float*>(ws);
-    uint8_t* scratch = ws + yslot_bytes(rows, topk, D) + (sh_bank ? yslot_bytes(rows, 1, D) : 0);
+    uint8_t* scratch = ws + yslot_bytes(rows, topk, D) + (sh_bank ? yslot_bytes(sh_rows, 1, D) : 0);
     MoeArgs r{};
     r.inds = inds;
     r.K = topk;
@@ -785,22 +805,23 @@ sx_status moe_run(sx_stream stream, const MoeGroup* groups, int ng, int Etot, co
                                        clamp_limit, yslot, scratch,
                                        group_slots(slots, rows, topk, groups[i].bank.gate.experts, Etot),
                                        plan.mode == 1 && plan.group == i ? sh_bank : nullptr, seg,
-                                       may_fold ? &r : nullptr, &folded);
+                                       may_fold ? &r : nullptr, &folded, own);
         if (st) return st;
     }
-    if (yslot_out) {  // the caller reduces the per-slot planes itself
+    if (plan.mode == 2) {
+        const sx_status st = shared_chain(stream, sh_bank, sh_dec, sh_x, dtype, sh_rows, rows * topk, clamp_limit,
+                                          yslot, scratch);
+        if (st) return st;
+    } else if (plan.mode == 3) {
+        const sx_status st = shared_expert_run(stream, sh_bank, sh_dec, sh_x, dtype, sh_rows, clamp_limit,
+                                               yslot + (size_t)rows * topk * D, scratch);
+        if (st) return st;
+    }
+    if (yslot_out) {  // the caller reduces the per-slot planes itself (the shared plane follows them)
         *yslot_out = yslot;
         return SX_OK;
     }
     if (folded) return SX_OK;
-    if (plan.mode == 2) {
-        const sx_status st = shared_chain(stream, sh_bank, sh_dec, x, dtype, rows, topk, clamp_limit, yslot, scratch);
-        if (st) return st;
-    } else if (plan.mode == 3) {
-        const sx_status st = shared_expert_run(stream, sh_bank, sh_dec, x, dtype, rows, clamp_limit,
-                                               yslot + (size_t)rows * topk * D, scratch);
-        if (st) return st;
-    }
     return cuda_status(launch_pdl(moe_reduce_kernel, dim3(rows, (D + kReduceCols - 1) / kReduceCols), dim3(128), 0,
                                   reinterpret_cast<cudaStream_t>(stream), r),
                        "moe reduce launch");
@@ -813,7 +834,8 @@ sx_status moe_impl(sx_stream stream, const sx_bank* bank, const sx_decode* dec, 
     if (!bank) return SX_ERR_NULL_POINTER;
     const MoeGroup g{*bank, 0};
     return moe_run(stream, &g, 1, bank->gate.experts, dec, x, dtype, rows, inds, scores, topk, shared, shared_gate,
-                   clamp_limit, y, workspace, workspace_bytes, partial, slots, nullptr, nullptr, nullptr, nullptr);
+                   clamp_limit, y, workspace, workspace_bytes, partial, slots, nullptr, nullptr, nullptr, nullptr,
+                   nullptr);
 }
 
 }  // namespace sx

@@ -67,6 +67,8 @@ struct MoeArgs {
     // slot ids sh_slot0 + row (past the routed slots) and score 1.  w_routed = 0: a launch of the
     // shared expert alone (no routing metadata read).
     int w_routed, sh_items, sh_slot0;
+    const void* sh_x;       // the shared expert's rows: x, or an expert-parallel rank's own rows
+    int sh_rows;
     const uint16_t* sh_gate_tr; const uint16_t* sh_gate_suh; const uint16_t* sh_gate_svh;
     const uint16_t* sh_up_tr;   const uint16_t* sh_up_suh;   const uint16_t* sh_up_svh;
     const uint16_t* sh_down_tr; const uint16_t* sh_down_suh; const uint16_t* sh_down_svh;
@@ -158,7 +160,7 @@ __device__ __forceinline__ bool work_item(const MoeArgs& a, int w, WorkItem& it)
         if (c >= a.sh_items) return false;
         it.e = 0;
         it.first = c * 8;
-        it.rows = min(8, a.R - c * 8);
+        it.rows = min(8, a.sh_rows - c * 8);
         it.shx = true;
         return true;
     }
@@ -222,8 +224,9 @@ __global__ void __launch_bounds__(kThreads, 3) moe_pair_kernel(MoeArgs a) {
             if (m < it.rows) {
                 const int row = it.shx ? slot_of[m] - a.sh_slot0 : slot_of[m] / a.K;
                 const size_t xoff = (size_t)row * a.D + base;
+                const void* xs = it.shx ? a.sh_x : a.x;
 #pragma unroll
-                for (int i = 0; i < 4; i++) v[i] = round_f16(load_act(a.x, xoff + i, a.xdt)) * h2f(suh_p[p][base + i]);
+                for (int i = 0; i < 4; i++) v[i] = round_f16(load_act(xs, xoff + i, a.xdt)) * h2f(suh_p[p][base + i]);
                 warp_hadamard128(v);
             }
             const uint16_t h[4] = {f2h(v[0]), f2h(v[1]), f2h(v[2]), f2h(v[3])};
