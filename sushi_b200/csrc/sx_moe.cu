@@ -1,6 +1,7 @@
 // Routed SwiGLU experts: sx_moe (root.moe / moeWithShared / moeWithGatedShared / moeClamped,
 // src/exl3/root.zig:51-125) and its workspace query.  Kernels in sx_moe_impl.cuh.
 #include <algorithm>
+#include <cmath>
 
 #include "sx_gemm_impl.cuh"
 #include "sx_internal.h"
@@ -151,7 +152,7 @@ __global__ void __launch_bounds__(1024) route_prep_kernel(MoeArgs a) {
             const int pos = base + __popc(peers & ((1u << lane) - 1u));
             a.order[off[e] + pos] = s;
             a.sorted_e[off[e] + pos] = (int)e;
-            if (a.chunk == 8 && pos < a.big_min) a.work_slots[(wb[e] + pos / 8) * 8 + pos % 8] = s;
+            if (a.chunk <= 8 && pos < a.big_min) a.work_slots[(wb[e] + pos / a.chunk) * 8 + pos % a.chunk] = s;
         }
     });
 }
@@ -182,6 +183,20 @@ bool use_gemm(int E, int R, int K, long long slots) {
     return slots >= 16LL * std::min<long long>(E, slots);
 }
 
+// Rows per work item of the decode chain: kSmallChunk when the routed slots spread over about as
+// many experts as there are slots (at most two rows per active expert expected for uniform
+// routing), so a CTA's B fragments hold two rows and its shared memory fits fewer k splits; else 8.
+#ifndef SX_CHAIN_SMALL_CHUNK
+#define SX_CHAIN_SMALL_CHUNK 2
+#endif
+constexpr int kSmallChunk = SX_CHAIN_SMALL_CHUNK;
+
+int chain_chunk(int E, int R, int K, long long slots) {
+    const double v = slots > 0 ? (double)slots : (double)R * K;
+    const double active = E * (1.0 - std::exp(-v / std::max(1, E)));
+    return v <= 2.0 * active ? kSmallChunk : 8;
+}
+
 // extra_rows: prepared-input rows past the routed slots (a shared expert's rows riding the chain).
 // bound: the routed slots known to be valid at most (-1: R*K); it sizes the work lists, the
 // sorted positions and the launches that run over them (not the per-slot planes, indexed by slot).
@@ -191,7 +206,7 @@ MoeWs moe_ws_layout(int E, int R, int K, int D, int I, int n_gu, int n_d, long l
     const int RK = bound >= 0 ? (int)std::min<long long>(bound, (long long)R * K) : R * K;
     w.gemm = use_gemm(E, R, K, slots);
     const bool big = w.gemm && gemm_rt_rate(n_gu) && gemm_rt_rate(n_d);
-    w.chunk = w.gemm ? kGemmRows : 8;
+    w.chunk = w.gemm ? kGemmRows : chain_chunk(E, R, K, slots);
     w.big_min = big ? kBigRows : 0x7FFFFFFF;
     w.big_chunk = 4 * kGemmRows;
     w.A_max = std::min(E, RK);
@@ -390,8 +405,12 @@ namespace {
 
 // The least split-K cluster size of a chain kernel over `units` (work items x output blocks):
 // enough CTAs to give every SM one; fit_split then grows it until two CTAs fit per SM.
+#ifndef SX_CHAIN_CTAS_PER_SM
+#define SX_CHAIN_CTAS_PER_SM 1
+#endif
 int min_split(long long units) {
-    const long long S = (sm_count() + std::max(1LL, units) - 1) / std::max(1LL, units);
+    const long long want = (long long)sm_count() * SX_CHAIN_CTAS_PER_SM;
+    const long long S = (want + std::max(1LL, units) - 1) / std::max(1LL, units);
     return (int)std::max(1LL, std::min(16LL, S));
 }
 
@@ -560,7 +579,7 @@ sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_de
     a.sh_x = fold_rows ? fold_rows->x : x;
     a.sh_rows = sh_rows;
     if (fold) {
-        a.sh_items = (sh_rows + 7) / 8;
+        a.sh_items = (sh_rows + L.chunk - 1) / L.chunk;
         a.sh_slot0 = rows * topk;
         set_shared_ptrs(a, *fold);
     }
@@ -682,7 +701,8 @@ sx_status shared_chain(sx_stream stream, const sx_bank* sh, const sx_decode* dec
     a.hprep = reinterpret_cast<uint16_t*>(ws);
     a.yslot = yslot;
     a.w_routed = 0;
-    a.sh_items = (rows + 7) / 8;
+    a.chunk = rows <= kSmallChunk ? kSmallChunk : 8;
+    a.sh_items = (rows + a.chunk - 1) / a.chunk;
     a.sh_slot0 = slot0;
     set_shared_ptrs(a, *sh);
     const cudaError_t e = chain_launch(a, kind_gu, sh->gate.n, sh->down.n, a.sh_items, a.sh_items,

@@ -54,7 +54,7 @@ struct MoeArgs {
     const void* shared_gate;// [R] x dtype logits, or null
     void* y;                // [R][D] x dtype
     float* partial;         // [R][D] f32: when set, the k-order sum lands here unrounded (no shared)
-    int chunk;              // rows per work item: 8 (decode chain) or kGemmRows (tensor-core path)
+    int chunk;              // rows per work item: 2 or 8 (decode chain) or kGemmRows (tensor-core path)
     int big_min;            // experts with this many rows or more go to the second list (INT_MAX: none)
     int big_chunk;          // rows per work item of the second list (4 row tiles per CTA)
     int* work_act4;         // second list: [W4_max]
@@ -159,8 +159,8 @@ __device__ __forceinline__ bool work_item(const MoeArgs& a, int w, WorkItem& it)
         const int c = w - a.w_routed;
         if (c >= a.sh_items) return false;
         it.e = 0;
-        it.first = c * 8;
-        it.rows = min(8, a.sh_rows - c * 8);
+        it.first = c * a.chunk;
+        it.rows = min(a.chunk, a.sh_rows - c * a.chunk);
         it.shx = true;
         return true;
     }
@@ -176,7 +176,7 @@ __device__ __forceinline__ bool work_item(const MoeArgs& a, int w, WorkItem& it)
 
 // The slot id of row t of a work item.
 __device__ __forceinline__ int work_slot(const MoeArgs& a, int w, const WorkItem& it, int t) {
-    return it.shx ? a.sh_slot0 + it.first + t : a.work_slots[w * 8 + t];
+    return it.shx ? a.sh_slot0 + it.first + t : a.work_slots[w * 8 + t];  // (chunk <= 8)
 }
 
 // ------------------------------------------------------------------ 2. gate + up + mid
@@ -192,7 +192,8 @@ __global__ void __launch_bounds__(kThreads, 3) moe_pair_kernel(MoeArgs a) {
     const int kb0 = (int)(((long long)split * KB) / S);
     const int kbl = (int)(((long long)(split + 1) * KB) / S) - kb0;
     const int kbl_max = (KB + S - 1) / S;
-    const CoreSmem s = core_smem<N, 2, 1>(smem, kbl_max);
+    const int mg = a.chunk;  // rows per work item: the B fragments hold this many rows
+    const CoreSmem s = core_smem<N, 2, 1>(smem, kbl_max, mg);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int OT = a.I / 16;
     const size_t per = (size_t)(a.D / 16) * OT * N;
@@ -215,10 +216,10 @@ __global__ void __launch_bounds__(kThreads, 3) moe_pair_kernel(MoeArgs a) {
     } else {
         const uint16_t* suh_p[2] = {it.shx ? a.sh_gate_suh : a.gate_suh + (size_t)it.e * a.D,
                                     it.shx ? a.sh_up_suh : a.up_suh + (size_t)it.e * a.D};
-        for (int item = warp; item < 2 * kbl * 8; item += kConsumerWarps) {
-            const int p = item / (kbl * 8);
-            const int kbi = (item / 8) % kbl;
-            const int m = item % 8;
+        for (int item = warp; item < 2 * kbl * mg; item += kConsumerWarps) {
+            const int p = item / (kbl * mg);
+            const int kbi = (item / mg) % kbl;
+            const int m = item % mg;
             const int base = (kb0 + kbi) * 128 + lane * 4;
             float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             if (m < it.rows) {
@@ -230,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 3) moe_pair_kernel(MoeArgs a) {
                 warp_hadamard128(v);
             }
             const uint16_t h[4] = {f2h(v[0]), f2h(v[1]), f2h(v[2]), f2h(v[3])};
-            bfrag_put4<1>(s.bfrag + p * s.bfrag_proj_stride, 8, kbi, m, lane, h);
+            bfrag_put4<1>(s.bfrag + p * s.bfrag_proj_stride, mg, kbi, m, lane, h);
         }
         consumers_sync<kConsumerWarps>();
         const DecParams dp[2] = {a.dp_gu, a.dp_gu};
@@ -283,7 +284,8 @@ __global__ void __launch_bounds__(kThreads, 3) moe_down_kernel(MoeArgs a) {
     const int kb0 = (int)(((long long)split * KB) / S);
     const int kbl = (int)(((long long)(split + 1) * KB) / S) - kb0;
     const int kbl_max = (KB + S - 1) / S;
-    const CoreSmem s = core_smem<N, 1, 1>(smem, kbl_max);
+    const int mg = a.chunk;  // rows per work item: the B fragments hold this many rows
+    const CoreSmem s = core_smem<N, 1, 1>(smem, kbl_max, mg);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int OT = a.D / 16;
     const size_t per = (size_t)(a.I / 16) * OT * N;
@@ -308,15 +310,15 @@ __global__ void __launch_bounds__(kThreads, 3) moe_down_kernel(MoeArgs a) {
         }
     } else {
         grid_dependency_wait();  // the prepared rows come from moe_pair
-        for (int item = warp; item < kbl * 8; item += kConsumerWarps) {
-            const int kbi = item / 8, m = item % 8;
+        for (int item = warp; item < kbl * mg; item += kConsumerWarps) {
+            const int kbi = item / mg, m = item % mg;
             const uint16_t* src = a.hprep + (size_t)slot_of[m] * a.I + (kb0 + kbi) * 128 + lane * 4;
             uint16_t h[4] = {0, 0, 0, 0};
             if (m < it.rows) {
 #pragma unroll
                 for (int i = 0; i < 4; i++) h[i] = src[i];
             }
-            bfrag_put4<1>(s.bfrag, 8, kbi, m, lane, h);
+            bfrag_put4<1>(s.bfrag, mg, kbi, m, lane, h);
         }
         consumers_sync<kConsumerWarps>();
         const DecParams dp[1] = {a.dp_down};

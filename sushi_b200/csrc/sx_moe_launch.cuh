@@ -41,29 +41,29 @@ int three_per_sm_smem();
 // at 64; taking three per SM also where S_min = 1 was no faster there and 3% slower on the stack
 // at 64 tokens.  More splits than needed pay the cluster reduce and per-CTA start-up more often.
 template <int N, int NP>
-static int fit_split(int S, int KB) {
+static int fit_split(int S, int KB, int mg) {
     S = S < KB ? S : KB;
     const size_t three = (size_t)three_per_sm_smem(), two = (size_t)two_per_sm_smem();
     if (S > 1)
         for (int c = S; c <= 16 && c <= KB; c++)
-            if (core_layout<N, NP, 1>((KB + c - 1) / c).total <= three) return c;
-    while (S < 16 && S < KB && core_layout<N, NP, 1>((KB + S - 1) / S).total > two) S++;
+            if (core_layout<N, NP, 1>((KB + c - 1) / c, mg).total <= three) return c;
+    while (S < 16 && S < KB && core_layout<N, NP, 1>((KB + S - 1) / S, mg).total > two) S++;
     return S;
 }
 
 template <int KIND, int N>
 static cudaError_t launch_pair_t(const MoeArgs& a, int S, int W_max, cudaStream_t stream) {
     const int KB = a.D / 128;
-    S = fit_split<N, 2>(S, KB);
-    const CoreLayout L = core_layout<N, 2, 1>((KB + S - 1) / S);
+    S = fit_split<N, 2>(S, KB, a.chunk);
+    const CoreLayout L = core_layout<N, 2, 1>((KB + S - 1) / S, a.chunk);
     return launch_clustered(moe_pair_kernel<KIND, N>, dim3(W_max, a.I / 128, S), S, L.total, stream, a);
 }
 
 template <int KIND, int N>
 static cudaError_t launch_down_t(const MoeArgs& a, int S, int W_max, cudaStream_t stream) {
     const int KB = a.I / 128;
-    S = fit_split<N, 1>(S, KB);
-    const CoreLayout L = core_layout<N, 1, 1>((KB + S - 1) / S);
+    S = fit_split<N, 1>(S, KB, a.chunk);
+    const CoreLayout L = core_layout<N, 1, 1>((KB + S - 1) / S, a.chunk);
     return launch_clustered(moe_down_kernel<KIND, N>, dim3(W_max, a.D / 128, S), S, L.total, stream, a);
 }
 
