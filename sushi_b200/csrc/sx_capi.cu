@@ -164,6 +164,7 @@ sx_status linear_impl(sx_stream stream, const sx_proj* proj, const sx_decode* de
         a.mask1 = dp.mask1;
         a.rot = dp.rot;
         a.out_scale = kind_scale(kind);
+        a.vec = reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(proj->suh) % 8 == 0;
         a.nseg = count;
         for (int i = 0; i < count; i++) {
             a.seg_end[i] = cols[i + 1] / 128;

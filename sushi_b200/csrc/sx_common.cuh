@@ -85,6 +85,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int co
     }
 }
 
+// ------------------------------------------------------------------ flags between GPUs
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Waits until *flag >= seq (wrap-safe), for at most ~2 s of wall time; on a timeout latches
+// DEV_TIMEOUT_PEER and returns false (the caller goes on: its outputs are undefined, nothing hangs).
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t seq) {
+    if ((int32_t)(ld_acquire_sys(flag) - seq) >= 0) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 0;; i++) {
+        __nanosleep(64);
+        if ((int32_t)(ld_acquire_sys(flag) - seq) >= 0) return true;
+        if ((i & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
+            latch_error(DEV_TIMEOUT_PEER);
+            return false;
+        }
+    }
+}
+
 // ------------------------------------------------------------------ bulk copies (TMA, 1-D)
 // global -> this CTA's shared memory, completing `bytes` on `bar`.  dst and src 16-byte aligned,
 // bytes a multiple of 16.  No multicast.
@@ -129,6 +151,32 @@ __device__ __forceinline__ void load_act4(const void* p, size_t i, int dt, float
 #pragma unroll
     for (int k = 0; k < 4; k++)
         v[k] = dt == 1 ? __half2float(__ushort_as_half(h[k])) : __bfloat162float(__ushort_as_bfloat16(h[k]));
+}
+
+// Four consecutive f16 values from element i (a multiple of 4) as floats: one 8-byte load when
+// `vec` (the array starts 8-byte aligned), else four 2-byte loads.
+__device__ __forceinline__ void load_half4(const uint16_t* p, size_t i, bool vec, float (&v)[4]) {
+    if (vec) {
+        const uint2 u = *reinterpret_cast<const uint2*>(p + i);
+        v[0] = __half2float(__ushort_as_half((uint16_t)u.x));
+        v[1] = __half2float(__ushort_as_half((uint16_t)(u.x >> 16)));
+        v[2] = __half2float(__ushort_as_half((uint16_t)u.y));
+        v[3] = __half2float(__ushort_as_half((uint16_t)(u.y >> 16)));
+        return;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; k++) v[k] = __half2float(__ushort_as_half(p[i + k]));
+}
+
+// Four consecutive activations from element i (a multiple of 4): load_act4 when `vec` (rows start
+// 16-byte aligned), else element by element.
+__device__ __forceinline__ void load_act4v(const void* p, size_t i, int dt, bool vec, float (&v)[4]) {
+    if (vec) {
+        load_act4(p, i, dt, v);
+        return;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; k++) v[k] = load_act(p, i + k, dt);
 }
 
 // v rounded to an activation dtype and back.

@@ -27,7 +27,13 @@ cudaError_t dispatch_n(const GemvArgs& a, int n, int groups, cudaStream_t stream
 // Consumer warps of the GEMV: 8, each owning one output tile across a stage's 8 input-tile rows,
 // at three CTAs per SM for up to 8 rows (measured on B200: faster than 16 warps at two CTAs per
 // SM on every sweep shape).
-constexpr int kGemvCW = 8;
+#ifndef SX_GEMV_CW
+#define SX_GEMV_CW 8
+#endif
+#ifndef SX_GEMV_MIN_BLOCKS
+#define SX_GEMV_MIN_BLOCKS 3
+#endif
+constexpr int kGemvCW = SX_GEMV_CW;
 constexpr int kGemvThreads = (kGemvCW + 1) * 32;
 
 // The RMS norm of the first linear of a stacked launch (project_rows.zig:394-456's finish, MLX's
@@ -61,7 +67,7 @@ __device__ __forceinline__ void gemv_norm_last(const GemvArgs& a, int lane, int 
 }
 
 template <int KIND, int N, int NB, bool W16>
-__global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 3 : 2) gemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, NB == 1 ? SX_GEMV_MIN_BLOCKS : 2) gemv_kernel(GemvArgs a) {
     constexpr int CW = kGemvCW;
     extern __shared__ __align__(128) uint8_t smem[];
     cg::cluster_group cluster = cg::this_cluster();
@@ -95,36 +101,48 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 3 : 2) gemv_kernel(Gem
             core_produce<N, 1>(s, tr, OT, ob, kb0, kbl);
         }
     } else {
-        // suh and svh are weights too: the warp's first prepare item's four suh values and, in
-        // rank 0, the lane's four svh values of the finish are read before the dependency wait,
-        // so neither read is a round trip after it.
-        const int items = kbl * NB * mg;
-        uint16_t suh0[4] = {0, 0, 0, 0};
-        if (warp < items) {
-            const int base = (kb0 + warp / (NB * mg)) * 128 + lane * 4;
-#pragma unroll
-            for (int i = 0; i < 4; i++) suh0[i] = suh[base + i];
-        }
+        // Prepare (prepareInput): warp w takes the CTA's input blocks w, w + CW, ...; per block and
+        // 8-row group the lane's four x values of every stored row are loaded together (one round
+        // of loads per block and group, not one per row), then each row is prepared: f16(x) *
+        // suh, Hadamard-128, f16, into its B fragments.  suh and svh are weights: the first
+        // block's suh and, in rank 0, the lane's four svh values of the finish are read before the
+        // dependency wait.
+        const bool vec = a.vec != 0;
+        float su[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (warp < kbl) load_half4(suh, (size_t)(kb0 + warp) * 128 + lane * 4, vec, su);
         if (split == 0) {
 #pragma unroll
             for (int i = 0; i < 4; i++) svh0[i] = svh[ob * 128 + lane * 4 + i];
         }
         grid_dependency_wait();  // x may come from the previous grid
-        // prepare: rows x input blocks, one warp per (block, row) of the stored rows
-        for (int item = warp; item < items; item += CW) {
-            const int kbi = item / (NB * mg);
-            const int m = ((item / mg) % NB) * 8 + item % mg;
+        for (int kbi = warp; kbi < kbl; kbi += CW) {
             const int base = (kb0 + kbi) * 128 + lane * 4;
-            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            if (m < a.rows) {
-                const size_t xoff = (size_t)g * a.x_group_stride + (size_t)m * a.in + base;
+            if (kbi != warp) load_half4(suh, base, vec, su);
 #pragma unroll
-                for (int i = 0; i < 4; i++)
-                    v[i] = round_f16(load_act(a.x, xoff + i, a.xdt)) * h2f(item == warp ? suh0[i] : suh[base + i]);
-                warp_hadamard128(v);
+            for (int nb = 0; nb < NB; nb++) {
+                float v[8][4];
+#pragma unroll
+                for (int gg = 0; gg < 8; gg++) {
+                    const int m = nb * 8 + gg;
+                    if (gg < mg && m < a.rows)
+                        load_act4v(a.x, (size_t)g * a.x_group_stride + (size_t)m * a.in + base, a.xdt, vec, v[gg]);
+                }
+#pragma unroll
+                for (int gg = 0; gg < 8; gg++) {
+                    const int m = nb * 8 + gg;
+                    if (gg >= mg) continue;  // rows of later lanes read row mg-1's fragments
+                    float (&vr)[4] = v[gg];
+                    if (m < a.rows) {
+#pragma unroll
+                        for (int i = 0; i < 4; i++) vr[i] = round_f16(vr[i]) * su[i];
+                        warp_hadamard128(vr);
+                    } else {
+                        vr[0] = vr[1] = vr[2] = vr[3] = 0.0f;
+                    }
+                    const uint16_t h[4] = {f2h(vr[0]), f2h(vr[1]), f2h(vr[2]), f2h(vr[3])};
+                    bfrag_put4<NB>(s.bfrag, mg, kbi, m, lane, h);
+                }
             }
-            const uint16_t h[4] = {f2h(v[0]), f2h(v[1]), f2h(v[2]), f2h(v[3])};
-            bfrag_put4<NB>(s.bfrag, mg, kbi, m, lane, h);
         }
         consumers_sync<CW>();
 

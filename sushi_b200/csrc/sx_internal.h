@@ -49,6 +49,10 @@ struct MoeSegments {
     const int* cnt;
     int cap, n;
     long long live_slots;  // the segments' routed slots when the host knows them (sizes the launches), else -1
+    // route_prep first waits (bounded) for wait_flags[g] >= *seq for every segment g, when set:
+    // the rows and counts arrive from other GPUs behind those flags
+    const uint32_t* wait_flags;
+    const uint32_t* seq;
 };
 
 // The rows a layer's shared expert runs over when they are not the routed rows (an expert-parallel

@@ -19,6 +19,7 @@ struct GemvArgs {
     long long y_group_stride;
     uint32_t wmask, mult, mask0, mask1, rot;
     float out_scale;
+    int vec;                   // x starts 16-byte aligned and suh 8-byte aligned: vector loads
     int pdl;                   // host side: launch with programmatic stream serialisation
     // Stacked linears sharing the input (nseg > 0): output blocks [seg_end[s-1], seg_end[s]) are
     // linear s, prepared with suh row s and written to ys[s] ([rows][ywidth[s]] in x's dtype).

@@ -78,6 +78,10 @@ __global__ void __launch_bounds__(1024) route_prep_kernel(MoeArgs a) {
     grid_launch_dependents();
     for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;
     grid_dependency_wait();  // the routing comes from the previous kernel
+    if (a.seg_wait) {  // an expert-parallel rank's received rows: every source's flag of this call
+        const uint32_t seq = *a.seg_seq;
+        for (int g = tid; g < a.nseg; g += blockDim.x) wait_flag(a.seg_wait + g, seq);
+    }
     __syncthreads();
     // The slots to sort, in warp-uniform strides: every slot, or an expert-parallel rank's live
     // places only (segment by segment).  body(s, in_range) runs on every lane of a warp at once.
@@ -575,6 +579,8 @@ sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_de
         a.seg_cnt = seg->cnt;
         a.seg_cap = seg->cap;
         a.nseg = seg->n;
+        a.seg_wait = seg->wait_flags;
+        a.seg_seq = seg->seq;
     }
     a.sh_x = fold_rows ? fold_rows->x : x;
     a.sh_rows = sh_rows;

@@ -83,6 +83,8 @@ struct MoeArgs {
     // reads the counts after its dependency wait and skips every other place.
     const int* seg_cnt;
     int seg_cap, nseg;
+    const uint32_t* seg_wait;  // route_prep waits for seg_wait[g] >= *seg_seq, g < nseg, when set
+    const uint32_t* seg_seq;
     // The reduce folded into moe_down (a one-group decode-chain layer, rounded output): rcount
     // [R][D/128] arrival counters, zeroed by route_prep; the last of a (token, output block)'s
     // planes to land (its live routed slots, plus the shared plane when sh_plane) makes that
@@ -216,22 +218,39 @@ __global__ void __launch_bounds__(kThreads, 3) moe_pair_kernel(MoeArgs a) {
     } else {
         const uint16_t* suh_p[2] = {it.shx ? a.sh_gate_suh : a.gate_suh + (size_t)it.e * a.D,
                                     it.shx ? a.sh_up_suh : a.up_suh + (size_t)it.e * a.D};
-        for (int item = warp; item < 2 * kbl * mg; item += kConsumerWarps) {
-            const int p = item / (kbl * mg);
-            const int kbi = (item / mg) % kbl;
-            const int m = item % mg;
+        // Prepare: warp w takes units w, w + 8, ... of the (projection, input block) units; per unit
+        // the lane's four suh values and the four x values of every row of the item are loaded
+        // together (one round of loads), then each row is prepared: f16(x) * suh, Hadamard-128,
+        // f16, into its B fragments.
+        const void* xs = it.shx ? a.sh_x : a.x;
+        const bool xvec = (reinterpret_cast<uintptr_t>(xs) & 15) == 0;
+        for (int u = warp; u < 2 * kbl; u += kConsumerWarps) {
+            const int p = u / kbl, kbi = u % kbl;
             const int base = (kb0 + kbi) * 128 + lane * 4;
-            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            if (m < it.rows) {
-                const int row = it.shx ? slot_of[m] - a.sh_slot0 : slot_of[m] / a.K;
-                const size_t xoff = (size_t)row * a.D + base;
-                const void* xs = it.shx ? a.sh_x : a.x;
+            float su[4];
+            load_half4(suh_p[p], base, (reinterpret_cast<uintptr_t>(suh_p[p]) & 7) == 0, su);
+            float v[8][4];
 #pragma unroll
-                for (int i = 0; i < 4; i++) v[i] = round_f16(load_act(xs, xoff + i, a.xdt)) * h2f(suh_p[p][base + i]);
-                warp_hadamard128(v);
+            for (int m = 0; m < 8; m++) {
+                if (m < mg && m < it.rows) {
+                    const int row = it.shx ? slot_of[m] - a.sh_slot0 : slot_of[m] / a.K;
+                    load_act4v(xs, (size_t)row * a.D + base, a.xdt, xvec, v[m]);
+                }
             }
-            const uint16_t h[4] = {f2h(v[0]), f2h(v[1]), f2h(v[2]), f2h(v[3])};
-            bfrag_put4<1>(s.bfrag + p * s.bfrag_proj_stride, mg, kbi, m, lane, h);
+#pragma unroll
+            for (int m = 0; m < 8; m++) {
+                if (m >= mg) continue;
+                float (&vr)[4] = v[m];
+                if (m < it.rows) {
+#pragma unroll
+                    for (int i = 0; i < 4; i++) vr[i] = round_f16(vr[i]) * su[i];
+                    warp_hadamard128(vr);
+                } else {
+                    vr[0] = vr[1] = vr[2] = vr[3] = 0.0f;
+                }
+                const uint16_t h[4] = {f2h(vr[0]), f2h(vr[1]), f2h(vr[2]), f2h(vr[3])};
+                bfrag_put4<1>(s.bfrag + p * s.bfrag_proj_stride, mg, kbi, m, lane, h);
+            }
         }
         consumers_sync<kConsumerWarps>();
         const DecParams dp[2] = {a.dp_gu, a.dp_gu};
@@ -310,13 +329,19 @@ __global__ void __launch_bounds__(kThreads, 3) moe_down_kernel(MoeArgs a) {
         }
     } else {
         grid_dependency_wait();  // the prepared rows come from moe_pair
+        const bool hvec = (reinterpret_cast<uintptr_t>(a.hprep) & 7) == 0;
         for (int item = warp; item < kbl * mg; item += kConsumerWarps) {
             const int kbi = item / mg, m = item % mg;
             const uint16_t* src = a.hprep + (size_t)slot_of[m] * a.I + (kb0 + kbi) * 128 + lane * 4;
             uint16_t h[4] = {0, 0, 0, 0};
             if (m < it.rows) {
+                if (hvec) {
+                    const uint2 u = *reinterpret_cast<const uint2*>(src);
+                    h[0] = (uint16_t)u.x, h[1] = (uint16_t)(u.x >> 16), h[2] = (uint16_t)u.y, h[3] = (uint16_t)(u.y >> 16);
+                } else {
 #pragma unroll
-                for (int i = 0; i < 4; i++) h[i] = src[i];
+                    for (int i = 0; i < 4; i++) h[i] = src[i];
+                }
             }
             bfrag_put4<1>(s.bfrag, mg, kbi, m, lane, h);
         }
