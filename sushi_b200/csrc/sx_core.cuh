@@ -69,7 +69,7 @@ __host__ __device__ inline CoreLayout core_layout(int kbl_max, int mg = 8) {
 
 struct CoreSmem {
     uint8_t* stages;
-    uint4* bfrag;          // [NP][kbl_max][8][NB][mg][4] entries of BFrag<NB>::BYTES
+    uint4* bfrag;          // [NP][kbl_max][NB][mg][8 tiles][4] entries of BFrag<NB>::BYTES
     int bfrag_proj_stride; // entries between projections
     int mg;                // fragment rows per 8-row group
     float* red;
@@ -130,28 +130,20 @@ __device__ __forceinline__ bool core_produce(const CoreSmem& s, const uint16_t* 
     return true;
 }
 
-// One prepared value v of row m at position pos (0..127) of local input block kbi, into the
-// B-fragment slot its MMA lane reads: lane (g = m%8, c), register slot by the input's row in
-// the tile (sx_decode.cuh: MMA1 takes inputs 2c, 2c+1 and MMA2 2c+8, 2c+9, each duplicated).
-// Rows m with m % 8 >= mg are not stored.
-template <int NB>
-__device__ __forceinline__ void bfrag_put(uint4* bfrag, int mg, int kbi, int m, int pos, uint16_t h) {
-    const int nb = m >> 3, gg = m & 7;
-    if (gg >= mg) return;
-    const int tk = pos >> 4, r = pos & 15;
-    const int c = (r & 7) >> 1;
-    const int slot = ((r >> 3) << 1) | (r & 1);
-    const size_t entry = (size_t)((((kbi * 8 + tk) * NB + nb) * mg + gg) * 4 + c);
-    if constexpr (BFrag<NB>::COMPACT) {
-        reinterpret_cast<uint16_t*>(bfrag)[entry * 4 + slot] = h;
-    } else {
-        reinterpret_cast<uint32_t*>(&bfrag[entry])[slot] = (uint32_t)h | ((uint32_t)h << 16);
-    }
+// B fragments in shared memory: entry (kbi, nb, gg, tk, c) at ((((kbi*NB + nb)*mg + gg)*8 + tk)*4 + c
+// holds the inputs 2c, 2c+1, 2c+8, 2c+9 of input tile tk of local block kbi for row nb*8 + gg, the
+// lane (g = gg, c)'s B registers of the doubled-k MMA (MMA1 takes inputs 2c, 2c+1 and MMA2 2c+8,
+// 2c+9, each duplicated; sx_decode.cuh).  Consecutive input tiles of one row are four entries
+// apart, so a consumer steps through a stage's tiles at compile-time offsets.  Rows with
+// gg >= mg are not stored (their lanes read row mg-1's).
+__host__ __device__ constexpr int bfrag_entry(int kbi, int nb, int gg, int tk, int c, int NB, int mg) {
+    return (((kbi * NB + nb) * mg + gg) * 8 + tk) * 4 + c;
 }
 
 // The four prepared values a lane holds (positions 4*lane .. 4*lane+3 of local input block kbi,
-// row m) in two stores: positions 4*lane and +1 fill slots s0 and s0+1 of entry c0, positions +2
-// and +3 the same slots of entry c0+1 (c0 = 2*(lane&1), s0 = 2*((lane>>1)&1); bfrag_put's mapping).
+// row m) in two stores: positions 4*lane and +1 (tile tk = lane/4, tile rows 4*(lane%4), +1) fill
+// slots s0 and s0+1 of entry c0, positions +2 and +3 the same slots of entry c0+1 (c0 =
+// 2*(lane&1), s0 = 2*((lane>>1)&1)).
 template <int NB>
 __device__ __forceinline__ void bfrag_put4(uint4* bfrag, int mg, int kbi, int m, int lane, const uint16_t (&h)[4]) {
     const int nb = m >> 3, gg = m & 7;
@@ -159,7 +151,7 @@ __device__ __forceinline__ void bfrag_put4(uint4* bfrag, int mg, int kbi, int m,
     const int tk = lane >> 2;
     const int c0 = (lane & 1) * 2;
     const int s0 = ((lane >> 1) & 1) * 2;
-    const size_t entry = (size_t)((((kbi * 8 + tk) * NB + nb) * mg + gg) * 4 + c0);
+    const size_t entry = (size_t)bfrag_entry(kbi, nb, gg, tk, c0, NB, mg);
 #pragma unroll
     for (int q = 0; q < 2; q++) {
         const uint16_t a = h[2 * q], b = h[2 * q + 1];
@@ -213,9 +205,13 @@ __device__ __forceinline__ bool core_consume(const CoreSmem& s, int kbl, const D
 #pragma unroll
             for (int e = 0; e < 4; e++) acc[p][nb][e] = acc2[p][nb][e] = 0.0f;
     // Lanes of rows past the stored mg read row mg-1's fragments instead of branching: their
-    // output columns belong to rows no caller reads.
+    // output columns belong to rows no caller reads.  A lane's B-fragment entry for tile j of a
+    // stage is a compile-time offset (4 j entries) from its entry for tile 0.
     const int gq = lane >> 2;
-    const int bf_lane = min(gq, s.mg - 1) * 4 + (lane & 3);
+    using BE = typename BFrag<NB>::Entry;
+    const int bf_lane = bfrag_entry(0, 0, min(gq, s.mg - 1), tr0, lane & 3, NB, s.mg);
+    const int bf_block = NB * s.mg * 32;  // entries per local input block
+    const int bf_group = s.mg * 32;       // entries between row groups
     bool ok = true;
     for (int i = 0; i < kbl; i++) {
         const int st = i % NST;
@@ -226,16 +222,14 @@ __device__ __forceinline__ bool core_consume(const CoreSmem& s, int kbl, const D
                 const uint32_t* base = reinterpret_cast<const uint32_t*>(s.stages + (size_t)st * Ring<N, NP>::STAGE_BYTES +
                                                                          p * Ring<N, NP>::PROJ_BYTES) +
                                        (tr0 * 8 + ot) * TILE_WORDS;
-                using BE = typename BFrag<NB>::Entry;
-                const BE* bf = reinterpret_cast<const BE*>(s.bfrag) + p * s.bfrag_proj_stride +
-                               (size_t)(i * 8 + tr0) * NB * s.mg * 4 + bf_lane;
+                const BE* bf = reinterpret_cast<const BE*>(s.bfrag) + p * s.bfrag_proj_stride + i * bf_block + bf_lane;
 #pragma unroll
                 for (int j = 0; j < TPW; j++) {
                     uint32_t a1[4], a2[4];
                     decode_lane_mma<KIND, N, W16>(base + j * 8 * TILE_WORDS, lf, dp[p], a1, a2);
 #pragma unroll
                     for (int nb = 0; nb < NB; nb++) {
-                        const uint4 b = bfrag_expand(bf[(j * NB + nb) * s.mg * 4]);
+                        const uint4 b = bfrag_expand(bf[nb * bf_group + j * 4]);
                         float(&d)[4] = (j & 1) ? acc2[p][nb] : acc[p][nb];
                         mma16816(d, a1[0], a1[1], a1[2], a1[3], b.x, b.y);
                         mma16816(d, a2[0], a2[1], a2[2], a2[3], b.z, b.w);

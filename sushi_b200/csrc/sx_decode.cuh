@@ -126,10 +126,19 @@ __device__ __forceinline__ uint32_t rotl32(uint32_t v, uint32_t r) { return __fu
 // with its k dimension doubled, both halves against the same input, so the tensor core performs
 // the half sum (src/exl3/expert_exl3.zig:267-301).  MUL1's register holds (weight, 0).
 template <int KIND, int N, bool W16>
+__device__ __forceinline__ void decode_r_q(const uint32_t (&r)[Funnel<N>::NR], const DecParams& dp, uint32_t (&q)[8]);
+
+template <int KIND, int N, bool W16>
 __device__ __forceinline__ void decode_lane_q(const uint32_t* tile_words, const LaneFunnel<N>& lf, const DecParams& dp,
                                               uint32_t (&q)[8]) {
     uint32_t r[Funnel<N>::NR];
     lane_stream<N>(tile_words, lf, r);
+    decode_r_q<KIND, N, W16>(r, dp, q);
+}
+
+// The eight codewords of a lane's stream registers hashed into MMA A-register values.
+template <int KIND, int N, bool W16>
+__device__ __forceinline__ void decode_r_q(const uint32_t (&r)[Funnel<N>::NR], const DecParams& dp, uint32_t (&q)[8]) {
     if constexpr (KIND == K_PAIR1) {
 #define SX_PAIR(J)                                                   \
     {                                                                \

@@ -25,15 +25,9 @@ template <int KIND, int NB, bool W16>
 cudaError_t dispatch_n(const GemvArgs& a, int n, int groups, cudaStream_t stream);
 
 // Consumer warps of the GEMV: 8, each owning one output tile across a stage's 8 input-tile rows,
-// at three CTAs per SM for up to 8 rows (measured on B200: faster than 16 warps at two CTAs per
-// SM on every sweep shape).
-#ifndef SX_GEMV_CW
-#define SX_GEMV_CW 8
-#endif
-#ifndef SX_GEMV_MIN_BLOCKS
-#define SX_GEMV_MIN_BLOCKS 3
-#endif
-constexpr int kGemvCW = SX_GEMV_CW;
+// compiled for three CTAs per SM up to 8 rows (measured on B200: faster than 16 warps at two CTAs
+// per SM on every sweep shape, and no slower than the same kernel given two CTAs' registers).
+constexpr int kGemvCW = 8;
 constexpr int kGemvThreads = (kGemvCW + 1) * 32;
 
 // The RMS norm of the first linear of a stacked launch (project_rows.zig:394-456's finish, MLX's
@@ -67,7 +61,7 @@ __device__ __forceinline__ void gemv_norm_last(const GemvArgs& a, int lane, int 
 }
 
 template <int KIND, int N, int NB, bool W16>
-__global__ void __launch_bounds__(kGemvThreads, NB == 1 ? SX_GEMV_MIN_BLOCKS : 2) gemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 3 : 2) gemv_kernel(GemvArgs a) {
     constexpr int CW = kGemvCW;
     extern __shared__ __align__(128) uint8_t smem[];
     cg::cluster_group cluster = cg::this_cluster();

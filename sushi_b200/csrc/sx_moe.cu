@@ -11,6 +11,8 @@ namespace sx {
 
 template <int KIND>
 cudaError_t moe_launch_kind(const MoeArgs& a, int n_gu, int n_d, int S_gu, int S_d, int W_max, cudaStream_t stream);
+template <int KIND>
+cudaError_t moe_launch_kind_direct(const MoeArgs& a, int n_gu, int n_d, int S_gu, int W, cudaStream_t stream);
 
 namespace {
 
@@ -431,6 +433,18 @@ cudaError_t chain_launch(const MoeArgs& a, int kind, int n_gu, int n_d, int item
     }
 }
 
+// The one-token chain over W direct items (moe_pair, then moe_down1).
+cudaError_t chain_launch_direct(const MoeArgs& a, int kind, int n_gu, int n_d, int W, cudaStream_t s) {
+    const int S_gu = min_split((long long)W * (a.I / 128));
+    switch (kind) {
+        case K_MCG: return moe_launch_kind_direct<K_MCG>(a, n_gu, n_d, S_gu, W, s);
+        case K_MUL1: return moe_launch_kind_direct<K_MUL1>(a, n_gu, n_d, S_gu, W, s);
+        case K_HASH: return moe_launch_kind_direct<K_HASH>(a, n_gu, n_d, S_gu, W, s);
+        case K_PAIR1: return moe_launch_kind_direct<K_PAIR1>(a, n_gu, n_d, S_gu, W, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
 }  // namespace
 
 }  // namespace sx
@@ -601,8 +615,22 @@ sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_de
     }
 
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    const size_t rp_smem = 3 * (size_t)E * sizeof(int);
     cudaError_t e = cudaSuccess;
+    // One token on the decode chain with the reduce folded (one group, no expert-parallel
+    // segments, at most 16 items): the token's slots are the work items, so no routing pass runs,
+    // and moe_down1 reduces over a cluster of the items.
+    const int direct_items = topk + (fold ? 1 : 0);
+    if (rows == 1 && a.rcount && !seg && !fold_rows && direct_items <= 16) {
+        a.direct = 1;
+        a.chunk = 1;
+        a.w_routed = topk;
+        a.sh_items = fold ? 1 : 0;
+        a.sh_slot0 = topk;
+        a.rcount = nullptr;
+        e = chain_launch_direct(a, kind_gu, bank->gate.n, bank->down.n, direct_items, s);
+        return e == cudaSuccess ? SX_OK : cuda_status(e, "moe one-token chain launch");
+    }
+    const size_t rp_smem = 3 * (size_t)E * sizeof(int);
     if (rp_smem > 48 * 1024) e = func_attrs((const void*)route_prep_kernel, (int)rp_smem, false);
     if (e == cudaSuccess) e = launch_pdl(route_prep_kernel, dim3(1), dim3(1024), rp_smem, s, a);
     if (e != cudaSuccess) return cuda_status(e, "route_prep launch");

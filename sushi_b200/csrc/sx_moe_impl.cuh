@@ -85,6 +85,10 @@ struct MoeArgs {
     int seg_cap, nseg;
     const uint32_t* seg_wait;  // route_prep waits for seg_wait[g] >= *seg_seq, g < nseg, when set
     const uint32_t* seg_seq;
+    // One token (direct != 0): no routing metadata; work item k < K is the token's slot k (its
+    // expert inds[k] - e_lo, one row, slot id k), item K the folded shared expert; the down
+    // projection and the reduce run as moe_down1 (a cluster over the items per output block).
+    int direct;
     // The reduce folded into moe_down (a one-group decode-chain layer, rounded output): rcount
     // [R][D/128] arrival counters, zeroed by route_prep; the last of a (token, output block)'s
     // planes to land (its live routed slots, plus the shared plane when sh_plane) makes that
@@ -93,16 +97,15 @@ struct MoeArgs {
 };
 
 // A token's routed sum `acc` (f32) made into its output value: rounded to the output dtype, then
-// the shared expert added (optionally sigmoid-gated, with MLX's bf16/f16 rounding steps), as
-// moeWithShared / moeWithGatedShared do (src/exl3/root.zig:56-92; moe_shared_fold.folded,
-// src/moe_shared_fold.zig:24).  idx = r * D + d.
-// has_sh: a shared term sh (already in the output dtype's values) is added.
-__device__ __forceinline__ float routed_finish(float acc, int xdt, bool has_sh, float sh, const void* shared_gate, int r) {
+// the shared expert added (optionally sigmoid-gated by the logit gl, with MLX's bf16/f16 rounding
+// steps), as moeWithShared / moeWithGatedShared do (src/exl3/root.zig:56-92;
+// moe_shared_fold.folded, src/moe_shared_fold.zig:24).  has_sh: a shared term sh (already in the
+// output dtype's values) is added.
+__device__ __forceinline__ float routed_finish_g(float acc, int xdt, bool has_sh, float sh, bool gated, float gl) {
     float y = acc;
     if (xdt != 0) y = xdt == 1 ? __half2float(__float2half_rn(y)) : __bfloat162float(__float2bfloat16_rn(y));
     if (has_sh) {
-        if (shared_gate) {
-            const float gl = load_act(shared_gate, r, xdt);
+        if (gated) {
             float sg = 1.0f / (1.0f + expf(-gl));
             if (xdt == 2) {
                 sg = __bfloat162float(__float2bfloat16_rn(sg));
@@ -117,6 +120,12 @@ __device__ __forceinline__ float routed_finish(float acc, int xdt, bool has_sh, 
         y = y + sh;
     }
     return y;
+}
+
+// routed_finish_g with token r's gate logit read from shared_gate [R] (null: no gate).
+__device__ __forceinline__ float routed_finish(float acc, int xdt, bool has_sh, float sh, const void* shared_gate, int r) {
+    const bool gated = has_sh && shared_gate;
+    return routed_finish_g(acc, xdt, has_sh, sh, gated, gated ? load_act(shared_gate, r, xdt) : 0.0f);
 }
 
 // moe_reduce's arithmetic for four outputs d..d+3 of token r: the live slots' planes in k order,
@@ -157,6 +166,15 @@ struct WorkItem {
 // The item count and the item's record are loaded together (one round of global loads; a record
 // past the count is never used).
 __device__ __forceinline__ bool work_item(const MoeArgs& a, int w, WorkItem& it) {
+    if (a.direct && w < a.K) {
+        const uint32_t e = a.inds[w] - (uint32_t)a.e_lo;
+        if (e >= (uint32_t)a.E) return false;  // the slot's expert is in no expert of this launch
+        it.e = (int)e;
+        it.first = w;
+        it.rows = 1;
+        it.shx = false;
+        return true;
+    }
     if (w >= a.w_routed) {
         const int c = w - a.w_routed;
         if (c >= a.sh_items) return false;
@@ -178,7 +196,7 @@ __device__ __forceinline__ bool work_item(const MoeArgs& a, int w, WorkItem& it)
 
 // The slot id of row t of a work item.
 __device__ __forceinline__ int work_slot(const MoeArgs& a, int w, const WorkItem& it, int t) {
-    return it.shx ? a.sh_slot0 + it.first + t : a.work_slots[w * 8 + t];  // (chunk <= 8)
+    return it.shx ? a.sh_slot0 + it.first + t : a.direct ? it.first : a.work_slots[w * 8 + t];  // (chunk <= 8)
 }
 
 // ------------------------------------------------------------------ 2. gate + up + mid
@@ -186,6 +204,7 @@ template <int KIND, int N>
 __global__ void __launch_bounds__(kThreads, 3) moe_pair_kernel(MoeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int slot_of[8];
+    __shared__ __align__(16) uint16_t mid_h[3][128];  // rank 0's finish: gate svh, up svh, down suh
     cg::cluster_group cluster = cg::this_cluster();
     const int ob = blockIdx.y;
     const int S = cluster.dim_blocks().z;
@@ -224,6 +243,26 @@ __global__ void __launch_bounds__(kThreads, 3) moe_pair_kernel(MoeArgs a) {
         // f16, into its B fragments.
         const void* xs = it.shx ? a.sh_x : a.x;
         const bool xvec = (reinterpret_cast<uintptr_t>(xs) & 15) == 0;
+        // rank 0's finish weights of this block (gate and up svh, down suh): read by the last
+        // consumer warp together with its prepare loads, kept in shared memory for the finish
+        const bool mid_loader = split == 0 && warp == kConsumerWarps - 1;
+        // (asynchronous copies straight into shared memory: no registers held across the prepare)
+        if (mid_loader) {
+            const uint16_t* mp[3] = {it.shx ? a.sh_gate_svh : a.gate_svh + (size_t)it.e * a.I,
+                                     it.shx ? a.sh_up_svh : a.up_svh + (size_t)it.e * a.I,
+                                     it.shx ? a.sh_down_suh : a.down_suh + (size_t)it.e * a.I};
+#pragma unroll
+            for (int q = 0; q < 3; q++) {
+                const uint16_t* src = mp[q] + (size_t)ob * 128 + lane * 4;
+                if ((reinterpret_cast<uintptr_t>(mp[q]) & 7) == 0) {
+                    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(&mid_h[q][lane * 4])), "l"(src)
+                                 : "memory");
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; i++) mid_h[q][lane * 4 + i] = src[i];
+                }
+            }
+        }
         for (int u = warp; u < 2 * kbl; u += kConsumerWarps) {
             const int p = u / kbl, kbi = u % kbl;
             const int base = (kb0 + kbi) * 128 + lane * 4;
@@ -252,6 +291,7 @@ __global__ void __launch_bounds__(kThreads, 3) moe_pair_kernel(MoeArgs a) {
                 bfrag_put4<1>(s.bfrag + p * s.bfrag_proj_stride, mg, kbi, m, lane, h);
             }
         }
+        if (mid_loader) asm volatile("cp.async.wait_all;" ::: "memory");
         consumers_sync<kConsumerWarps>();
         const DecParams dp[2] = {a.dp_gu, a.dp_gu};
         float acc[2][1][4];
@@ -268,19 +308,16 @@ __global__ void __launch_bounds__(kThreads, 3) moe_pair_kernel(MoeArgs a) {
         warp_hadamard128(g);
         warp_hadamard128(u);
         float h[4];
-        const uint16_t* gsv = it.shx ? a.sh_gate_svh : a.gate_svh + (size_t)it.e * a.I;
-        const uint16_t* usv = it.shx ? a.sh_up_svh : a.up_svh + (size_t)it.e * a.I;
-        const uint16_t* dsu = it.shx ? a.sh_down_suh : a.down_suh + (size_t)it.e * a.I;
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            const int o = ob * 128 + lane * 4 + i;
-            float gv = g[i] * a.scale_gu * h2f(gsv[o]);
-            float uv = u[i] * a.scale_gu * h2f(usv[o]);
+            const int o = lane * 4 + i;
+            float gv = g[i] * a.scale_gu * h2f(mid_h[0][o]);
+            float uv = u[i] * a.scale_gu * h2f(mid_h[1][o]);
             if (a.clamp > 0.0f) {
                 gv = fminf(gv, a.clamp);
                 uv = fminf(fmaxf(uv, -a.clamp), a.clamp);
             }
-            h[i] = gv / (1.0f + expf(-gv)) * uv * h2f(dsu[o]);
+            h[i] = gv / (1.0f + expf(-gv)) * uv * h2f(mid_h[2][o]);
         }
         warp_hadamard128(h);
         uint16_t* dst = a.hprep + (size_t)slot_of[m] * a.I + ob * 128 + lane * 4;
@@ -378,6 +415,131 @@ __global__ void __launch_bounds__(kThreads, 3) moe_down_kernel(MoeArgs a) {
                 reduce_outputs4(a, r, ob * 128 + lane * 4);
             }
         }
+    }
+    cluster.sync();
+}
+
+// ------------------------------------------------------------------ 3'. one token: down + reduce
+// A one-token layer (direct work items): grid (D/128 output blocks, W items), clusters of the W
+// items of one output block.  Rank w runs item w's down GEMV over the whole intermediate (its
+// expert's weights stream before the dependency wait, as in moe_down), finishes it as moe_down
+// does (H128 of its sum, svh, the slot's score) into its own shared memory; rank 0 then adds the
+// live slots' blocks in k order over distributed shared memory, rounds and adds the shared term
+// (the shared item's block rounded, or the caller's shared row, gated): moe_reduce's arithmetic
+// with no per-slot planes and no arrival counters.  (The codebooks other than MCG need the
+// registers of two CTAs per SM here.)
+template <int KIND, int N>
+__global__ void __launch_bounds__(kThreads, KIND == K_MCG ? 3 : 2) moe_down1_kernel(MoeArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    cg::cluster_group cluster = cg::this_cluster();
+    const int ob = blockIdx.x;
+    const int w = blockIdx.y;  // the item, and the rank in the cluster
+    const int KB = a.I / 128;
+    const CoreSmem s = core_smem<N, 1, 1>(smem, KB, 1);
+    float* fin = s.red + 128;  // the finished block (row 1 of the reduction area: one row here)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int OT = a.D / 16;
+    const size_t per = (size_t)(a.I / 16) * OT * N;
+    core_init_barriers<N, 1, kConsumerWarps>(s);
+    grid_launch_dependents();
+    // Routing is complete here (moe_pair lets this grid launch after its own dependency wait):
+    // the item, its finish's svh values and score are read before this grid's wait.
+    // (kept in shared memory across the main loop, not in registers)
+    __shared__ __align__(16) float fin_sv[128];
+    __shared__ float fin_sc;
+    WorkItem it;
+    const bool has = work_item(a, w, it);
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        if (lane == 0 && has) {
+            const uint16_t* const tr[1] = {it.shx ? a.sh_down_tr : a.down_tr + (size_t)it.e * per};
+            core_produce<N, 1>(s, tr, OT, ob, 0, KB);
+        }
+    } else {
+        if (has && warp == 0) {
+            const uint16_t* dsv = it.shx ? a.sh_down_svh : a.down_svh + (size_t)it.e * a.D;
+            float sv[4];
+            load_half4(dsv, (size_t)ob * 128 + lane * 4, (reinterpret_cast<uintptr_t>(dsv) & 7) == 0, sv);
+            *reinterpret_cast<float4*>(fin_sv + lane * 4) = make_float4(sv[0], sv[1], sv[2], sv[3]);
+            if (lane == 0) fin_sc = (it.shx ? 1.0f : a.scores[w]) * a.scale_down;
+        }
+        const int hrow = has ? work_slot(a, w, it, 0) : 0;
+        grid_dependency_wait();  // the prepared rows come from moe_pair
+        if (has) {
+            const bool hvec = (reinterpret_cast<uintptr_t>(a.hprep) & 7) == 0;
+            for (int kbi = warp; kbi < KB; kbi += kConsumerWarps) {
+                const uint16_t* src = a.hprep + (size_t)hrow * a.I + kbi * 128 + lane * 4;
+                uint16_t h[4];
+                if (hvec) {
+                    const uint2 u = *reinterpret_cast<const uint2*>(src);
+                    h[0] = (uint16_t)u.x, h[1] = (uint16_t)(u.x >> 16), h[2] = (uint16_t)u.y, h[3] = (uint16_t)(u.y >> 16);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; i++) h[i] = src[i];
+                }
+                bfrag_put4<1>(s.bfrag, 1, kbi, 0, lane, h);
+            }
+            consumers_sync<kConsumerWarps>();
+            const DecParams dp[1] = {a.dp_down};
+            float acc[1][1][4];
+            core_consume<KIND, N, 1, 1, false, kConsumerWarps>(s, KB, dp, acc);
+            core_reduce<1, 1, kConsumerWarps>(s.red, acc);
+            consumers_sync<kConsumerWarps>();
+            if (warp == 0) {
+                // moe_down's finish of an unsplit block (0 + partial, as its one-rank cluster sum)
+                const float4 t = *reinterpret_cast<const float4*>(s.red + lane * 4);
+                float d[4] = {0.0f + t.x, 0.0f + t.y, 0.0f + t.z, 0.0f + t.w};
+                warp_hadamard128(d);
+                const float4 sv = *reinterpret_cast<const float4*>(fin_sv + lane * 4);
+                const float sc = fin_sc;
+                float4 f;
+                f.x = d[0] * sv.x * sc;
+                f.y = d[1] * sv.y * sc;
+                f.z = d[2] * sv.z * sc;
+                f.w = d[3] * sv.w * sc;
+                *reinterpret_cast<float4*>(fin + lane * 4) = f;
+            }
+        }
+    }
+
+    // Rank 0's sum: the live slots (a ballot over the slot ids, read before the barrier, as are
+    // the caller's shared row and the gate) loaded from every rank at once, added in k order.
+    const int d0 = ob * 128 + lane * 4;
+    unsigned live = 0u;
+    float sh[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float gate = 0.0f;
+    if (w == 0 && warp == 0) {
+        live = __ballot_sync(0xffffffffu, lane < a.K && a.inds[lane] - (uint32_t)a.e_lo < (uint32_t)a.E);
+        if (!a.sh_plane && a.shared) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) sh[i] = load_act(a.shared, d0 + i, a.xdt);
+        }
+        if (a.shared_gate) gate = load_act(a.shared_gate, 0, a.xdt);
+    }
+    cluster.sync();
+    if (w == 0 && warp == 0) {
+        float4 v[16];
+#pragma unroll
+        for (int k = 0; k < 16; k++)
+            if ((live >> k) & 1u) v[k] = *reinterpret_cast<const float4*>(cluster.map_shared_rank(fin, k) + lane * 4);
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (!((live >> k) & 1u)) continue;
+            acc[0] += v[k].x;
+            acc[1] += v[k].y;
+            acc[2] += v[k].z;
+            acc[3] += v[k].w;
+        }
+        if (a.sh_plane) {
+            const float4 s4 = *reinterpret_cast<const float4*>(cluster.map_shared_rank(fin, a.K) + lane * 4);
+            sh[0] = round_act(s4.x, a.xdt), sh[1] = round_act(s4.y, a.xdt), sh[2] = round_act(s4.z, a.xdt);
+            sh[3] = round_act(s4.w, a.xdt);
+        }
+        const bool has_sh = a.sh_plane || a.shared;
+#pragma unroll
+        for (int i = 0; i < 4; i++) store_act(a.y, d0 + i, a.xdt, routed_finish_g(acc[i], a.xdt, has_sh, sh[i], a.shared_gate != nullptr, gate));
     }
     cluster.sync();
 }

@@ -40,10 +40,14 @@ int three_per_sm_smem();
 // at 1 / 8 / 64 tokens, the 16-layer 7168/2048 stack within 1% at 1 token, 6% faster at 8 and 1%
 // at 64; taking three per SM also where S_min = 1 was no faster there and 3% slower on the stack
 // at 64 tokens.  More splits than needed pay the cluster reduce and per-CTA start-up more often.
+// Static shared memory of the chain kernels (slot ids, the pair finish's weights), counted against
+// the per-SM budget next to the dynamic carve-up.
+constexpr size_t kChainStaticSmem = 2048;
+
 template <int N, int NP>
 static int fit_split(int S, int KB, int mg) {
     S = S < KB ? S : KB;
-    const size_t three = (size_t)three_per_sm_smem(), two = (size_t)two_per_sm_smem();
+    const size_t three = (size_t)three_per_sm_smem() - kChainStaticSmem, two = (size_t)two_per_sm_smem() - kChainStaticSmem;
     if (S > 1)
         for (int c = S; c <= 16 && c <= KB; c++)
             if (core_layout<N, NP, 1>((KB + c - 1) / c, mg).total <= three) return c;
@@ -65,6 +69,30 @@ static cudaError_t launch_down_t(const MoeArgs& a, int S, int W_max, cudaStream_
     S = fit_split<N, 1>(S, KB, a.chunk);
     const CoreLayout L = core_layout<N, 1, 1>((KB + S - 1) / S, a.chunk);
     return launch_clustered(moe_down_kernel<KIND, N>, dim3(W_max, a.D / 128, S), S, L.total, stream, a);
+}
+
+// The one-token down + reduce (moe_down1): grid (D/128, W) in clusters of the W items.
+template <int KIND, int N>
+static cudaError_t launch_down1_t(const MoeArgs& a, int W, cudaStream_t stream) {
+    const CoreLayout L = core_layout<N, 1, 1>(a.I / 128, 1);
+    auto kern = moe_down1_kernel<KIND, N>;
+    const cudaError_t e = func_attrs((const void*)kern, (int)L.total, W > 8);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.D / 128, W, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = L.total;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = W;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 #define SX_MOE_N_LIST(X) \
@@ -95,6 +123,28 @@ cudaError_t moe_launch_kind(const MoeArgs& a, int n_gu, int n_d, int S_gu, int S
     }
 #undef SX_PAIR_CASE
 #undef SX_DOWN_CASE
+    return e;
+}
+
+// The one-token chain: moe_pair over the W direct items, then moe_down1.
+template <int KIND>
+cudaError_t moe_launch_kind_direct(const MoeArgs& a, int n_gu, int n_d, int S_gu, int W, cudaStream_t stream) {
+    cudaError_t e = cudaErrorInvalidValue;
+#define SX_PAIR_CASE(NN) \
+    case NN: e = launch_pair_t<KIND, NN>(a, S_gu, W, stream); break;
+#define SX_DOWN1_CASE(NN) \
+    case NN: e = launch_down1_t<KIND, NN>(a, W, stream); break;
+    if constexpr (KIND == K_PAIR1) {
+        switch (n_gu) { SX_MOE_N_LIST_PAIR1(SX_PAIR_CASE) default: return cudaErrorInvalidValue; }
+        if (e != cudaSuccess) return e;
+        switch (n_d) { SX_MOE_N_LIST_PAIR1(SX_DOWN1_CASE) default: return cudaErrorInvalidValue; }
+    } else {
+        switch (n_gu) { SX_MOE_N_LIST(SX_PAIR_CASE) default: return cudaErrorInvalidValue; }
+        if (e != cudaSuccess) return e;
+        switch (n_d) { SX_MOE_N_LIST(SX_DOWN1_CASE) default: return cudaErrorInvalidValue; }
+    }
+#undef SX_PAIR_CASE
+#undef SX_DOWN1_CASE
     return e;
 }
 

@@ -3,4 +3,5 @@
 
 namespace sx {
 template cudaError_t moe_launch_kind<K_PAIR1>(const MoeArgs&, int, int, int, int, int, cudaStream_t);
+template cudaError_t moe_launch_kind_direct<K_PAIR1>(const MoeArgs&, int, int, int, int, cudaStream_t);
 }  // namespace sx

@@ -46,14 +46,42 @@ __device__ __forceinline__ void warp_argmax_lowest(float& v, int& idx) {
 __device__ __forceinline__ void router_gate_partials(const void* gx, const void* gw, int gk, int dt, float* gp) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int groups = (gk + 1023) / 1024;
+    // The four chunks' x and w are loaded before any product (16-byte loads when both vectors
+    // start 16-byte aligned: a chunk is 8 elements at a multiple of 8), one round of loads.
+    const bool vec = ((reinterpret_cast<uintptr_t>(gx) | reinterpret_cast<uintptr_t>(gw)) & 15) == 0;
     for (int vs = warp - 1; vs < groups; vs += kRouterThreads / 32 - 1) {
         float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        for (int i = 0; i < 32; i += 8) {
-            const int idx = vs * 1024 + lane * 8 + i * 32;
+        float xv[4][8], wv[4][8];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int idx = vs * 1024 + lane * 8 + q * 256;
+            if (idx + 8 <= gk) {
+                if (vec) {
+                    const uint4 ux = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(gx) + idx);
+                    const uint4 uw = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(gw) + idx);
+                    const uint32_t px[4] = {ux.x, ux.y, ux.z, ux.w}, pw[4] = {uw.x, uw.y, uw.z, uw.w};
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const uint16_t hx = (uint16_t)(px[j >> 1] >> (16 * (j & 1)));
+                        const uint16_t hw = (uint16_t)(pw[j >> 1] >> (16 * (j & 1)));
+                        xv[q][j] = dt == 1 ? __half2float(__ushort_as_half(hx)) : __bfloat162float(__ushort_as_bfloat16(hx));
+                        wv[q][j] = dt == 1 ? __half2float(__ushort_as_half(hw)) : __bfloat162float(__ushort_as_bfloat16(hw));
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        xv[q][j] = load_act(gx, idx + j, dt);
+                        wv[q][j] = load_act(gw, idx + j, dt);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int idx = vs * 1024 + lane * 8 + q * 256;
             if (idx + 8 <= gk) {
 #pragma unroll
-                for (int j = 0; j < 8; j++)
-                    c[j & 3] = __fadd_rn(c[j & 3], __fmul_rn(load_act(gx, idx + j, dt), load_act(gw, idx + j, dt)));
+                for (int j = 0; j < 8; j++) c[j & 3] = __fadd_rn(c[j & 3], __fmul_rn(xv[q][j], wv[q][j]));
             }
         }
         float ga = __fadd_rn(__fadd_rn(__fadd_rn(c[0], c[1]), c[2]), c[3]);
@@ -84,6 +112,11 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(const void* __re
     const size_t lbase = (size_t)row * E;
     const bool sigmoid = mode != SX_ROUTER_SOFTMAX;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // Programmatic dependent launch: the next grid (a routed layer's first kernel, which waits for
+    // this grid before reading the picks) may start launching now; this grid waits for the one
+    // that wrote the logits before reading them.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     float lmax = -CUDART_INF_F;
     for (int e = tid; e < E; e += blockDim.x) {
@@ -96,6 +129,7 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(const void* __re
             wraw[e] = sg;
         } else {
             key[e] = l;
+            wraw[e] = l;  // the picked logits' weights read it back (the key is masked when picked)
             lmax = fmaxf(lmax, l);
         }
     }
@@ -155,30 +189,79 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(const void* __re
         __syncwarp();
     }
 
-    for (int r = 0; r < K; r++) {
-        float best = -CUDART_INF_F;
-        int bidx = 0x7fffffff;
-        for (int e = lane; e < E; e += 32) {
-            const float v = key[e];
-            if (v > best) {
-                best = v;
-                bidx = e;
+    // k rounds of "max, then mask", ties to the lowest id.  Each key becomes an order-preserving
+    // integer (-inf and NaN: 0, never picked, as they lose every strict comparison; -0 as +0); a
+    // round is a warp max over the lanes' best keys and a warp min over the ids holding it (one
+    // redux each), and only the lane that held the pick rescans its keys.  With no key left the
+    // pick is the last expert, as the comparison form gives.  Up to 512 experts a lane holds its
+    // keys (e = lane + 32 i) in registers, so a rescan is a run of compares with no loads.
+    auto ordered = [](float v) -> uint32_t {
+        if (!(v > -CUDART_INF_F)) return 0u;  // -inf, NaN
+        const uint32_t u = v == 0.0f ? 0u : __float_as_uint(v);
+        return (u >> 31) ? ~u : (u | 0x80000000u);
+    };
+    uint32_t bk;
+    int bi;
+    if (E <= 512) {
+        uint32_t kv[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) kv[i] = lane + 32 * i < E ? ordered(key[lane + 32 * i]) : 0u;
+        auto rescan = [&]() {
+            bk = 0u;
+            bi = 0x7fffffff;
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                if (kv[i] > bk) {
+                    bk = kv[i];
+                    bi = lane + 32 * i;
+                }
+            }
+        };
+        rescan();
+        for (int r = 0; r < K; r++) {
+            const uint32_t top = __reduce_max_sync(0xffffffffu, bk);
+            int pick = (int)__reduce_min_sync(0xffffffffu, (top != 0u && bk == top) ? (uint32_t)bi : 0xffffffffu);
+            if (top == 0u) pick = E - 1;
+            if (lane == 0) sel[r] = pick;
+            if (lane == (pick & 31)) {
+#pragma unroll
+                for (int i = 0; i < 16; i++)
+                    if (lane + 32 * i == pick) kv[i] = 0u;
+                rescan();
             }
         }
-        warp_argmax_lowest(best, bidx);
-        if (bidx >= E) bidx = E - 1;
-        if (lane == 0) {
-            sel[r] = bidx;
-            key[bidx] = -CUDART_INF_F;
+    } else {
+        auto lane_best = [&]() {
+            bk = 0u;
+            bi = 0x7fffffff;
+            for (int e = lane; e < E; e += 32) {
+                const uint32_t k = ordered(key[e]);
+                if (k > bk) {
+                    bk = k;
+                    bi = e;
+                }
+            }
+        };
+        lane_best();
+        for (int r = 0; r < K; r++) {
+            const uint32_t top = __reduce_max_sync(0xffffffffu, bk);
+            int pick = (int)__reduce_min_sync(0xffffffffu, (top != 0u && bk == top) ? (uint32_t)bi : 0xffffffffu);
+            if (top == 0u) pick = E - 1;
+            if (lane == 0) sel[r] = pick;
+            if (lane == (pick & 31)) {
+                key[pick] = -CUDART_INF_F;
+                lane_best();
+            }
+            __syncwarp();
         }
-        __syncwarp();
     }
+    __syncwarp();
 
     float w = 0.0f;
     int myidx = 0;
     if (lane < K) {
         myidx = sel[lane];
-        w = sigmoid ? wraw[myidx] : expf(load_act(logits, lbase + myidx, ldt) - smax) * snorm;
+        w = sigmoid ? wraw[myidx] : expf(wraw[myidx] - smax) * snorm;
     }
     float tot = 0.0f;
     for (int j = 0; j < K; j++) tot += __shfl_sync(0xffffffffu, w, j);
@@ -224,10 +307,20 @@ sx_status router_launch(sx_stream stream, const void* logits, sx_dtype ldt, cons
             return SX_ERR_ROUTER_DECLINED;
     }
     const size_t smem = (size_t)2 * experts * sizeof(float);
-    router_kernel<<<rows, kRouterThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
-        logits, (int)ldt, bias, experts, k, mode, renorm, scale, n_group, topk_group, inds, scores, gx, gw, gk,
-        (int)gdt, glogit);
-    return cuda_status(cudaGetLastError(), "router launch");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(rows, 1, 1);
+    cfg.blockDim = dim3(kRouterThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, router_kernel, logits, (int)ldt, bias, (int)experts, (int)k, (int)mode,
+                                          (int)renorm, scale, (int)n_group, (int)topk_group, inds, scores, gx, gw,
+                                          (int)gk, (int)gdt, glogit),
+                       "router launch");
 }
 
 }  // namespace

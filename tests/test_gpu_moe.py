@@ -317,6 +317,53 @@ def test_moe_wide_hidden_decode_chain(sx):
     assert sx.device_error() == 0
 
 
+@pytest.mark.parametrize("k,folded", [(15, True), (16, True), (16, False), (10, True)])
+def test_moe_one_token_items(sx, k, folded):
+    """One token: its k slots (and a folded shared expert) are the decode chain's work items and a
+    cluster of them per output block reduces in k order (up to 16 items); 17 items take the routed
+    chain.  Both against the f64 truth of the routed sum plus the shared expert."""
+    E, D, I, T = 40, 512, 256, 1
+    bank_np = _bank(800 + k, E, D, I, 32, 32)
+    sh_np = _bank(900 + k, 1, D, I, 32, 32)
+    oargs, dec = dec_args(orc.CB_MCG, 16)
+    x = synth.activations(k, T, D)
+    inds, wts = _route(k + 1, T, E, k)
+    xt = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    b, shb = _sx_bank(sx, bank_np), _sx_bank(sx, sh_np)
+    ii, ww = torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda()
+    xf = xt.float().cpu().numpy()
+    truth = _truth(bank_np, D, I, 32, 32, oargs, xf, inds, wts)
+    if folded:
+        y = to_f32(sx.moe_folded(xt, b, shb, ii, ww, dec))
+        sh_e = tuple(tuple(a[None] for a in proj) for proj in sh_np)  # (one-expert packs come squeezed)
+        truth = truth + _truth(sh_e, D, I, 32, 32, oargs, xf, np.zeros((T, 1), np.int32), np.ones((T, 1), np.float32))
+    else:
+        y = to_f32(sx.moe(xt, b, ii, ww, dec))
+    torch.cuda.synchronize()
+    assert sx.device_error() == 0
+    assert max_rel(y, truth) <= MAX_REL_TOL, max_rel(y, truth)
+    assert rel_rms(y, truth) <= REL_RMS_TOL, rel_rms(y, truth)
+
+
+def test_moe_one_token_skips_slots_outside_the_bank(sx):
+    """A one-token layer whose slots name ids past the bank (another rank's experts, sentinels)
+    leaves those slots out of the sum, as the routed chain does."""
+    E, D, I, k, T = 16, 256, 128, 6, 1
+    bank_np = _bank(55, E, D, I, 32, 32)
+    oargs, dec = dec_args(orc.CB_MCG, 16)
+    x = synth.activations(56, T, D)
+    inds, wts = _route(57, T, E, k)
+    inds[0, 1] = E
+    inds[0, 4] = E + 100
+    xt = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    y = to_f32(sx.moe(xt, _sx_bank(sx, bank_np), torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda(), dec))
+    live = [j for j in range(k) if inds[0, j] < E]
+    truth = _truth(bank_np, D, I, 32, 32, oargs, xt.float().cpu().numpy(), inds[:, live], wts[:, live])
+    torch.cuda.synchronize()
+    assert sx.device_error() == 0
+    assert max_rel(y, truth) <= MAX_REL_TOL, max_rel(y, truth)
+
+
 def _unfused(sx, x, bank, shb, inds, wts, dec, gate, shared_dec=None, ragged=False, clamp=0):
     """The composition sx_moe_folded replaces: the shared expert as its own one-expert layer, its
     output passed to the routed layer."""
