@@ -422,9 +422,10 @@ sx_status sx_ep_reserve_peer(sx_ep* ep, size_t bytes);
 /* The reserved peer-buffer bytes (0: the NCCL transport). */
 size_t sx_ep_peer_reserved(const sx_ep* ep);
 
-/* Phase timing of the communicator's calls (diagnostics; not for calls recorded in a CUDA graph):
- * with `enable`, every sx_ep_moe* call records CUDA events on its stream at its phase boundaries,
- * and sx_ep_phase_ms gives the last call's six phase durations in ms (waiting for its end):
+/* Phase timing of the communicator's calls (diagnostics): with `enable`, every sx_ep_moe* call
+ * records CUDA events on its stream at its phase boundaries (external event records, so a call
+ * recorded in a CUDA graph records them at each replay), and sx_ep_phase_ms gives the last
+ * recorded call's six phase durations in ms (waiting for its end):
  *   [0] plan + dispatch (peer: the row stores; NCCL: the send blocks' gather)
  *   [1] peer: waiting for every rank's rows; NCCL: the dispatch all-to-all
  *   [2] the local experts over the received rows

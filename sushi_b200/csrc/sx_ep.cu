@@ -228,7 +228,11 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(CombineArgs a) {
 //   recv_slots[g]        the slots of those rows on this rank's experts
 //   disp_done[g], red_done  this rank's own CTA counters (last CTA signals), reset by that CTA
 constexpr int kCtrlSeq = 0, kCtrlDispFlag = kPeerMax, kCtrlCombFlag = 2 * kPeerMax, kCtrlRecvCnt = 3 * kPeerMax,
-              kCtrlRecvSlots = 4 * kPeerMax, kCtrlDispDone = 5 * kPeerMax, kCtrlRedDone = 6 * kPeerMax;
+              kCtrlRecvSlots = 4 * kPeerMax, kCtrlDispDone = 5 * kPeerMax, kCtrlRedDone = 6 * kPeerMax,
+              kCtrlPlanDone = 6 * kPeerMax + 1;
+// Up to this many rows per rank one kernel plans and dispatches (each CTA of a destination
+// recomputes that destination's list, which costs little at these sizes, and stores its share).
+constexpr int kFusedDispatchRows = 64;
 // From this many rows per rank a call reads the received counts back to the host (one host
 // synchronisation) and sizes the expert chain's launches to the rows and slots it received; below
 // it the launches are sized for every place and the call never waits on the host.
@@ -265,33 +269,12 @@ struct PeerArgs {
 
 __device__ __forceinline__ uint32_t* ctrl(uint8_t* base) { return reinterpret_cast<uint32_t*>(base); }
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// Waits until *flag >= seq (wrap-safe), for at most ~2 s of wall time; on a timeout latches
-// DEV_TIMEOUT_PEER and returns false (the caller goes on: its outputs are undefined, nothing hangs).
-__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t seq) {
-    if ((int32_t)(ld_acquire_sys(flag) - seq) >= 0) return true;
-    const uint64_t t0 = global_timer_ns();
-    for (uint32_t i = 0;; i++) {
-        __nanosleep(64);
-        if ((int32_t)(ld_acquire_sys(flag) - seq) >= 0) return true;
-        if ((i & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
-            latch_error(DEV_TIMEOUT_PEER);
-            return false;
-        }
-    }
 }
 
 // The last of `total` CTAs to arrive on `counter` (a word of this rank's own control block)
@@ -376,6 +359,66 @@ __global__ void __launch_bounds__(256) ep_peer_dispatch_kernel(EpArgs a, const i
         st_relaxed_sys(&ctrl(dst)[kCtrlRecvSlots + p.me], (uint32_t)cnt[a.world + d]);
         __threadfence_system();
         st_release_sys(&ctrl(dst)[kCtrlDispFlag + p.me], seq);
+    }
+}
+
+// Plan and dispatch in one kernel for small calls (grid: B x G blocks; rows <= 256): CTA (x, d)
+// computes destination d's list and slot count (x == 0 also writes the places the combine reads),
+// stores its share of the list's rows and slots into d's receive region, and arrives on d's
+// counter; the last to arrive stores the counts and raises d's flag.  The call's number is read
+// by every CTA before it arrives, and the last CTA of the grid advances it.
+__global__ void __launch_bounds__(256) ep_peer_plan_dispatch_kernel(EpArgs a, PeerArgs p) {
+    __shared__ int list[256];
+    __shared__ int warp_sums[8];
+    __shared__ int slot_sum;
+    const int d = blockIdx.y;
+    uint32_t* c = ctrl(p.base[p.me]);
+    uint8_t* dst = p.base[d];
+    const uint32_t seq = c[kCtrlSeq] + 1u;
+    if (threadIdx.x == 0) slot_sum = 0;
+    const int r = threadIdx.x;
+    int flag = 0, slots = 0;
+    if (r < a.rows) {
+        for (int k = 0; k < a.K; k++) {
+            const uint32_t e = a.inds[(size_t)r * a.K + k];
+            if (e < (uint32_t)a.Etot && (int)(e / (uint32_t)a.El) == d) {
+                flag = 1;
+                slots++;
+            }
+        }
+    }
+    int n;
+    const int idx = block_scan_256(flag, warp_sums, &n);
+    if (flag) list[idx] = r;
+    if (slots) atomicAdd(&slot_sum, slots);
+    if (blockIdx.x == 0 && r < a.rows) a.pos[(size_t)r * a.world + d] = flag ? idx : -1;
+    __syncthreads();
+    const size_t row_bytes = (size_t)a.D * a.esz;
+    const size_t slot0 = (size_t)p.me * a.cap;
+    uint32_t* ids = reinterpret_cast<uint32_t*>(dst + p.lay.recv_ids);
+    float* sc = reinterpret_cast<float*>(dst + p.lay.recv_sc);
+    for (int i = blockIdx.x; i < n; i += gridDim.x) {
+        const int rr = list[i];
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.x) + (size_t)rr * row_bytes);
+        uint4* out = reinterpret_cast<uint4*>(dst + p.lay.recv_x + (slot0 + i) * row_bytes);
+        for (size_t v = threadIdx.x; v < row_bytes / 16; v += blockDim.x) out[v] = src[v];
+        for (int k = threadIdx.x; k < a.K; k += blockDim.x) {
+            const uint32_t e = a.inds[(size_t)rr * a.K + k];
+            const bool here = e < (uint32_t)a.Etot && (int)(e / (uint32_t)a.El) == d;
+            ids[(slot0 + i) * a.K + k] = here ? e - (uint32_t)(d * a.El) : kSentinel;
+            sc[(slot0 + i) * a.K + k] = here ? a.scores[(size_t)rr * a.K + k] : 0.0f;
+        }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (last_to_arrive(&c[kCtrlDispDone + d], gridDim.x)) {
+            st_relaxed_sys(&ctrl(dst)[kCtrlRecvCnt + p.me], (uint32_t)n);
+            st_relaxed_sys(&ctrl(dst)[kCtrlRecvSlots + p.me], (uint32_t)slot_sum);
+            __threadfence_system();
+            st_release_sys(&ctrl(dst)[kCtrlDispFlag + p.me], seq);
+        }
+        if (last_to_arrive(&c[kCtrlPlanDone], gridDim.x * gridDim.y)) c[kCtrlSeq] = seq;
     }
 }
 
@@ -811,9 +854,14 @@ size_t sx_ep_ragged_workspace_bytes(const sx_ep* ep, const sx_ragged* local, int
 namespace sx {
 namespace {
 
-// Records phase boundary i of the call on `s` when phase timing is on.
+// Records phase boundary i of the call on `s` when phase timing is on: a plain record, or during
+// stream capture an external one (the graph records it at each replay).
 void mark(sx_ep* ep, int i, cudaStream_t s) {
-    if (ep->timing) cudaEventRecord(ep->phase[i], s);
+    if (!ep->timing) return;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cs) != cudaSuccess) cs = cudaStreamCaptureStatusNone;
+    if (cs == cudaStreamCaptureStatusActive) cudaEventRecordWithFlags(ep->phase[i], s, cudaEventRecordExternal);
+    else cudaEventRecord(ep->phase[i], s);
 }
 
 // The peer transport's call after the admission checks and the shared-expert fork: plan,
@@ -837,22 +885,33 @@ sx_status ep_peer_moe(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int n
     int* cnt = reinterpret_cast<int*>(ws + L.cnt);
 
     mark(ep, 0, s);
-    ep_peer_plan_kernel<<<G, 256, 0, s>>>(a, cnt, reinterpret_cast<uint32_t*>(own));
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_status(e, "ep peer plan launch");
-    const int B = std::max(1, std::min(C, std::max(4, 8 * sm_count() / G)));
-    ep_peer_dispatch_kernel<<<dim3(B, G), 256, 0, s>>>(a, cnt, pa);
-    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "ep peer dispatch launch");
+    cudaError_t e = cudaSuccess;
+    if (C <= kFusedDispatchRows) {
+        const int B = std::max(1, std::min(C, 8));
+        ep_peer_plan_dispatch_kernel<<<dim3(B, G), 256, 0, s>>>(a, pa);
+        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "ep peer plan+dispatch launch");
+    } else {
+        ep_peer_plan_kernel<<<G, 256, 0, s>>>(a, cnt, reinterpret_cast<uint32_t*>(own));
+        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "ep peer plan launch");
+        const int B = std::max(1, std::min(C, std::max(4, 8 * sm_count() / G)));
+        ep_peer_dispatch_kernel<<<dim3(B, G), 256, 0, s>>>(a, cnt, pa);
+        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "ep peer dispatch launch");
+    }
     sx_status st = fork_side();  // the shared expert on the side stream (large calls)
     if (st) return st;
     mark(ep, 1, s);
-    ep_peer_recv_wait_kernel<<<1, 128, 0, s>>>(pa, G);
-    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "ep peer wait launch");
+    // The wait for every rank's rows: its own kernel when the counts come back to the host, else
+    // the first thing route_prep does (MoeSegments::wait_flags).
+    const bool host_sized = C >= kHostSizedRows;
+    if (host_sized) {
+        ep_peer_recv_wait_kernel<<<1, 128, 0, s>>>(pa, G);
+        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "ep peer wait launch");
+    }
 
     // Large calls: the received counts come back to the host, and the chain's launches are sized
     // to them (the places' bound would launch mostly idle CTAs once rows_cap x world is large).
     long long live_rows = (long long)places, live_slots = -1;
-    if (C >= kHostSizedRows) {
+    if (host_sized) {
         e = cudaMemcpyAsync(ep->host_counts, own + kCtrlRecvCnt * sizeof(uint32_t), 2 * kPeerMax * sizeof(uint32_t),
                             cudaMemcpyDeviceToHost, s);
         if (e == cudaSuccess) e = cudaStreamSynchronize(s);
@@ -865,7 +924,9 @@ sx_status ep_peer_moe(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int n
         live_slots = std::min(live_slots, live_rows * topk);
     }
     mark(ep, 2, s);
-    const MoeSegments seg{reinterpret_cast<const int*>(own) + kCtrlRecvCnt, C, G, live_slots};
+    const MoeSegments seg{reinterpret_cast<const int*>(own) + kCtrlRecvCnt, C, G, live_slots,
+                          host_sized ? nullptr : reinterpret_cast<const uint32_t*>(own) + kCtrlDispFlag,
+                          reinterpret_cast<const uint32_t*>(own) + kCtrlSeq};
     const uint32_t* ids = reinterpret_cast<const uint32_t*>(own + PL.recv_ids);
     float* yslot = nullptr;
     // the shared expert over this rank's own rows rides the local chain (fold_bank, small calls)

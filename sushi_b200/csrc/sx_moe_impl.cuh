@@ -426,10 +426,10 @@ __global__ void __launch_bounds__(kThreads, 3) moe_down_kernel(MoeArgs a) {
 // does (H128 of its sum, svh, the slot's score) into its own shared memory; rank 0 then adds the
 // live slots' blocks in k order over distributed shared memory, rounds and adds the shared term
 // (the shared item's block rounded, or the caller's shared row, gated): moe_reduce's arithmetic
-// with no per-slot planes and no arrival counters.  (The codebooks other than MCG need the
-// registers of two CTAs per SM here.)
+// with no per-slot planes and no arrival counters.  (The codebooks other than MCG, and MCG above
+// 6 bits per weight, need the registers of two CTAs per SM here.)
 template <int KIND, int N>
-__global__ void __launch_bounds__(kThreads, KIND == K_MCG ? 3 : 2) moe_down1_kernel(MoeArgs a) {
+__global__ void __launch_bounds__(kThreads, KIND == K_MCG && N <= 96 ? 3 : 2) moe_down1_kernel(MoeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     cg::cluster_group cluster = cg::this_cluster();
     const int ob = blockIdx.x;

@@ -571,7 +571,8 @@ class ExpertParallel:
     PHASES = ("plan_dispatch", "wait_rows", "local_experts", "reduce_push", "shared_join", "combine")
 
     def phase_timing(self, enable: bool = True):
-        """sx_ep_phase_timing: CUDA events at each call's phase boundaries (not under graph capture)."""
+        """sx_ep_phase_timing: CUDA events at each call's phase boundaries (recorded at each graph
+        replay when the call is captured)."""
         _check(lib().sx_ep_phase_timing(self._h, 1 if enable else 0))
 
     def phase_ms(self) -> dict:

@@ -305,6 +305,44 @@ def test_ep_peer_world1_graph_replays(sx):
         ep.destroy()
 
 
+def test_ep_phase_timing_eager_and_in_a_graph(sx):
+    """sx_ep_phase_timing: an eager call records its phase events as plain records, a captured call
+    as the graph's external records; either way sx_ep_phase_ms gives six finite, non-negative
+    durations and the results stay sx_moe's."""
+    E, D, I, k, T = 16, 256, 128, 4, 2
+    bank_np = _bank_np(620, E, D, I, 32)
+    _, dec = dec_args(orc.CB_MCG, 16)
+    b = _bank(sx, bank_np)
+    inds, wts = _route(621, T, E, k)
+    ii, ww = torch.from_numpy(inds).cuda(), torch.from_numpy(wts).cuda()
+    x = torch.from_numpy(synth.activations(622, T, D)).cuda().to(torch.bfloat16)
+    ep = sx.ExpertParallel(sx.ExpertParallel.unique_id(), 1, 0, "peer")
+    stream = torch.cuda.Stream()
+    try:
+        with torch.cuda.stream(stream):
+            ep.phase_timing(True)
+            y = ep.moe(x, b, E, ii, ww, dec, rows_cap=T)
+            eager = ep.phase_ms()
+            assert torch.equal(y, sx.moe(x, b, ii, ww, dec))
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                y2 = ep.moe(x, b, E, ii, ww, dec, rows_cap=T)
+            g.replay()
+            graphed = ep.phase_ms()
+            torch.cuda.synchronize()
+            assert torch.equal(y2, sx.moe(x, b, ii, ww, dec))
+            ep.phase_timing(False)
+            del g
+        for ph in (eager, graphed):
+            assert set(ph) == set(sx.ExpertParallel.PHASES)
+            assert all(np.isfinite(v) and v >= 0.0 for v in ph.values()), ph
+        assert sx.device_error() == 0
+    finally:
+        torch.cuda.synchronize()
+        ep.destroy()
+
+
 def test_ep_peer_reservation_grows_and_releases(sx):
     """A call larger than the reservation grows it (a collective step of the communicator); a
     reservation of 0 returns the communicator to the NCCL transport; results stay sx_moe's."""
