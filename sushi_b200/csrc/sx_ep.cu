@@ -18,6 +18,7 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <utility>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -269,6 +270,14 @@ struct PeerArgs {
 
 __device__ __forceinline__ uint32_t* ctrl(uint8_t* base) { return reinterpret_cast<uint32_t*>(base); }
 
+// Programmatic dependent launch of the peer kernels: the next kernel of the stream may start its
+// launch at once; this one waits for its predecessor's completion before any global access (so
+// the order of calls, and of the peer-buffer reuse that follows from it, is the stream order).
+__device__ __forceinline__ void ep_pdl_enter() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -277,12 +286,18 @@ __device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// A CTA's stores (peer ones included) become visible at system scope before its arrival: called
+// by thread 0 after a block barrier that follows the CTA's stores, one system fence for the whole
+// CTA (the barrier orders the other threads' stores before it), as a flag protocol over NVLink
+// needs no fence per thread.
+__device__ __forceinline__ void cta_stores_released() { __threadfence_system(); }
+
 // The last of `total` CTAs to arrive on `counter` (a word of this rank's own control block)
-// returns true, with every arriving CTA's earlier stores (peer ones included) visible at system
-// scope first; it resets the counter for the next call.  Called by thread 0 after a block barrier
-// that follows every thread's __threadfence_system().
+// returns true, after every arriving CTA's stores (each released by cta_stores_released before its
+// arrival) are ordered before its own later stores; it resets the counter for the next call.  One
+// CTA arrives last without an atomic.  Called by thread 0 after cta_stores_released().
 __device__ __forceinline__ bool last_to_arrive(uint32_t* counter, uint32_t total) {
-    __threadfence_system();
+    if (total == 1) return true;
     const uint32_t prev = atomicAdd(counter, 1u);
     if (prev + 1 != total) return false;
     __threadfence_system();
@@ -352,13 +367,14 @@ __global__ void __launch_bounds__(256) ep_peer_dispatch_kernel(EpArgs a, const i
             sc[(slot0 + i) * a.K + k] = here ? a.scores[(size_t)r * a.K + k] : 0.0f;
         }
     }
-    __threadfence_system();
     __syncthreads();
-    if (threadIdx.x == 0 && last_to_arrive(&ctrl(p.base[p.me])[kCtrlDispDone + d], gridDim.x)) {
-        st_relaxed_sys(&ctrl(dst)[kCtrlRecvCnt + p.me], (uint32_t)n);
-        st_relaxed_sys(&ctrl(dst)[kCtrlRecvSlots + p.me], (uint32_t)cnt[a.world + d]);
-        __threadfence_system();
-        st_release_sys(&ctrl(dst)[kCtrlDispFlag + p.me], seq);
+    if (threadIdx.x == 0) {
+        cta_stores_released();
+        if (last_to_arrive(&ctrl(p.base[p.me])[kCtrlDispDone + d], gridDim.x)) {
+            st_relaxed_sys(&ctrl(dst)[kCtrlRecvCnt + p.me], (uint32_t)n);
+            st_relaxed_sys(&ctrl(dst)[kCtrlRecvSlots + p.me], (uint32_t)cnt[a.world + d]);
+            st_release_sys(&ctrl(dst)[kCtrlDispFlag + p.me], seq);  // the counts and rows before the flag
+        }
     }
 }
 
@@ -371,6 +387,7 @@ __global__ void __launch_bounds__(256) ep_peer_plan_dispatch_kernel(EpArgs a, Pe
     __shared__ int list[256];
     __shared__ int warp_sums[8];
     __shared__ int slot_sum;
+    ep_pdl_enter();
     const int d = blockIdx.y;
     uint32_t* c = ctrl(p.base[p.me]);
     uint8_t* dst = p.base[d];
@@ -409,16 +426,21 @@ __global__ void __launch_bounds__(256) ep_peer_plan_dispatch_kernel(EpArgs a, Pe
             sc[(slot0 + i) * a.K + k] = here ? a.scores[(size_t)rr * a.K + k] : 0.0f;
         }
     }
-    __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
+        cta_stores_released();
         if (last_to_arrive(&c[kCtrlDispDone + d], gridDim.x)) {
             st_relaxed_sys(&ctrl(dst)[kCtrlRecvCnt + p.me], (uint32_t)n);
             st_relaxed_sys(&ctrl(dst)[kCtrlRecvSlots + p.me], (uint32_t)slot_sum);
-            __threadfence_system();
-            st_release_sys(&ctrl(dst)[kCtrlDispFlag + p.me], seq);
+            st_release_sys(&ctrl(dst)[kCtrlDispFlag + p.me], seq);  // the counts and rows before the flag
         }
-        if (last_to_arrive(&c[kCtrlPlanDone], gridDim.x * gridDim.y)) c[kCtrlSeq] = seq;
+        // every CTA read the call's number before arriving: the last one advances it (later
+        // kernels of the stream read it)
+        if (atomicAdd(&c[kCtrlPlanDone], 1u) + 1 == gridDim.x * gridDim.y) {
+            __threadfence();  // after every CTA's read of the number (each fenced before arriving)
+            c[kCtrlPlanDone] = 0;
+            c[kCtrlSeq] = seq;
+        }
     }
 }
 
@@ -441,6 +463,7 @@ struct ReducePushArgs {
 
 __global__ void __launch_bounds__(128) ep_peer_reduce_push_kernel(ReducePushArgs a, PeerArgs p) {
     __shared__ int pre[kPeerMax + 1];
+    ep_pdl_enter();
     uint32_t* c = ctrl(p.base[p.me]);
     const uint32_t seq = c[kCtrlSeq];
     if (threadIdx.x == 0) {
@@ -474,10 +497,11 @@ __global__ void __launch_bounds__(128) ep_peer_reduce_push_kernel(ReducePushArgs
         float* dst = reinterpret_cast<float*>(p.base[g] + p.lay.part) + ((size_t)p.me * a.cap + i) * a.D + d;
         *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
     }
-    __threadfence_system();
     __syncthreads();
-    if (threadIdx.x == 0 && last_to_arrive(&c[kCtrlRedDone], gridDim.x)) {
-        for (int g = 0; g < a.world; g++) st_release_sys(&ctrl(p.base[g])[kCtrlCombFlag + p.me], seq);
+    if (threadIdx.x == 0) {
+        cta_stores_released();
+        if (last_to_arrive(&c[kCtrlRedDone], gridDim.x))
+            for (int g = 0; g < a.world; g++) st_release_sys(&ctrl(p.base[g])[kCtrlCombFlag + p.me], seq);
     }
 }
 
@@ -485,6 +509,7 @@ __global__ void __launch_bounds__(128) ep_peer_reduce_push_kernel(ReducePushArgs
 // rank's partials of this call, then as ep_combine_kernel with the partials in this rank's part
 // region ([g][place]).
 __global__ void __launch_bounds__(256) ep_peer_combine_kernel(CombineArgs a, PeerArgs p) {
+    ep_pdl_enter();
     uint32_t* c = ctrl(p.base[p.me]);
     const uint32_t seq = c[kCtrlSeq];
     if (threadIdx.x < 32)
@@ -854,6 +879,21 @@ size_t sx_ep_ragged_workspace_bytes(const sx_ep* ep, const sx_ragged* local, int
 namespace sx {
 namespace {
 
+// A peer kernel launched with programmatic dependent launch (its first act: ep_pdl_enter).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ep(void (*kern)(KArgs...), dim3 grid, int threads, cudaStream_t s, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(threads, 1, 1);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // Records phase boundary i of the call on `s` when phase timing is on: a plain record, or during
 // stream capture an external one (the graph records it at each replay).
 void mark(sx_ep* ep, int i, cudaStream_t s) {
@@ -888,8 +928,8 @@ sx_status ep_peer_moe(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int n
     cudaError_t e = cudaSuccess;
     if (C <= kFusedDispatchRows) {
         const int B = std::max(1, std::min(C, 8));
-        ep_peer_plan_dispatch_kernel<<<dim3(B, G), 256, 0, s>>>(a, pa);
-        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "ep peer plan+dispatch launch");
+        if ((e = launch_ep(ep_peer_plan_dispatch_kernel, dim3(B, G), 256, s, a, pa)) != cudaSuccess)
+            return cuda_status(e, "ep peer plan+dispatch launch");
     } else {
         ep_peer_plan_kernel<<<G, 256, 0, s>>>(a, cnt, reinterpret_cast<uint32_t*>(own));
         if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "ep peer plan launch");
@@ -943,8 +983,8 @@ sx_status ep_peer_moe(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int n
     const ReducePushArgs rp{yslot, ids, G, C, topk, D, El};
     const long long units = std::max(1LL, live_rows) * ((D + 511) / 512);
     const int grid = (int)std::max(1LL, std::min(units, (long long)8 * sm_count()));
-    ep_peer_reduce_push_kernel<<<grid, 128, 0, s>>>(rp, pa);
-    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "ep peer reduce launch");
+    if ((e = launch_ep(ep_peer_reduce_push_kernel, dim3(grid), 128, s, rp, pa)) != cudaSuccess)
+        return cuda_status(e, "ep peer reduce launch");
     mark(ep, 4, s);
 
     if ((st = join(SX_OK))) return st;
@@ -960,8 +1000,7 @@ sx_status ep_peer_moe(sx_ep* ep, sx_stream stream, const MoeGroup* groups, int n
     c.D = D;
     c.world = G;
     c.xdt = dtype;
-    ep_peer_combine_kernel<<<std::max(rows, 1), 256, 0, s>>>(c, pa);
-    e = cudaGetLastError();
+    e = launch_ep(ep_peer_combine_kernel, dim3(std::max(rows, 1)), 256, s, c, pa);
     mark(ep, 6, s);
     return cuda_status(e, "ep peer combine launch");
 }

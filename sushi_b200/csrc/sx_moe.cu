@@ -420,6 +420,14 @@ int min_split(long long units) {
     return (int)std::max(1LL, std::min(16LL, S));
 }
 
+// Direct items of an expert-parallel rank's call at most (a few tokens per rank: every received
+// slot one item, most of them other ranks' sentinels that exit at once), and the down launch's
+// items x output blocks at most: past that the dead items' CTAs cost more than the routing pass
+// (measured at two GPUs: the 7168-wide DeepSeek layers at 8 tokens per rank, 7168 CTAs per
+// group, took 20.7 ms per stack against 15.1 routed).
+constexpr long long kDirectEpItems = 512;
+constexpr long long kDirectEpCtas = 2048;
+
 // The pair and down launches of the decode chain over `items` work items.
 cudaError_t chain_launch(const MoeArgs& a, int kind, int n_gu, int n_d, int items, int active, cudaStream_t s) {
     const int S_gu = min_split((long long)active * (a.I / 128));
@@ -619,6 +627,24 @@ sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_de
     // One token on the decode chain with the reduce folded (one group, no expert-parallel
     // segments, at most 16 items): the token's slots are the work items, so no routing pass runs,
     // and moe_down1 reduces over a cluster of the items.
+    // An expert-parallel rank's small call (launches sized for every place, no host-read counts):
+    // every received slot is a direct item (dead ones exit at once), no routing pass; moe_down
+    // writes the per-slot planes the rank's reduce reads.  The k splits are the ones the routed
+    // chain would take (its active items and chunk), so the per-slot arithmetic is the same: a
+    // world of one gives sx_moe's bits.
+    const long long ep_items = (long long)rows * topk + (fold ? sh_rows : 0);
+    if (seg && seg->wait_flags && !reduce && !L.gemm && ep_items <= kDirectEpItems &&
+        ep_items * (D / 128) <= kDirectEpCtas) {
+        const int routed_active = L.A_max + a.sh_items;
+        a.split_chunk = a.chunk;
+        a.direct = 1;
+        a.chunk = 1;
+        a.w_routed = rows * topk;
+        a.sh_items = fold ? sh_rows : 0;
+        a.sh_slot0 = rows * topk;
+        e = chain_launch(a, kind_gu, bank->gate.n, bank->down.n, (int)ep_items, routed_active, s);
+        return e == cudaSuccess ? SX_OK : cuda_status(e, "moe expert-parallel direct chain launch");
+    }
     const int direct_items = topk + (fold ? 1 : 0);
     if (rows == 1 && a.rcount && !seg && !fold_rows && direct_items <= 16) {
         a.direct = 1;

@@ -55,6 +55,7 @@ struct MoeArgs {
     void* y;                // [R][D] x dtype
     float* partial;         // [R][D] f32: when set, the k-order sum lands here unrounded (no shared)
     int chunk;              // rows per work item: 2 or 8 (decode chain) or kGemmRows (tensor-core path)
+    int split_chunk;        // when set, the chunk the k splits are fitted for (direct items taking the routed chain's splits)
     int big_min;            // experts with this many rows or more go to the second list (INT_MAX: none)
     int big_chunk;          // rows per work item of the second list (4 row tiles per CTA)
     int* work_act4;         // second list: [W4_max]
@@ -85,9 +86,11 @@ struct MoeArgs {
     int seg_cap, nseg;
     const uint32_t* seg_wait;  // route_prep waits for seg_wait[g] >= *seg_seq, g < nseg, when set
     const uint32_t* seg_seq;
-    // One token (direct != 0): no routing metadata; work item k < K is the token's slot k (its
-    // expert inds[k] - e_lo, one row, slot id k), item K the folded shared expert; the down
-    // projection and the reduce run as moe_down1 (a cluster over the items per output block).
+    // Direct items (direct != 0): no routing metadata; work item w < w_routed is slot w (its expert
+    // inds[w] - e_lo, one row: w / K, slot id w), later items the folded shared expert's rows.  One
+    // token: the down projection and the reduce run as moe_down1 (a cluster over the items per
+    // output block).  An expert-parallel rank's small call: item w lives once its source's flag is
+    // up and its place is within the rows that source sent; moe_down writes the per-slot planes.
     int direct;
     // The reduce folded into moe_down (a one-group decode-chain layer, rounded output): rcount
     // [R][D/128] arrival counters, zeroed by route_prep; the last of a (token, output block)'s
@@ -166,7 +169,12 @@ struct WorkItem {
 // The item count and the item's record are loaded together (one round of global loads; a record
 // past the count is never used).
 __device__ __forceinline__ bool work_item(const MoeArgs& a, int w, WorkItem& it) {
-    if (a.direct && w < a.K) {
+    if (a.direct && w < a.w_routed) {
+        if (a.seg_cnt) {  // an expert-parallel rank's received place w / K: live once its source's rows arrived
+            const int place = w / a.K, g = place / a.seg_cap, i = place % a.seg_cap;
+            if (a.seg_wait) wait_flag(a.seg_wait + g, *a.seg_seq);
+            if (i >= min(max(a.seg_cnt[g], 0), a.seg_cap)) return false;
+        }
         const uint32_t e = a.inds[w] - (uint32_t)a.e_lo;
         if (e >= (uint32_t)a.E) return false;  // the slot's expert is in no expert of this launch
         it.e = (int)e;
@@ -191,6 +199,25 @@ __device__ __forceinline__ bool work_item(const MoeArgs& a, int w, WorkItem& it)
     it.first = rec.y;
     it.rows = rec.z;
     it.shx = false;
+    return true;
+}
+
+// work_item for the one-token down kernel (direct items, no expert-parallel segments).
+__device__ __forceinline__ bool work_item_token(const MoeArgs& a, int w, WorkItem& it) {
+    if (w < a.K) {
+        const uint32_t e = a.inds[w] - (uint32_t)a.e_lo;
+        if (e >= (uint32_t)a.E) return false;
+        it.e = (int)e;
+        it.first = w;
+        it.rows = 1;
+        it.shx = false;
+        return true;
+    }
+    if (w - a.K >= a.sh_items) return false;
+    it.e = 0;
+    it.first = 0;
+    it.rows = 1;
+    it.shx = true;
     return true;
 }
 
@@ -448,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, KIND == K_MCG && N <= 96 ? 3 : 2) mo
     __shared__ __align__(16) float fin_sv[128];
     __shared__ float fin_sc;
     WorkItem it;
-    const bool has = work_item(a, w, it);
+    const bool has = work_item_token(a, w, it);
     __syncthreads();
 
     if (warp == kConsumerWarps) {
@@ -519,18 +546,22 @@ __global__ void __launch_bounds__(kThreads, KIND == K_MCG && N <= 96 ? 3 : 2) mo
     }
     cluster.sync();
     if (w == 0 && warp == 0) {
-        float4 v[16];
-#pragma unroll
-        for (int k = 0; k < 16; k++)
-            if ((live >> k) & 1u) v[k] = *reinterpret_cast<const float4*>(cluster.map_shared_rank(fin, k) + lane * 4);
         float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int k = 0; k < 16; k++) {
-            if (!((live >> k) & 1u)) continue;
-            acc[0] += v[k].x;
-            acc[1] += v[k].y;
-            acc[2] += v[k].z;
-            acc[3] += v[k].w;
+        for (int k0 = 0; k0 < 16; k0 += 8) {  // eight ranks' loads in flight at a time
+            float4 v[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                if ((live >> (k0 + k)) & 1u)
+                    v[k] = *reinterpret_cast<const float4*>(cluster.map_shared_rank(fin, k0 + k) + lane * 4);
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                if (!((live >> (k0 + k)) & 1u)) continue;
+                acc[0] += v[k].x;
+                acc[1] += v[k].y;
+                acc[2] += v[k].z;
+                acc[3] += v[k].w;
+            }
         }
         if (a.sh_plane) {
             const float4 s4 = *reinterpret_cast<const float4*>(cluster.map_shared_rank(fin, a.K) + lane * 4);

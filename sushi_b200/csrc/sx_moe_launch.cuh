@@ -58,7 +58,7 @@ static int fit_split(int S, int KB, int mg) {
 template <int KIND, int N>
 static cudaError_t launch_pair_t(const MoeArgs& a, int S, int W_max, cudaStream_t stream) {
     const int KB = a.D / 128;
-    S = fit_split<N, 2>(S, KB, a.chunk);
+    S = fit_split<N, 2>(S, KB, a.split_chunk ? a.split_chunk : a.chunk);
     const CoreLayout L = core_layout<N, 2, 1>((KB + S - 1) / S, a.chunk);
     return launch_clustered(moe_pair_kernel<KIND, N>, dim3(W_max, a.I / 128, S), S, L.total, stream, a);
 }
@@ -66,7 +66,7 @@ static cudaError_t launch_pair_t(const MoeArgs& a, int S, int W_max, cudaStream_
 template <int KIND, int N>
 static cudaError_t launch_down_t(const MoeArgs& a, int S, int W_max, cudaStream_t stream) {
     const int KB = a.I / 128;
-    S = fit_split<N, 1>(S, KB, a.chunk);
+    S = fit_split<N, 1>(S, KB, a.split_chunk ? a.split_chunk : a.chunk);
     const CoreLayout L = core_layout<N, 1, 1>((KB + S - 1) / S, a.chunk);
     return launch_clustered(moe_down_kernel<KIND, N>, dim3(W_max, a.D / 128, S), S, L.total, stream, a);
 }
