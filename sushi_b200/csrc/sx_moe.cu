@@ -420,6 +420,22 @@ int min_split(long long units) {
     return (int)std::max(1LL, std::min(16LL, S));
 }
 
+// moe_pair's split over one row's items (the one-token chain, and an expert-parallel call whose
+// places hold one row): the largest S <= 16 whose CTAs (units * S) all fit at three per SM and
+// whose ranks all get input blocks (KB in chunks of ceil(KB / S)).  So few items still occupy
+// every SM with two or three CTAs of short k ranges, and an SM that holds one CTA more carries
+// less.  Measured on B200, 512 experts 2048/512, one token (11 items x 4 output blocks), the
+// routed call in a loop of calls: S = 3 / 4 / 6 / 8 / 16 took 36.0 / 30.0 / 28.0 / 24.7 / 34.5 us
+// (16: two waves).
+int one_row_split(long long units, int KB) {
+    const long long cap = (long long)sm_count() * 3;
+    for (int S = 16; S > 1; S--) {
+        const int chunk = (KB + S - 1) / S;
+        if (units * S <= cap && (KB + chunk - 1) / chunk == S) return S;
+    }
+    return min_split(units);
+}
+
 // Direct items of an expert-parallel rank's call at most (a few tokens per rank: every received
 // slot one item, most of them other ranks' sentinels that exit at once), and the down launch's
 // items x output blocks at most: past that the dead items' CTAs cost more than the routing pass
@@ -429,8 +445,10 @@ constexpr long long kDirectEpItems = 512;
 constexpr long long kDirectEpCtas = 2048;
 
 // The pair and down launches of the decode chain over `items` work items.
-cudaError_t chain_launch(const MoeArgs& a, int kind, int n_gu, int n_d, int items, int active, cudaStream_t s) {
-    const int S_gu = min_split((long long)active * (a.I / 128));
+cudaError_t chain_launch(const MoeArgs& a, int kind, int n_gu, int n_d, int items, int active, cudaStream_t s,
+                         bool one_row = false) {
+    const int S_gu = one_row ? one_row_split((long long)active * (a.I / 128), a.D / 128)
+                             : min_split((long long)active * (a.I / 128));
     const int S_d = min_split((long long)active * (a.D / 128));
     switch (kind) {
         case K_MCG: return moe_launch_kind<K_MCG>(a, n_gu, n_d, S_gu, S_d, items, s);
@@ -443,7 +461,7 @@ cudaError_t chain_launch(const MoeArgs& a, int kind, int n_gu, int n_d, int item
 
 // The one-token chain over W direct items (moe_pair, then moe_down1).
 cudaError_t chain_launch_direct(const MoeArgs& a, int kind, int n_gu, int n_d, int W, cudaStream_t s) {
-    const int S_gu = min_split((long long)W * (a.I / 128));
+    const int S_gu = one_row_split((long long)W * (a.I / 128), a.D / 128);
     switch (kind) {
         case K_MCG: return moe_launch_kind_direct<K_MCG>(a, n_gu, n_d, S_gu, W, s);
         case K_MUL1: return moe_launch_kind_direct<K_MUL1>(a, n_gu, n_d, S_gu, W, s);
@@ -642,7 +660,7 @@ sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_de
         a.w_routed = rows * topk;
         a.sh_items = fold ? sh_rows : 0;
         a.sh_slot0 = rows * topk;
-        e = chain_launch(a, kind_gu, bank->gate.n, bank->down.n, (int)ep_items, routed_active, s);
+        e = chain_launch(a, kind_gu, bank->gate.n, bank->down.n, (int)ep_items, routed_active, s, rows == 1);
         return e == cudaSuccess ? SX_OK : cuda_status(e, "moe expert-parallel direct chain launch");
     }
     const int direct_items = topk + (fold ? 1 : 0);
