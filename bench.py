@@ -243,6 +243,9 @@ def main():
     ap.add_argument("--profile", default=None, choices=["gemv", "moe", "gemm", "prefill"],
                     help="a small fixed case for ncu: --warmup launches, then --steps launches, no graphs")
     ap.add_argument("--profile-tokens", type=int, default=8, help="tokens of the --profile moe layer")
+    ap.add_argument("--profile-rows", type=int, default=1024, help="rows of the --profile gemm projection")
+    ap.add_argument("--profile-shape", default="4096x14336", choices=["4096x14336", "2048x7168", "7168x2048"],
+                    help="out x in of the --profile gemm projection")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -939,8 +942,9 @@ def deepseek_bench(sx, torch, args, stream, tf_peak):
 
 def run_profile(args):
     """ncu case: the 4096x14336 K2 (n32) M=1 projection (config 1's rate, the sweep's largest
-    shape) over 12 distinct weight copies (176 MB > L2), or the bench's MoE decode layer at
-    --profile-tokens tokens (8 by default)."""
+    shape) over 12 distinct weight copies (176 MB > L2); the tensor-core projection of
+    --profile-shape at K2 over --profile-rows rows (weight copies past twice L2); the prefill layer;
+    or the bench's MoE decode layer at --profile-tokens tokens (8 by default)."""
     import torch
 
     import sushi_b200 as sx
@@ -956,7 +960,9 @@ def run_profile(args):
         print("profile case done", flush=True)
         return
     if args.profile == "gemm":
-        in_f, out_f, n, copies, rows = 14336, 4096, 32, 4, 1024
+        out_f, in_f = (int(v) for v in args.profile_shape.split("x"))
+        n, rows = 32, args.profile_rows
+        copies = max(4, -(-2 * L2_BYTES // (in_f * out_f * n // 128)))  # weights past L2 between launches
         tr = torch.randint(-32768, 32768, (copies, in_f // 16, out_f // 16, n), dtype=torch.int16, device="cuda")
         su = (torch.randint(0, 2, (copies, in_f), device="cuda").half() * 2 - 1) * 0.05
         sv = torch.randint(0, 2, (copies, out_f), device="cuda").half() * 2 - 1
