@@ -14,7 +14,7 @@ namespace sx {
 
 template <int KIND>
 cudaError_t gemm_dispatch(const CUtensorMap& pmap, const GemmArgs& a, int n, int rt, int items, int S,
-                          cudaStream_t stream, bool pair);
+                          cudaStream_t stream, bool pair, int nt);
 
 // P[r][kb*128 + i] = f16(H128(f16(x[r]) * suh)) for one (row, 128-input block) per warp: the
 // reference's prepareInput (src/exl3/expert_exl3.zig:490-501).
@@ -35,11 +35,11 @@ __global__ void __launch_bounds__(256) prep_rows_kernel(const void* x, int xdt, 
     *reinterpret_cast<uint2*>(P + (size_t)r * in + base) = h;
 }
 
-// The TMA map of a [rows, in] f16 matrix read in (kGemmRows x 64) tiles, 128-byte swizzled.
-cudaError_t prep_map(CUtensorMap* m, const uint16_t* P, int rows, int in) {
+// The TMA map of a [rows, in] f16 matrix read in (box_rows x 64) tiles, 128-byte swizzled.
+cudaError_t prep_map(CUtensorMap* m, const uint16_t* P, int rows, int in, int box_rows) {
     const cuuint64_t dims[2] = {(cuuint64_t)in, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)in * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)kGemmKC, (cuuint32_t)kGemmRows};
+    const cuuint32_t box[2] = {(cuuint32_t)kGemmKC, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     // The driver entry point is looked up through the runtime, so the library loads on hosts
     // without a driver (its CPU-side tests) and needs no link against libcuda.
@@ -61,12 +61,12 @@ cudaError_t prep_map(CUtensorMap* m, const uint16_t* P, int rows, int in) {
 }
 
 cudaError_t gemm_launch(int kind, const CUtensorMap& pmap, const GemmArgs& a, int n, int rt, int items, int S,
-                        cudaStream_t stream, bool pair) {
+                        cudaStream_t stream, bool pair, int nt) {
     switch (kind) {
-        case K_MCG: return gemm_dispatch<K_MCG>(pmap, a, n, rt, items, S, stream, pair);
-        case K_MUL1: return gemm_dispatch<K_MUL1>(pmap, a, n, rt, items, S, stream, pair);
-        case K_HASH: return gemm_dispatch<K_HASH>(pmap, a, n, rt, items, S, stream, pair);
-        case K_PAIR1: return gemm_dispatch<K_PAIR1>(pmap, a, n, rt, items, S, stream, pair);
+        case K_MCG: return gemm_dispatch<K_MCG>(pmap, a, n, rt, items, S, stream, pair, nt);
+        case K_MUL1: return gemm_dispatch<K_MUL1>(pmap, a, n, rt, items, S, stream, pair, nt);
+        case K_HASH: return gemm_dispatch<K_HASH>(pmap, a, n, rt, items, S, stream, pair, nt);
+        case K_PAIR1: return gemm_dispatch<K_PAIR1>(pmap, a, n, rt, items, S, stream, pair, nt);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -163,8 +163,11 @@ extern "C" sx_status sx_linear_gemm(sx_stream stream, const sx_proj* proj, const
     prep_rows_kernel<<<(warps + 7) / 8, 256, 0, s>>>(x, dtype, proj->suh, rows, in, P);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_status(e, "prep launch");
+    // At most 16 rows: 16-row tiles (the MMA's N and the prepared-row copy cover the live rows, so
+    // a stage is 20 KB and the ring twice as deep); else 128-row tiles.
+    const int nt = rows <= kGemmRowsNarrow ? kGemmRowsNarrow : kGemmRows;
     CUtensorMap pmap;
-    if ((e = prep_map(&pmap, P, rows, in)) != cudaSuccess) return cuda_status(e, "cuTensorMapEncodeTiled");
+    if ((e = prep_map(&pmap, P, rows, in, nt)) != cudaSuccess) return cuda_status(e, "cuTensorMapEncodeTiled");
     GemmArgs a{};
     a.trellis = proj->trellis;
     a.tr_expert = 0;
@@ -178,8 +181,8 @@ extern "C" sx_status sx_linear_gemm(sx_stream stream, const sx_proj* proj, const
     a.y = y;
     a.ydt = dtype;
     const int rt = gemm_rt(rows, proj->n);
-    const int items = (rows + kGemmRows * rt - 1) / (kGemmRows * rt);
+    const int items = (rows + nt * rt - 1) / (nt * rt);
     const int S = gemm_split((long long)items * (out / 128), in / kGemmKC);
-    e = gemm_launch(kind, pmap, a, proj->n, rt, items, S, s, false);
+    e = gemm_launch(kind, pmap, a, proj->n, rt, items, S, s, false, nt);
     return cuda_status(e, "gemm launch");
 }

@@ -30,6 +30,7 @@ constexpr int kGemmDecWarps = 16;                       // decoders, then the ep
 constexpr int kGemmThreads = (kGemmDecWarps + 2) * 32;  // + producer warp + MMA warp
 constexpr int kGemmKC = 64;                             // inputs per stage (one 128-byte swizzle row)
 constexpr int kGemmRows = 128;                          // NT: rows per CTA tile (the MMA's N)
+constexpr int kGemmRowsNarrow = 16;                     // NT of a dense call of at most 16 rows
 
 enum GemmMode : int {
     GEMM_OUT_ACT = 0,   // y[row][o] in the activation dtype
@@ -71,18 +72,21 @@ struct GemmLayout {
     static constexpr int B_TILE = NT * kGemmKC * 2;     // 16 KB per row tile
     static constexpr int B_BYTES = (PAIR ? RT / 2 : RT) * B_TILE;
     static constexpr int T_BYTES = 4 * 8 * N * 2;       // 32 trellis tiles
-    // One row tile: as many stages as fit in 224 KB (5 or 6; at most 8), since a stage's cycle
-    // (copies, decode, MMA, commit) is longer than its decode and only the ring depth hides it.
+    // One row tile: as many stages as fit in 223 KB (5 or 6 at 128 rows, 10 or 11 at 16; at most
+    // 12), since a stage's cycle (copies, decode, MMA, commit) is longer than its decode and only
+    // the ring depth hides it.
     static constexpr int STAGE1 = 128 * kGemmKC * 2 + NT * kGemmKC * 2 + 4 * 8 * N * 2;
-    static constexpr int NST1 = (223 * 1024) / STAGE1 < 8 ? (223 * 1024) / STAGE1 : 8;
+    static constexpr int NST1 = (223 * 1024) / STAGE1 < 12 ? (223 * 1024) / STAGE1 : 12;
     static constexpr int NST = PAIR ? 4 : (RT == 1 ? NST1 : (RT == 2 ? 3 : 2));
-    static constexpr int TMEM_COLS = NT * RT;
+    static constexpr int TMEM_COLS = NT * RT < 32 ? 32 : NT * RT;  // an allocation is 32 columns at least
     static constexpr int A_OFF = 0;
     static constexpr int B_OFF = A_OFF + NST * A_BYTES;
     static constexpr int T_OFF = B_OFF + NST * B_BYTES;
     static constexpr int BAR_OFF = (T_OFF + NST * T_BYTES + 15) / 16 * 16;
     static constexpr int TOTAL = BAR_OFF + (5 * NST + 1) * 8 + 16;
-    static constexpr int RED_BYTES = NT * 128 * 4;      // one row tile's accumulator in f32, reusing A and B
+    // one row tile's accumulator in f32, reusing A and B (32 rows at least: the epilogue moves
+    // tensor memory out 32 columns at a time)
+    static constexpr int RED_BYTES = (NT < 32 ? 32 : NT) * 128 * 4;
     static_assert(RED_BYTES <= T_OFF, "accumulator staging fits in the A/B ring");
     static_assert(TMEM_COLS <= 512, "tensor memory holds 512 columns");
     static_assert(!PAIR || RT == 4, "the pair kernel holds two 256-row blocks");

@@ -11,9 +11,8 @@ namespace sx {
 // no cluster waits for another to drain (cached per kernel, cluster count and split); 1 if none.
 int gemm_coresident_split(const void* kern, int smem, int threads, dim3 grid_xy, int S);
 
-template <int KIND, int N, int RT, bool PAIR = false>
+template <int KIND, int N, int RT, bool PAIR = false, int NT = kGemmRows>
 static cudaError_t launch_gemm_t(const CUtensorMap& pmap, const GemmArgs& a, int items, int S, cudaStream_t stream) {
-    constexpr int NT = kGemmRows;
     if (PAIR && (S != 1 || (a.out / 128) % 2)) return cudaErrorInvalidValue;  // pairs: no split, even blocks
     auto kern = gemm_kernel<KIND, N, NT, RT, false, PAIR>;
     const int smem = GemmLayout<N, NT, RT, PAIR>::ALLOC;
@@ -51,9 +50,12 @@ static cudaError_t launch_gemm_t(const CUtensorMap& pmap, const GemmArgs& a, int
 
 template <int KIND>
 cudaError_t gemm_dispatch(const CUtensorMap& pmap, const GemmArgs& a, int n, int rt, int items, int S,
-                          cudaStream_t stream, bool pair) {
+                          cudaStream_t stream, bool pair, int nt) {
+    const bool narrow = nt == kGemmRowsNarrow;
+    if (nt != kGemmRows && (!narrow || rt != 1 || pair)) return cudaErrorInvalidValue;
 #define SX_CASE(NN) \
-    case NN: return launch_gemm_t<KIND, NN, 1>(pmap, a, items, S, stream);
+    case NN: return narrow ? launch_gemm_t<KIND, NN, 1, false, kGemmRowsNarrow>(pmap, a, items, S, stream) \
+                           : launch_gemm_t<KIND, NN, 1>(pmap, a, items, S, stream);
 #define SX_CASE4(NN) \
     case NN: return pair ? launch_gemm_t<KIND, NN, 4, true>(pmap, a, items, S, stream) \
                          : launch_gemm_t<KIND, NN, 4>(pmap, a, items, S, stream);

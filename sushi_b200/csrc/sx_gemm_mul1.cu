@@ -2,5 +2,5 @@
 #include "sx_gemm_launch.cuh"
 
 namespace sx {
-template cudaError_t gemm_dispatch<K_MUL1>(const CUtensorMap&, const GemmArgs&, int, int, int, int, cudaStream_t, bool);
+template cudaError_t gemm_dispatch<K_MUL1>(const CUtensorMap&, const GemmArgs&, int, int, int, int, cudaStream_t, bool, int);
 }  // namespace sx

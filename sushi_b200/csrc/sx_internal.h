@@ -17,13 +17,16 @@ int sm_count();
 struct GemmArgs;
 // The tensor-core projection (sx_gemm.cu): the TMA map of a [rows, in] f16 matrix of prepared
 // rows, the split-K choice, and the launch over codebook families and rates.
-cudaError_t prep_map(CUtensorMap* m, const uint16_t* P, int rows, int in);
+// box_rows: the rows of one tile (the launch's NT: 128, or 16 for a dense call of at most 16 rows).
+cudaError_t prep_map(CUtensorMap* m, const uint16_t* P, int rows, int in, int box_rows);
 int gemm_split(long long ctas, int chunks);
 int gemm_rt(long long rows, int n);
 bool gemm_rt_rate(int n);  // rates with four-row-tile tensor-core kernels
 // pair: the CTA-pair (cta_group::2) kernel for rt == 4 (no split, an even count of output blocks).
+// nt: rows per tile, 128, or 16 (one row tile, no pair: the MMA's N and the prepared-row tile are
+// the 16 live rows).
 cudaError_t gemm_launch(int kind, const CUtensorMap& pmap, const GemmArgs& a, int n, int rt, int items, int S,
-                        cudaStream_t stream, bool pair = false);
+                        cudaStream_t stream, bool pair = false, int nt = 128);
 
 // sx_moe's body; with `partial` set, the routed k-order sums land there in f32, unrounded and
 // without the shared expert (an expert-parallel rank's share of its peers' tokens), and y is unused.

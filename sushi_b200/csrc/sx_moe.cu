@@ -696,8 +696,9 @@ sx_status moe_group(sx_stream stream, const sx_bank* bank, int e_lo, const sx_de
         moe_prep_kernel<<<dim3(pos_grid.x, D / 128), 256, 0, s>>>(a);
         if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e, "moe prep launch");
         CUtensorMap mg, mu, mh;
-        if ((e = prep_map(&mg, a.tg, RK, D)) != cudaSuccess || (e = prep_map(&mu, a.tu, RK, D)) != cudaSuccess ||
-            (e = prep_map(&mh, a.hprep, RK, I)) != cudaSuccess)
+        if ((e = prep_map(&mg, a.tg, RK, D, kGemmRows)) != cudaSuccess ||
+            (e = prep_map(&mu, a.tu, RK, D, kGemmRows)) != cudaSuccess ||
+            (e = prep_map(&mh, a.hprep, RK, I, kGemmRows)) != cudaSuccess)
             return cuda_status(e, "cuTensorMapEncodeTiled");
         // two launches per projection: list 1 (chunks of 128 rows, one row tile per CTA) and list 2
         // (chunks of 512 rows of the experts with many rows, four row tiles per CTA)

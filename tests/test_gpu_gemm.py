@@ -68,6 +68,16 @@ def test_gemm_codebooks(sx, cb, w, n):
     _check(sx, 512, 256, n, 24, cb=cb, w=w)
 
 
+@pytest.mark.parametrize("rows", [1, 7, 16])
+def test_gemm_sixteen_row_tiles(sx, rows):
+    """At most 16 rows the projection runs 16-row tiles (MMA N = 16, a 16-row prepared-row copy):
+    the same result bar, over codebooks and a k split."""
+    _check(sx, 2048, 512, 32, rows)
+    _check(sx, 512, 256, 24, rows, cb=orc.CB_PAIR1)
+    _check(sx, 512, 256, 32, rows, cb=orc.CB_MUL1)
+    _check(sx, 7168, 256, 48, rows, cb=orc.CB_STD1)
+
+
 @pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
 def test_gemm_dtypes(sx, dtype):
     _check(sx, 512, 256, 32, 20, dtype=dtype)
