@@ -7,7 +7,8 @@ the C ABI twice in a row and hold each result to the workspace entry point's out
 bar the other parity tests use (and, since the kernels are the same, expect the very same bits);
 at the decode sizes of BASELINE configs[2] (512 experts, hidden 2048, intermediate 512, K2, top-10,
 one and 64 tokens, which fit the buffer) they also hold it to the oracle's f64 truth.  They check
-the refusal above the buffer's size and that a malformed call gets sx_moe's own refusal.
+the refusal above the buffer's size and that a malformed call gets sx_moe's own refusal, and they
+capture the call into a CUDA graph and replay it over new inputs.
 Collected last (file name) so a failure here leaves every other test already run; it depends on
 no state another test leaves behind.
 """
@@ -70,6 +71,56 @@ def test_static_scratch_moe_matches_workspace_moe_twice_in_a_row():
         assert np.isfinite(got).all()
         assert max_rel(got, want) <= MAX_REL_TOL
         np.testing.assert_array_equal(got, want)
+
+
+def test_static_scratch_moe_replays_from_a_cuda_graph():
+    """The use the entry point exists for: one warm call, the layer captured into a CUDA graph
+    (no allocation, no host read inside), then replays over new inputs written into the captured
+    buffers; each replay gives sx_moe's bits for the inputs of that replay."""
+    import sushi_b200 as sx
+    from sushi_b200 import _lib
+
+    L = _lib.load()
+    E, D, I, k, T = 16, 512, 256, 4, 5
+    bank, _ = _bank(sx, E, D, I, 32, seed=940)
+    dec = sx.Decode(sx.Codebook.MCG, 16)
+    b, d = bank.c(), dec.c()
+    rng = np.random.default_rng(41)
+
+    def route():
+        ii = np.stack([rng.choice(E, k, replace=False) for _ in range(T)]).astype(np.int32)
+        return torch.from_numpy(ii).cuda(), torch.from_numpy((0.1 + rng.random((T, k)) * 0.3).astype(np.float32)).cuda()
+
+    x = torch.randn((T, D), device="cuda").to(torch.bfloat16)
+    inds, scores = route()
+    y = torch.empty((T, D), device="cuda", dtype=torch.bfloat16)
+    stream = torch.cuda.Stream()
+
+    def call():
+        h = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        st = L.sx_moe_static_scratch(h, ctypes.byref(b), ctypes.byref(d), x.data_ptr(), 2, T, inds.data_ptr(),
+                                     scores.data_ptr(), k, None, None, 0, y.data_ptr())
+        assert st == 0, L.sx_status_name(st).decode()
+
+    with torch.cuda.stream(stream):
+        call()  # warm: kernel attributes are set outside the capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        call()
+    for rep in range(2):
+        x.copy_(torch.randn((T, D), device="cuda").to(torch.bfloat16))
+        ni, ns = route()
+        inds.copy_(ni)
+        scores.copy_(ns)
+        y.fill_(float("nan"))
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        want = sx.moe(x, bank, inds, scores, dec)
+        assert torch.equal(y, want), rep
+    del g
+    assert L.sx_device_error(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
 
 
 @pytest.fixture(scope="module")
